@@ -1,0 +1,178 @@
+/*
+ * b200moe.h -- C ABI of the B200 (sm_100a) routed-expert MoE layer.
+ *
+ * This is the drop-in boundary for the reference build's routed-expert
+ * FusedMoE quant-method plugin.  Reference interfaces replaced (paths relative
+ * to the reference project; EXP = engine/src/vllm/model_executor/layers/fused_moe/experts):
+ *
+ *   b200moe_layer_create / _destroy   NativeV41Moe.__init__ / three_tier
+ *                                     (EXP/nvfp4_8r_native.py:645-745, 770-808):
+ *                                     fixed buffers sized for max_tokens, all
+ *                                     kernels ready before any graph capture.
+ *   b200moe_set_slot_maps             tiers.slot_maps -> slot_of_expert maps
+ *                                     (EXP/nvfp4_8r_tiers.py:169-179;
+ *                                     EXP/nvfp4_8r_native.py:687-717).
+ *   b200moe_load_fp4 / _load_iq2      NativeExpertSet.from_raw / IqWarmBank
+ *                                     (EXP/nvfp4_8r_native.py:275-323, 522-570):
+ *                                     records into HBM in the kernels' layout.
+ *   b200moe_route                     the engine router that produces
+ *                                     (topk_ids, topk_weights) ahead of
+ *                                     engine/patches/gguf_moe.patch:53.
+ *   b200moe_forward                   NativeV41Moe.forward
+ *                                     (EXP/nvfp4_8r_native.py:913-961): decode,
+ *                                     1 <= M <= max_tokens, no host sync, no
+ *                                     allocation, CUDA-graph capturable.
+ *   b200moe_forward_prefill           NativeV41Moe.forward_prefill
+ *                                     (EXP/nvfp4_8r_native.py:970-1094): any
+ *                                     T <= max_prefill_tokens.
+ *   b200moe_route_plan                GroupPlanner.plan / the _compact chain
+ *                                     (EXP/nvfp4_8r_group_plan.py:163-332;
+ *                                     EXP/nvfp4_8r_native.py:806-889): the
+ *                                     reference's perm / gids / goff / iq tables.
+ *   b200moe_quantize_nvfp4 / _mxfp4   offline packing (the reference's packs were
+ *   b200moe_fold_nvfp4_to_mxfp4       made by NVIDIA and folded by
+ *                                     harness/benchmarks/nvfp4_8r/build_packs.py:120-151).
+ *
+ * Conventions: every function returns an int status (b200moe_status).  Device
+ * pointers are plain CUDA device addresses on the layer's device; `stream` is a
+ * cudaStream_t passed as void*.  Nothing here allocates after create, and
+ * nothing in forward / forward_prefill / route synchronizes with the host.
+ */
+#ifndef B200MOE_H_
+#define B200MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  B200MOE_OK = 0,
+  B200MOE_ERR_INVALID_ARG = 1, /* shape, count, pointer or config refused on the host */
+  B200MOE_ERR_DTYPE = 2,       /* unsupported dtype code */
+  B200MOE_ERR_ALIGN = 3,       /* a pointer without the alignment the layout needs */
+  B200MOE_ERR_CUDA = 4,        /* a CUDA runtime call failed */
+  B200MOE_ERR_BOUNDS = 5,      /* a kernel found an id, slot or offset out of range */
+  B200MOE_ERR_TIMEOUT = 6,     /* a bounded device wait ran out */
+  B200MOE_ERR_FORMAT = 7,      /* a packed value the format forbids (E4M3 NaN, E8M0 255) */
+  B200MOE_ERR_RANGE = 8,       /* a value the kernel layout cannot hold */
+  B200MOE_ERR_NOMEM = 9,       /* device allocation failed at create */
+  B200MOE_ERR_STATE = 10       /* call out of order (weights or maps not set) */
+} b200moe_status;
+
+typedef enum { B200MOE_F16 = 0, B200MOE_BF16 = 1, B200MOE_F32 = 2 } b200moe_dtype;
+
+typedef enum { B200MOE_NVFP4 = 0, B200MOE_MXFP4 = 1, B200MOE_IQ2XXS = 2 } b200moe_format;
+
+/* Shape and residency of one layer on one GPU.  Bank 0 holds FP4 experts
+ * (NVFP4 or MXFP4), bank 1 IQ2_XXS experts; the slot maps say which expert id
+ * sits in which slot of which bank. */
+typedef struct {
+  int32_t hidden;             /* H: multiple of 256 */
+  int32_t inter;              /* I: multiple of 128 (256 when bank 1 is used) */
+  int32_t num_experts;        /* E: global expert ids 0..E-1, E <= 1024 */
+  int32_t top_k;              /* k: 1..16 */
+  int32_t max_tokens;         /* decode M limit of b200moe_forward, 1..64 */
+  int32_t max_prefill_tokens; /* T limit of forward_prefill (0: no prefill workspace) */
+  int32_t fp4_format;         /* B200MOE_NVFP4 or B200MOE_MXFP4 */
+  int32_t n_fp4;              /* slots in bank 0 */
+  int32_t n_iq2;              /* slots in bank 1 */
+  float swiglu_limit;         /* limited SwiGLU bound (reference: 10.0) */
+} b200moe_config;
+
+typedef struct b200moe_layer b200moe_layer;
+
+const char* b200moe_status_name(int status);
+/* Library version string and the CUDA architecture it was built for. */
+const char* b200moe_version(void);
+
+int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** out);
+int b200moe_layer_destroy(b200moe_layer* layer);
+
+/* Host int32 [E] maps: slot of each expert in bank 0 / bank 1, -1 where absent.
+ * Every expert must sit in exactly one bank, and each bank's slots must be
+ * covered exactly once. */
+int b200moe_set_slot_maps(b200moe_layer* layer, const int32_t* fp4_slot, const int32_t* iq2_slot);
+
+/* IQ2_XXS codebook: grid int8 [256][8] and ksigns uint8 [128] (host). */
+int b200moe_set_iq2_tables(b200moe_layer* layer, const int8_t* grid, const uint8_t* ksigns);
+
+/* Load n consecutive bank-0 slots from natural-layout device arrays:
+ *   w13_codes [n][2I][H/2] (W1 rows then W3 rows, low nibble = even element),
+ *   w13_scales [n][2I][H/bs], w2_codes [n][H][I/2], w2_scales [n][H][I/bs],
+ *   bs = 16 (E4M3, NVFP4) or 32 (E8M0, MXFP4);
+ *   globals: device float [n][3] = (W1, W3, W2) FP32 global scales for NVFP4;
+ *   ignored (may be NULL) for MXFP4. */
+int b200moe_load_fp4(b200moe_layer* layer, void* stream, int slot_begin, int n,
+                     const uint8_t* w13_codes, const uint8_t* w13_scales, const uint8_t* w2_codes,
+                     const uint8_t* w2_scales, const float* globals);
+
+/* Load n consecutive bank-1 slots from ggml IQ2_XXS blocks (66 bytes per 256):
+ * w1, w3 [n][I][H/256][66], w2 [n][H][I/256][66] (device). */
+int b200moe_load_iq2(b200moe_layer* layer, void* stream, int slot_begin, int n, const uint8_t* w1,
+                     const uint8_t* w3, const uint8_t* w2);
+
+/* Router: logits fp32 [T][E] -> topk_ids int32 [T][k], topk_weights fp32 [T][k]:
+ * softmax top-k with renormalised weights (ties to the smaller id). */
+int b200moe_route(b200moe_layer* layer, void* stream, const float* logits, int32_t* topk_ids,
+                  float* topk_weights, int T);
+
+/* Decode forward: x [M][H] (f16 or bf16), ids int32 [M][k], weights fp32 [M][k]
+ * -> out fp32 [M][H] = sum over slots (slot order) of w * expert(x). */
+int b200moe_forward(b200moe_layer* layer, void* stream, const void* x, int x_dtype,
+                    const int32_t* topk_ids, const float* topk_weights, float* out, int M);
+
+/* Prefill forward: same contract for any 1 <= T <= max_prefill_tokens. */
+int b200moe_forward_prefill(b200moe_layer* layer, void* stream, const void* x, int x_dtype,
+                            const int32_t* topk_ids, const float* topk_weights, float* out, int T);
+
+/* Wait for `stream`, then read and clear the layer's kernel error word.
+ * Returns the status the bits map to (B200MOE_OK when none); *bits gets them. */
+int b200moe_check_errors(b200moe_layer* layer, void* stream, uint32_t* bits);
+
+/* Debug taps.  set_debug_y13 (device pointer or NULL): the W13 launch also
+ * writes y13 fp16 [rows][2I] by route position.  debug_perm copies the route
+ * permutation of the last forward (route index at each sorted position) into
+ * dst (device int32 [n]) on `stream`. */
+int b200moe_set_debug_y13(b200moe_layer* layer, void* y13);
+int b200moe_debug_perm(const b200moe_layer* layer, void* stream, int32_t* dst, int n);
+/* Copy the SwiGLU output rows (fp16 [rows][I], by sorted route position) of the
+ * last forward into dst (device). */
+int b200moe_debug_inter(const b200moe_layer* layer, void* stream, void* dst, int rows);
+
+/* Timing hook: with n > 0 cudaEvent_t handles, forward / forward_prefill
+ * record events[0] on the stream before their first launch and events[j + 1]
+ * after launch j ([bf16 copy], plan, W13 per bank, W2 per bank).  n = 0 turns
+ * it off.  The events stay owned by the caller. */
+int b200moe_set_timing_events(b200moe_layer* layer, void* const* events, int n);
+
+/* Reference route plan (GroupPlanner.plan semantics), one launch:
+ *   key = hot_slot[id] if >= 0, else (split) n_hot + second_slot[id] if >= 0,
+ *   else n_hot + n_second; perm = stable sort of keys; gids_hot/goff_hot the
+ *   HBM launch tables; with `host` the rotated second-launch tables; with
+ *   iq_slot non-NULL the IQ slot of every route.  n <= 4096 routes. */
+int b200moe_route_plan(void* stream, const int32_t* ids, int n, int num_experts,
+                       const int32_t* hot_slot, const int32_t* second_slot, int n_hot, int n_second,
+                       int split, int host, const int32_t* iq_slot, int32_t* perm,
+                       int32_t* gids_hot, int32_t* goff_hot, int32_t* gids_host, int32_t* goff_host,
+                       int32_t* iq_out, uint32_t* err);
+
+/* Packing (device arrays): fp32 W [rows][k] -> NVFP4 codes [rows][k/2],
+ * E4M3 scales [rows][k/16], global (device float, one) / MXFP4 codes and E8M0
+ * [rows][k/32].  Same rounding as the oracle: RNE, ties to even, saturating. */
+int b200moe_quantize_nvfp4(void* stream, const float* w, int rows, int k, uint8_t* codes,
+                           uint8_t* scales, float* global_scale);
+int b200moe_quantize_mxfp4(void* stream, const float* w, int rows, int k, uint8_t* codes,
+                           uint8_t* e8m0, uint32_t* err);
+/* Exact NVFP4 -> MXFP4 fold; a block that cannot fold sets kErrRange in *err. */
+int b200moe_fold_nvfp4_to_mxfp4(void* stream, const uint8_t* codes, const uint8_t* scales,
+                                const float* global_scale, int rows, int k, uint8_t* out_codes,
+                                uint8_t* out_e8m0, uint32_t* err);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200MOE_H_ */

@@ -1,0 +1,369 @@
+"""GPU parity of the CUDA path (through the C ABI) against the oracle.
+
+Bit-exact: packing (NVFP4 / MXFP4 quantizers, the fold), the route plan
+(against the reference's own tables), gating, the SwiGLU step.  Tolerance:
+layer outputs within rel-L2 1e-2 of the fp32 dequant-then-matmul reference
+(the reference's own acceptance rule, harness/benchmarks/nvfp4_8r/accept_p2.py:36).
+"""
+
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import golden_inputs as gi
+import torch_ref as tr
+from oracle import moe_oracle as mo
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+TOL = 1e-2  # rel-L2 of a layer output vs the fp32 dequant reference
+
+
+@pytest.fixture(scope="module")
+def dev(pkg):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    d = torch.device("cuda", 0)
+    torch.cuda.set_device(d)
+    return d
+
+
+def sha(a) -> str:
+    import hashlib
+
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+# ------------------------------------------------------------------ packing
+def _quant_inputs():
+    rng = np.random.default_rng(7)
+    w = rng.normal(0, 0.02, (256, 2048)).astype(np.float32)
+    w[3, :16] = 0.0                                     # all-zero block
+    w[4, :32] = -0.0                                    # negative zeros
+    w[5, 16:32] = np.float32(0.001) * mo.E2M1_MAG[rng.integers(0, 8, 16)]  # exact grid values
+    w[6, :] = rng.normal(0, 50.0, 2048)                 # large values
+    w[7, 32:64] = 1e-30                                 # tiny values
+    return w
+
+
+def test_quantize_nvfp4_bit_exact(dev, pkg):
+    from b200moe import packing
+
+    w = _quant_inputs()
+    c, s, g = packing.quantize_nvfp4(torch.from_numpy(w).to(dev))
+    rc, rs, rg = mo.nvfp4_quantize(w)
+    assert np.float32(g.item()).view(np.uint32) == np.float32(rg).view(np.uint32)
+    assert np.array_equal(s.cpu().numpy(), rs)
+    assert np.array_equal(c.cpu().numpy(), rc)
+
+
+def test_quantize_mxfp4_bit_exact(dev, pkg):
+    from b200moe import packing
+
+    w = _quant_inputs()
+    c, e = packing.quantize_mxfp4(torch.from_numpy(w).to(dev))
+    rc, re_ = mo.mxfp4_quantize(w)
+    assert np.array_equal(e.cpu().numpy(), re_)
+    assert np.array_equal(c.cpu().numpy(), rc)
+
+
+def test_fold_matches_reference_golden(dev, pkg):
+    from b200moe import packing
+
+    with np.load(GOLDEN / "packing.npz") as z:
+        meta = json.loads(bytes(z["meta"]).decode())
+    codes, bits, glob = gi.fold_inputs(True)
+    oc, oe = packing.fold_nvfp4_to_mxfp4(torch.from_numpy(codes).to(dev), torch.from_numpy(bits).to(dev),
+                                         torch.tensor([glob], device=dev))
+    assert sha(oc.cpu().numpy()) == meta["fold_ok"]["codes_sha256"]
+    assert sha(oe.cpu().numpy()) == meta["fold_ok"]["scales_sha256"]
+    codes, bits, glob = gi.fold_inputs(False)
+    with pytest.raises(packing.PackError, match="cannot fold"):
+        packing.fold_nvfp4_to_mxfp4(torch.from_numpy(codes).to(dev), torch.from_numpy(bits).to(dev),
+                                    torch.tensor([glob], device=dev))
+
+
+# ------------------------------------------------------------------ routing
+def test_route_plan_matches_reference_golden(dev, pkg):
+    from b200moe import packing
+
+    with np.load(GOLDEN / "route_plan.npz") as z:
+        data = {k: z[k] for k in z.files}
+    meta = json.loads(bytes(data["meta"]).decode())
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.int32)).to(dev)  # noqa: E731
+    for c in meta:
+        j, kind = c["map"], c["kind"]
+        ids = data[f"c{c['case']}_ids"]
+        hot, cold, host, iq = (data[f"map{j}_{n}"] for n in ("hot", "cold", "host", "iq"))
+        if kind == "resident":
+            got = packing.route_plan(t(ids), t(hot), None, 384)
+        elif kind == "two_tier":
+            got = packing.route_plan(t(ids), t(hot), t(cold), c["n_hot"], c["n_cold"], host=True)
+        else:
+            got = packing.route_plan(t(ids), t(hot), t(host), c["n_hot"], c["n_cold"], host=c["host_in_decode"],
+                                     iq_slot=t(iq))
+            assert np.array_equal(got["iq"].cpu().numpy(), data[f"c{c['case']}_iq"].reshape(-1))
+        want = [(data[f"c{c['case']}_l{li}_perm"], data[f"c{c['case']}_l{li}_gids"],
+                 data[f"c{c['case']}_l{li}_goff"]) for li in range(c["launches"])]
+        assert np.array_equal(got["perm"].cpu().numpy(), want[0][0]), c
+        assert np.array_equal(got["gids_hot"].cpu().numpy(), want[0][1]), c
+        assert np.array_equal(got["goff_hot"].cpu().numpy(), want[0][2]), c
+        if len(want) == 2:
+            assert np.array_equal(got["gids_host"].cpu().numpy(), want[1][1]), c
+            assert np.array_equal(got["goff_host"].cpu().numpy(), want[1][2]), c
+
+
+def test_route_plan_large_and_repeated(dev, pkg):
+    from b200moe import packing
+
+    rng = np.random.default_rng(9)
+    tier = rng.choice([0, 1, 2], 384, p=[0.5, 0.3, 0.2]).astype(np.int8)
+    maps = mo.slot_maps(tier)
+    n_hot, n_cold = int((tier == 0).sum()), int((tier != 0).sum())
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.int32)).to(dev)  # noqa: E731
+    for ids in (rng.integers(0, 384, (512, 8)), np.full((64, 8), 7), rng.integers(0, 384, (4096, 1))):
+        got = packing.route_plan(t(ids), t(maps["hot"]), t(maps["host"]), n_hot, n_cold, host=True,
+                                 iq_slot=t(maps["iq"]))
+        want = mo.group_plan(ids, maps["hot"], maps["host"], n_hot, n_cold, True, True, maps["iq"])
+        for k, v in want.items():
+            assert np.array_equal(got[k].cpu().numpy(), v), k
+
+
+def test_gating_bit_exact(dev, pkg):
+    from b200moe import moe, tiers
+
+    for (T, E, K) in ((8, 64, 6), (64, 384, 8), (300, 384, 8)):
+        layer = moe.B200NativeMoe(hidden=256, inter=128, num_experts=E, top_k=K, max_tokens=8,
+                                  tier=np.zeros(E, np.int8), device=dev)
+        rng = np.random.default_rng(T)
+        lg = rng.normal(0, 1, (T, E)).astype(np.float32)
+        lg[0, :5] = 0.25  # ties
+        lg[1, 7] = lg[1, 9] = 3.0
+        ids, w = layer.route(torch.from_numpy(lg).to(dev))
+        rid, rw = mo.route(lg, K)
+        assert np.array_equal(ids.cpu().numpy(), rid)
+        assert np.array_equal(w.cpu().numpy().view(np.uint32), rw.view(np.uint32))
+        layer.close()
+        del tiers
+
+
+# --------------------------------------------------------------- layers
+def _fp4_dequant(bank, fmt, inter):
+    def dq(e):
+        if fmt == "nvfp4":
+            g = bank.globals[e]
+            w13 = torch.cat([tr.nvfp4_decode(bank.w13_codes[e, :inter], bank.w13_scales[e, :inter], g[0]),
+                             tr.nvfp4_decode(bank.w13_codes[e, inter:], bank.w13_scales[e, inter:], g[1])])
+            return w13, tr.nvfp4_decode(bank.w2_codes[e], bank.w2_scales[e], g[2])
+        return (tr.mxfp4_decode(bank.w13_codes[e], bank.w13_scales[e]),
+                tr.mxfp4_decode(bank.w2_codes[e], bank.w2_scales[e]))
+    return dq
+
+
+def _make_layer(dev, H, I, E, K, max_tokens, fmt="nvfp4", tier=None, seed=0, max_prefill=0):
+    from b200moe import moe, synth, tiers
+
+    tier = np.zeros(E, np.int8) if tier is None else tier
+    layer = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K, max_tokens=max_tokens, tier=tier,
+                              fp4_format=fmt, device=dev, max_prefill_tokens=max_prefill)
+    n_hot, n_iq = int((tier == tiers.HOT).sum()), int((tier == tiers.WARM).sum())
+    fp4 = synth.make_fp4_bank(n_hot, H, I, fmt, seed, dev) if n_hot else None
+    iq2 = synth.make_iq2_bank(n_iq, H, I, seed + 1, dev) if n_iq else None
+    if fp4 is not None:
+        synth.load_bank(layer, fp4)
+    if iq2 is not None:
+        layer.set_iq2_tables()
+        synth.load_bank(layer, iq2)
+    layer.check_errors()
+    grid, ksigns = mo.iq2xxs_tables()
+    fp4_dq = _fp4_dequant(fp4, fmt, I) if fp4 is not None else None
+
+    def dequant(e):
+        if tier[e] == tiers.HOT:
+            return fp4_dq(int(layer.fp4_slot[e]))
+        s = int(layer.iq2_slot[e])
+        return (torch.cat([tr.iq2xxs_decode(iq2.w1[s], grid, ksigns), tr.iq2xxs_decode(iq2.w3[s], grid, ksigns)]),
+                tr.iq2xxs_decode(iq2.w2[s], grid, ksigns))
+
+    return layer, dequant, fp4, iq2
+
+
+def test_torch_ref_matches_oracle(dev, pkg):
+    codes, scales, glob = gi.nvfp4_decode_inputs()
+    a = tr.nvfp4_decode(torch.from_numpy(codes[:64]).to(dev), torch.from_numpy(scales[:64]).to(dev), glob)
+    assert np.array_equal(a.cpu().numpy().view(np.uint32), mo.nvfp4_decode(codes[:64], scales[:64], glob).view(np.uint32))
+    grid, ksigns = mo.iq2xxs_tables()
+    blocks = gi.iq2_inputs()
+    b = tr.iq2xxs_decode(torch.from_numpy(blocks).to(dev), grid, ksigns)
+    assert np.array_equal(b.cpu().numpy().view(np.uint32), mo.iq2xxs_decode(blocks, grid, ksigns).view(np.uint32))
+
+
+def test_c0_layer_vs_numpy_oracle(dev, pkg):
+    """Config 0: T=8, hidden 2048, 64 experts, top-6, I=1408, NVFP4, bf16 x."""
+    H, I, E, K, T = 2048, 1408, 64, 6, 8
+    layer, _, bank, _ = _make_layer(dev, H, I, E, K, 8, seed=0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
+    router = torch.randn((E, H), generator=g, device=dev) * 0.02
+    logits = (x.float() @ router.T).contiguous()
+    ids, w = layer.route(logits)
+    out = layer.forward(x, ids, w).clone()
+    layer.check_errors()
+    nb = {k: v.cpu().numpy() for k, v in vars(bank).items() if isinstance(v, torch.Tensor)}
+
+    def dequant(e):
+        gl = nb["globals"][e]
+        return (np.concatenate([mo.nvfp4_decode(nb["w13_codes"][e, :I], nb["w13_scales"][e, :I], gl[0]),
+                                mo.nvfp4_decode(nb["w13_codes"][e, I:], nb["w13_scales"][e, I:], gl[1])]),
+                mo.nvfp4_decode(nb["w2_codes"][e], nb["w2_scales"][e], gl[2]))
+
+    rid, rw = mo.route(logits.cpu().numpy(), K)
+    assert np.array_equal(ids.cpu().numpy(), rid)
+    ref = mo.layer_forward(x.float().cpu().numpy(), rid, rw, dequant)
+    err = mo.rel_l2(out.cpu().numpy(), ref)
+    assert err < TOL, err
+    # dequant against fp32 (config 0's check): decode = the fp32 weights' nearest grid values
+    layer.close()
+
+
+@pytest.fixture(scope="module")
+def c1(dev, pkg):
+    layer, dequant, bank, _ = _make_layer(dev, 4096, 2048, 384, 8, 64, seed=1000)
+    yield layer, dequant
+    layer.close()
+
+
+@pytest.mark.parametrize("m", [1, 8, 32, 64])
+def test_c1_decode_layer(dev, c1, m):
+    layer, dequant = c1
+    g = torch.Generator(device=dev).manual_seed(1000 + m)
+    x = torch.randn((m, 4096), generator=g, device=dev).to(torch.bfloat16)
+    logits = torch.randn((m, 384), generator=g, device=dev)
+    ids, w = layer.route(logits)
+    out = layer.forward(x, ids, w).clone()
+    layer.check_errors()
+    ref = tr.layer_forward(x, ids.long(), w, dequant)
+    err = tr.rel_l2(out, ref)
+    assert err < TOL, err
+    again = layer.forward(x, ids, w).clone()
+    assert torch.equal(out, again), "forward is not deterministic"
+
+
+def test_c1_graph_replay_equals_eager(dev, c1):
+    layer, _ = c1
+    m = 6
+    g = torch.Generator(device=dev).manual_seed(77)
+    x = torch.randn((m, 4096), generator=g, device=dev).to(torch.float16)
+    ids, w = layer.route(torch.randn((m, 384), generator=g, device=dev))
+    eager = layer.forward(x, ids, w).clone()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        layer.forward(x, ids, w)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = layer.forward(x, ids, w)
+    layer.out.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager)
+
+
+def test_swiglu_bit_exact_vs_torch_chain(dev, pkg):
+    """The fused SwiGLU = the reference's three torch lines (nvfp4_8r_native.py:937-939)
+    applied to the kernel's own fp16 y13, bit for bit."""
+    H, I, E, K, M = 1024, 512, 32, 4, 16
+    layer, _, _, _ = _make_layer(dev, H, I, E, K, M, seed=5)
+    y13 = torch.zeros((M * K, 2 * I), dtype=torch.float16, device=dev)
+    layer.set_debug_y13(y13)
+    g = torch.Generator(device=dev).manual_seed(5)
+    x = (torch.randn((M, H), generator=g, device=dev) * 30).to(torch.float16)  # large: exercises the clamps
+    ids, w = layer.route(torch.randn((M, E), generator=g, device=dev))
+    layer.forward(x, ids, w)
+    inter = layer.debug_inter(M * K)
+    layer.check_errors()
+    gg = y13[:, :I].float().clamp(max=10.0)
+    u = y13[:, I:].float().clamp(-10.0, 10.0)
+    chain = (torch.nn.functional.silu(gg) * u).to(torch.float16)
+    assert torch.equal(inter.view(torch.int16), chain.view(torch.int16))
+    assert (y13.float().abs() > 10).any()  # the clamps were active
+    layer.set_debug_y13(None)
+    layer.close()
+
+
+def test_mxfp4_layer(dev, pkg):
+    H, I, E, K, M = 1024, 512, 32, 4, 12
+    layer, dequant, _, _ = _make_layer(dev, H, I, E, K, M, fmt="mxfp4", seed=3)
+    g = torch.Generator(device=dev).manual_seed(3)
+    x = torch.randn((M, H), generator=g, device=dev).to(torch.bfloat16)
+    ids, w = layer.route(torch.randn((M, E), generator=g, device=dev))
+    out = layer.forward(x, ids, w).clone()
+    layer.check_errors()
+    assert tr.rel_l2(out, tr.layer_forward(x, ids.long(), w, dequant)) < TOL
+    layer.close()
+
+
+def test_mixed_tier_layer(dev, pkg):
+    """Config 2 shapes: 150 NVFP4 (HOT) + 234 IQ2_XXS (WARM) experts, Zipf routing, M=32."""
+    from b200moe import synth, tiers
+
+    tier, rank = tiers.zipf_tier(384, 150, seed=2)
+    layer, dequant, _, _ = _make_layer(dev, 4096, 2048, 384, 8, 32, tier=tier, seed=2)
+    g = torch.Generator(device=dev).manual_seed(2032)
+    x = torch.randn((32, 4096), generator=g, device=dev).to(torch.bfloat16)
+    ids, w = layer.route(synth.zipf_logits(32, rank, 1.0, 1.1, 2032, dev))
+    out = layer.forward(x, ids, w).clone()
+    layer.check_errors()
+    assert (tier[ids.cpu().numpy()] == tiers.WARM).any() and (tier[ids.cpu().numpy()] == tiers.HOT).any()
+    assert tr.rel_l2(out, tr.layer_forward(x, ids.long(), w, dequant)) < TOL
+    layer.close()
+
+
+def test_prefill_and_apply(dev, pkg):
+    from b200moe import moe
+
+    H, I, E, K = 1024, 512, 32, 4
+    layer, dequant, _, _ = _make_layer(dev, H, I, E, K, 4, seed=4, max_prefill=300)
+    g = torch.Generator(device=dev).manual_seed(4)
+    x = torch.randn((300, H), generator=g, device=dev).to(torch.float16)
+    ids, w = layer.route(torch.randn((300, E), generator=g, device=dev))
+    out = layer.forward_prefill(x, ids, w)
+    layer.check_errors()
+    assert tr.rel_l2(out, tr.layer_forward(x, ids.long(), w, dequant)) < TOL
+    method = moe.B200NativeMoEMethod(layer)
+
+    class FakeLayer:
+        apply_router_weight_on_input = False
+        activation = "silu"
+
+    y = method.apply(FakeLayer(), x[:3], w[:3], ids[:3].long())
+    assert y.dtype == torch.float16 and y.shape == (3, H)
+    assert torch.equal(y, out[:3].to(torch.float16)) or tr.rel_l2(y.float(), out[:3]) < 1e-3
+    y = method.apply(FakeLayer(), x, w, ids)
+    assert y.shape == (300, H)
+    layer.close()
+
+
+def test_bad_expert_id_reports_bounds_then_recovers(dev, pkg):
+    from b200moe import _lib
+
+    H, I, E, K, M = 512, 256, 16, 4, 4
+    layer, dequant, _, _ = _make_layer(dev, H, I, E, K, M, seed=6)
+    x = torch.randn((M, H), device=dev).to(torch.float16)
+    ids = torch.tensor([[0, 1, 2, 3], [4, 5, 999, 7], [8, 9, 10, 11], [-1, 13, 14, 15]], dtype=torch.int32, device=dev)
+    w = torch.full((M, K), 0.25, device=dev)
+    layer.forward(x, ids, w)
+    with pytest.raises(_lib.B200MoeError, match="BOUNDS"):
+        layer.check_errors()
+    ids[1, 2] = 6
+    ids[3, 0] = 12
+    out = layer.forward(x, ids, w).clone()
+    layer.check_errors()
+    assert tr.rel_l2(out, tr.layer_forward(x, ids.long(), w, dequant)) < TOL
+    layer.close()

@@ -1,0 +1,106 @@
+// Internal launchers shared between the library's translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace b200moe {
+
+// ---- packing (pack.cu)
+int launch_fp4_prepack(cudaStream_t s, int fmt, int hidden, int inter, int n, const uint8_t* w13c,
+                       const uint8_t* w13s, const uint8_t* w2c, const uint8_t* w2s, float* slot_globals,
+                       int* span_scratch, uint8_t* bank_slot0, int64_t slot_stride, int64_t w13_bytes,
+                       uint32_t* err);
+int launch_iq2_prepack(cudaStream_t s, int hidden, int inter, int n, const uint8_t* w1, const uint8_t* w3,
+                       const uint8_t* w2, uint8_t* bank_slot0, int64_t slot_stride, int64_t w13_bytes);
+
+// ---- routing (route.cu)
+struct Chunk {  // one route chunk of one expert group: routes perm[begin .. begin+count)
+  int32_t slot;
+  int32_t begin;
+  int32_t count;
+  int32_t pad;
+};
+
+struct PlanArgs {
+  const int32_t* ids;  // [n] expert id per route (flat t*k + slot)
+  int n;
+  int num_experts;
+  // product keys: key_of_expert[e] in [0, n_keys) or -1 (not on this GPU / invalid)
+  const int32_t* key_of_expert;
+  int n_keys;
+  // reference-parity keys (used when key_of_expert == nullptr)
+  const int32_t* hot_slot;
+  const int32_t* second_slot;
+  int n_hot, n_second, split, host;
+  const int32_t* iq_slot;
+  // outputs
+  int32_t* perm;        // [n]
+  // product: chunk lists of up to two banks (bank b = keys [key_lo[b], key_hi[b]))
+  int n_banks;
+  int key_lo[2], key_hi[2], rc[2], max_chunks[2];
+  Chunk* chunks[2];
+  int32_t* n_chunks;    // [2]
+  const float* w_in;    // [n] router weights (product)
+  float* w_eff;         // [n] weight used by the combine (0 for a route without an expert)
+  // product: a route without an expert gets a zero yw row and its completion
+  // counts (so the fused combine still sees k arrivals per token and tile)
+  float* yw;            // [n][H]
+  int32_t* counters;    // [tokens][H/32]
+  float* out;           // [tokens][H]
+  int H;
+  int top_k;
+  // reference-parity tables
+  int32_t* gids_hot;
+  int32_t* goff_hot;
+  int32_t* gids_host;
+  int32_t* goff_host;
+  int32_t* iq_out;
+  uint32_t* err;
+};
+
+size_t plan_smem_bytes(int n_keys);
+int launch_plan(cudaStream_t s, const PlanArgs& a);
+int launch_gating(cudaStream_t s, const float* logits, int T, int E, int k, int32_t* ids, float* w,
+                  uint32_t* err);
+int launch_convert_bf16(cudaStream_t s, const void* x, int64_t n, void* x16);
+
+// ---- decode / skinny grouped GEMV (gemv.cu)
+struct GemvArgs {
+  int fmt;                    // 0 NVFP4, 1 MXFP4, 2 IQ2_XXS
+  int epi;                    // 0: W13 -> SwiGLU -> inter; 1: W2 -> weighted combine
+  int ks;                     // K splits per item (1, 2, 4, 8)
+  const uint8_t* region;      // slot 0 of this projection region
+  int64_t slot_stride;        // bytes between slots
+  int n_slots;
+  const float* globals;       // [slots][3] or nullptr
+  int K;                      // reduction length
+  int n_tp;                   // tile pairs per expert in this region
+  const Chunk* chunks;
+  const int32_t* n_chunks;    // device count of this bank's chunks
+  int bank;                   // index into n_chunks
+  const int32_t* perm;        // [S]
+  int S;
+  int top_k;
+  const void* xsrc;           // f16 rows
+  int x_by_token;             // 1: row perm[p] / k; 0: row p
+  int64_t x_row_stride;       // elements
+  int n_x_rows;               // rows available in xsrc (bounds check)
+  void* inter;                // W13 output f16 [S][inter_stride]
+  int inter_stride;
+  void* dbg_y13;              // optional f16 [S][2 * inter_stride]
+  float limit;
+  const float* w_eff;         // [S] by route index
+  float* yw;                  // [S][H] by route index
+  int32_t* counters;          // [tokens][H/32]
+  float* out;                 // [tokens][H]
+  int H;
+  const uint32_t* iq2_tables; // grid f16 [256][8] then sign masks [128][4]
+  uint32_t* err;
+  int grid;                   // persistent CTAs
+};
+
+size_t gemv_smem_bytes(int fmt, int ks);
+int launch_gemv(cudaStream_t s, const GemvArgs& a);
+
+}  // namespace b200moe

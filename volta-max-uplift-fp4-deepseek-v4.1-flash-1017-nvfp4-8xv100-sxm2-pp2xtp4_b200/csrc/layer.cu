@@ -1,0 +1,501 @@
+// The layer object and the C ABI of include/b200moe.h.
+//
+// A layer owns its expert banks (prepacked HBM layout, see layout.cuh), the
+// slot maps, and a workspace sized at create for max_tokens (decode) and
+// max_prefill_tokens; forward never allocates and never waits for the host.
+// The forward is: [bf16 -> f16 copy] -> route plan (one CTA) -> per bank
+// W13 (+ SwiGLU) -> per bank W2 (+ slot-order combine into `out`).
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+#include "layout.cuh"
+
+using namespace b200moe;
+
+struct b200moe_layer {
+  b200moe_config cfg;
+  int device = 0;
+  int grid = 148;
+  // banks: 0 = FP4 (NVFP4 / MXFP4), 1 = IQ2_XXS
+  uint8_t* bank[2] = {nullptr, nullptr};
+  BankGeom geom[2] = {};
+  float* globals = nullptr;        // [n_fp4][3]
+  int* span = nullptr;             // [n_fp4][3][2] MXFP4 load scratch
+  uint32_t* iq2_tables = nullptr;  // grid f16, sign masks, scale f16x2
+  int32_t* key_of_expert = nullptr;
+  bool maps_set = false, tables_set = false;
+  // workspace
+  int s_max = 0, t_max = 0;
+  int32_t* perm = nullptr;
+  float* w_eff = nullptr;
+  Chunk* chunks[2] = {nullptr, nullptr};
+  int max_chunks = 0;
+  int32_t* n_chunks = nullptr;
+  __half* x16 = nullptr;
+  __half* inter = nullptr;
+  float* yw = nullptr;
+  int32_t* counters = nullptr;
+  uint32_t* err = nullptr;
+  void* dbg_y13 = nullptr;
+  // optional timing: events[0] at forward start, events[j + 1] after launch j
+  cudaEvent_t events[16] = {};
+  int n_events = 0;
+};
+
+namespace {
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+template <typename T>
+int dalloc(T** p, size_t count) {
+  if (count == 0) {
+    *p = nullptr;
+    return B200MOE_OK;
+  }
+  if (cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T)) != cudaSuccess) {
+    cudaGetLastError();
+    *p = nullptr;
+    return B200MOE_ERR_NOMEM;
+  }
+  return B200MOE_OK;
+}
+
+void free_layer(b200moe_layer* L) {
+  void* ptrs[] = {L->bank[0], L->bank[1], L->globals, L->span, L->iq2_tables, L->key_of_expert, L->perm,
+                  L->w_eff, L->chunks[0], L->chunks[1], L->n_chunks, L->x16, L->inter, L->yw,
+                  L->counters, L->err};
+  for (void* p : ptrs)
+    if (p) cudaFree(p);
+}
+
+bool aligned(const void* p, int a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// K splits of a bank's launches: the split whose items fill the SMs best
+// (fewer splits on a tie).  Both projections must divide into KS slices.
+int choose_ks(const b200moe_layer* L, int bank, int rows) {
+  const auto& c = L->cfg;
+  const int kt = bank == 0 ? kFp4KTile : kIq2KTile;
+  const int n_slots = bank == 0 ? c.n_fp4 : c.n_iq2;
+  const int routes = rows * c.top_k;
+  const double e = double(n_slots);
+  const double groups = std::max(1.0, std::min(double(routes), e * (1.0 - pow(1.0 - 1.0 / std::max(e, 1.0), routes))));
+  int best = 1;
+  double best_eff = -1;
+  for (int ks : {1, 2, 4, 8}) {
+    if ((c.hidden / kt) % ks || (c.inter / kt) % ks) continue;
+    const int rc = 16 / ks;
+    const double chunks = std::max(groups, std::ceil(routes / double(rc)));
+    const double items = chunks * double(c.inter / 16) / double(8 / ks);
+    const double waves = std::ceil(items / L->grid);
+    const double eff = items / (waves * L->grid);
+    if (eff > best_eff + 0.02) {
+      best_eff = eff;
+      best = ks;
+    }
+  }
+  return best;
+}
+
+struct Marks {
+  const b200moe_layer* L;
+  cudaStream_t s;
+  int next = 0;
+  void mark() {
+    if (next < L->n_events) cudaEventRecord(L->events[next], s);
+    ++next;
+  }
+};
+
+int run_forward(b200moe_layer* L, cudaStream_t s, const void* x, int x_dtype, const int32_t* ids,
+                const float* w, float* out, int m) {
+  const auto& c = L->cfg;
+  Marks marks{L, s};
+  if (!L->maps_set) return B200MOE_ERR_STATE;
+  if (c.n_iq2 > 0 && !L->tables_set) return B200MOE_ERR_STATE;
+  if (!x || !ids || !w || !out) return B200MOE_ERR_INVALID_ARG;
+  if (x_dtype != B200MOE_F16 && x_dtype != B200MOE_BF16) return B200MOE_ERR_DTYPE;
+  if (!aligned(x, 16) || !aligned(out, 16)) return B200MOE_ERR_ALIGN;
+  const int S = m * c.top_k;
+  const __half* xsrc = static_cast<const __half*>(x);
+  marks.mark();
+  if (x_dtype == B200MOE_BF16) {
+    if (launch_convert_bf16(s, x, int64_t(m) * c.hidden, L->x16)) return B200MOE_ERR_CUDA;
+    xsrc = L->x16;
+    marks.mark();
+  }
+  int ks[2] = {choose_ks(L, 0, m), choose_ks(L, 1, m)};
+  PlanArgs p{};
+  p.ids = ids;
+  p.n = S;
+  p.num_experts = c.num_experts;
+  p.key_of_expert = L->key_of_expert;
+  p.n_keys = c.n_fp4 + c.n_iq2;
+  p.perm = L->perm;
+  p.n_banks = 2;
+  p.key_lo[0] = 0;
+  p.key_hi[0] = c.n_fp4;
+  p.key_lo[1] = c.n_fp4;
+  p.key_hi[1] = c.n_fp4 + c.n_iq2;
+  for (int b = 0; b < 2; ++b) {
+    p.rc[b] = 16 / ks[b];
+    p.max_chunks[b] = L->max_chunks;
+    p.chunks[b] = L->chunks[b];
+  }
+  p.n_chunks = L->n_chunks;
+  p.w_in = w;
+  p.w_eff = L->w_eff;
+  p.yw = L->yw;
+  p.counters = L->counters;
+  p.out = out;
+  p.H = c.hidden;
+  p.top_k = c.top_k;
+  p.err = L->err;
+  if (launch_plan(s, p)) return B200MOE_ERR_CUDA;
+  marks.mark();
+  for (int epi = 0; epi < 2; ++epi) {
+    for (int b = 0; b < 2; ++b) {
+      const int n_slots = b == 0 ? c.n_fp4 : c.n_iq2;
+      if (n_slots == 0) continue;
+      GemvArgs g{};
+      g.fmt = b == 0 ? c.fp4_format : 2;
+      g.epi = epi;
+      g.ks = ks[b];
+      g.region = L->bank[b] + (epi == 0 ? 0 : L->geom[b].w13_bytes);
+      g.slot_stride = L->geom[b].slot_bytes;
+      g.n_slots = n_slots;
+      g.globals = b == 0 ? L->globals : nullptr;
+      g.K = epi == 0 ? c.hidden : c.inter;
+      g.n_tp = epi == 0 ? c.inter / 16 : c.hidden / 32;
+      g.chunks = L->chunks[b];
+      g.n_chunks = L->n_chunks;
+      g.bank = b;
+      g.perm = L->perm;
+      g.S = S;
+      g.top_k = c.top_k;
+      g.xsrc = epi == 0 ? static_cast<const void*>(xsrc) : static_cast<const void*>(L->inter);
+      g.x_by_token = epi == 0;
+      g.x_row_stride = epi == 0 ? c.hidden : c.inter;
+      g.n_x_rows = epi == 0 ? m : S;
+      g.inter = L->inter;
+      g.inter_stride = c.inter;
+      g.dbg_y13 = L->dbg_y13;
+      g.limit = c.swiglu_limit;
+      g.w_eff = L->w_eff;
+      g.yw = L->yw;
+      g.counters = L->counters;
+      g.out = out;
+      g.H = c.hidden;
+      g.iq2_tables = L->iq2_tables;
+      g.err = L->err;
+      g.grid = L->grid;
+      if (launch_gemv(s, g)) return B200MOE_ERR_CUDA;
+      marks.mark();
+    }
+  }
+  return B200MOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* b200moe_status_name(int status) {
+  switch (status) {
+    case B200MOE_OK: return "B200MOE_OK";
+    case B200MOE_ERR_INVALID_ARG: return "B200MOE_ERR_INVALID_ARG";
+    case B200MOE_ERR_DTYPE: return "B200MOE_ERR_DTYPE";
+    case B200MOE_ERR_ALIGN: return "B200MOE_ERR_ALIGN";
+    case B200MOE_ERR_CUDA: return "B200MOE_ERR_CUDA";
+    case B200MOE_ERR_BOUNDS: return "B200MOE_ERR_BOUNDS";
+    case B200MOE_ERR_TIMEOUT: return "B200MOE_ERR_TIMEOUT";
+    case B200MOE_ERR_FORMAT: return "B200MOE_ERR_FORMAT";
+    case B200MOE_ERR_RANGE: return "B200MOE_ERR_RANGE";
+    case B200MOE_ERR_NOMEM: return "B200MOE_ERR_NOMEM";
+    case B200MOE_ERR_STATE: return "B200MOE_ERR_STATE";
+    default: return "B200MOE_ERR_UNKNOWN";
+  }
+}
+
+const char* b200moe_version(void) { return "b200moe 0.1 sm_100a"; }
+
+int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** out) {
+  if (!cfg || !out) return B200MOE_ERR_INVALID_ARG;
+  *out = nullptr;
+  const b200moe_config c = *cfg;
+  if (c.hidden < 256 || c.hidden % 256 || c.inter < 128 || c.inter % 128 || c.num_experts < 1 ||
+      c.num_experts > 1024 || c.top_k < 1 || c.top_k > 16 || c.top_k > c.num_experts || c.max_tokens < 1 ||
+      c.max_tokens > 64 || c.max_prefill_tokens < 0 || c.n_fp4 < 0 || c.n_iq2 < 0 ||
+      c.n_fp4 + c.n_iq2 < 1 || c.n_fp4 + c.n_iq2 > c.num_experts || !(c.swiglu_limit > 0.f))
+    return B200MOE_ERR_INVALID_ARG;
+  if (c.fp4_format != B200MOE_NVFP4 && c.fp4_format != B200MOE_MXFP4) return B200MOE_ERR_INVALID_ARG;
+  if (c.n_iq2 > 0 && c.inter % 256) return B200MOE_ERR_INVALID_ARG;
+  DeviceGuard guard(device);
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return B200MOE_ERR_CUDA;
+  if (prop.major != 10) return B200MOE_ERR_CUDA;  // built for sm_100a only
+  auto* L = new b200moe_layer();
+  L->cfg = c;
+  L->device = device;
+  L->grid = prop.multiProcessorCount;
+  L->geom[0] = fp4_geom(c.fp4_format, c.hidden, c.inter);
+  L->geom[1] = iq2_geom(c.hidden, c.inter);
+  L->t_max = std::max(c.max_tokens, c.max_prefill_tokens);
+  L->s_max = L->t_max * c.top_k;
+  L->max_chunks = L->s_max + c.num_experts;
+  int st = B200MOE_OK;
+  auto take = [&](int r) {
+    if (st == B200MOE_OK) st = r;
+  };
+  take(dalloc(&L->bank[0], size_t(c.n_fp4) * L->geom[0].slot_bytes));
+  take(dalloc(&L->bank[1], size_t(c.n_iq2) * L->geom[1].slot_bytes));
+  take(dalloc(&L->globals, size_t(std::max(c.n_fp4, 1)) * 3));
+  take(dalloc(&L->span, size_t(std::max(c.n_fp4, 1)) * 6));
+  take(dalloc(&L->iq2_tables, 256 * 4 + 128 * 4 + 16));
+  take(dalloc(&L->key_of_expert, size_t(c.num_experts)));
+  take(dalloc(&L->perm, size_t(L->s_max)));
+  take(dalloc(&L->w_eff, size_t(L->s_max)));
+  take(dalloc(&L->chunks[0], size_t(L->max_chunks)));
+  take(dalloc(&L->chunks[1], size_t(L->max_chunks)));
+  take(dalloc(&L->n_chunks, 2));
+  take(dalloc(&L->x16, size_t(L->t_max) * c.hidden));
+  take(dalloc(&L->inter, size_t(L->s_max) * c.inter));
+  take(dalloc(&L->yw, size_t(L->s_max) * c.hidden));
+  take(dalloc(&L->counters, size_t(L->t_max) * (c.hidden / 32)));
+  take(dalloc(&L->err, 1));
+  if (st == B200MOE_OK) {
+    if (cudaMemset(L->counters, 0, size_t(L->t_max) * (c.hidden / 32) * 4) != cudaSuccess ||
+        cudaMemset(L->err, 0, 4) != cudaSuccess || cudaMemset(L->n_chunks, 0, 8) != cudaSuccess ||
+        cudaMemset(L->inter, 0, size_t(L->s_max) * c.inter * 2) != cudaSuccess ||
+        cudaMemset(L->globals, 0, size_t(std::max(c.n_fp4, 1)) * 12) != cudaSuccess ||
+        cudaDeviceSynchronize() != cudaSuccess)
+      st = B200MOE_ERR_CUDA;
+  }
+  if (st != B200MOE_OK) {
+    free_layer(L);
+    delete L;
+    return st;
+  }
+  *out = L;
+  return B200MOE_OK;
+}
+
+int b200moe_layer_destroy(b200moe_layer* L) {
+  if (!L) return B200MOE_ERR_INVALID_ARG;
+  DeviceGuard guard(L->device);
+  cudaDeviceSynchronize();
+  free_layer(L);
+  delete L;
+  return B200MOE_OK;
+}
+
+int b200moe_set_slot_maps(b200moe_layer* L, const int32_t* fp4_slot, const int32_t* iq2_slot) {
+  if (!L || !fp4_slot) return B200MOE_ERR_INVALID_ARG;
+  const auto& c = L->cfg;
+  std::vector<int32_t> key(c.num_experts, -1);
+  std::vector<int> seen0(c.n_fp4, 0), seen1(c.n_iq2, 0);
+  for (int e = 0; e < c.num_experts; ++e) {
+    const int a = fp4_slot[e], b = iq2_slot ? iq2_slot[e] : -1;
+    if (a >= c.n_fp4 || b >= c.n_iq2 || a < -1 || b < -1) return B200MOE_ERR_INVALID_ARG;
+    if (a >= 0 && b >= 0) return B200MOE_ERR_INVALID_ARG;  // one bank per expert
+    if (a >= 0) {
+      if (seen0[a]++) return B200MOE_ERR_INVALID_ARG;
+      key[e] = a;
+    } else if (b >= 0) {
+      if (seen1[b]++) return B200MOE_ERR_INVALID_ARG;
+      key[e] = c.n_fp4 + b;
+    }
+  }
+  for (int v : seen0)
+    if (v != 1) return B200MOE_ERR_INVALID_ARG;
+  for (int v : seen1)
+    if (v != 1) return B200MOE_ERR_INVALID_ARG;
+  DeviceGuard guard(L->device);
+  if (cudaMemcpy(L->key_of_expert, key.data(), key.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+    return B200MOE_ERR_CUDA;
+  L->maps_set = true;
+  return B200MOE_OK;
+}
+
+int b200moe_set_iq2_tables(b200moe_layer* L, const int8_t* grid, const uint8_t* ksigns) {
+  if (!L || !grid || !ksigns) return B200MOE_ERR_INVALID_ARG;
+  std::vector<uint32_t> t(256 * 4 + 128 * 4 + 16);
+  auto h = [](float v) {
+    __half x = __float2half_rn(v);
+    return uint32_t(*reinterpret_cast<uint16_t*>(&x));
+  };
+  for (int e = 0; e < 256; ++e)
+    for (int p = 0; p < 4; ++p) {
+      const int8_t g0 = grid[e * 8 + 2 * p], g1 = grid[e * 8 + 2 * p + 1];
+      if (g0 < 0 || g1 < 0) return B200MOE_ERR_INVALID_ARG;  // ggml's grid values are positive
+      t[e * 4 + p] = h(float(g0)) | (h(float(g1)) << 16);
+    }
+  for (int si = 0; si < 128; ++si) {
+    const uint32_t sb = ksigns[si];
+    for (int p = 0; p < 4; ++p)
+      t[1024 + si * 4 + p] = (((sb >> (2 * p)) & 1u) << 15) | (((sb >> (2 * p + 1)) & 1u) << 31);
+  }
+  for (int s = 0; s < 16; ++s) t[1024 + 512 + s] = h(0.5f + s) * 0x10001u;
+  DeviceGuard guard(L->device);
+  if (cudaMemcpy(L->iq2_tables, t.data(), t.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+    return B200MOE_ERR_CUDA;
+  L->tables_set = true;
+  return B200MOE_OK;
+}
+
+int b200moe_load_fp4(b200moe_layer* L, void* stream, int slot_begin, int n, const uint8_t* w13c,
+                     const uint8_t* w13s, const uint8_t* w2c, const uint8_t* w2s, const float* globals) {
+  if (!L || !w13c || !w13s || !w2c || !w2s || n < 1 || slot_begin < 0 || slot_begin + n > L->cfg.n_fp4)
+    return B200MOE_ERR_INVALID_ARG;
+  const auto& c = L->cfg;
+  if (c.fp4_format == B200MOE_NVFP4 && !globals) return B200MOE_ERR_INVALID_ARG;
+  if (!aligned(w13c, 16) || !aligned(w2c, 16) || !aligned(w13s, 4) || !aligned(w2s, 4)) return B200MOE_ERR_ALIGN;
+  DeviceGuard guard(L->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* gdst = L->globals + size_t(slot_begin) * 3;
+  if (c.fp4_format == B200MOE_NVFP4 &&
+      cudaMemcpyAsync(gdst, globals, size_t(n) * 12, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+    return B200MOE_ERR_CUDA;
+  uint8_t* dst = L->bank[0] + size_t(slot_begin) * L->geom[0].slot_bytes;
+  if (launch_fp4_prepack(s, c.fp4_format, c.hidden, c.inter, n, w13c, w13s, w2c, w2s, gdst, L->span, dst,
+                         L->geom[0].slot_bytes, L->geom[0].w13_bytes, L->err))
+    return B200MOE_ERR_CUDA;
+  return B200MOE_OK;
+}
+
+int b200moe_load_iq2(b200moe_layer* L, void* stream, int slot_begin, int n, const uint8_t* w1,
+                     const uint8_t* w3, const uint8_t* w2) {
+  if (!L || !w1 || !w3 || !w2 || n < 1 || slot_begin < 0 || slot_begin + n > L->cfg.n_iq2)
+    return B200MOE_ERR_INVALID_ARG;
+  const auto& c = L->cfg;
+  DeviceGuard guard(L->device);
+  uint8_t* dst = L->bank[1] + size_t(slot_begin) * L->geom[1].slot_bytes;
+  if (launch_iq2_prepack(static_cast<cudaStream_t>(stream), c.hidden, c.inter, n, w1, w3, w2, dst,
+                         L->geom[1].slot_bytes, L->geom[1].w13_bytes))
+    return B200MOE_ERR_CUDA;
+  return B200MOE_OK;
+}
+
+int b200moe_route(b200moe_layer* L, void* stream, const float* logits, int32_t* ids, float* w, int T) {
+  if (!L || !logits || !ids || !w || T < 1) return B200MOE_ERR_INVALID_ARG;
+  DeviceGuard guard(L->device);
+  if (launch_gating(static_cast<cudaStream_t>(stream), logits, T, L->cfg.num_experts, L->cfg.top_k, ids, w, L->err))
+    return B200MOE_ERR_CUDA;
+  return B200MOE_OK;
+}
+
+int b200moe_forward(b200moe_layer* L, void* stream, const void* x, int x_dtype, const int32_t* ids,
+                    const float* w, float* out, int M) {
+  if (!L || M < 1 || M > L->cfg.max_tokens) return B200MOE_ERR_INVALID_ARG;
+  DeviceGuard guard(L->device);
+  return run_forward(L, static_cast<cudaStream_t>(stream), x, x_dtype, ids, w, out, M);
+}
+
+int b200moe_forward_prefill(b200moe_layer* L, void* stream, const void* x, int x_dtype, const int32_t* ids,
+                            const float* w, float* out, int T) {
+  if (!L || T < 1 || T > L->t_max) return B200MOE_ERR_INVALID_ARG;
+  DeviceGuard guard(L->device);
+  return run_forward(L, static_cast<cudaStream_t>(stream), x, x_dtype, ids, w, out, T);
+}
+
+int b200moe_check_errors(b200moe_layer* L, void* stream, uint32_t* bits) {
+  if (!L) return B200MOE_ERR_INVALID_ARG;
+  DeviceGuard guard(L->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaStreamSynchronize(s) != cudaSuccess) return B200MOE_ERR_CUDA;
+  uint32_t e = 0;
+  if (cudaMemcpy(&e, L->err, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return B200MOE_ERR_CUDA;
+  if (cudaMemset(L->err, 0, 4) != cudaSuccess) return B200MOE_ERR_CUDA;
+  if (bits) *bits = e;
+  // after an error the combine counters may hold partial counts: start clean
+  if (e && cudaMemset(L->counters, 0, size_t(L->t_max) * (L->cfg.hidden / 32) * 4) != cudaSuccess)
+    return B200MOE_ERR_CUDA;
+  if (e & kErrBounds) return B200MOE_ERR_BOUNDS;
+  if (e & kErrTimeout) return B200MOE_ERR_TIMEOUT;
+  if (e & kErrFormat) return B200MOE_ERR_FORMAT;
+  if (e & kErrRange) return B200MOE_ERR_RANGE;
+  return B200MOE_OK;
+}
+
+int b200moe_set_debug_y13(b200moe_layer* L, void* y13) {
+  if (!L) return B200MOE_ERR_INVALID_ARG;
+  L->dbg_y13 = y13;
+  return B200MOE_OK;
+}
+
+int b200moe_debug_perm(const b200moe_layer* L, void* stream, int32_t* dst, int n) {
+  if (!L || !dst || n < 1 || n > L->s_max) return B200MOE_ERR_INVALID_ARG;
+  DeviceGuard guard(L->device);
+  if (cudaMemcpyAsync(dst, L->perm, size_t(n) * 4, cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream)) !=
+      cudaSuccess)
+    return B200MOE_ERR_CUDA;
+  return B200MOE_OK;
+}
+
+int b200moe_set_timing_events(b200moe_layer* L, void* const* events, int n) {
+  if (!L || n < 0 || n > 16 || (n > 0 && !events)) return B200MOE_ERR_INVALID_ARG;
+  for (int i = 0; i < n; ++i) L->events[i] = static_cast<cudaEvent_t>(events[i]);
+  L->n_events = n;
+  return B200MOE_OK;
+}
+
+int b200moe_debug_inter(const b200moe_layer* L, void* stream, void* dst, int rows) {
+  if (!L || !dst || rows < 1 || rows > L->s_max) return B200MOE_ERR_INVALID_ARG;
+  DeviceGuard guard(L->device);
+  if (cudaMemcpyAsync(dst, L->inter, size_t(rows) * L->cfg.inter * 2, cudaMemcpyDeviceToDevice,
+                      static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return B200MOE_ERR_CUDA;
+  return B200MOE_OK;
+}
+
+int b200moe_route_plan(void* stream, const int32_t* ids, int n, int num_experts, const int32_t* hot_slot,
+                       const int32_t* second_slot, int n_hot, int n_second, int split, int host,
+                       const int32_t* iq_slot, int32_t* perm, int32_t* gids_hot, int32_t* goff_hot,
+                       int32_t* gids_host, int32_t* goff_host, int32_t* iq_out, uint32_t* err) {
+  if (!ids || n < 1 || n > 4096 || !hot_slot || !perm || !gids_hot || !goff_hot || num_experts < 1 || n_hot < 1)
+    return B200MOE_ERR_INVALID_ARG;
+  if (split && (!second_slot || n_second < 1)) return B200MOE_ERR_INVALID_ARG;
+  if (host && (!split || !gids_host || !goff_host)) return B200MOE_ERR_INVALID_ARG;
+  if ((iq_slot == nullptr) != (iq_out == nullptr)) return B200MOE_ERR_INVALID_ARG;
+  if (n_hot + (split ? n_second : 0) + 1 > 4096) return B200MOE_ERR_INVALID_ARG;
+  PlanArgs p{};
+  p.ids = ids;
+  p.n = n;
+  p.num_experts = num_experts;
+  p.hot_slot = hot_slot;
+  p.second_slot = second_slot;
+  p.n_hot = n_hot;
+  p.n_second = split ? n_second : 1;
+  p.split = split;
+  p.host = host;
+  p.iq_slot = iq_slot;
+  p.perm = perm;
+  p.gids_hot = gids_hot;
+  p.goff_hot = goff_hot;
+  p.gids_host = gids_host;
+  p.goff_host = goff_host;
+  p.iq_out = iq_out;
+  p.err = err;
+  if (launch_plan(static_cast<cudaStream_t>(stream), p)) return B200MOE_ERR_CUDA;
+  return B200MOE_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,367 @@
+// Routing kernels: softmax top-k gating, the stable token -> expert permute
+// with its group tables, and the bf16 -> f16 activation copy.
+//
+// The permute is a stable counting sort by key in one CTA (1024 threads):
+// each warp owns a contiguous run of routes, counts its keys with match_any,
+// the per-warp counts become per-warp offsets, and a second pass scatters each
+// route to start[key] + (earlier warps' count) + (rank among equal keys in its
+// batch).  That is exactly the stable argsort of the reference chain
+// (engine/.../experts/nvfp4_8r_native.py:806-822) and the rank definition of
+// the reference's one-launch plan (engine/.../experts/nvfp4_8r_group_plan.py:13-24),
+// for any number of routes, not just the reference's 96.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <float.h>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace b200moe {
+
+constexpr int kPlanThreads = 1024;
+
+// In-place exclusive scan of arr[0..len) in shared memory by the whole CTA;
+// returns the total.  Every thread of the CTA must call it.
+__device__ int block_exclusive_scan(int* arr, int len, int* wsum) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int seg = (len + kPlanThreads - 1) / kPlanThreads;
+  const int lo = tid * seg, hi = min(len, lo + seg);
+  int local = 0;
+  for (int i = lo; i < hi; ++i) local += arr[i];
+  int inc = local;
+  for (int o = 1; o < 32; o <<= 1) {
+    int v = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += v;
+  }
+  if (lane == 31) wsum[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    int v = wsum[lane];
+    int s = v;
+    for (int o = 1; o < 32; o <<= 1) {
+      int u = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += u;
+    }
+    wsum[lane] = s - v;   // exclusive warp base
+    if (lane == 31) wsum[32] = s;
+  }
+  __syncthreads();
+  int run = wsum[warp] + inc - local;
+  for (int i = lo; i < hi; ++i) {
+    int v = arr[i];
+    arr[i] = run;
+    run += v;
+  }
+  const int total = wsum[32];
+  __syncthreads();
+  return total;
+}
+
+__device__ __forceinline__ int plan_key(const PlanArgs& a, int i, int sentinel) {
+  const int e = a.ids[i];
+  if (e < 0 || e >= a.num_experts) {
+    set_error(a.err, kErrBounds);
+    return sentinel;
+  }
+  if (a.key_of_expert) {
+    const int k = a.key_of_expert[e];
+    if (k < 0 || k >= a.n_keys) {
+      set_error(a.err, kErrBounds);
+      return sentinel;
+    }
+    return k;
+  }
+  const int hot = a.hot_slot[e];
+  if (!a.split) {
+    if (hot < 0 || hot >= a.n_hot) {
+      set_error(a.err, kErrBounds);
+      return sentinel;
+    }
+    return hot;
+  }
+  if (hot >= 0) return hot;
+  const int sec = a.second_slot[e];
+  return sec >= 0 ? a.n_hot + sec : a.n_hot + a.n_second;
+}
+
+// Keys: product mode [0, n_keys) plus one sentinel bucket n_keys for a route
+// without an expert; reference mode [0, n_hot) (resident) or
+// [0, n_hot + n_second] (split, the last key being the WARM sentinel).
+__global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanArgs a) {
+  extern __shared__ int smem[];
+  __shared__ int wsum[33];
+  __shared__ int misc[8];
+  const bool product = a.key_of_expert != nullptr;
+  const int nk = product ? a.n_keys + 1 : (a.split ? a.n_hot + a.n_second + 1 : a.n_hot + 1);
+  const int sentinel = product ? a.n_keys : nk - 1;
+  int* hist = smem;             // [32][nk]
+  int* start = hist + 32 * nk;  // [nk]
+  int* aux = start + nk;        // [nk]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n = a.n;
+  for (int i = tid; i < 32 * nk; i += kPlanThreads) hist[i] = 0;
+  __syncthreads();
+  const int per_warp = ((n + 31) / 32 + 31) / 32 * 32;
+  const int wlo = min(n, warp * per_warp), whi = min(n, wlo + per_warp);
+  // pass 1: per-warp key counts
+  for (int base = wlo; base < whi; base += 32) {
+    const int i = base + lane;
+    const int key = i < whi ? plan_key(a, i, sentinel) : -1;
+    const unsigned mask = __match_any_sync(0xffffffffu, key);
+    if (key >= 0 && lane == __ffs(mask) - 1) hist[warp * nk + key] += __popc(mask);
+    __syncwarp();
+  }
+  __syncthreads();
+  // per-key totals and per-warp offsets
+  for (int key = tid; key < nk; key += kPlanThreads) {
+    int run = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int c = hist[w * nk + key];
+      hist[w * nk + key] = run;
+      run += c;
+    }
+    aux[key] = run;
+    start[key] = run;
+  }
+  __syncthreads();
+  block_exclusive_scan(start, nk, wsum);
+  // pass 2: stable scatter
+  for (int base = wlo; base < whi; base += 32) {
+    const int i = base + lane;
+    const int key = i < whi ? plan_key(a, i, sentinel) : -1;
+    const unsigned mask = __match_any_sync(0xffffffffu, key);
+    if (key >= 0) {
+      const int rank = __popc(mask & ((1u << lane) - 1u));
+      const int pos = start[key] + hist[warp * nk + key] + rank;
+      a.perm[pos] = i;
+      if (product && a.w_eff) a.w_eff[i] = key < a.n_keys ? a.w_in[i] : 0.f;
+      if (a.iq_out) a.iq_out[i] = a.iq_slot[a.ids[i]];
+    }
+    __syncwarp();
+    if (key >= 0 && lane == __ffs(mask) - 1) hist[warp * nk + key] += __popc(mask);
+    __syncwarp();
+  }
+  __syncthreads();
+
+  if (product && aux[nk - 1] > 0 && a.yw) {
+    // routes without an expert (sorted last): zero their rows, count them done
+    const int first = start[nk - 1], cnt = aux[nk - 1];
+    const int tiles = a.H / 32;
+    for (int64_t idx = tid; idx < int64_t(cnt) * a.H; idx += kPlanThreads) {
+      const int route = a.perm[first + int(idx / a.H)];
+      a.yw[int64_t(route) * a.H + idx % a.H] = 0.f;
+    }
+    __threadfence();
+    __syncthreads();
+    for (int idx = tid; idx < cnt * tiles; idx += kPlanThreads) {
+      const int route = a.perm[first + idx / tiles], tile = idx % tiles;
+      const int tok = route / a.top_k;
+      int* c = a.counters + int64_t(tok) * tiles + tile;
+      if (atomicAdd(c, 1) == a.top_k - 1) {  // every route of this token lacked an expert
+        for (int r = 0; r < 32; ++r) a.out[int64_t(tok) * a.H + 32 * tile + r] = 0.f;
+        *c = 0;
+      }
+    }
+    __syncthreads();
+  }
+
+  if (product) {
+    // route chunks of every bank: ceil(count / rc) chunks per non-empty key
+    for (int b = 0; b < a.n_banks; ++b) {
+      const int lo = a.key_lo[b], hi = a.key_hi[b], rc = a.rc[b];
+      int* nch = hist;  // hist is free now: reuse as [nk]
+      for (int key = tid; key < nk; key += kPlanThreads)
+        nch[key] = (key >= lo && key < hi) ? (aux[key] + rc - 1) / rc : 0;
+      __syncthreads();
+      const int total = block_exclusive_scan(nch, nk, wsum);
+      for (int key = lo + tid; key < hi; key += kPlanThreads) {
+        const int cnt = aux[key];
+        int c = nch[key];
+        for (int off = 0; off < cnt; off += rc, ++c) {
+          if (c < a.max_chunks[b]) {
+            Chunk ch;
+            ch.slot = key - lo;
+            ch.begin = start[key] + off;
+            ch.count = min(rc, cnt - off);
+            ch.pad = 0;
+            a.chunks[b][c] = ch;
+          }
+        }
+      }
+      if (tid == 0) {
+        if (total > a.max_chunks[b]) set_error(a.err, kErrRange);
+        a.n_chunks[b] = min(total, a.max_chunks[b]);
+      }
+      __syncthreads();
+    }
+    return;
+  }
+
+  // reference-parity tables (EXP/nvfp4_8r_group_plan.py:13-24)
+  if (tid == 0) {
+    int count_hot = 0, count_native = 0, groups_hot = 0, n_groups = 0, last = -1;
+    for (int key = 0; key < nk; ++key) {
+      const int c = aux[key];
+      if (c == 0) continue;
+      ++n_groups;
+      last = key;
+      if (key < a.n_hot) { count_hot += c; ++groups_hot; }
+      if (key < a.n_hot + a.n_second) count_native += c;
+    }
+    misc[0] = count_hot; misc[1] = count_native; misc[2] = groups_hot; misc[3] = n_groups; misc[4] = last;
+  }
+  int* gidx = hist;  // reuse: group index of each key
+  for (int key = tid; key < nk; key += kPlanThreads) gidx[key] = aux[key] > 0 ? 1 : 0;
+  __syncthreads();
+  block_exclusive_scan(gidx, nk, wsum);
+  const int count_hot = misc[0], count_native = misc[1], groups_hot = misc[2], n_groups = misc[3], last = misc[4];
+  for (int key = tid; key < nk; key += kPlanThreads) {
+    if (aux[key] == 0) continue;
+    const int g = gidx[key];
+    a.goff_hot[g] = min(start[key], count_hot);
+    a.gids_hot[g] = key < a.n_hot ? key : 0;
+    if (a.host) {
+      const int t = g - groups_hot;
+      if (t >= 0) {
+        a.goff_host[t] = min(start[key], count_native);
+        a.gids_host[t] = min(max(key - a.n_hot, 0), a.n_second - 1);
+      }
+    }
+  }
+  for (int g = n_groups + tid; g <= n; g += kPlanThreads) {
+    a.goff_hot[g] = count_hot;
+    if (g < n) a.gids_hot[g] = 0;
+  }
+  if (a.host) {
+    const int fill = n_groups == n ? min(max(last - a.n_hot, 0), a.n_second - 1) : 0;
+    for (int t = n_groups - groups_hot + tid; t <= n; t += kPlanThreads) {
+      a.goff_host[t] = count_native;
+      if (t < n) a.gids_host[t] = fill;
+    }
+  }
+}
+
+size_t plan_smem_bytes(int n_keys_total) { return size_t(34) * n_keys_total * sizeof(int); }
+
+int launch_plan(cudaStream_t s, const PlanArgs& a) {
+  const bool product = a.key_of_expert != nullptr;
+  const int nk = product ? a.n_keys + 1 : (a.split ? a.n_hot + a.n_second + 1 : a.n_hot + 1);
+  const size_t smem = plan_smem_bytes(nk);
+  if (smem > 200 * 1024) return -1;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr_set = true;
+  }
+  plan_kernel<<<1, kPlanThreads, smem, s>>>(a);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// ------------------------------------------------------------------ gating
+// One warp per token.  ids: the k largest logits, larger first, ties to the
+// smaller id.  weights: exp(l - l_max) in double for the k chosen, summed in
+// rank order, divided, rounded once to float.
+template <int MAXV>
+__global__ void gating_kernel(const float* __restrict__ logits, int T, int E, int k, int32_t* __restrict__ ids,
+                              float* __restrict__ w, uint32_t* err) {
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < T; t += warps) {
+    const float* row = logits + int64_t(t) * E;
+    float v[MAXV];
+#pragma unroll
+    for (int j = 0; j < MAXV; ++j) {
+      const int idx = lane + 32 * j;
+      v[j] = idx < E ? row[idx] : -INFINITY;
+      if (idx < E && !isfinite(v[j])) {
+        set_error(err, kErrFormat);
+        v[j] = -FLT_MAX;
+      }
+    }
+    float sel_v[16];
+    int sel_i[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      if (r >= k) break;
+      float best = -INFINITY;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int j = 0; j < MAXV; ++j) {
+        const int idx = lane + 32 * j;
+        if (idx < E && v[j] != -INFINITY && (v[j] > best || (v[j] == best && idx < bi))) {
+          best = v[j];
+          bi = idx;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > best || (ov == best && oi < bi)) {
+          best = ov;
+          bi = oi;
+        }
+      }
+      sel_v[r] = best;
+      sel_i[r] = bi;
+#pragma unroll
+      for (int j = 0; j < MAXV; ++j)
+        if (lane + 32 * j == bi) v[j] = -INFINITY;
+    }
+    if (lane == 0) {
+      double ex[16];
+      double total = 0.0;
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {
+        if (r >= k) break;
+        ex[r] = exp(double(sel_v[r]) - double(sel_v[0]));
+        total = total + ex[r];
+      }
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {
+        if (r >= k) break;
+        ids[int64_t(t) * k + r] = sel_i[r];
+        w[int64_t(t) * k + r] = float(ex[r] / total);
+      }
+    }
+  }
+}
+
+int launch_gating(cudaStream_t s, const float* logits, int T, int E, int k, int32_t* ids, float* w,
+                  uint32_t* err) {
+  const int threads = 256;
+  int blocks = (T + 7) / 8;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (blocks < 1) blocks = 1;
+  if (E <= 128) gating_kernel<4><<<blocks, threads, 0, s>>>(logits, T, E, k, ids, w, err);
+  else if (E <= 256) gating_kernel<8><<<blocks, threads, 0, s>>>(logits, T, E, k, ids, w, err);
+  else if (E <= 512) gating_kernel<16><<<blocks, threads, 0, s>>>(logits, T, E, k, ids, w, err);
+  else gating_kernel<32><<<blocks, threads, 0, s>>>(logits, T, E, k, ids, w, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+// ------------------------------------------------------- bf16 -> f16 copy
+__global__ void convert_bf16_kernel(const uint4* __restrict__ x, int64_t n8, uint4* __restrict__ y) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n8; i += int64_t(gridDim.x) * blockDim.x) {
+    uint4 v = x[i];
+    uint32_t in[4] = {v.x, v.y, v.z, v.w}, out[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float lo = __uint_as_float(in[j] << 16), hi = __uint_as_float(in[j] & 0xffff0000u);
+      __half2 h = __floats2half2_rn(lo, hi);
+      out[j] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    y[i] = make_uint4(out[0], out[1], out[2], out[3]);
+  }
+}
+
+int launch_convert_bf16(cudaStream_t s, const void* x, int64_t n, void* x16) {
+  const int64_t n8 = n / 8;
+  int blocks = int((n8 + 255) / 256);
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  if (blocks < 1) blocks = 1;
+  convert_bf16_kernel<<<blocks, 256, 0, s>>>(static_cast<const uint4*>(x), n8, static_cast<uint4*>(x16));
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+}  // namespace b200moe
