@@ -135,7 +135,7 @@ def test_route_plan_large_and_repeated(dev, pkg):
 
 
 def test_gating_bit_exact(dev, pkg):
-    from b200moe import moe, tiers
+    from b200moe import moe
 
     for (T, E, K) in ((8, 64, 6), (64, 384, 8), (300, 384, 8)):
         layer = moe.B200NativeMoe(hidden=256, inter=128, num_experts=E, top_k=K, max_tokens=8,
@@ -149,7 +149,6 @@ def test_gating_bit_exact(dev, pkg):
         assert np.array_equal(ids.cpu().numpy(), rid)
         assert np.array_equal(w.cpu().numpy().view(np.uint32), rw.view(np.uint32))
         layer.close()
-        del tiers
 
 
 # --------------------------------------------------------------- layers

@@ -183,7 +183,7 @@ __global__ void mx_globals_kernel(const int* __restrict__ span, int n_slots, flo
 }
 
 // One CTA of 128 threads per unit (tile pair x K tile).  Threads 0..127 write
-// the 2 x 1024 code bytes (16 each); the first 2*SB threads write one scale byte.
+// the 2 x 1024 code bytes (16 each), then the 2 * SB scale bytes in a strided loop.
 template <int FMT>
 __global__ void fp4_prepack_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ scales,
                                    int rows_per_slot, int k, int n_tp, int pair_rows_second,
@@ -218,8 +218,8 @@ __global__ void fp4_prepack_kernel(const uint8_t* __restrict__ codes, const uint
     *reinterpret_cast<uint4*>(out + mt * kCodesPerTile + h * 512 + lane * 16) =
         make_uint4(wv[0], wv[1], wv[2], wv[3]);
   }
-  if (t < 2 * SB) {
-    const int mt = t / SB, i = t % SB;
+  for (int idx = t; idx < 2 * SB; idx += blockDim.x) {
+    const int mt = idx / SB, i = idx % SB;
     uint32_t byte;
     if (FMT == 0) {  // [r 8][qb 2][h 2][c 4]
       const int r = i >> 4, qb = (i >> 3) & 1, h = (i >> 2) & 1, c = i & 3;
