@@ -57,6 +57,10 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--m", type=int, default=64, choices=[1, 8, 32, 64])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--experts", type=int, default=E,
+                    help="routed experts (384 = configs[1]; fewer only for a small ncu capture)")
+    ap.add_argument("--profile", action="store_true",
+                    help="warm-up + timed steps only (no per-launch, e2e or CPU passes): the ncu command")
     return ap.parse_args()
 
 
@@ -78,11 +82,16 @@ class Clocks:
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.err = tempfile.NamedTemporaryFile("w+", suffix=".err", delete=False)
+        visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if visible:
+            gpu_index = int(visible.split(",")[gpu_index])
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                       "-lms", "200", "-i", str(gpu_index)], stdout=self.f, stderr=subprocess.DEVNULL)
-        except OSError:
+                                       "-lms", "200", "-i", str(gpu_index)], stdout=self.f, stderr=self.err)
+        except OSError as exc:
             self.p = None
+            self.error = str(exc)
 
     def stop(self) -> dict | None:
         if self.p is None:
@@ -93,8 +102,11 @@ class Clocks:
         except subprocess.TimeoutExpired:
             self.p.kill()
         self.f.flush()
-        rows = [r.split(",") for r in Path(self.f.name).read_text().strip().splitlines() if r.strip()]
+        text = Path(self.f.name).read_text()
+        rows = [r.split(",") for r in text.strip().splitlines() if r.strip()]
+        err = Path(self.err.name).read_text().strip()
         os.unlink(self.f.name)
+        os.unlink(self.err.name)
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
@@ -107,7 +119,7 @@ class Clocks:
             except (ValueError, IndexError):
                 continue
         if not sm:
-            return None
+            return {"error": (err or text)[:200]}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
@@ -170,6 +182,12 @@ def main() -> None:
                     "inputs smaller than L2 at this M: weights may stay cached across steps",
               "parallelism": f"replicas x{world}" if world > 1 else "single GPU"}
 
+    n_exp = args.experts
+    if n_exp != E:
+        config["workload"] += f" (ncu capture case: {n_exp} experts)"
+        config["experts"] = n_exp
+        logits = logits[:, :n_exp].contiguous()
+
     if args.impl == "reference":
         if rank == 0:
             bank = synth.make_fp4_bank(E, H, I, "nvfp4", 1000, dev)
@@ -211,11 +229,23 @@ def main() -> None:
             dist.destroy_process_group()
         return
 
-    bank = synth.make_fp4_bank(E, H, I, "nvfp4", 1000, dev)
-    layer = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, max_tokens=64,
-                              tier=np.zeros(E, np.int8), device=dev)
+    bank = synth.make_fp4_bank(n_exp, H, I, "nvfp4", 1000, dev)
+    layer = moe.B200NativeMoe(hidden=H, inter=I, num_experts=n_exp, top_k=K_TOP, max_tokens=64,
+                              tier=np.zeros(n_exp, np.int8), device=dev)
     synth.load_bank(layer, bank)
     layer.check_errors()
+    if args.profile:
+        del bank
+        torch.cuda.synchronize()
+        for _ in range(args.warmup):
+            layer.forward(x, *layer.route(logits))
+        for _ in range(args.steps):
+            layer.forward(x, *layer.route(logits))
+        torch.cuda.synchronize()
+        layer.check_errors()
+        layer.close()
+        print(json.dumps({"profile_run": True, "experts": n_exp, "m": m}), flush=True)
+        return
 
     def step():
         ids, w = layer.route(logits)

@@ -27,16 +27,19 @@ namespace b200moe {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;
-constexpr int kStages = 6;
 constexpr int kRouteSlots = 16;  // activation row slots per stage (KS * route chunk)
 
+// FP4: two CTAs per SM (18 warps) with a 4-stage ring each; IQ2: one CTA with 6.
 template <int FMT>
 struct Fmt {
   static constexpr int KT = FMT == 2 ? kIq2KTile : kFp4KTile;            // K per unit
   static constexpr int U = FMT == 2 ? kIq2UnitBytes : fp4_unit_bytes(FMT); // unit bytes
   static constexpr int XRS = 2 * KT + 64;                                // x row slot bytes
   static constexpr int STAGE = kConsumerWarps * U + kRouteSlots * XRS;
+  static constexpr int CTAS = FMT == 2 ? 1 : 2;                          // CTAs per SM
+  static constexpr int STAGES = CTAS == 2 ? 4 : 6;
 };
+constexpr int kMaxStages = 6;
 
 constexpr int kRedBytes = kConsumerWarps * 32 * 16 * 4;
 constexpr int kIq2TableWords = 256 * 4 + 128 * 4 + 16;  // grid f16, sign masks, (0.5 + s) f16x2
@@ -44,7 +47,7 @@ constexpr int kListInts = 1 + 2 * 128;
 
 template <int FMT>
 constexpr size_t smem_total() {
-  return 128 + size_t(kStages) * Fmt<FMT>::STAGE + kRedBytes + (FMT == 2 ? kIq2TableWords * 4 : 0) +
+  return 128 + size_t(Fmt<FMT>::STAGES) * Fmt<FMT>::STAGE + kRedBytes + (FMT == 2 ? kIq2TableWords * 4 : 0) +
          kListInts * 4;
 }
 
@@ -52,9 +55,14 @@ size_t gemv_smem_bytes(int fmt, int) {
   return fmt == 0 ? smem_total<0>() : fmt == 1 ? smem_total<1>() : smem_total<2>();
 }
 
+int gemv_ctas_per_sm(int fmt) { return fmt == 2 ? Fmt<2>::CTAS : Fmt<0>::CTAS; }
+
 // ---------------------------------------------------------------- FP4 step
+// acc[mt][nt][j]: one accumulator per k16 step parity, so each tile has two
+// independent MMA chains; they are summed in the epilogue.
 template <int FMT>
-__device__ __forceinline__ void fp4_step(uint32_t wb, uint32_t xb, int ntiles, int lane, float (&acc)[2][2][4]) {
+__device__ __forceinline__ void fp4_step(uint32_t wb, uint32_t xb, int ntiles, int lane,
+                                         float (&acc)[2][2][2][4]) {
   constexpr int XRS = Fmt<FMT>::XRS;
   const int r = lane >> 2, q = lane & 3;
   uint4 cw[2][2];
@@ -93,14 +101,14 @@ __device__ __forceinline__ void fp4_step(uint32_t wb, uint32_t xb, int ntiles, i
       a[3] = hmul2(e2m1x2_byte<1>(w1), s1);
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
-        if (nt < ntiles) mma_16816(acc[mt][nt], a, xv[nt].x, xv[nt].y);
+        if (nt < ntiles) mma_16816(acc[mt][nt][0], a, xv[nt].x, xv[nt].y);
       a[0] = hmul2(e2m1x2_byte<2>(w0), s0);
       a[1] = hmul2(e2m1x2_byte<2>(w1), s1);
       a[2] = hmul2(e2m1x2_byte<3>(w0), s0);
       a[3] = hmul2(e2m1x2_byte<3>(w1), s1);
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
-        if (nt < ntiles) mma_16816(acc[mt][nt], a, xv[nt].z, xv[nt].w);
+        if (nt < ntiles) mma_16816(acc[mt][nt][1], a, xv[nt].z, xv[nt].w);
     }
   }
 }
@@ -109,7 +117,7 @@ __device__ __forceinline__ void fp4_step(uint32_t wb, uint32_t xb, int ntiles, i
 // One 256-wide super-block.  A = grid * sign * (0.5 + s) is exact in f16; the
 // super-block scale d * 0.25 is applied to a per-block partial in FP32.
 __device__ __forceinline__ void iq2_step(uint32_t wb, uint32_t xb, uint32_t tbl, int ntiles, int lane,
-                                         float (&acc)[2][2][4]) {
+                                         float (&acc)[2][2][2][4]) {
   constexpr int XRS = Fmt<2>::XRS;
   const int r = lane >> 2, q = lane & 3;
   float t[2][2][4];
@@ -169,10 +177,10 @@ __device__ __forceinline__ void iq2_step(uint32_t wb, uint32_t xb, uint32_t tbl,
     const float d0 = __low2float(d2) * 0.25f, d1 = __high2float(d2) * 0.25f;
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
-      acc[mt][nt][0] = fmaf(t[mt][nt][0], d0, acc[mt][nt][0]);
-      acc[mt][nt][1] = fmaf(t[mt][nt][1], d0, acc[mt][nt][1]);
-      acc[mt][nt][2] = fmaf(t[mt][nt][2], d1, acc[mt][nt][2]);
-      acc[mt][nt][3] = fmaf(t[mt][nt][3], d1, acc[mt][nt][3]);
+      acc[mt][nt][0][0] = fmaf(t[mt][nt][0], d0, acc[mt][nt][0][0]);
+      acc[mt][nt][0][1] = fmaf(t[mt][nt][1], d0, acc[mt][nt][0][1]);
+      acc[mt][nt][0][2] = fmaf(t[mt][nt][2], d1, acc[mt][nt][0][2]);
+      acc[mt][nt][0][3] = fmaf(t[mt][nt][3], d1, acc[mt][nt][0][3]);
     }
   }
 }
@@ -193,15 +201,16 @@ __device__ __forceinline__ __half swiglu_one(float g, float u, float limit) {
 }
 
 template <int FMT, int EPI, int KS>
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, Fmt<FMT>::CTAS) gemv_kernel(const GemvArgs a) {
   using F = Fmt<FMT>;
+  constexpr int kStages = F::STAGES;
   constexpr int TP = kConsumerWarps / KS;  // tile pairs per item
   constexpr int RC = kRouteSlots / KS;     // routes per chunk
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kStages;
   uint8_t* stages = smem + 128;
-  float* red = reinterpret_cast<float*>(stages + size_t(kStages) * F::STAGE);
+  float* red = reinterpret_cast<float*>(stages + size_t(kStages) * F::STAGE);  // [warp][16][lane]
   uint32_t* tables = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(red) + kRedBytes);
   int* list = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(tables) + (FMT == 2 ? kIq2TableWords * 4 : 0));
   __shared__ int abort_flag;
@@ -296,13 +305,15 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
       const int rb = item % n_rb;
       const int tp = rb * TP + tpl;
       const int ntiles = (ch.count + 7) >> 3;
-      float acc[2][2][4];
+      float acc2[2][2][2][4];
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) acc[mt][nt][i] = 0.f;
+          for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc2[mt][nt][j][i] = 0.f;
       for (int st = 0; st < steps; ++st, ++g) {
         const int s = g % kStages;
         const uint32_t ph = (g / kStages) & 1u;
@@ -315,24 +326,31 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
         const uint32_t sb = smem_u32(stages + size_t(s) * F::STAGE);
         const uint32_t wb = sb + warp * F::U;
         const uint32_t xb = sb + kConsumerWarps * F::U + ks * RC * F::XRS;
-        if (FMT == 2) iq2_step(wb, xb, tbl, ntiles, lane, acc);
-        else fp4_step<FMT>(wb, xb, ntiles, lane, acc);
+        if (FMT == 2) iq2_step(wb, xb, tbl, ntiles, lane, acc2);
+        else fp4_step<FMT>(wb, xb, ntiles, lane, acc2);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
       }
+      float acc[2][2][4];
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[mt][nt][i] = acc2[mt][nt][0][i] + acc2[mt][nt][1][i];
       // split-K partials: fixed order ks = 0, 1, ..
       if (KS > 1) {
-        float* mine = red + (warp * 32 + lane) * 16;
+        float* mine = red + warp * 32 * 16 + lane;
         if (ks != 0) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) mine[i] = (&acc[0][0][0])[i];
+          for (int i = 0; i < 16; ++i) mine[i * 32] = (&acc[0][0][0])[i];
         }
         named_bar(1, kConsumerWarps * 32);
         if (ks == 0) {
           for (int kk = 1; kk < KS; ++kk) {
-            const float* other = red + ((warp + kk) * 32 + lane) * 16;
+            const float* other = red + (warp + kk) * 32 * 16 + lane;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) (&acc[0][0][0])[i] += other[i];
+            for (int i = 0; i < 16; ++i) (&acc[0][0][0])[i] += other[i * 32];
           }
         }
         named_bar(1, kConsumerWarps * 32);

@@ -101,6 +101,7 @@ struct GemvArgs {
 };
 
 size_t gemv_smem_bytes(int fmt, int ks);
+int gemv_ctas_per_sm(int fmt);
 int launch_gemv(cudaStream_t s, const GemvArgs& a);
 
 }  // namespace b200moe

@@ -105,8 +105,9 @@ int choose_ks(const b200moe_layer* L, int bank, int rows) {
     const int rc = 16 / ks;
     const double chunks = std::max(groups, std::ceil(routes / double(rc)));
     const double items = chunks * double(c.inter / 16) / double(8 / ks);
-    const double waves = std::ceil(items / L->grid);
-    const double eff = items / (waves * L->grid);
+    const int slots = L->grid * gemv_ctas_per_sm(bank == 0 ? c.fp4_format : 2);
+    const double waves = std::ceil(items / slots);
+    const double eff = items / (waves * slots);
     if (eff > best_eff + 0.02) {
       best_eff = eff;
       best = ks;
@@ -206,7 +207,7 @@ int run_forward(b200moe_layer* L, cudaStream_t s, const void* x, int x_dtype, co
       g.H = c.hidden;
       g.iq2_tables = L->iq2_tables;
       g.err = L->err;
-      g.grid = L->grid;
+      g.grid = L->grid * gemv_ctas_per_sm(g.fmt);
       if (launch_gemv(s, g)) return B200MOE_ERR_CUDA;
       marks.mark();
     }
