@@ -128,6 +128,24 @@ int b200moe_forward(b200moe_layer* layer, void* stream, const void* x, int x_dty
 int b200moe_forward_prefill(b200moe_layer* layer, void* stream, const void* x, int x_dtype,
                             const int32_t* topk_ids, const float* topk_weights, float* out, int T);
 
+/* Decode forward that allocates nothing.  No counterpart in the reference:
+ * the reference's decode buffers are allocated with the layer.
+ *
+ * Same contract and kernels as b200moe_forward, but the per-call scratch
+ * (route permutation, route chunks, fp16 activations, SwiGLU rows, weighted
+ * route rows, combine counters) sits in one fixed array inside this library
+ * instead of the layer's workspace.  It is for callers that cannot allocate
+ * device memory when they run a decode step, e.g. an engine that gives all
+ * free HBM to its KV cache after start-up and allows no cudaMalloc later.
+ * Limits: M <= 16, top_k <= 8, hidden <= 4096, inter <= 2048, and at most 512
+ * experts held by the layer; larger sizes return B200MOE_ERR_RANGE.  The array
+ * (about 2.6 MB) is held on every GPU that loads the library until exit.  The
+ * first call on a device looks up the array's device address; make that first
+ * call before any stream capture.  Every call shares the array and zeroes its
+ * combine counters on `stream` first; calls that overlap on the GPU race. */
+int b200moe_forward_static(b200moe_layer* layer, void* stream, const void* x, int x_dtype,
+                           const int32_t* topk_ids, const float* topk_weights, float* out, int M);
+
 /* Wait for `stream`, then read and clear the layer's kernel error word.
  * Returns the status the bits map to (B200MOE_OK when none); *bits gets them. */
 int b200moe_check_errors(b200moe_layer* layer, void* stream, uint32_t* bits);

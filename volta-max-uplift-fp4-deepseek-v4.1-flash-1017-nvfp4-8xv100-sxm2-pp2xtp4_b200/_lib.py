@@ -53,6 +53,7 @@ SIGNATURES = {
     "b200moe_route": ([P, P, P, P, P, I32], I32),
     "b200moe_forward": ([P, P, P, I32, P, P, P, I32], I32),
     "b200moe_forward_prefill": ([P, P, P, I32, P, P, P, I32], I32),
+    "b200moe_forward_static": ([P, P, P, I32, P, P, P, I32], I32),
     "b200moe_check_errors": ([P, P, ctypes.POINTER(ctypes.c_uint32)], I32),
     "b200moe_set_debug_y13": ([P, P], I32),
     "b200moe_debug_perm": ([P, P, P, I32], I32),

@@ -12,6 +12,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <mutex>
 #include <vector>
 
 #include "common.cuh"
@@ -500,3 +501,168 @@ int b200moe_route_plan(void* stream, const int32_t* ids, int n, int num_experts,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Decode forward with a fixed, library-owned workspace (no allocation).
+//
+// b200moe_forward keeps its per-call intermediates (route permutation, route
+// chunks, fp16 activations, SwiGLU rows, weighted route rows, combine
+// counters) in a workspace that b200moe_layer_create allocates for each layer.
+// Some callers cannot allocate device memory at the time they need a decode
+// forward: an engine that hands all free HBM to its KV cache after start-up
+// and forbids later cudaMalloc calls, or code that must run where its own
+// allocator may not be entered.  b200moe_forward_static runs the same kernels
+// with that workspace taken from one array compiled into this library, so
+// the call allocates nothing.  The array lives on every GPU that loads the
+// library until the process exits, it is shared by all layers and all calls,
+// and calls that overlap on the GPU race on it.
+namespace {
+
+constexpr int kStaticMaxTokens = 16;
+constexpr int kStaticMaxTopK = 8;
+constexpr int kStaticMaxHidden = 4096;
+constexpr int kStaticMaxInter = 2048;
+constexpr int kStaticMaxSlots = 512;  // experts held by one layer on this GPU
+constexpr int kStaticRoutes = kStaticMaxTokens * kStaticMaxTopK;
+constexpr size_t kStaticMaxChunks = kStaticRoutes + kStaticMaxSlots;
+
+constexpr size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+constexpr size_t kOffPerm = 0;
+constexpr size_t kOffWeff = kOffPerm + align256(kStaticRoutes * 4);
+constexpr size_t kOffChunks0 = kOffWeff + align256(kStaticRoutes * 4);
+constexpr size_t kOffChunks1 = kOffChunks0 + align256(kStaticMaxChunks * sizeof(Chunk));
+constexpr size_t kOffNChunks = kOffChunks1 + align256(kStaticMaxChunks * sizeof(Chunk));
+constexpr size_t kOffX16 = kOffNChunks + 256;
+constexpr size_t kOffInter = kOffX16 + align256(size_t(kStaticMaxTokens) * kStaticMaxHidden * 2);
+constexpr size_t kOffYw = kOffInter + align256(size_t(kStaticRoutes) * kStaticMaxInter * 2);
+constexpr size_t kOffCounters = kOffYw + align256(size_t(kStaticRoutes) * kStaticMaxHidden * 4);
+constexpr size_t kStaticScratchBytes = kOffCounters + align256(size_t(kStaticMaxTokens) * (kStaticMaxHidden / 32) * 4);
+
+// About 2.6 MB per GPU (see the limits above).
+static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
+
+// Device address of g_static_scratch per device, looked up on the first call
+// on that device (the host-side name of the array is not a device address).
+constexpr int kMaxDevices = 64;
+uint8_t* g_scratch_addr[kMaxDevices] = {};
+std::mutex g_scratch_mutex;
+
+int static_scratch(int device, uint8_t** out) {
+  if (device < 0 || device >= kMaxDevices) return B200MOE_ERR_INVALID_ARG;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (!g_scratch_addr[device]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || !p) {
+      cudaGetLastError();
+      return B200MOE_ERR_CUDA;
+    }
+    g_scratch_addr[device] = static_cast<uint8_t*>(p);
+  }
+  *out = g_scratch_addr[device];
+  return B200MOE_OK;
+}
+
+}  // namespace
+
+extern "C" int b200moe_forward_static(b200moe_layer* L, void* stream, const void* x, int x_dtype,
+                                      const int32_t* ids, const float* w, float* out, int M) {
+  if (!L || M < 1) return B200MOE_ERR_INVALID_ARG;
+  const auto& c = L->cfg;
+  if (M > kStaticMaxTokens || c.top_k > kStaticMaxTopK || c.hidden > kStaticMaxHidden ||
+      c.inter > kStaticMaxInter || c.n_fp4 + c.n_iq2 > kStaticMaxSlots)
+    return B200MOE_ERR_RANGE;
+  if (!L->maps_set) return B200MOE_ERR_STATE;
+  if (c.n_iq2 > 0 && !L->tables_set) return B200MOE_ERR_STATE;
+  if (!x || !ids || !w || !out) return B200MOE_ERR_INVALID_ARG;
+  if (x_dtype != B200MOE_F16 && x_dtype != B200MOE_BF16) return B200MOE_ERR_DTYPE;
+  if (!aligned(x, 16) || !aligned(out, 16)) return B200MOE_ERR_ALIGN;
+  DeviceGuard guard(L->device);
+  uint8_t* ws = nullptr;
+  if (int st = static_scratch(L->device, &ws)) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t* perm = reinterpret_cast<int32_t*>(ws + kOffPerm);
+  float* w_eff = reinterpret_cast<float*>(ws + kOffWeff);
+  Chunk* chunks[2] = {reinterpret_cast<Chunk*>(ws + kOffChunks0), reinterpret_cast<Chunk*>(ws + kOffChunks1)};
+  int32_t* n_chunks = reinterpret_cast<int32_t*>(ws + kOffNChunks);
+  __half* x16 = reinterpret_cast<__half*>(ws + kOffX16);
+  __half* inter = reinterpret_cast<__half*>(ws + kOffInter);
+  float* yw = reinterpret_cast<float*>(ws + kOffYw);
+  int32_t* counters = reinterpret_cast<int32_t*>(ws + kOffCounters);
+  // The array keeps the previous call's contents: the combine counters must
+  // start at zero, and the SwiGLU rows are read whole by the W2 launch.
+  if (cudaMemsetAsync(counters, 0, size_t(M) * (c.hidden / 32) * 4, s) != cudaSuccess) return B200MOE_ERR_CUDA;
+  const int S = M * c.top_k;
+  const __half* xsrc = static_cast<const __half*>(x);
+  if (x_dtype == B200MOE_BF16) {
+    if (launch_convert_bf16(s, x, int64_t(M) * c.hidden, x16)) return B200MOE_ERR_CUDA;
+    xsrc = x16;
+  }
+  int ks[2] = {choose_ks(L, 0, M), choose_ks(L, 1, M)};
+  PlanArgs p{};
+  p.ids = ids;
+  p.n = S;
+  p.num_experts = c.num_experts;
+  p.key_of_expert = L->key_of_expert;
+  p.n_keys = c.n_fp4 + c.n_iq2;
+  p.perm = perm;
+  p.n_banks = 2;
+  p.key_lo[0] = 0;
+  p.key_hi[0] = c.n_fp4;
+  p.key_lo[1] = c.n_fp4;
+  p.key_hi[1] = c.n_fp4 + c.n_iq2;
+  for (int b = 0; b < 2; ++b) {
+    p.rc[b] = 16 / ks[b];
+    p.max_chunks[b] = int(kStaticMaxChunks);
+    p.chunks[b] = chunks[b];
+  }
+  p.n_chunks = n_chunks;
+  p.w_in = w;
+  p.w_eff = w_eff;
+  p.yw = yw;
+  p.counters = counters;
+  p.out = out;
+  p.H = c.hidden;
+  p.top_k = c.top_k;
+  p.err = L->err;
+  if (launch_plan(s, p)) return B200MOE_ERR_CUDA;
+  for (int epi = 0; epi < 2; ++epi) {
+    for (int b = 0; b < 2; ++b) {
+      const int n_slots = b == 0 ? c.n_fp4 : c.n_iq2;
+      if (n_slots == 0) continue;
+      GemvArgs g{};
+      g.fmt = b == 0 ? c.fp4_format : 2;
+      g.epi = epi;
+      g.ks = ks[b];
+      g.region = L->bank[b] + (epi == 0 ? 0 : L->geom[b].w13_bytes);
+      g.slot_stride = L->geom[b].slot_bytes;
+      g.n_slots = n_slots;
+      g.globals = b == 0 ? L->globals : nullptr;
+      g.K = epi == 0 ? c.hidden : c.inter;
+      g.n_tp = epi == 0 ? c.inter / 16 : c.hidden / 32;
+      g.chunks = chunks[b];
+      g.n_chunks = n_chunks;
+      g.bank = b;
+      g.perm = perm;
+      g.S = S;
+      g.top_k = c.top_k;
+      g.xsrc = epi == 0 ? static_cast<const void*>(xsrc) : static_cast<const void*>(inter);
+      g.x_by_token = epi == 0;
+      g.x_row_stride = epi == 0 ? c.hidden : c.inter;
+      g.n_x_rows = epi == 0 ? M : S;
+      g.inter = inter;
+      g.inter_stride = c.inter;
+      g.dbg_y13 = nullptr;
+      g.limit = c.swiglu_limit;
+      g.w_eff = w_eff;
+      g.yw = yw;
+      g.counters = counters;
+      g.out = out;
+      g.H = c.hidden;
+      g.iq2_tables = L->iq2_tables;
+      g.err = L->err;
+      g.grid = L->grid * gemv_ctas_per_sm(g.fmt);
+      if (launch_gemv(s, g)) return B200MOE_ERR_CUDA;
+    }
+  }
+  return B200MOE_OK;
+}

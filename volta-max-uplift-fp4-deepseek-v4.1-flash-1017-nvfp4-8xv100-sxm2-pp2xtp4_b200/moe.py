@@ -163,6 +163,19 @@ class B200NativeMoe:
             self._h, _stream(), x.data_ptr(), dt, topk_ids.data_ptr(), topk_weights.data_ptr(), out.data_ptr(), m))
         return out
 
+    def forward_static(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
+                       out: torch.Tensor) -> torch.Tensor:
+        """Decode forward that allocates nothing: its scratch is one array built
+        into the library (M <= 16, top-k <= 8, hidden <= 4096, inter <= 2048,
+        <= 512 experts on this GPU), for callers that may not allocate device
+        memory at decode time.  Writes the caller's fp32 ``out`` [M, H].  Calls
+        share that array, so they must not overlap on the GPU."""
+        m, dt = self._check_io(x, topk_ids, topk_weights)
+        _want("out", out, torch.float32, (m, self.hidden), self.device)
+        _lib.check("b200moe_forward_static", _lib.lib().b200moe_forward_static(
+            self._h, _stream(), x.data_ptr(), dt, topk_ids.data_ptr(), topk_weights.data_ptr(), out.data_ptr(), m))
+        return out
+
     def check_errors(self) -> None:
         """Synchronize and raise if a kernel recorded an error since the last check."""
         bits = ctypes.c_uint32(0)
