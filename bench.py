@@ -32,9 +32,7 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 from pathlib import Path
 
@@ -73,54 +71,60 @@ def peaks() -> dict:
 
 
 class Clocks:
-    """nvidia-smi sampled every 200 ms while the timed region runs."""
+    """SM clock and throttle reasons polled through NVML every 2 ms while the
+    timed region runs (reading only; no setting is changed)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown"}
 
-    def __init__(self, gpu_index: int):
-        self.idx = gpu_index
-        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-        self.err = tempfile.NamedTemporaryFile("w+", suffix=".err", delete=False)
-        visible = os.environ.get("CUDA_VISIBLE_DEVICES")
-        if visible:
-            gpu_index = int(visible.split(",")[gpu_index])
+    def __init__(self, device):
+        import threading
+
+        self.samples, self.bits, self.error = [], 0, None
+        self.max_mhz = None
         try:
-            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                       "-lms", "200", "-i", str(gpu_index)], stdout=self.f, stderr=self.err)
-        except OSError as exc:
-            self.p = None
-            self.error = str(exc)
+            import pynvml
 
-    def stop(self) -> dict | None:
-        if self.p is None:
-            return None
-        self.p.terminate()
-        try:
-            self.p.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.p.kill()
-        self.f.flush()
-        text = Path(self.f.name).read_text()
-        rows = [r.split(",") for r in text.strip().splitlines() if r.strip()]
-        err = Path(self.err.name).read_text().strip()
-        os.unlink(self.f.name)
-        os.unlink(self.err.name)
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            import torch
+
+            props = torch.cuda.get_device_properties(device)
             try:
-                sm.append(float(r[1]))
-                mx = float(r[2])
-                for n, v in zip(names, r[5:9]):
-                    if v.strip().lower() == "active":
-                        reasons.add(n)
-            except (ValueError, IndexError):
-                continue
-        if not sm:
-            return {"error": (err or text)[:200]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+                bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+                self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(device.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as exc:  # no NVML: report why
+            self.error = f"nvml unavailable: {exc}"[:200]
+            return
+        self.stop_flag = threading.Event()
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
+
+    def _run(self):
+        nv = self.nv
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop_flag.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                self.bits |= int(get_reasons(self.h))
+            except Exception as exc:
+                self.error = str(exc)[:200]
+                return
+            self.stop_flag.wait(0.002)
+
+    def stop(self) -> dict:
+        if self.error and not self.samples:
+            return {"error": self.error}
+        self.stop_flag.set()
+        self.t.join(timeout=2)
+        if not self.samples:
+            return {"error": self.error or "no samples"}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(n for b, n in self.REASONS.items() if self.bits & b),
+                "samples": len(self.samples), "source": "nvml, polled every 2 ms during the timed region"}
 
 
 def cpu_layer_tokens_per_s(bank, ids_np, w_np, x_np, m, reps=2) -> dict:
@@ -260,7 +264,7 @@ def main() -> None:
     # ---- value: K steps, inputs resident, CUDA events on the current stream
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks = Clocks(dev.index) if rank == 0 else None
+    clocks = Clocks(dev) if rank == 0 else None
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()

@@ -80,6 +80,8 @@ typedef struct {
   int32_t n_fp4;              /* slots in bank 0 */
   int32_t n_iq2;              /* slots in bank 1 */
   float swiglu_limit;         /* limited SwiGLU bound (reference: 10.0) */
+  int32_t prefill_gemm;       /* forward_prefill's FP4 bank: 0 = the skinny decode kernels,
+                                 1 = the tcgen05 grouped GEMM (route tiles of 128) */
 } b200moe_config;
 
 typedef struct b200moe_layer b200moe_layer;
@@ -132,14 +134,14 @@ int b200moe_forward_prefill(b200moe_layer* layer, void* stream, const void* x, i
  * the reference's decode buffers are allocated with the layer.
  *
  * Same contract and kernels as b200moe_forward, but the per-call scratch
- * (route permutation, route chunks, fp16 activations, SwiGLU rows, weighted
- * route rows, combine counters) sits in one fixed array inside this library
+ * (route permutation, route chunks, fp16 activations, SwiGLU rows, W2 route
+ * rows, combine counters) sits in one fixed array inside this library
  * instead of the layer's workspace.  It is for callers that cannot allocate
  * device memory when they run a decode step, e.g. an engine that gives all
  * free HBM to its KV cache after start-up and allows no cudaMalloc later.
  * Limits: M <= 16, top_k <= 8, hidden <= 4096, inter <= 2048, and at most 512
  * experts held by the layer; larger sizes return B200MOE_ERR_RANGE.  The array
- * (about 2.6 MB) is held on every GPU that loads the library until exit.  The
+ * (about 1.7 MB) is held on every GPU that loads the library until exit.  The
  * first call on a device looks up the array's device address; make that first
  * call before any stream capture.  Every call shares the array and zeroes its
  * combine counters on `stream` first; calls that overlap on the GPU race. */

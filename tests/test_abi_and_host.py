@@ -52,7 +52,7 @@ def test_status_names_and_version(lib):
 def test_config_struct_layout(pkg):
     from b200moe import _lib
 
-    assert ctypes.sizeof(_lib.Config) == 40
+    assert ctypes.sizeof(_lib.Config) == 44
     text = HEADER.read_text()
     block = text[text.index("typedef struct {"):text.index("} b200moe_config;")]
     fields = re.findall(r"(?:int32_t|float)\s+(\w+);", block)
@@ -63,9 +63,9 @@ def test_create_refuses_bad_config_without_gpu(lib, pkg):
     from b200moe import _lib
 
     h = ctypes.c_void_p()
-    bad = _lib.Config(300, 2048, 384, 8, 64, 0, 0, 384, 0, 10.0)  # hidden not a multiple of 256
+    bad = _lib.Config(300, 2048, 384, 8, 64, 0, 0, 384, 0, 10.0, 0)  # hidden not a multiple of 256
     assert lib.b200moe_layer_create(ctypes.byref(bad), 0, ctypes.byref(h)) == 1
-    bad = _lib.Config(4096, 2048, 384, 8, 65, 0, 0, 384, 0, 10.0)  # max_tokens > 64
+    bad = _lib.Config(4096, 2048, 384, 8, 65, 0, 0, 384, 0, 10.0, 0)  # max_tokens > 64
     assert lib.b200moe_layer_create(ctypes.byref(bad), 0, ctypes.byref(h)) == 1
 
 

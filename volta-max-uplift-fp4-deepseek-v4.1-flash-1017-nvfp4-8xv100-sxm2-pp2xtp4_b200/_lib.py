@@ -37,7 +37,8 @@ class Config(ctypes.Structure):
     _fields_ = [("hidden", ctypes.c_int32), ("inter", ctypes.c_int32), ("num_experts", ctypes.c_int32),
                 ("top_k", ctypes.c_int32), ("max_tokens", ctypes.c_int32),
                 ("max_prefill_tokens", ctypes.c_int32), ("fp4_format", ctypes.c_int32),
-                ("n_fp4", ctypes.c_int32), ("n_iq2", ctypes.c_int32), ("swiglu_limit", ctypes.c_float)]
+                ("n_fp4", ctypes.c_int32), ("n_iq2", ctypes.c_int32), ("swiglu_limit", ctypes.c_float),
+                ("prefill_gemm", ctypes.c_int32)]
 
 
 # name -> (argtypes, restype); every symbol include/b200moe.h declares

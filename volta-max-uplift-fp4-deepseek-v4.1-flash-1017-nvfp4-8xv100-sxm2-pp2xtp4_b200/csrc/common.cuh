@@ -62,12 +62,14 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// try_wait with a suspend-time hint: a warp whose phase is not complete sleeps
+// (up to 1 ms) until it completes instead of spinning on the issue slots.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
-      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
       : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
       : "memory");
   return done != 0;
 }
@@ -78,7 +80,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   const uint64_t t0 = global_timer_ns();
   for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 255u && global_timer_ns() - t0 > kWaitLimitNs) {
+    if ((it & 3u) == 3u && global_timer_ns() - t0 > kWaitLimitNs) {
       set_error(err, kErrTimeout);
       return false;
     }
@@ -135,6 +137,20 @@ __device__ __forceinline__ uint32_t e2m1x2_byte(uint32_t word) {
         : "=r"(out)
         : "r"(word));
   return out;
+}
+
+// Four bytes of E2M1 pairs (8 values, low nibble first) -> four f16x2, each
+// multiplied by the f16x2 scale s2: one unpack for the whole word.  Exact when
+// value x scale is representable in f16 (always for the E4M3 / rebased E8M0 scales).
+__device__ __forceinline__ void e2m1x8_scaled(uint32_t w, uint32_t s2, uint32_t (&o)[4]) {
+  asm("{ .reg .b8 b0, b1, b2, b3; .reg .b32 h0, h1, h2, h3;\n"
+      " mov.b32 {b0, b1, b2, b3}, %4;\n"
+      " cvt.rn.f16x2.e2m1x2 h0, b0;\n cvt.rn.f16x2.e2m1x2 h1, b1;\n"
+      " cvt.rn.f16x2.e2m1x2 h2, b2;\n cvt.rn.f16x2.e2m1x2 h3, b3;\n"
+      " mul.rn.f16x2 %0, h0, %5;\n mul.rn.f16x2 %1, h1, %5;\n"
+      " mul.rn.f16x2 %2, h2, %5;\n mul.rn.f16x2 %3, h3, %5; }"
+      : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
+      : "r"(w), "r"(s2));
 }
 
 // Two E4M3 bytes (low byte = lower half) -> f16x2.  Exact.

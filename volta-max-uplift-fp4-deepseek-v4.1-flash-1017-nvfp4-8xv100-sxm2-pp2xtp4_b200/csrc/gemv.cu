@@ -13,9 +13,10 @@
 // cores (m16n8k16, f32 accumulate), routes as the N dimension.
 //   EPI 0 (W13): y13 = acc * global, rounded to fp16 as the reference's y13 is,
 //     then the limited SwiGLU in FP32 -> fp16 inter rows (by route position).
-//   EPI 1 (W2): yw[route] = acc * global * router weight (fp32); the CTA that
-//     completes a (token, 32-row tile) -- counted with one atomic per route --
-//     sums the token's k route rows in slot order and writes out.  The sum is
+//   EPI 1 (W2): y2[route] = fp16(acc * global), the reference's fp16 y2 row;
+//     the CTA that completes a (token, 32-row tile) -- counted with one atomic
+//     per route -- forms sum over slots of f32(y2) * router weight in slot
+//     order (the reference's weighted reduce) and writes out.  The sum is
 //     always taken in slot order, so the result does not depend on timing.
 #include <cuda_runtime.h>
 
@@ -94,21 +95,17 @@ __device__ __forceinline__ void fp4_step(uint32_t wb, uint32_t xb, int ntiles, i
       }
       const uint32_t w0 = c == 0 ? cw[mt][0].x : c == 1 ? cw[mt][0].y : c == 2 ? cw[mt][0].z : cw[mt][0].w;
       const uint32_t w1 = c == 0 ? cw[mt][1].x : c == 1 ? cw[mt][1].y : c == 2 ? cw[mt][1].z : cw[mt][1].w;
-      uint32_t a[4];
-      a[0] = hmul2(e2m1x2_byte<0>(w0), s0);
-      a[1] = hmul2(e2m1x2_byte<0>(w1), s1);
-      a[2] = hmul2(e2m1x2_byte<1>(w0), s0);
-      a[3] = hmul2(e2m1x2_byte<1>(w1), s1);
+      uint32_t o0[4], o1[4];
+      e2m1x8_scaled(w0, s0, o0);  // row r: bytes 0,1 -> k16 step 0, bytes 2,3 -> step 1
+      e2m1x8_scaled(w1, s1, o1);  // row r + 8
+      uint32_t a[4] = {o0[0], o1[0], o0[1], o1[1]};
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
         if (nt < ntiles) mma_16816(acc[mt][nt][0], a, xv[nt].x, xv[nt].y);
-      a[0] = hmul2(e2m1x2_byte<2>(w0), s0);
-      a[1] = hmul2(e2m1x2_byte<2>(w1), s1);
-      a[2] = hmul2(e2m1x2_byte<3>(w0), s0);
-      a[3] = hmul2(e2m1x2_byte<3>(w1), s1);
+      uint32_t a2[4] = {o0[2], o1[2], o0[3], o1[3]};
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
-        if (nt < ntiles) mma_16816(acc[mt][nt][1], a, xv[nt].z, xv[nt].w);
+        if (nt < ntiles) mma_16816(acc[mt][nt][1], a2, xv[nt].z, xv[nt].w);
     }
   }
 }
@@ -390,12 +387,12 @@ __global__ void __launch_bounds__(kGemvThreads, Fmt<FMT>::CTAS) gemv_kernel(cons
               const int n = nt * 8 + 2 * q + e;
               if (n >= ch.count) continue;
               const int route = a.perm[ch.begin + n];
-              const float wr = a.w_eff[route];
-              float* yrow = a.yw + int64_t(route) * a.H;
+              __half* yrow = static_cast<__half*>(a.y2) + int64_t(route) * a.H;
 #pragma unroll
               for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-                for (int h = 0; h < 2; ++h) yrow[32 * tp + 16 * mt + r + 8 * h] = (acc[mt][nt][2 * h + e] * g2) * wr;
+                for (int h = 0; h < 2; ++h)
+                  yrow[32 * tp + 16 * mt + r + 8 * h] = __float2half_rn(acc[mt][nt][2 * h + e] * g2);
             }
         }
       }
@@ -423,9 +420,13 @@ __global__ void __launch_bounds__(kGemvThreads, Fmt<FMT>::CTAS) gemv_kernel(cons
           const int tok = list[1 + 2 * e], tile = list[2 + 2 * e];
           __threadfence();
           const int row = 32 * tile + lane;
+          const unsigned short* y2 = static_cast<const unsigned short*>(a.y2);
           float sum = 0.f;
-          for (int slot = 0; slot < a.top_k; ++slot)
-            sum += __ldcg(a.yw + (int64_t(tok) * a.top_k + slot) * a.H + row);
+          for (int slot = 0; slot < a.top_k; ++slot) {
+            const int route = tok * a.top_k + slot;
+            const float y = __half2float(__ushort_as_half(__ldcg(y2 + int64_t(route) * a.H + row)));
+            sum = __fmaf_rn(y, __ldcg(a.w_eff + route), sum);
+          }
           a.out[int64_t(tok) * a.H + row] = sum;
           if (lane == 0) a.counters[int64_t(tok) * (a.H / 32) + tile] = 0;
         }

@@ -43,9 +43,9 @@ struct PlanArgs {
   int32_t* n_chunks;    // [2]
   const float* w_in;    // [n] router weights (product)
   float* w_eff;         // [n] weight used by the combine (0 for a route without an expert)
-  // product: a route without an expert gets a zero yw row and its completion
+  // product: a route without an expert gets a zero y2 row and its completion
   // counts (so the fused combine still sees k arrivals per token and tile)
-  float* yw;            // [n][H]
+  void* y2;             // fp16 [n][H] W2 rows by route index
   int32_t* counters;    // [tokens][H/32]
   float* out;           // [tokens][H]
   int H;
@@ -91,7 +91,7 @@ struct GemvArgs {
   void* dbg_y13;              // optional f16 [S][2 * inter_stride]
   float limit;
   const float* w_eff;         // [S] by route index
-  float* yw;                  // [S][H] by route index
+  void* y2;                   // fp16 [S][H] W2 rows (x global, unweighted) by route index
   int32_t* counters;          // [tokens][H/32]
   float* out;                 // [tokens][H]
   int H;
@@ -100,8 +100,41 @@ struct GemvArgs {
   int grid;                   // persistent CTAs
 };
 
+// ---- prefill grouped GEMM on tcgen05 (gemm_tc.cu)
+struct TcArgs;
+int make_token_map(void* map_out, const void* base, int64_t rows, int64_t cols);
+size_t tc_map_bytes();
+int launch_gather_rows(cudaStream_t s, const void* x, int bf16, const int32_t* perm, int S, int k, int H,
+                       void* xperm);
+constexpr int kTcTokenTile = 128;
+
 size_t gemv_smem_bytes(int fmt, int ks);
 int gemv_ctas_per_sm(int fmt);
 int launch_gemv(cudaStream_t s, const GemvArgs& a);
+
+struct TcArgs {
+  const uint8_t* region;   // slot 0 of the W13 or W2 region (decode bank layout)
+  int64_t slot_stride;
+  int n_slots;
+  const float* globals;    // [slots][3]
+  int K;                   // H (W13) or I (W2)
+  int n_rt;                // row tiles of 256 weight rows: I/128 (W13) or H/256 (W2)
+  const Chunk* chunks;     // token tiles (<= 128 routes each) of this bank
+  const int32_t* n_chunks;
+  int bank;
+  const int32_t* perm;
+  int S;
+  int top_k;
+  void* inter;             // W13 output f16 [S][I] by sorted position
+  int inter_stride;
+  float limit;
+  const float* w_eff;
+  void* y2;                // fp16 [S][H] W2 rows by route index
+  int32_t* counters;
+  float* out;
+  int H;
+  uint32_t* err;
+};
+int launch_tc_gemm(cudaStream_t s, int fmt, int epi, const TcArgs& a, const void* map, int grid);
 
 }  // namespace b200moe

@@ -42,10 +42,14 @@ struct b200moe_layer {
   int32_t* n_chunks = nullptr;
   __half* x16 = nullptr;
   __half* inter = nullptr;
-  float* yw = nullptr;
+  __half* y2 = nullptr;
   int32_t* counters = nullptr;
   uint32_t* err = nullptr;
   void* dbg_y13 = nullptr;
+  // prefill on tcgen05: permuted fp16 token rows and the TMA maps of the two B operands
+  __half* xperm = nullptr;
+  alignas(128) unsigned char map_x[128] = {};
+  alignas(128) unsigned char map_inter[128] = {};
   // optional timing: events[0] at forward start, events[j + 1] after launch j
   cudaEvent_t events[16] = {};
   int n_events = 0;
@@ -82,8 +86,8 @@ int dalloc(T** p, size_t count) {
 
 void free_layer(b200moe_layer* L) {
   void* ptrs[] = {L->bank[0], L->bank[1], L->globals, L->span, L->iq2_tables, L->key_of_expert, L->perm,
-                  L->w_eff, L->chunks[0], L->chunks[1], L->n_chunks, L->x16, L->inter, L->yw,
-                  L->counters, L->err};
+                  L->w_eff, L->chunks[0], L->chunks[1], L->n_chunks, L->x16, L->inter, L->y2,
+                  L->counters, L->err, L->xperm};
   for (void* p : ptrs)
     if (p) cudaFree(p);
 }
@@ -128,7 +132,7 @@ struct Marks {
 };
 
 int run_forward(b200moe_layer* L, cudaStream_t s, const void* x, int x_dtype, const int32_t* ids,
-                const float* w, float* out, int m) {
+                const float* w, float* out, int m, bool prefill = false) {
   const auto& c = L->cfg;
   Marks marks{L, s};
   if (!L->maps_set) return B200MOE_ERR_STATE;
@@ -145,6 +149,8 @@ int run_forward(b200moe_layer* L, cudaStream_t s, const void* x, int x_dtype, co
     marks.mark();
   }
   int ks[2] = {choose_ks(L, 0, m), choose_ks(L, 1, m)};
+  // prefill with the tcgen05 GEMM: the FP4 bank's chunks are 128-route token tiles
+  const bool tc = prefill && c.prefill_gemm && c.n_fp4 > 0 && L->xperm;
   PlanArgs p{};
   p.ids = ids;
   p.n = S;
@@ -158,14 +164,14 @@ int run_forward(b200moe_layer* L, cudaStream_t s, const void* x, int x_dtype, co
   p.key_lo[1] = c.n_fp4;
   p.key_hi[1] = c.n_fp4 + c.n_iq2;
   for (int b = 0; b < 2; ++b) {
-    p.rc[b] = 16 / ks[b];
+    p.rc[b] = (tc && b == 0) ? kTcTokenTile : 16 / ks[b];
     p.max_chunks[b] = L->max_chunks;
     p.chunks[b] = L->chunks[b];
   }
   p.n_chunks = L->n_chunks;
   p.w_in = w;
   p.w_eff = L->w_eff;
-  p.yw = L->yw;
+  p.y2 = L->y2;
   p.counters = L->counters;
   p.out = out;
   p.H = c.hidden;
@@ -173,10 +179,43 @@ int run_forward(b200moe_layer* L, cudaStream_t s, const void* x, int x_dtype, co
   p.err = L->err;
   if (launch_plan(s, p)) return B200MOE_ERR_CUDA;
   marks.mark();
+  if (tc) {
+    if (launch_gather_rows(s, x, x_dtype == B200MOE_BF16, L->perm, S, c.top_k, c.hidden, L->xperm))
+      return B200MOE_ERR_CUDA;
+    marks.mark();
+  }
   for (int epi = 0; epi < 2; ++epi) {
     for (int b = 0; b < 2; ++b) {
       const int n_slots = b == 0 ? c.n_fp4 : c.n_iq2;
       if (n_slots == 0) continue;
+      if (tc && b == 0) {
+        TcArgs t{};
+        t.region = L->bank[0] + (epi == 0 ? 0 : L->geom[0].w13_bytes);
+        t.slot_stride = L->geom[0].slot_bytes;
+        t.n_slots = n_slots;
+        t.globals = L->globals;
+        t.K = epi == 0 ? c.hidden : c.inter;
+        t.n_rt = epi == 0 ? c.inter / 128 : c.hidden / 256;
+        t.chunks = L->chunks[0];
+        t.n_chunks = L->n_chunks;
+        t.bank = 0;
+        t.perm = L->perm;
+        t.S = S;
+        t.top_k = c.top_k;
+        t.inter = L->inter;
+        t.inter_stride = c.inter;
+        t.limit = c.swiglu_limit;
+        t.w_eff = L->w_eff;
+        t.y2 = L->y2;
+        t.counters = L->counters;
+        t.out = out;
+        t.H = c.hidden;
+        t.err = L->err;
+        if (launch_tc_gemm(s, c.fp4_format, epi, t, epi == 0 ? L->map_x : L->map_inter, L->grid))
+          return B200MOE_ERR_CUDA;
+        marks.mark();
+        continue;
+      }
       GemvArgs g{};
       g.fmt = b == 0 ? c.fp4_format : 2;
       g.epi = epi;
@@ -202,7 +241,7 @@ int run_forward(b200moe_layer* L, cudaStream_t s, const void* x, int x_dtype, co
       g.dbg_y13 = L->dbg_y13;
       g.limit = c.swiglu_limit;
       g.w_eff = L->w_eff;
-      g.yw = L->yw;
+      g.y2 = L->y2;
       g.counters = L->counters;
       g.out = out;
       g.H = c.hidden;
@@ -250,6 +289,7 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
     return B200MOE_ERR_INVALID_ARG;
   if (c.fp4_format != B200MOE_NVFP4 && c.fp4_format != B200MOE_MXFP4) return B200MOE_ERR_INVALID_ARG;
   if (c.n_iq2 > 0 && c.inter % 256) return B200MOE_ERR_INVALID_ARG;
+  if (c.prefill_gemm != 0 && c.prefill_gemm != 1) return B200MOE_ERR_INVALID_ARG;
   DeviceGuard guard(device);
   cudaDeviceProp prop;
   if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return B200MOE_ERR_CUDA;
@@ -280,9 +320,15 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
   take(dalloc(&L->n_chunks, 2));
   take(dalloc(&L->x16, size_t(L->t_max) * c.hidden));
   take(dalloc(&L->inter, size_t(L->s_max) * c.inter));
-  take(dalloc(&L->yw, size_t(L->s_max) * c.hidden));
+  take(dalloc(&L->y2, size_t(L->s_max) * c.hidden));
   take(dalloc(&L->counters, size_t(L->t_max) * (c.hidden / 32)));
   take(dalloc(&L->err, 1));
+  if (c.prefill_gemm && c.max_prefill_tokens > 0 && c.n_fp4 > 0) {
+    take(dalloc(&L->xperm, size_t(L->s_max) * c.hidden));
+    if (st == B200MOE_OK && (make_token_map(L->map_x, L->xperm, L->s_max, c.hidden) ||
+                             make_token_map(L->map_inter, L->inter, L->s_max, c.inter)))
+      st = B200MOE_ERR_CUDA;
+  }
   if (st == B200MOE_OK) {
     if (cudaMemset(L->counters, 0, size_t(L->t_max) * (c.hidden / 32) * 4) != cudaSuccess ||
         cudaMemset(L->err, 0, 4) != cudaSuccess || cudaMemset(L->n_chunks, 0, 8) != cudaSuccess ||
@@ -415,7 +461,7 @@ int b200moe_forward_prefill(b200moe_layer* L, void* stream, const void* x, int x
                             const float* w, float* out, int T) {
   if (!L || T < 1 || T > L->t_max) return B200MOE_ERR_INVALID_ARG;
   DeviceGuard guard(L->device);
-  return run_forward(L, static_cast<cudaStream_t>(stream), x, x_dtype, ids, w, out, T);
+  return run_forward(L, static_cast<cudaStream_t>(stream), x, x_dtype, ids, w, out, T, true);
 }
 
 int b200moe_check_errors(b200moe_layer* L, void* stream, uint32_t* bits) {
@@ -506,7 +552,7 @@ int b200moe_route_plan(void* stream, const int32_t* ids, int n, int num_experts,
 // Decode forward with a fixed, library-owned workspace (no allocation).
 //
 // b200moe_forward keeps its per-call intermediates (route permutation, route
-// chunks, fp16 activations, SwiGLU rows, weighted route rows, combine
+// chunks, fp16 activations, SwiGLU rows, W2 route rows, combine
 // counters) in a workspace that b200moe_layer_create allocates for each layer.
 // Some callers cannot allocate device memory at the time they need a decode
 // forward: an engine that hands all free HBM to its KV cache after start-up
@@ -535,10 +581,10 @@ constexpr size_t kOffNChunks = kOffChunks1 + align256(kStaticMaxChunks * sizeof(
 constexpr size_t kOffX16 = kOffNChunks + 256;
 constexpr size_t kOffInter = kOffX16 + align256(size_t(kStaticMaxTokens) * kStaticMaxHidden * 2);
 constexpr size_t kOffYw = kOffInter + align256(size_t(kStaticRoutes) * kStaticMaxInter * 2);
-constexpr size_t kOffCounters = kOffYw + align256(size_t(kStaticRoutes) * kStaticMaxHidden * 4);
+constexpr size_t kOffCounters = kOffYw + align256(size_t(kStaticRoutes) * kStaticMaxHidden * 2);
 constexpr size_t kStaticScratchBytes = kOffCounters + align256(size_t(kStaticMaxTokens) * (kStaticMaxHidden / 32) * 4);
 
-// About 2.6 MB per GPU (see the limits above).
+// About 1.7 MB per GPU (see the limits above).
 static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
 
 // Device address of g_static_scratch per device, looked up on the first call
@@ -586,7 +632,7 @@ extern "C" int b200moe_forward_static(b200moe_layer* L, void* stream, const void
   int32_t* n_chunks = reinterpret_cast<int32_t*>(ws + kOffNChunks);
   __half* x16 = reinterpret_cast<__half*>(ws + kOffX16);
   __half* inter = reinterpret_cast<__half*>(ws + kOffInter);
-  float* yw = reinterpret_cast<float*>(ws + kOffYw);
+  __half* y2 = reinterpret_cast<__half*>(ws + kOffYw);
   int32_t* counters = reinterpret_cast<int32_t*>(ws + kOffCounters);
   // The array keeps the previous call's contents: the combine counters must
   // start at zero, and the SwiGLU rows are read whole by the W2 launch.
@@ -618,7 +664,7 @@ extern "C" int b200moe_forward_static(b200moe_layer* L, void* stream, const void
   p.n_chunks = n_chunks;
   p.w_in = w;
   p.w_eff = w_eff;
-  p.yw = yw;
+  p.y2 = y2;
   p.counters = counters;
   p.out = out;
   p.H = c.hidden;
@@ -654,7 +700,7 @@ extern "C" int b200moe_forward_static(b200moe_layer* L, void* stream, const void
       g.dbg_y13 = nullptr;
       g.limit = c.swiglu_limit;
       g.w_eff = w_eff;
-      g.yw = yw;
+      g.y2 = y2;
       g.counters = counters;
       g.out = out;
       g.H = c.hidden;

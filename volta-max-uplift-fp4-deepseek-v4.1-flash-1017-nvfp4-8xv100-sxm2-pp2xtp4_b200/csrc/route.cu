@@ -143,13 +143,13 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanArgs a) {
   }
   __syncthreads();
 
-  if (product && aux[nk - 1] > 0 && a.yw) {
+  if (product && aux[nk - 1] > 0 && a.y2) {
     // routes without an expert (sorted last): zero their rows, count them done
     const int first = start[nk - 1], cnt = aux[nk - 1];
     const int tiles = a.H / 32;
     for (int64_t idx = tid; idx < int64_t(cnt) * a.H; idx += kPlanThreads) {
       const int route = a.perm[first + int(idx / a.H)];
-      a.yw[int64_t(route) * a.H + idx % a.H] = 0.f;
+      static_cast<__half*>(a.y2)[int64_t(route) * a.H + idx % a.H] = __float2half_rn(0.f);
     }
     __threadfence();
     __syncthreads();

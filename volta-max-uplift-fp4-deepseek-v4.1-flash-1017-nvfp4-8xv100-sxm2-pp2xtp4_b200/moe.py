@@ -42,14 +42,20 @@ class B200NativeMoe:
     expert is local.  Buffers are fixed at construction (``max_tokens`` for the
     graph-capturable decode ``forward``, ``max_prefill_tokens`` for
     ``forward_prefill``); forward never allocates or syncs with the host.
+    ``prefill_gemm`` picks forward_prefill's kernel for the FP4 bank:
+    "tcgen05" (the tensor-core grouped GEMM, 128-route tiles) or "skinny"
+    (the decode kernels, 16-route chunks); IQ2_XXS experts always use the latter.
     """
 
     def __init__(self, *, hidden: int, inter: int, num_experts: int, top_k: int, max_tokens: int,
                  tier, fp4_format: str = "nvfp4", max_prefill_tokens: int = 0,
                  swiglu_limit: float = SWIGLU_LIMIT, device: torch.device | int | None = None,
-                 rank: int = 0, world: int = 1):
+                 rank: int = 0, world: int = 1, prefill_gemm: str = "tcgen05"):
         if fp4_format not in ("nvfp4", "mxfp4"):
             raise ValueError(f"fp4_format must be nvfp4 or mxfp4, got {fp4_format!r}")
+        if prefill_gemm not in ("tcgen05", "skinny"):
+            raise ValueError(f"prefill_gemm must be tcgen05 or skinny, got {prefill_gemm!r}")
+        self.prefill_gemm = prefill_gemm
         dev = torch.device("cuda", torch.cuda.current_device() if device is None else
                            (device if isinstance(device, int) else device.index))
         if dev.index is None:
@@ -65,7 +71,7 @@ class B200NativeMoe:
         self.fp4_slot, self.iq2_slot = fp4_map, iq2_map
         cfg = _lib.Config(hidden, inter, num_experts, top_k, max_tokens, max_prefill_tokens,
                           _lib.NVFP4 if fp4_format == "nvfp4" else _lib.MXFP4, self.n_fp4, self.n_iq2,
-                          float(swiglu_limit))
+                          float(swiglu_limit), 1 if prefill_gemm == "tcgen05" else 0)
         handle = ctypes.c_void_p()
         L = _lib.lib()
         _lib.check("b200moe_layer_create", L.b200moe_layer_create(ctypes.byref(cfg), dev.index, ctypes.byref(handle)))
