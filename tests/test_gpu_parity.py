@@ -366,3 +366,52 @@ def test_bad_expert_id_reports_bounds_then_recovers(dev, pkg):
     layer.check_errors()
     assert tr.rel_l2(out, tr.layer_forward(x, ids.long(), w, dequant)) < TOL
     layer.close()
+
+
+# ------------------------------------------------------- prefill on tcgen05
+@pytest.mark.parametrize("fmt", ["mxfp4", "nvfp4"])
+def test_prefill_tcgen05_vs_reference_and_skinny(dev, pkg, fmt):
+    """configs[3]-shaped layer (hidden 4096, inter 2048, top-8) at 32 experts:
+    ~128 routes per expert, so token tiles are full, partial and split."""
+    from b200moe import moe, synth
+
+    H, I, E, K, T = 4096, 2048, 32, 8, 512
+    outs = {}
+    for mode in ("tcgen05", "skinny"):
+        layer = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K, max_tokens=4, tier=np.zeros(E, np.int8),
+                                  fp4_format=fmt, device=dev, max_prefill_tokens=T, prefill_gemm=mode)
+        bank = synth.make_fp4_bank(E, H, I, fmt, 31, dev)
+        synth.load_bank(layer, bank)
+        g = torch.Generator(device=dev).manual_seed(3000 + T // 1024)
+        x = torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
+        ids, w = layer.route(torch.rand((T, E), generator=g, device=dev))
+        out = layer.forward_prefill(x, ids, w)
+        again = layer.forward_prefill(x, ids, w)
+        layer.check_errors()
+        assert torch.equal(out, again), "prefill is not deterministic"
+        outs[mode] = out
+        if mode == "tcgen05":
+            ref = tr.layer_forward(x, ids.long(), w, _fp4_dequant(bank, fmt, I))
+            assert tr.rel_l2(out, ref) < TOL
+        layer.close()
+    assert tr.rel_l2(outs["tcgen05"], outs["skinny"]) < 2e-3
+
+
+def test_prefill_tcgen05_skewed_mixed_tier(dev, pkg):
+    """Zipf routing (some experts > 128 routes, some with one) over an NVFP4
+    bank on tcgen05 plus an IQ2_XXS bank on the skinny kernels, sharing one
+    combine."""
+    from b200moe import synth, tiers
+
+    H, I, E, K, T = 4096, 2048, 48, 8, 384
+    tier, rank = tiers.zipf_tier(E, 30, seed=9)
+    layer, dequant, _, _ = _make_layer(dev, H, I, E, K, 4, tier=tier, seed=9, max_prefill=T)
+    g = torch.Generator(device=dev).manual_seed(9)
+    x = torch.randn((T, H), generator=g, device=dev).to(torch.float16)
+    ids, w = layer.route(synth.zipf_logits(T, rank, 2.0, 1.1, 9, dev))
+    counts = torch.bincount(ids.reshape(-1).long(), minlength=E)
+    assert counts.max() > 128 and (counts[counts > 0].min() < 16)
+    out = layer.forward_prefill(x, ids, w)
+    layer.check_errors()
+    assert tr.rel_l2(out, tr.layer_forward(x, ids.long(), w, dequant)) < TOL
+    layer.close()
