@@ -179,6 +179,35 @@ int b200moe_route_plan(void* stream, const int32_t* ids, int n, int num_experts,
                        int32_t* gids_hot, int32_t* goff_hot, int32_t* gids_host, int32_t* goff_host,
                        int32_t* iq_out, uint32_t* err);
 
+/* ---- Expert parallelism (no counterpart in the reference, which refuses EP:
+ * engine/patches/gguf_moe.patch:57-58).  Expert e lives on rank
+ * owner_of_expert[e]; the exchange is NCCL all-to-all issued by the host. */
+
+/* Softmax top-k gating without a layer (same rule as b200moe_route). */
+int b200moe_gate(void* stream, const float* logits, int T, int num_experts, int top_k, int32_t* topk_ids,
+                 float* topk_weights, uint32_t* err);
+
+/* Bytes of device workspace b200moe_ep_dispatch needs for max_routes = T * k. */
+size_t b200moe_ep_workspace_bytes(int max_routes, int world);
+
+/* Sort this GPU's T * k routes by owner rank (stable), count them per rank
+ * (send_counts, device int32 [world]) and gather, in that order, each route's
+ * fp16 activation row (send_rows [T*k][H]) and expert id (send_experts);
+ * route_pos[route] = its position in that order. */
+int b200moe_ep_dispatch(void* stream, const void* x, int x_dtype, const int32_t* topk_ids, int T, int k,
+                        int num_experts, int world, const int32_t* owner_of_expert, int H, void* send_rows,
+                        int32_t* send_experts, int32_t* route_pos, int32_t* send_counts, void* workspace,
+                        size_t workspace_bytes, uint32_t* err);
+
+/* out[t] = residual[t] (if non-NULL) + sum over slots, in slot order, of
+ * fma(f32(y2[route_pos[t*k + s]]), w[t*k + s]) for y2 fp16 [T*k][H] returned
+ * by the owners in dispatch order -- the single-GPU combine's arithmetic. */
+int b200moe_ep_combine(void* stream, const void* y2, const int32_t* route_pos, const float* topk_weights, int T,
+                       int k, int H, const float* residual, float* out);
+
+/* fp32 -> fp16 copy of n values (n % 4 == 0), round to nearest. */
+int b200moe_f32_to_f16(void* stream, const float* x, int64_t n, void* y);
+
 /* Packing (device arrays): fp32 W [rows][k] -> NVFP4 codes [rows][k/2],
  * E4M3 scales [rows][k/16], global (device float, one) / MXFP4 codes and E8M0
  * [rows][k/32].  Same rounding as the oracle: RNE, ties to even, saturating. */

@@ -1,0 +1,71 @@
+"""One rank of the expert-parallel parity check (launched by torchrun from
+tests/test_gpu_ep.py): every rank builds the same seeded experts, runs the
+sharded layer on its own tokens and the full single-GPU layer on the same
+tokens, and writes the relative L2 distance per case to a JSON file."""
+
+from __future__ import annotations
+
+import datetime
+import json
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+import __graft_entry__  # noqa: E402
+
+__graft_entry__.load_package()
+from b200moe import ep, moe, synth, tiers  # noqa: E402
+
+
+def main(out_path: str) -> None:
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
+    dev = torch.device("cuda", torch.cuda.current_device())
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    H, I, E, K, T = 1024, 512, 64, 6, 48
+    tier, pop_rank = tiers.zipf_tier(E, 40, seed=3)
+    n_hot, n_iq = int((tier == tiers.HOT).sum()), int((tier == tiers.WARM).sum())
+    fp4 = synth.make_fp4_bank(n_hot, H, I, "nvfp4", 11, dev)
+    iq2 = synth.make_iq2_bank(n_iq, H, I, 12, dev)
+    full = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K, max_tokens=64, tier=tier, device=dev)
+    synth.load_bank(full, fp4)
+    full.set_iq2_tables()
+    synth.load_bank(full, iq2)
+    sharded = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K, tokens=T, tier=tier, device=dev)
+    sharded.set_iq2_tables()
+    synth.load_local(sharded.layer, tier, fp4, iq2)
+    res = {}
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    cases = {"zipf": (T, synth.zipf_logits(T, pop_rank, 1.0, 1.1, 200 + rank, dev)),
+             "ragged": (17 + 9 * rank, torch.randn((17 + 9 * rank, E), generator=g, device=dev)),
+             # every route of every rank goes to rank 0's experts
+             "one_owner": (T, torch.where(torch.arange(E, device=dev) < E // world, 5.0, -5.0).expand(T, E)
+                           + 0.1 * torch.randn((T, E), generator=g, device=dev))}
+    for name, (t, logits) in cases.items():
+        x = torch.randn((t, H), generator=g, device=dev).to(torch.bfloat16)
+        resid = torch.randn((t, H), generator=g, device=dev)
+        ids, w = sharded.route(logits.contiguous())
+        y = sharded.forward(x, ids, w, residual=resid)
+        ref = full.forward_prefill(x, ids, w) if t > 64 else full.forward(x, ids, w).clone()
+        sharded.check_errors()
+        full.check_errors()
+        d = (y - resid - ref).norm() / ref.norm()
+        res[name] = float(d)
+        res[name + "_comm_ms"] = sharded.comm_ms()
+        res[name + "_owner_counts"] = sharded.send_counts.cpu().tolist()
+    dist.barrier()
+    with open(f"{out_path}.{rank}", "w") as f:
+        json.dump(res, f)
+    sharded.close()
+    full.close()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main(sys.argv[1])

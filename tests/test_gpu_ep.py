@@ -1,0 +1,95 @@
+"""Expert-parallel layer on the GPU: dispatch -> owner compute -> combine
+against the full single-GPU layer on the same tokens (world 1 here; world 2
+over NCCL through torchrun when the box has two GPUs)."""
+
+from __future__ import annotations
+
+import json
+import os
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-3  # two fp16-y2 paths whose split-K sums differ in order
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    return torch.device("cuda", 0)
+
+
+def test_ep_world1_matches_layer(dev, pkg):
+    from b200moe import ep, moe, synth, tiers
+
+    H, I, E, K, T = 1024, 512, 64, 6, 48
+    tier, pop_rank = tiers.zipf_tier(E, 40, seed=3)
+    n_hot, n_iq = int((tier == tiers.HOT).sum()), int((tier == tiers.WARM).sum())
+    fp4 = synth.make_fp4_bank(n_hot, H, I, "nvfp4", 11, dev)
+    iq2 = synth.make_iq2_bank(n_iq, H, I, 12, dev)
+    full = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K, max_tokens=64, tier=tier, device=dev)
+    synth.load_bank(full, fp4)
+    full.set_iq2_tables()
+    synth.load_bank(full, iq2)
+    sharded = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K, tokens=T, tier=tier, device=dev)
+    sharded.set_iq2_tables()
+    synth.load_local(sharded.layer, tier, fp4, iq2)
+    g = torch.Generator(device=dev).manual_seed(5)
+    x = torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
+    logits = synth.zipf_logits(T, pop_rank, 1.0, 1.1, 6, dev)
+    ids, w = sharded.route(logits)
+    ids2, w2 = full.route(logits)
+    assert torch.equal(ids, ids2) and torch.equal(w, w2)
+    ref = full.forward(x, ids, w).clone()
+    y = sharded.forward(x, ids, w)
+    sharded.check_errors()
+    assert float((y - ref).norm() / ref.norm()) < TOL
+    resid = torch.randn((T, H), generator=g, device=dev)
+    y_r = sharded.forward(x, ids, w, residual=resid)
+    assert torch.equal(y_r, y + resid)
+    assert torch.equal(sharded.send_counts.cpu(), torch.tensor([T * K], dtype=torch.int32))
+    # a route without an expert: flagged, contributes nothing, the layer recovers
+    bad = ids.clone()
+    bad[3, 2] = E + 7
+    y_b = sharded.forward(x, bad, w)
+    from b200moe import _lib
+
+    with pytest.raises(_lib.B200MoeError) as ei:
+        sharded.check_errors()
+    assert ei.value.status == 5
+    w_b = w.clone()
+    w_b[3, 2] = 0.0
+    y_z = sharded.forward(x, ids, w_b)
+    sharded.check_errors()
+    assert float((y_b[3] - y_z[3]).norm() / y_z[3].norm()) < TOL
+    assert torch.equal(sharded.forward(x, ids, w), y)
+    sharded.close()
+    full.close()
+
+
+def test_ep_two_gpus_nccl(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    out = tmp_path / "ep"
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={port}",
+           str(Path(__file__).with_name("ep_worker.py")), str(out)]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    for rank in range(2):
+        res = json.loads(Path(f"{out}.{rank}").read_text())
+        for case in ("zipf", "ragged", "one_owner"):
+            assert res[case] < TOL, (rank, case, res)
+        assert res["one_owner_owner_counts"][1] == 0
+        assert res["zipf_comm_ms"] > 0

@@ -41,6 +41,7 @@ struct PlanArgs {
   int key_lo[2], key_hi[2], rc[2], max_chunks[2];
   Chunk* chunks[2];
   int32_t* n_chunks;    // [2]
+  int32_t* key_counts;  // optional [n_keys]: routes per key (product mode)
   const float* w_in;    // [n] router weights (product)
   float* w_eff;         // [n] weight used by the combine (0 for a route without an expert)
   // product: a route without an expert gets a zero y2 row and its completion

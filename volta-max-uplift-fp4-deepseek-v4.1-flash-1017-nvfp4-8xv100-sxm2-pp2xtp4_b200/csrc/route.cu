@@ -165,6 +165,9 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanArgs a) {
     __syncthreads();
   }
 
+  if (product && a.key_counts)
+    for (int key = tid; key < a.n_keys; key += kPlanThreads) a.key_counts[key] = aux[key];
+
   if (product) {
     // route chunks of every bank: ceil(count / rc) chunks per non-empty key
     for (int b = 0; b < a.n_banks; ++b) {

@@ -106,3 +106,27 @@ def zipf_logits(tokens: int, rank, alpha: float, s: float, seed: int, device) ->
     logp = -s * torch.log(r + 1.0)
     u = torch.rand((tokens, r.numel()), generator=g, device=device).clamp_(1e-12, 1 - 1e-7)
     return (alpha * logp)[None, :] - torch.log(-torch.log(u))
+
+
+def load_local(layer, tier, fp4: Fp4Bank | None, iq2: Iq2Bank | None) -> None:
+    """Load one rank's experts from banks that hold every expert of the layer:
+    the bank of a format is indexed by the expert's rank among that format's
+    experts (ascending id); a rank's experts of a format are a contiguous run."""
+    import numpy as np
+
+    from . import tiers as tiersmod
+
+    maps = tiersmod.slot_maps(tier)
+    for fmt, bank, local, glob in (("fp4", fp4, layer.fp4_slot, maps.hot), ("iq2", iq2, layer.iq2_slot, maps.iq)):
+        mine = np.flatnonzero(local >= 0)
+        if mine.size == 0:
+            continue
+        g0, n = int(glob[mine[0]]), mine.size
+        if not np.array_equal(glob[mine], np.arange(g0, g0 + n)) or not np.array_equal(local[mine], np.arange(n)):
+            raise ValueError("local experts of a format must be a contiguous run of the bank")
+        if fmt == "fp4":
+            layer.load_fp4(0, bank.w13_codes[g0:g0 + n], bank.w13_scales[g0:g0 + n], bank.w2_codes[g0:g0 + n],
+                           bank.w2_scales[g0:g0 + n], None if bank.globals is None else bank.globals[g0:g0 + n])
+        else:
+            layer.load_iq2(0, bank.w1[g0:g0 + n].contiguous(), bank.w3[g0:g0 + n].contiguous(),
+                           bank.w2[g0:g0 + n].contiguous())
