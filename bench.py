@@ -22,8 +22,14 @@ weights, far above the 126 MB L2, so no flush is needed (``config.l2``).
 
 ``--impl reference`` times that CPU implementation alone on this workload (the
 reference's own GPU kernels are V100-only and are not in its source tree).
-Multi-GPU (torchrun): expert parallel is the next step; until then each rank
-runs an independent replica of the layer (weak scaling, no collective).
+
+Multi-GPU (torchrun, N ranks): expert parallel.  Rank r owns experts
+[r*384/N, (r+1)*384/N); each rank is home to its own M = 64 tokens (weak
+scaling: tokens per GPU fixed), gates them, dispatches every route to its
+owner over NCCL all-to-all, runs its local experts on the routes it receives
+and combines the returned rows in slot order.  ``value`` = N*M / (max over
+ranks of the step time); ``exposed_comm_ms`` = the all-to-all time on the
+critical path (counts + rows out, y2 back), from CUDA events.
 """
 
 from __future__ import annotations
@@ -50,13 +56,16 @@ EXPERT_BYTES = W13_BYTES + W2_BYTES            # 14,155,776
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--m", type=int, default=64, choices=[1, 8, 32, 64])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--experts", type=int, default=E,
                     help="routed experts (384 = configs[1]; fewer only for a small ncu capture)")
+    ap.add_argument("--split-k", type=int, default=0,
+                    help="fix the GEMV split-K (0 = chosen per launch; set only to give a small ncu capture "
+                         "the split-K of the full-size run)")
     ap.add_argument("--profile", action="store_true",
                     help="warm-up + timed steps only (no per-launch, e2e or CPU passes): the ncu command")
     return ap.parse_args()
@@ -127,6 +136,25 @@ class Clocks:
                 "samples": len(self.samples), "source": "nvml, polled every 2 ms during the timed region"}
 
 
+def measured_traffic(distinct: int) -> dict | None:
+    """DRAM bytes of one W13 launch from the committed ncu summary
+    (dram__bytes_read.sum + dram__bytes_write.sum of this bench's W13 launch),
+    scaled from the captured routing's distinct experts to this one's."""
+    import re
+
+    p = ROOT / "profiles" / "gemv_w13_c1_decode.md"
+    if not p.exists():
+        return None
+    txt = p.read_text()
+    m1 = re.search(r"traffic_bytes_per_launch:\s*([0-9.e+]+)", txt)
+    m2 = re.search(r"captured_distinct_experts:\s*([0-9]+)", txt)
+    if not (m1 and m2):
+        return None
+    b, d = float(m1.group(1)), int(m2.group(1))
+    return {"bytes": b * distinct / d, "captured_bytes": b, "captured_distinct_experts": d,
+            "source": "profiles/gemv_w13_c1_decode.md (ncu dram__bytes_read.sum + dram__bytes_write.sum)"}
+
+
 def cpu_layer_tokens_per_s(bank, ids_np, w_np, x_np, m, reps=2) -> dict:
     """The C oracle (OpenMP, all host cores) on the full layer of this routing."""
     from oracle import cpu_layer
@@ -146,6 +174,114 @@ def cpu_layer_tokens_per_s(bank, ids_np, w_np, x_np, m, reps=2) -> dict:
     return {"value": m / dt, "unit": "tokens/s", "cores": cpu_layer.threads(), "kind": "port",
             "sample": f"full layer at M={m} ({used.size} routed experts), {reps} timed runs, "
                       f"{dt * 1e3:.1f} ms per layer", "ms_per_layer": dt * 1e3}
+
+
+def run_expert_parallel(args, dev, rank, world, x, logits, config, maxall) -> None:
+    """N ranks, expert parallel over NCCL (see the module docstring)."""
+    import torch
+    import torch.distributed as dist
+
+    from b200moe import ep, synth
+
+    m = args.m
+    tier = np.zeros(E, np.int8)
+    layer = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, tokens=m, tier=tier, device=dev)
+    n_local = int((layer.layer.fp4_slot >= 0).sum())
+    bank = synth.make_fp4_bank(n_local, H, I, "nvfp4", 1000 + rank, dev)
+    synth.load_bank(layer.layer, bank)
+    del bank
+    # each rank is home to its own tokens
+    g = torch.Generator(device=dev).manual_seed(1000 + m + 7919 * rank)
+    x = torch.randn((m, H), generator=g, device=dev).to(torch.bfloat16)
+    logits = torch.randn((m, E), generator=g, device=dev)
+    out = torch.empty((m, H), dtype=torch.float32, device=dev)
+    config = dict(config, parallelism=f"expert parallel x{world} (NCCL all-to-all)", experts_per_gpu=n_local,
+                  tokens_per_step=m * world)
+    config["workload"] += f", expert parallel over {world} GPUs, {m} tokens per GPU"
+
+    def step():
+        ids, w = layer.route(logits)
+        return layer.forward(x, ids, w, out=out)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    layer.check_errors()
+
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = Clocks(dev) if rank == 0 else None
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = clocks.stop() if clocks else None
+    ms = maxall(e0.elapsed_time(e1) / args.steps)
+    layer.check_errors()
+    value = world * m / (ms / 1e3)
+
+    # exposed communication and the local W13 launch (separate pass: these read events every step)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    layer.layer.set_timing_events(evs)  # start, convert, plan, W13, W2 of the local expert run
+    comm, w13_ms, used = 0.0, 0.0, 0
+    for _ in range(args.steps):
+        step()
+        torch.cuda.synchronize()
+        comm += layer.comm_ms()
+        w13_ms += evs[2].elapsed_time(evs[3])
+        used += layer.local_experts_used()
+    layer.layer.set_timing_events(None)
+    comm, w13_ms, used = comm / args.steps, w13_ms / args.steps, used / args.steps
+    comm_max = maxall(comm)
+    pk = peaks()
+    achieved = used * W13_BYTES / (w13_ms / 1e3) / 1e9
+    frac_min = -maxall(-achieved / pk["hbm_gbs"])
+
+    # e2e through the public API with host buffers
+    hx = x.cpu().pin_memory()
+    hl = logits.cpu().pin_memory()
+    hout = torch.empty((m, H), dtype=torch.float32).pin_memory()
+    dx, dl = torch.empty_like(x), torch.empty_like(logits)
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        dx.copy_(hx, non_blocking=True)
+        dl.copy_(hl, non_blocking=True)
+        ids2, w2 = layer.route(dl)
+        hout.copy_(layer.forward(dx, ids2, w2, out=out), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = maxall(e0.elapsed_time(e1) / args.steps)
+    layer.check_errors()
+    if rank == 0:
+        line = {
+            "metric": "MoE-layer tokens/s (decode M=64) & % HBM roofline",
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded; random-init NVFP4 experts)", "config": config,
+            "roofline": {"bound": "hbm", "kernel": "gemv_kernel W13 (+SwiGLU) of rank 0's local experts",
+                         "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / pk["hbm_gbs"], "min_frac_over_ranks": frac_min,
+                         "peak_source": pk["source"], "traffic": None,
+                         "algorithmic_bytes_per_launch": used * W13_BYTES, "distinct_local_experts": used,
+                         "launch_ms": w13_ms},
+            "exposed_comm_ms": comm_max,
+            "e2e": {"value": world * m / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(hx.numel() * hx.element_size() + hl.numel() * hl.element_size()),
+                    "d2h_bytes_per_step": int(hout.numel() * hout.element_size()), "ms_per_step": e2e_ms},
+            # gating; dispatch plan, row gather, metadata; local convert, plan, W13, W2; f32->f16; combine
+            "gpu_launches": 10 * args.steps,
+            "cpu_baseline": None,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    layer.close()
+    dist.barrier()
+    dist.destroy_process_group()
 
 
 def main() -> None:
@@ -233,11 +369,18 @@ def main() -> None:
             dist.destroy_process_group()
         return
 
+    if world > 1:
+        run_expert_parallel(args, dev, rank, world, x, logits, config, maxall)
+        return
+
     bank = synth.make_fp4_bank(n_exp, H, I, "nvfp4", 1000, dev)
     layer = moe.B200NativeMoe(hidden=H, inter=I, num_experts=n_exp, top_k=K_TOP, max_tokens=64,
                               tier=np.zeros(n_exp, np.int8), device=dev)
     synth.load_bank(layer, bank)
     layer.check_errors()
+    if args.split_k:
+        layer.set_split_k(args.split_k, 0)
+        config["split_k"] = args.split_k
     if args.profile:
         del bank
         torch.cuda.synchronize()
@@ -247,8 +390,11 @@ def main() -> None:
             layer.forward(x, *layer.route(logits))
         torch.cuda.synchronize()
         layer.check_errors()
+        distinct = int(torch.unique(layer.route(logits)[0]).numel())
         layer.close()
-        print(json.dumps({"profile_run": True, "experts": n_exp, "m": m}), flush=True)
+        print(json.dumps({"profile_run": True, "experts": n_exp, "m": m, "distinct_experts": distinct,
+                          "w13_algorithmic_bytes": distinct * W13_BYTES,
+                          "w2_algorithmic_bytes": distinct * W2_BYTES}), flush=True)
         return
 
     def step():
@@ -294,10 +440,7 @@ def main() -> None:
     pk = peaks()
     achieved = distinct * W13_BYTES / (t_w13_ms / 1e3) / 1e9
     layer_bytes = distinct * EXPERT_BYTES
-    traffic = None
-    prof = ROOT / "profiles" / "traffic_gemv_w13_c1.json"
-    if prof.exists():
-        traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
+    traffic = measured_traffic(distinct)
 
     # ---- e2e through the public API, host buffers in pinned memory
     hx = x.cpu().pin_memory()
@@ -335,7 +478,8 @@ def main() -> None:
             "data": "synthetic (seeded; random-init NVFP4 experts)", "config": config,
             "roofline": {"bound": "hbm", "kernel": "gemv_kernel W13 (+SwiGLU)", "achieved": achieved,
                          "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
-                         "peak_source": pk["source"], "traffic": traffic,
+                         "peak_source": pk["source"], "traffic": traffic["bytes"] if traffic else None,
+                         "traffic_detail": traffic,
                          "algorithmic_bytes_per_launch": distinct * W13_BYTES, "distinct_experts": distinct,
                          "launch_ms": t_w13_ms},
             "layer_roofline": {"bytes": layer_bytes, "ms": float(per.sum()),

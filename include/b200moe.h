@@ -162,9 +162,20 @@ int b200moe_debug_perm(const b200moe_layer* layer, void* stream, int32_t* dst, i
  * last forward into dst (device). */
 int b200moe_debug_inter(const b200moe_layer* layer, void* stream, void* dst, int rows);
 
+/* Split-K of the skinny GEMV per bank (ks in {1, 2, 4, 8}; K tiles of hidden
+ * and inter divisible by ks; 0 = the default: the route plan chooses it on
+ * the device for every call from that call's routing, so a captured graph
+ * adapts at replay and equal inputs always give equal bits).  A route's output bits depend only on ks, so two layers with the
+ * same fixed ks give bit-equal y2 rows whatever else they route (the
+ * expert-parallel owner and the single-GPU layer).  No reference counterpart:
+ * the reference's QPN grid rule (test_p3_split_groups.py:33-41) fixes its
+ * K split from the shape alone. */
+int b200moe_set_split_k(b200moe_layer* layer, int ks_fp4, int ks_iq2);
+
 /* Timing hook: with n > 0 cudaEvent_t handles, forward / forward_prefill
  * record events[0] on the stream before their first launch and events[j + 1]
- * after launch j ([bf16 copy], plan, W13 per bank, W2 per bank).  n = 0 turns
+ * after launch j (bf16 copy, recorded also when x is fp16 and nothing is
+ * copied; plan; [prefill with tcgen05: row gather]; W13 per bank; W2 per bank).  n = 0 turns
  * it off.  The events stay owned by the caller. */
 int b200moe_set_timing_events(b200moe_layer* layer, void* const* events, int n);
 

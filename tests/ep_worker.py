@@ -38,8 +38,17 @@ def main(out_path: str) -> None:
     full.set_iq2_tables()
     synth.load_bank(full, iq2)
     sharded = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K, tokens=T, tier=tier, device=dev)
+    exact = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K, tokens=T, tier=tier, device=dev,
+                                 split_k=(2, 2))
     sharded.set_iq2_tables()
     synth.load_local(sharded.layer, tier, fp4, iq2)
+    exact.set_iq2_tables()
+    synth.load_local(exact.layer, tier, fp4, iq2)
+    full2 = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K, max_tokens=64, tier=tier, device=dev)
+    synth.load_bank(full2, fp4)
+    full2.set_iq2_tables()
+    synth.load_bank(full2, iq2)
+    full2.set_split_k(2, 2)
     res = {}
     g = torch.Generator(device=dev).manual_seed(100 + rank)
     cases = {"zipf": (T, synth.zipf_logits(T, pop_rank, 1.0, 1.1, 200 + rank, dev)),
@@ -59,11 +68,18 @@ def main(out_path: str) -> None:
         res[name] = float(d)
         res[name + "_comm_ms"] = sharded.comm_ms()
         res[name + "_owner_counts"] = sharded.send_counts.cpu().tolist()
+        # fixed split-K on both sides: the sharded layer equals the single-GPU one bit for bit
+        y_exact = exact.forward(x, ids, w)
+        ref_exact = full2.forward(x, ids, w).clone()
+        exact.check_errors()
+        res[name + "_bitequal"] = bool(torch.equal(y_exact, ref_exact))
     dist.barrier()
     with open(f"{out_path}.{rank}", "w") as f:
         json.dump(res, f)
     sharded.close()
+    exact.close()
     full.close()
+    full2.close()
     dist.destroy_process_group()
 
 

@@ -70,6 +70,13 @@ def test_ep_world1_matches_layer(dev, pkg):
     sharded.check_errors()
     assert float((y_b[3] - y_z[3]).norm() / y_z[3].norm()) < TOL
     assert torch.equal(sharded.forward(x, ids, w), y)
+    # same fixed split-K on both sides: bit-equal to the single-GPU layer
+    full.set_split_k(2, 2)
+    sharded.layer.set_split_k(2, 2)
+    ref = full.forward(x, ids, w).clone()
+    assert torch.equal(sharded.forward(x, ids, w), ref)
+    with pytest.raises(_lib.B200MoeError):
+        full.set_split_k(3, 0)
     sharded.close()
     full.close()
 
@@ -91,5 +98,6 @@ def test_ep_two_gpus_nccl(tmp_path):
         res = json.loads(Path(f"{out}.{rank}").read_text())
         for case in ("zipf", "ragged", "one_owner"):
             assert res[case] < TOL, (rank, case, res)
+            assert res[case + "_bitequal"], (rank, case)
         assert res["one_owner_owner_counts"][1] == 0
         assert res["zipf_comm_ms"] > 0

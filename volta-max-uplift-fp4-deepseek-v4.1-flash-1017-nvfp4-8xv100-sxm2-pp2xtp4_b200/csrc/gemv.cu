@@ -4,11 +4,13 @@
 // external skinny_moe_qpn_sm70) plus its SwiGLU (nvfp4_8r_swiglu.py) and weighted
 // reduce (_mtp_weighted_reduce, restated at nvfp4_8r_iq_tail.py:106-120).
 //
-// Persistent CTAs (one per SM) walk work items (route chunk x row block).  Warp 8
-// is the producer: it streams each item's prepacked weight units and the chunk's
-// activation rows into a 6-stage shared-memory ring with cp.async.bulk, completion
-// counted on mbarriers.  Warps 0..7 consume: each owns one tile pair (32 weight
-// rows) of the item and a K slice; it dequantizes 4-bit codes to f16 in
+// Persistent CTAs (two per SM for FP4, one for IQ2) walk work items (route chunk
+// x row block).  Warp 8 is the producer: it streams each item's prepacked weight
+// units and the chunk's activation rows into a shared-memory ring (4 stages FP4,
+// 6 IQ2) with cp.async.bulk, completion counted on mbarriers.  Warps 0..7
+// consume: each owns one tile pair (32 weight rows) of the item and one of ks K
+// slices (ks = the split-K the route plan chose for this call, read at run
+// time; a chunk holds 16 / ks routes); it dequantizes 4-bit codes to f16 in
 // registers (cvt.e2m1x2, block scale exact in f16) and multiplies on the tensor
 // cores (m16n8k16, f32 accumulate), routes as the N dimension.
 //   EPI 0 (W13): y13 = acc * global, rounded to fp16 as the reference's y13 is,
@@ -20,6 +22,8 @@
 //     always taken in slot order, so the result does not depend on timing.
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "internal.h"
 #include "layout.cuh"
@@ -28,7 +32,7 @@ namespace b200moe {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;
-constexpr int kRouteSlots = 16;  // activation row slots per stage (KS * route chunk)
+constexpr int kRouteSlots = kRouteSlotsPerChunk;  // activation row slots per stage (KS * route chunk)
 
 // FP4: two CTAs per SM (18 warps) with a 4-stage ring each; IQ2: one CTA with 6.
 template <int FMT>
@@ -198,12 +202,11 @@ __device__ __forceinline__ __half swiglu_one(float g, float u, float limit) {
 }
 
 template <int FMT, int EPI, int KS>
-__global__ void __launch_bounds__(kGemvThreads, Fmt<FMT>::CTAS) gemv_kernel(const GemvArgs a) {
+__device__ __forceinline__ void gemv_body(const GemvArgs& a, uint8_t* smem) {
   using F = Fmt<FMT>;
   constexpr int kStages = F::STAGES;
   constexpr int TP = kConsumerWarps / KS;  // tile pairs per item
   constexpr int RC = kRouteSlots / KS;     // routes per chunk
-  extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kStages;
   uint8_t* stages = smem + 128;
@@ -438,35 +441,43 @@ __global__ void __launch_bounds__(kGemvThreads, Fmt<FMT>::CTAS) gemv_kernel(cons
   __syncthreads();
 }
 
-template <int FMT, int EPI, int KS>
-static int launch_one(cudaStream_t s, const GemvArgs& a) {
-  const size_t smem = smem_total<FMT>();
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(gemv_kernel<FMT, EPI, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
-        cudaSuccess)
-      return -1;
-    attr = true;
+// One kernel per format and epilogue; the split-K is read from the device
+// (chosen by the route plan from this call's chunk counts), so the choice
+// follows the routing without a host round trip, also inside a CUDA graph.
+template <int FMT, int EPI>
+__global__ void __launch_bounds__(kGemvThreads, Fmt<FMT>::CTAS) gemv_kernel(const GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  switch (a.ks_sel[a.bank]) {
+    case 1: gemv_body<FMT, EPI, 1>(a, smem); break;
+    case 2: gemv_body<FMT, EPI, 2>(a, smem); break;
+    case 4: gemv_body<FMT, EPI, 4>(a, smem); break;
+    case 8: gemv_body<FMT, EPI, 8>(a, smem); break;
+    default:
+      if (threadIdx.x == 0) set_error(a.err, kErrRange);
   }
-  gemv_kernel<FMT, EPI, KS><<<a.grid, kGemvThreads, smem, s>>>(a);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 template <int FMT, int EPI>
-static int launch_ks(cudaStream_t s, const GemvArgs& a) {
-  switch (a.ks) {
-    case 1: return launch_one<FMT, EPI, 1>(s, a);
-    case 2: return launch_one<FMT, EPI, 2>(s, a);
-    case 4: return launch_one<FMT, EPI, 4>(s, a);
-    case 8: return launch_one<FMT, EPI, 8>(s, a);
-    default: return -1;
+static int launch_one(cudaStream_t s, const GemvArgs& a) {
+  const size_t smem = smem_total<FMT>();
+  static std::atomic<uint64_t> attr_set{0};  // devices whose attribute is set
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return -1;
+  if (!(attr_set.load() >> dev & 1)) {
+    if (cudaFuncSetAttribute(gemv_kernel<FMT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
+        cudaSuccess)
+      return -1;
+    attr_set.fetch_or(uint64_t(1) << dev);
   }
+  gemv_kernel<FMT, EPI><<<a.grid, kGemvThreads, smem, s>>>(a);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 int launch_gemv(cudaStream_t s, const GemvArgs& a) {
-  if (a.fmt == 0) return a.epi == 0 ? launch_ks<0, 0>(s, a) : launch_ks<0, 1>(s, a);
-  if (a.fmt == 1) return a.epi == 0 ? launch_ks<1, 0>(s, a) : launch_ks<1, 1>(s, a);
-  if (a.fmt == 2) return a.epi == 0 ? launch_ks<2, 0>(s, a) : launch_ks<2, 1>(s, a);
+  if (!a.ks_sel) return -1;
+  if (a.fmt == 0) return a.epi == 0 ? launch_one<0, 0>(s, a) : launch_one<0, 1>(s, a);
+  if (a.fmt == 1) return a.epi == 0 ? launch_one<1, 0>(s, a) : launch_one<1, 1>(s, a);
+  if (a.fmt == 2) return a.epi == 0 ? launch_one<2, 0>(s, a) : launch_one<2, 1>(s, a);
   return -1;
 }
 

@@ -6,6 +6,9 @@
 
 namespace b200moe {
 
+// Activation rows staged per GEMV stage: a chunk holds 16 / ks routes.
+constexpr int kRouteSlotsPerChunk = 16;
+
 // ---- packing (pack.cu)
 int launch_fp4_prepack(cudaStream_t s, int fmt, int hidden, int inter, int n, const uint8_t* w13c,
                        const uint8_t* w13s, const uint8_t* w2c, const uint8_t* w2s, float* slot_globals,
@@ -20,6 +23,17 @@ struct Chunk {  // one route chunk of one expert group: routes perm[begin .. beg
   int32_t begin;
   int32_t count;
   int32_t pad;
+};
+
+// Time model of one bank's skinny GEMV (W13 + W2) for the split-K choice:
+// waves of items over the persistent CTA slots, a wave taking the longer of
+// one CTA streaming its item and all busy CTAs sharing HBM, plus a fixed cost.
+struct KsModel {
+  int allowed;        // bit j set: ks = 1 << j divides both projections' K tiles
+  float slots;        // persistent CTA slots (SMs x CTAs per SM)
+  float bpe;          // weight bytes per K element of a 32-row tile pair
+  float bw_cta, bw_hbm, per_wave;  // bytes/s of one CTA, of HBM; seconds per wave
+  float tiles[2], kdim[2];         // tile pairs and K of W13 and W2
 };
 
 struct PlanArgs {
@@ -42,6 +56,11 @@ struct PlanArgs {
   Chunk* chunks[2];
   int32_t* n_chunks;    // [2]
   int32_t* key_counts;  // optional [n_keys]: routes per key (product mode)
+  // product: a bank with rc[b] == 0 gets its split-K chosen here from this
+  // plan's exact chunk counts (ks_model[b]); ks_sel[b] receives the split-K the
+  // GEMV of bank b runs with (16 / rc for a fixed rc)
+  KsModel ks_model[2];
+  int32_t* ks_sel;
   const float* w_in;    // [n] router weights (product)
   float* w_eff;         // [n] weight used by the combine (0 for a route without an expert)
   // product: a route without an expert gets a zero y2 row and its completion
@@ -70,7 +89,7 @@ int launch_convert_bf16(cudaStream_t s, const void* x, int64_t n, void* x16);
 struct GemvArgs {
   int fmt;                    // 0 NVFP4, 1 MXFP4, 2 IQ2_XXS
   int epi;                    // 0: W13 -> SwiGLU -> inter; 1: W2 -> weighted combine
-  int ks;                     // K splits per item (1, 2, 4, 8)
+  const int32_t* ks_sel;      // device [2]: K splits per item (1, 2, 4, 8) of each bank, set by the plan
   const uint8_t* region;      // slot 0 of this projection region
   int64_t slot_stride;        // bytes between slots
   int n_slots;

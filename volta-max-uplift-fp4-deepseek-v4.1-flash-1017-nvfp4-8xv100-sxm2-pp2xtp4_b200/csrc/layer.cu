@@ -33,6 +33,8 @@ struct b200moe_layer {
   uint32_t* iq2_tables = nullptr;  // grid f16, sign masks, scale f16x2
   int32_t* key_of_expert = nullptr;
   bool maps_set = false, tables_set = false;
+  int ks_fixed[2] = {0, 0};  // split-K per bank set by the caller (0: chosen per launch)
+
   // workspace
   int s_max = 0, t_max = 0;
   int32_t* perm = nullptr;
@@ -40,6 +42,7 @@ struct b200moe_layer {
   Chunk* chunks[2] = {nullptr, nullptr};
   int max_chunks = 0;
   int32_t* n_chunks = nullptr;
+  int32_t* ks_sel = nullptr;  // [2] split-K per bank, written by the route plan
   __half* x16 = nullptr;
   __half* inter = nullptr;
   __half* y2 = nullptr;
@@ -87,38 +90,44 @@ int dalloc(T** p, size_t count) {
 void free_layer(b200moe_layer* L) {
   void* ptrs[] = {L->bank[0], L->bank[1], L->globals, L->span, L->iq2_tables, L->key_of_expert, L->perm,
                   L->w_eff, L->chunks[0], L->chunks[1], L->n_chunks, L->x16, L->inter, L->y2,
-                  L->counters, L->err, L->xperm};
+                  L->counters, L->err, L->xperm, L->ks_sel};
   for (void* p : ptrs)
     if (p) cudaFree(p);
 }
 
 bool aligned(const void* p, int a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-// K splits of a bank's launches: the split whose items fill the SMs best
-// (fewer splits on a tie).  Both projections must divide into KS slices.
-int choose_ks(const b200moe_layer* L, int bank, int rows) {
+// Split-K of a bank's skinny GEMV: fixed by the caller (rc = 16 / ks), or 0 =
+// chosen by the route plan on the device from this call's chunk counts with
+// the model below.  ks warps share the K of a tile pair and a chunk holds
+// 16 / ks routes, so a larger ks gives more chunks (each re-reads its expert's
+// weights) and more, smaller items.  The constants were fitted on B200 sweeps
+// (M = 1..64, one and two banks, both formats): one FP4 CTA streams about
+// 18.4 GB/s (two per SM) and one IQ2 CTA about 6 GB/s (ALU-bound decode); all
+// busy CTAs share about 4.8 TB/s (FP4) or 2 TB/s (IQ2); 2 us fixed per wave.
+int fixed_rc(const b200moe_layer* L, int bank) {
+  return L->ks_fixed[bank] ? kRouteSlotsPerChunk / L->ks_fixed[bank] : 0;
+}
+
+KsModel ks_model(const b200moe_layer* L, int bank) {
   const auto& c = L->cfg;
-  const int kt = bank == 0 ? kFp4KTile : kIq2KTile;
-  const int n_slots = bank == 0 ? c.n_fp4 : c.n_iq2;
-  const int routes = rows * c.top_k;
-  const double e = double(n_slots);
-  const double groups = std::max(1.0, std::min(double(routes), e * (1.0 - pow(1.0 - 1.0 / std::max(e, 1.0), routes))));
-  int best = 1;
-  double best_eff = -1;
-  for (int ks : {1, 2, 4, 8}) {
-    if ((c.hidden / kt) % ks || (c.inter / kt) % ks) continue;
-    const int rc = 16 / ks;
-    const double chunks = std::max(groups, std::ceil(routes / double(rc)));
-    const double items = chunks * double(c.inter / 16) / double(8 / ks);
-    const int slots = L->grid * gemv_ctas_per_sm(bank == 0 ? c.fp4_format : 2);
-    const double waves = std::ceil(items / slots);
-    const double eff = items / (waves * slots);
-    if (eff > best_eff + 0.02) {
-      best_eff = eff;
-      best = ks;
-    }
+  const bool iq2 = bank == 1;
+  const int kt = iq2 ? kIq2KTile : kFp4KTile;
+  KsModel m{};
+  for (int j = 0; j < 4; ++j) {
+    const int ks = 1 << j;
+    if ((c.hidden / kt) % ks == 0 && (c.inter / kt) % ks == 0) m.allowed |= 1 << j;
   }
-  return best;
+  m.slots = float(L->grid * gemv_ctas_per_sm(iq2 ? 2 : c.fp4_format));
+  m.bpe = iq2 ? 32.f * 66.f / 256.f : (c.fp4_format == B200MOE_NVFP4 ? 18.f : 17.f);
+  m.bw_cta = iq2 ? 6e9f : 18.4e9f;
+  m.bw_hbm = iq2 ? 2.0e12f : 4.8e12f;
+  m.per_wave = 2e-6f;
+  m.tiles[0] = float(c.inter / 16);
+  m.tiles[1] = float(c.hidden / 32);
+  m.kdim[0] = float(c.hidden);
+  m.kdim[1] = float(c.inter);
+  return m;
 }
 
 struct Marks {
@@ -146,9 +155,8 @@ int run_forward(b200moe_layer* L, cudaStream_t s, const void* x, int x_dtype, co
   if (x_dtype == B200MOE_BF16) {
     if (launch_convert_bf16(s, x, int64_t(m) * c.hidden, L->x16)) return B200MOE_ERR_CUDA;
     xsrc = L->x16;
-    marks.mark();
   }
-  int ks[2] = {choose_ks(L, 0, m), choose_ks(L, 1, m)};
+  marks.mark();  // after the bf16 conversion (or none): the event layout does not depend on x's dtype
   // prefill with the tcgen05 GEMM: the FP4 bank's chunks are 128-route token tiles
   const bool tc = prefill && c.prefill_gemm && c.n_fp4 > 0 && L->xperm;
   PlanArgs p{};
@@ -164,7 +172,8 @@ int run_forward(b200moe_layer* L, cudaStream_t s, const void* x, int x_dtype, co
   p.key_lo[1] = c.n_fp4;
   p.key_hi[1] = c.n_fp4 + c.n_iq2;
   for (int b = 0; b < 2; ++b) {
-    p.rc[b] = (tc && b == 0) ? kTcTokenTile : 16 / ks[b];
+    p.rc[b] = (tc && b == 0) ? kTcTokenTile : fixed_rc(L, b);
+    p.ks_model[b] = ks_model(L, b);
     p.max_chunks[b] = L->max_chunks;
     p.chunks[b] = L->chunks[b];
   }
@@ -176,6 +185,7 @@ int run_forward(b200moe_layer* L, cudaStream_t s, const void* x, int x_dtype, co
   p.out = out;
   p.H = c.hidden;
   p.top_k = c.top_k;
+  p.ks_sel = L->ks_sel;
   p.err = L->err;
   if (launch_plan(s, p)) return B200MOE_ERR_CUDA;
   marks.mark();
@@ -219,7 +229,7 @@ int run_forward(b200moe_layer* L, cudaStream_t s, const void* x, int x_dtype, co
       GemvArgs g{};
       g.fmt = b == 0 ? c.fp4_format : 2;
       g.epi = epi;
-      g.ks = ks[b];
+      g.ks_sel = L->ks_sel;
       g.region = L->bank[b] + (epi == 0 ? 0 : L->geom[b].w13_bytes);
       g.slot_stride = L->geom[b].slot_bytes;
       g.n_slots = n_slots;
@@ -323,6 +333,7 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
   take(dalloc(&L->y2, size_t(L->s_max) * c.hidden));
   take(dalloc(&L->counters, size_t(L->t_max) * (c.hidden / 32)));
   take(dalloc(&L->err, 1));
+  take(dalloc(&L->ks_sel, 2));
   if (c.prefill_gemm && c.max_prefill_tokens > 0 && c.n_fp4 > 0) {
     take(dalloc(&L->xperm, size_t(L->s_max) * c.hidden));
     if (st == B200MOE_OK && (make_token_map(L->map_x, L->xperm, L->s_max, c.hidden) ||
@@ -505,6 +516,20 @@ int b200moe_set_timing_events(b200moe_layer* L, void* const* events, int n) {
   return B200MOE_OK;
 }
 
+int b200moe_set_split_k(b200moe_layer* L, int ks_fp4, int ks_iq2) {
+  if (!L) return B200MOE_ERR_INVALID_ARG;
+  const auto& c = L->cfg;
+  const int ks[2] = {ks_fp4, ks_iq2};
+  for (int b = 0; b < 2; ++b) {
+    const int kt = b == 0 ? kFp4KTile : kIq2KTile;
+    if (ks[b] != 0 && ks[b] != 1 && ks[b] != 2 && ks[b] != 4 && ks[b] != 8) return B200MOE_ERR_INVALID_ARG;
+    if (ks[b] && ((c.hidden / kt) % ks[b] || (c.inter / kt) % ks[b])) return B200MOE_ERR_INVALID_ARG;
+  }
+  L->ks_fixed[0] = ks_fp4;
+  L->ks_fixed[1] = ks_iq2;
+  return B200MOE_OK;
+}
+
 int b200moe_debug_inter(const b200moe_layer* L, void* stream, void* dst, int rows) {
   if (!L || !dst || rows < 1 || rows > L->s_max) return B200MOE_ERR_INVALID_ARG;
   DeviceGuard guard(L->device);
@@ -578,6 +603,7 @@ constexpr size_t kOffWeff = kOffPerm + align256(kStaticRoutes * 4);
 constexpr size_t kOffChunks0 = kOffWeff + align256(kStaticRoutes * 4);
 constexpr size_t kOffChunks1 = kOffChunks0 + align256(kStaticMaxChunks * sizeof(Chunk));
 constexpr size_t kOffNChunks = kOffChunks1 + align256(kStaticMaxChunks * sizeof(Chunk));
+constexpr size_t kOffKsSel = kOffNChunks + 64;
 constexpr size_t kOffX16 = kOffNChunks + 256;
 constexpr size_t kOffInter = kOffX16 + align256(size_t(kStaticMaxTokens) * kStaticMaxHidden * 2);
 constexpr size_t kOffYw = kOffInter + align256(size_t(kStaticRoutes) * kStaticMaxInter * 2);
@@ -643,7 +669,7 @@ extern "C" int b200moe_forward_static(b200moe_layer* L, void* stream, const void
     if (launch_convert_bf16(s, x, int64_t(M) * c.hidden, x16)) return B200MOE_ERR_CUDA;
     xsrc = x16;
   }
-  int ks[2] = {choose_ks(L, 0, M), choose_ks(L, 1, M)};
+  int32_t* ks_sel = reinterpret_cast<int32_t*>(ws + kOffKsSel);
   PlanArgs p{};
   p.ids = ids;
   p.n = S;
@@ -657,7 +683,8 @@ extern "C" int b200moe_forward_static(b200moe_layer* L, void* stream, const void
   p.key_lo[1] = c.n_fp4;
   p.key_hi[1] = c.n_fp4 + c.n_iq2;
   for (int b = 0; b < 2; ++b) {
-    p.rc[b] = 16 / ks[b];
+    p.rc[b] = fixed_rc(L, b);
+    p.ks_model[b] = ks_model(L, b);
     p.max_chunks[b] = int(kStaticMaxChunks);
     p.chunks[b] = chunks[b];
   }
@@ -669,6 +696,7 @@ extern "C" int b200moe_forward_static(b200moe_layer* L, void* stream, const void
   p.out = out;
   p.H = c.hidden;
   p.top_k = c.top_k;
+  p.ks_sel = ks_sel;
   p.err = L->err;
   if (launch_plan(s, p)) return B200MOE_ERR_CUDA;
   for (int epi = 0; epi < 2; ++epi) {
@@ -678,7 +706,7 @@ extern "C" int b200moe_forward_static(b200moe_layer* L, void* stream, const void
       GemvArgs g{};
       g.fmt = b == 0 ? c.fp4_format : 2;
       g.epi = epi;
-      g.ks = ks[b];
+      g.ks_sel = ks_sel;
       g.region = L->bank[b] + (epi == 0 ? 0 : L->geom[b].w13_bytes);
       g.slot_stride = L->geom[b].slot_bytes;
       g.n_slots = n_slots;

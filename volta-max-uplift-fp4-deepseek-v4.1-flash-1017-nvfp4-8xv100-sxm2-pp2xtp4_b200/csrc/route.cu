@@ -168,10 +168,57 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanArgs a) {
   if (product && a.key_counts)
     for (int key = tid; key < a.n_keys; key += kPlanThreads) a.key_counts[key] = aux[key];
 
+  __shared__ int rc_sel[2];
+  if (product) {
+    // chunk counts of every bank at 16, 8, 4 and 2 routes per chunk
+    __shared__ int st[2][4];
+    if (tid < 8) st[tid / 4][tid % 4] = 0;
+    __syncthreads();
+    for (int b = 0; b < a.n_banks; ++b)
+      for (int key = a.key_lo[b] + tid; key < a.key_hi[b]; key += kPlanThreads) {
+        const int c = aux[key];
+        if (c == 0) continue;
+        atomicAdd(&st[b][0], (c + 15) / 16);
+        atomicAdd(&st[b][1], (c + 7) / 8);
+        atomicAdd(&st[b][2], (c + 3) / 4);
+        atomicAdd(&st[b][3], (c + 1) / 2);
+      }
+    __syncthreads();
+    if (tid < a.n_banks) {
+      const int b = tid;
+      int rc = a.rc[b];
+      if (rc == 0) {  // split-K of this bank from the model over this plan's chunk counts
+        const KsModel& m = a.ks_model[b];
+        int best = 1;
+        float best_t = 3.0e38f;
+        for (int j = 0; j < 4; ++j) {
+          if (!(m.allowed >> j & 1)) continue;
+          const int ks = 1 << j;
+          const float chunks = fmaxf(1.f, float(st[b][j]));
+          float t = 0.f;
+          for (int p = 0; p < 2; ++p) {
+            const float items = chunks * m.tiles[p] / (8.f / ks);
+            const float bytes = (8.f / ks) * m.kdim[p] * m.bpe;
+            const float waves = ceilf(items / m.slots);
+            t += waves * (fmaxf(bytes / m.bw_cta, fminf(items, m.slots) * bytes / m.bw_hbm) + m.per_wave);
+          }
+          if (t < best_t * 0.999999f) {
+            best_t = t;
+            best = ks;
+          }
+        }
+        rc = kRouteSlotsPerChunk / best;
+      }
+      rc_sel[b] = rc;
+      if (a.ks_sel) a.ks_sel[b] = max(1, kRouteSlotsPerChunk / rc);
+    }
+    __syncthreads();
+  }
+
   if (product) {
     // route chunks of every bank: ceil(count / rc) chunks per non-empty key
     for (int b = 0; b < a.n_banks; ++b) {
-      const int lo = a.key_lo[b], hi = a.key_hi[b], rc = a.rc[b];
+      const int lo = a.key_lo[b], hi = a.key_hi[b], rc = rc_sel[b];
       int* nch = hist;  // hist is free now: reuse as [nk]
       for (int key = tid; key < nk; key += kPlanThreads)
         nch[key] = (key >= lo && key < hi) ? (aux[key] + rc - 1) / rc : 0;

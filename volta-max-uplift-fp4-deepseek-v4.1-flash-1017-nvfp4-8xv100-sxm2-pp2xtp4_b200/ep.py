@@ -81,10 +81,13 @@ class ExpertParallelMoe:
     """One routed-MoE layer with its experts sharded over a process group.
 
     ``tokens`` bounds the tokens one rank passes per forward.  Local experts
-    run with the skinny kernels (a rank sees few routes per expert at decode)."""
+    run with the skinny kernels (a rank sees few routes per expert at decode).
+    With ``split_k`` fixed here and on a single-GPU layer, the outputs of the
+    two are bit-equal (same per-route rows, same slot-order combine)."""
 
     def __init__(self, *, hidden: int, inter: int, num_experts: int, top_k: int, tokens: int, tier,
-                 fp4_format: str = "nvfp4", group=None, device: torch.device | None = None):
+                 fp4_format: str = "nvfp4", group=None, device: torch.device | None = None,
+                 split_k: tuple[int, int] | None = None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -99,6 +102,8 @@ class ExpertParallelMoe:
                                    max_tokens=min(64, r_max), max_prefill_tokens=r_max, tier=self.tier,
                                    fp4_format=fp4_format, device=dev, rank=self.rank, world=self.world,
                                    prefill_gemm="skinny")
+        if split_k is not None:
+            self.layer.set_split_k(*split_k)
         self.owner = torch.from_numpy(owner_of_expert(num_experts, self.world)).to(dev)
         f16 = dict(dtype=torch.float16, device=dev)
         i32 = dict(dtype=torch.int32, device=dev)
@@ -116,6 +121,7 @@ class ExpertParallelMoe:
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         self._ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
         self._timed = False
+        self.last_routes_in = 0
 
     # weights go to the local layer (slots = this rank's experts of each format, ascending id)
     def load_fp4(self, *args, **kw):
@@ -151,6 +157,7 @@ class ExpertParallelMoe:
         # routes whose id has no owner are sorted last and never sent
         send_split, recv_split = exchange_counts(self.send_counts, self.world, self.group)
         S_ok, R = int(sum(send_split)), int(sum(recv_split))
+        self.last_routes_in = R
         if self.world > 1:
             dist.all_to_all_single(self.recv_rows[:R], self.send_rows[:S_ok], recv_split, send_split,
                                    group=self.group)
@@ -177,6 +184,13 @@ class ExpertParallelMoe:
             _lib.ptr(residual), out.data_ptr()))
         self._timed = self.world > 1
         return out
+
+    def local_experts_used(self) -> int:
+        """Distinct local experts the last forward ran (host sync)."""
+        if self.last_routes_in == 0:
+            return 0
+        eid = (self.recv_eid if self.world > 1 else self.send_eid)[:self.last_routes_in]
+        return int(torch.unique(eid).numel())
 
     def comm_ms(self) -> float:
         """Exchange time (counts + rows + ids out, y2 back) of the last forward;

@@ -196,6 +196,11 @@ class B200NativeMoe:
         _lib.check("b200moe_debug_perm", _lib.lib().b200moe_debug_perm(self._h, _stream(), out.data_ptr(), n))
         return out
 
+    def set_split_k(self, ks_fp4: int = 0, ks_iq2: int = 0) -> None:
+        """Fix the GEMV split-K per bank (1, 2, 4 or 8; 0 = chosen per launch).
+        Layers with the same fixed split-K give bit-equal rows per route."""
+        _lib.check("b200moe_set_split_k", _lib.lib().b200moe_set_split_k(self._h, int(ks_fp4), int(ks_iq2)))
+
     def set_timing_events(self, events) -> None:
         """Record torch.cuda.Event objects between the forward's launches (None: off)."""
         events = list(events or [])
