@@ -75,10 +75,28 @@ __device__ __forceinline__ void fp4_step(uint32_t wb, uint32_t xb, int ntiles, i
   for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
     for (int h = 0; h < 2; ++h) cw[mt][h] = lds128(wb + mt * 1024 + h * 512 + lane * 16);
-  uint2 sc[2];
+  // block scales of this thread's rows (r, r + 8) for the 4 K chunks of the
+  // stage, as f16x2 with the scale in both halves: sh[mt][row half][chunk]
+  uint32_t sh[2][2][4];
 #pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
-    sc[mt] = FMT == 0 ? lds64(wb + 2048 + mt * 128 + (r * 2 + (q >> 1)) * 8) : lds64(wb + 2048 + mt * 64 + r * 8);
+  for (int mt = 0; mt < 2; ++mt) {
+    const uint2 sc = FMT == 0 ? lds64(wb + 2048 + mt * 128 + (r * 2 + (q >> 1)) * 8) : lds64(wb + 2048 + mt * 64 + r * 8);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t v = h == 0 ? sc.x : sc.y;  // bytes: chunks 0..3
+      if (FMT == 0) {
+        const uint32_t h01 = e4m3x2_to_f16x2(v), h23 = e4m3x2_to_f16x2(v >> 16);
+        sh[mt][h][0] = lo_half2(h01);
+        sh[mt][h][1] = hi_half2(h01);
+        sh[mt][h][2] = lo_half2(h23);
+        sh[mt][h][3] = hi_half2(h23);
+      } else {
+        // rebased E8M0 exponent b -> f16 2^(b - 15) in both halves: b << 10 | b << 26
+#pragma unroll
+        for (int c = 0; c < 4; ++c) sh[mt][h][c] = __byte_perm(v, 0, 0x0404u | (c << 12) | (c << 4)) << 2;
+      }
+    }
+  }
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     uint4 xv[2];
@@ -87,16 +105,7 @@ __device__ __forceinline__ void fp4_step(uint32_t wb, uint32_t xb, int ntiles, i
       if (nt < ntiles) xv[nt] = lds128(xb + (nt * 8 + r) * XRS + c * 64 + q * 16);
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt) {
-      uint32_t s0, s1;
-      const uint32_t b0 = (sc[mt].x >> (8 * c)) & 255u, b1 = (sc[mt].y >> (8 * c)) & 255u;
-      if (FMT == 0) {
-        const uint32_t sp = e4m3x2_to_f16x2(b0 | (b1 << 8));
-        s0 = lo_half2(sp);
-        s1 = hi_half2(sp);
-      } else {
-        s0 = (b0 << 10) * 0x10001u;
-        s1 = (b1 << 10) * 0x10001u;
-      }
+      const uint32_t s0 = sh[mt][0][c], s1 = sh[mt][1][c];
       const uint32_t w0 = c == 0 ? cw[mt][0].x : c == 1 ? cw[mt][0].y : c == 2 ? cw[mt][0].z : cw[mt][0].w;
       const uint32_t w1 = c == 0 ? cw[mt][1].x : c == 1 ? cw[mt][1].y : c == 2 ? cw[mt][1].z : cw[mt][1].w;
       uint32_t o0[4], o1[4];
