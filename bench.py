@@ -146,8 +146,8 @@ def measured_traffic(distinct: int) -> dict | None:
     if not p.exists():
         return None
     txt = p.read_text()
-    m1 = re.search(r"traffic_bytes_per_launch:\s*([0-9.e+]+)", txt)
-    m2 = re.search(r"captured_distinct_experts:\s*([0-9]+)", txt)
+    m1 = re.search(r"^traffic_bytes_per_launch:\s*([0-9.e+]+)", txt, re.M)
+    m2 = re.search(r"^captured_distinct_experts:\s*([0-9]+)", txt, re.M)
     if not (m1 and m2):
         return None
     b, d = float(m1.group(1)), int(m2.group(1))
