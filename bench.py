@@ -507,11 +507,11 @@ def run_c2(job) -> None:
     ms, clk = job.timed(run, args.steps)
     layer.check_errors()
     del graph
-    # events: start, convert, plan, W13 fp4, W13 iq2, W2 fp4, W2 iq2
-    per = per_launch(layer, step, args.steps, 7)
+    # events: start, convert, x int8 blocks, plan, W13 fp4, W13 iq2, SwiGLU int8 blocks, W2 fp4, W2 iq2
+    per = per_launch(layer, step, args.steps, 9)
     pk = peaks()
-    launches = {"w13_fp4": (per[2], hot_used.size * W13_BYTES), "w13_iq2": (per[3], iq_used.size * IQ_W13_BYTES),
-                "w2_fp4": (per[4], hot_used.size * W2_BYTES), "w2_iq2": (per[5], iq_used.size * IQ_W2_BYTES)}
+    launches = {"w13_fp4": (per[3], hot_used.size * W13_BYTES), "w13_iq2": (per[4], iq_used.size * IQ_W13_BYTES),
+                "w2_fp4": (per[6], hot_used.size * W2_BYTES), "w2_iq2": (per[7], iq_used.size * IQ_W2_BYTES)}
     dom = max(launches, key=lambda k: launches[k][0])
     t_dom, b_dom = launches[dom]
     achieved = b_dom / (t_dom / 1e3) / 1e9
@@ -532,11 +532,13 @@ def run_c2(job) -> None:
             "layer_roofline": {"bytes": layer_bytes, "ms": float(per.sum()),
                                "achieved_gbs": layer_bytes / (per.sum() / 1e3) / 1e9,
                                "frac": layer_bytes / (per.sum() / 1e3) / 1e9 / pk["hbm_gbs"],
-                               "launch_ms": {"convert": float(per[0]), "plan": float(per[1]),
+                               "launch_ms": {"convert": float(per[0]), "x_int8": float(per[1]), "plan": float(per[2]),
+                                             "inter_int8": float(per[5]),
                                              **{k: float(v[0]) for k, v in launches.items()}}},
             "e2e": dict({"value": job.world * m / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms},
                         **e2e_bytes),
-            "gpu_launches": 7 * args.steps,  # gating, bf16 copy, plan, W13 x 2 banks, W2 x 2 banks
+            # gating, bf16 copy, x int8 blocks, plan, W13 x 2 banks, SwiGLU int8 blocks, W2 x 2 banks
+            "gpu_launches": 9 * args.steps,
             "cpu_baseline": cpu,
             "clocks": clk,
         })

@@ -324,6 +324,26 @@ def test_mixed_tier_layer(dev, pkg):
     layer.close()
 
 
+@pytest.mark.parametrize("m", [1, 16, 64])
+def test_all_iq2_layer(dev, pkg, m):
+    """Every expert IQ2_XXS: the int8 tensor path (two-plane int8 activations)
+    against the fp32 dequant-then-matmul reference, with a tighter bar than the
+    layer rule, since nothing else in the layer dilutes the IQ2 error."""
+    from b200moe import tiers
+
+    E = 64
+    tier = np.full(E, tiers.WARM, np.int8)
+    layer, dequant, _, _ = _make_layer(dev, 2048, 1024, E, 8, 64, tier=tier, seed=9)
+    g = torch.Generator(device=dev).manual_seed(90 + m)
+    x = torch.randn((m, 2048), generator=g, device=dev).to(torch.bfloat16)
+    ids, w = layer.route(torch.randn((m, E), generator=g, device=dev))
+    out = layer.forward(x, ids, w).clone()
+    layer.check_errors()
+    err = tr.rel_l2(out, tr.layer_forward(x, ids.long(), w, dequant))
+    assert err < 2e-3, err
+    layer.close()
+
+
 def test_prefill_and_apply(dev, pkg):
     from b200moe import moe
 

@@ -22,6 +22,7 @@
 //     always taken in slot order, so the result does not depend on timing.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 
 #include "common.cuh"
@@ -39,7 +40,9 @@ template <int FMT>
 struct Fmt {
   static constexpr int KT = FMT == 2 ? kIq2KTile : kFp4KTile;            // K per unit
   static constexpr int U = FMT == 2 ? kIq2UnitBytes : fp4_unit_bytes(FMT); // unit bytes
-  static constexpr int XRS = 2 * KT + 64;                                // x row slot bytes
+  // activation bytes of one row per K tile (f16 for FP4; int8 + scale for IQ2)
+  static constexpr int XB = FMT == 2 ? kIq2XBlockBytes : 2 * KT;
+  static constexpr int XRS = FMT == 2 ? 544 : 2 * KT + 64;               // x row slot bytes
   static constexpr int STAGE = kConsumerWarps * U + kRouteSlots * XRS;
   static constexpr int CTAS = FMT == 2 ? 1 : 2;                          // CTAs per SM
   static constexpr int STAGES = CTAS == 2 ? 4 : 6;
@@ -47,7 +50,6 @@ struct Fmt {
 constexpr int kMaxStages = 6;
 
 constexpr int kRedBytes = kConsumerWarps * 32 * 16 * 4;
-constexpr int kIq2TableWords = 256 * 4 + 128 * 4 + 16;  // grid f16, sign masks, (0.5 + s) f16x2
 constexpr int kListInts = 1 + 2 * 128;
 
 template <int FMT>
@@ -124,21 +126,31 @@ __device__ __forceinline__ void fp4_step(uint32_t wb, uint32_t xb, int ntiles, i
 }
 
 // ---------------------------------------------------------------- IQ2 step
-// One 256-wide super-block.  A = grid * sign * (0.5 + s) is exact in f16; the
-// super-block scale d * 0.25 is applied to a per-block partial in FP32.
+// One 256-wide super-block on the int8 tensor path.  A weight is
+// g * sign * (2s + 1) * d / 8 (ggml's IQ2_XXS: d * (0.5 + s) * 0.25 * g * sign)
+// and an activation sx * (q1 + q2 / 254).  Per 32-wide sub-block the int8
+// weights g * sign come from two 4-byte table reads and two byte permutes and
+// meet both activation planes (two m16n8k32); each s32 partial is scaled by
+// the integer 2s + 1 of its row, so the super-block sums stay exact in s32;
+// (t1 + t2 / 254) * d / 8 * sx is applied once in FP32.
+// Thread q owns elements 8q..8q+7 of each sub-block (grid entry q), which are
+// the MMA's K positions 4q..4q+3 and 16+4q..16+4q+3, for weights and activations alike.
 __device__ __forceinline__ void iq2_step(uint32_t wb, uint32_t xb, uint32_t tbl, int ntiles, int lane,
                                          float (&acc)[2][2][2][4]) {
   constexpr int XRS = Fmt<2>::XRS;
+  constexpr uint32_t kPos = 0x002B1908u, kNeg = 0x00D5E7F8u;  // bytes 8, 25, 43, 0 and -8, -25, -43, 0
   const int r = lane >> 2, q = lane & 3;
-  float t[2][2][4];
+  int t[2][2][2][4];  // [plane][mt][nt][i]
 #pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
+  for (int pl = 0; pl < 2; ++pl)
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
+    for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) t[mt][nt][i] = 0.f;
-  const uint32_t tgrid = tbl, tsign = tbl + 256 * 16, tscale = tbl + 256 * 16 + 128 * 16;
-#pragma unroll 1
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) t[pl][mt][nt][i] = 0;
+  const uint32_t tsign = tbl + 256 * 4;
+#pragma unroll 2
   for (int ibp = 0; ibp < 4; ++ibp) {
     uint4 qw[2][2];
 #pragma unroll
@@ -148,49 +160,60 @@ __device__ __forceinline__ void iq2_step(uint32_t wb, uint32_t xb, uint32_t tbl,
 #pragma unroll
     for (int i2 = 0; i2 < 2; ++i2) {
       const int ib = 2 * ibp + i2;
-      uint4 xv[2];
+      uint2 xv[2][2];  // [plane][nt]
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
-        if (nt < ntiles) xv[nt] = lds128(xb + (nt * 8 + r) * XRS + ib * 64 + q * 16);
+        if (nt < ntiles) {
+          xv[0][nt] = lds64(xb + (nt * 8 + r) * XRS + ib * 32 + q * 8);
+          xv[1][nt] = lds64(xb + (nt * 8 + r) * XRS + 256 + ib * 32 + q * 8);
+        }
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt) {
-        uint32_t v[2][4];
+        uint32_t sel[2];
+        int c[2];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const uint32_t a0 = i2 == 0 ? qw[mt][h].x : qw[mt][h].z;
           const uint32_t a1 = i2 == 0 ? qw[mt][h].y : qw[mt][h].w;
           const uint32_t gi = (a0 >> (8 * q)) & 255u;
           const uint32_t si = (a1 >> (7 * q)) & 127u;
-          const uint32_t sc = lds32(tscale + (a1 >> 28) * 4);
-          const uint4 g4 = lds128(tgrid + gi * 16);
-          const uint4 m4 = lds128(tsign + si * 16);
-          v[h][0] = hmul2(g4.x ^ m4.x, sc);
-          v[h][1] = hmul2(g4.y ^ m4.y, sc);
-          v[h][2] = hmul2(g4.z ^ m4.z, sc);
-          v[h][3] = hmul2(g4.w ^ m4.w, sc);
+          sel[h] = lds32(tbl + gi * 4) | lds32(tsign + si * 4);
+          c[h] = int(((a1 >> 27) & 0x1Eu) | 1u);
         }
-        uint32_t a[4] = {v[0][0], v[1][0], v[0][1], v[1][1]};
+        const uint32_t a[4] = {__byte_perm(kPos, kNeg, sel[0]), __byte_perm(kPos, kNeg, sel[1]),
+                               __byte_perm(kPos, kNeg, sel[0] >> 16), __byte_perm(kPos, kNeg, sel[1] >> 16)};
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-          if (nt < ntiles) mma_16816(t[mt][nt], a, xv[nt].x, xv[nt].y);
-        uint32_t a2[4] = {v[0][2], v[1][2], v[0][3], v[1][3]};
+        for (int nt = 0; nt < 2; ++nt) {
+          if (nt < ntiles) {
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-          if (nt < ntiles) mma_16816(t[mt][nt], a2, xv[nt].z, xv[nt].w);
+            for (int pl = 0; pl < 2; ++pl) {
+              int d[4] = {0, 0, 0, 0};
+              mma_16832_s8(d, a, xv[pl][nt].x, xv[pl][nt].y);
+              t[pl][mt][nt][0] += d[0] * c[0];
+              t[pl][mt][nt][1] += d[1] * c[0];
+              t[pl][mt][nt][2] += d[2] * c[1];
+              t[pl][mt][nt][3] += d[3] * c[1];
+            }
+          }
+        }
       }
     }
   }
+  constexpr float kPlane2 = 1.f / 254.f;
 #pragma unroll
   for (int mt = 0; mt < 2; ++mt) {
     const uint32_t dp = lds32(wb + 2048 + mt * 32 + r * 4);
     const __half2 d2 = *reinterpret_cast<const __half2*>(&dp);
-    const float d0 = __low2float(d2) * 0.25f, d1 = __high2float(d2) * 0.25f;
+    const float d0 = __low2float(d2) * 0.125f, d1 = __high2float(d2) * 0.125f;
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
-      acc[mt][nt][0][0] = fmaf(t[mt][nt][0], d0, acc[mt][nt][0][0]);
-      acc[mt][nt][0][1] = fmaf(t[mt][nt][1], d0, acc[mt][nt][0][1]);
-      acc[mt][nt][0][2] = fmaf(t[mt][nt][2], d1, acc[mt][nt][0][2]);
-      acc[mt][nt][0][3] = fmaf(t[mt][nt][3], d1, acc[mt][nt][0][3]);
+      if (nt >= ntiles) continue;
+      const float sx0 = __uint_as_float(lds32(xb + (nt * 8 + 2 * q) * XRS + 512));
+      const float sx1 = __uint_as_float(lds32(xb + (nt * 8 + 2 * q + 1) * XRS + 512));
+      const float sc[4] = {d0 * sx0, d0 * sx1, d1 * sx0, d1 * sx1};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        acc[mt][nt][0][i] = fmaf(fmaf(float(t[1][mt][nt][i]), kPlane2, float(t[0][mt][nt][i])), sc[i], acc[mt][nt][0][i]);
     }
   }
 }
@@ -270,7 +293,7 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, uint8_t* smem) {
           xrow = 0;
         }
       }
-      const uint32_t tx = uint32_t(kConsumerWarps * F::U + KS * ch.count * 2 * F::KT);
+      const uint32_t tx = uint32_t(kConsumerWarps * F::U + KS * ch.count * F::XB);
       for (int st = 0; st < steps; ++st, ++g) {
         const int s = g % kStages;
         const uint32_t ph = (g / kStages) & 1u;
@@ -291,8 +314,10 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, uint8_t* smem) {
           bulk_g2s_hint(sb + lane * F::U, wbase + (int64_t(tp) * n_kt + kt) * F::U, F::U, &full[s], pol);
         } else if (xlane) {
           const int kt = xks * steps + st;
-          const uint8_t* src = static_cast<const uint8_t*>(a.xsrc) + (xrow * a.x_row_stride + int64_t(kt) * F::KT) * 2;
-          bulk_g2s(sb + kConsumerWarps * F::U + xi * F::XRS, src, 2 * F::KT, &full[s]);
+          // f16 rows (FP4) or int8 blocks of kIq2XBlockBytes per K tile (IQ2)
+          const uint8_t* src = static_cast<const uint8_t*>(a.xsrc) +
+                               (FMT == 2 ? (xrow * n_kt + kt) * F::XB : (xrow * a.x_row_stride + int64_t(kt) * F::KT) * 2);
+          bulk_g2s(sb + kConsumerWarps * F::U + xi * F::XRS, src, F::XB, &full[s]);
         }
       }
     }
@@ -448,6 +473,62 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, uint8_t* smem) {
     }
   }
   __syncthreads();
+}
+
+// fp16 rows -> the IQ2 op's int8 activation blocks: per row and 256-wide K
+// tile, q1 = rn(x * 127 / amax), q2 = rn((x - q1 * s) * 254 * 127 / amax)
+// (both clamped to +-127), s = amax / 127 as f32 (0 for an all-zero block),
+// kIq2XBlockBytes per block.  One warp per block.
+// Rows [range[0], range[1]) when `range` is given (device: the IQ2 bank's
+// sorted positions from the route plan), else [0, rows).
+__global__ void quant_s8_kernel(const __half* __restrict__ src, int64_t src_stride, int K, int rows,
+                                const int32_t* __restrict__ range, uint8_t* __restrict__ dst) {
+  const int lane = threadIdx.x & 31;
+  const int n_kt = K / kIq2KTile;
+  const int lo = range ? range[0] : 0, hi = range ? min(range[1], rows) : rows;
+  const int64_t n_blocks = int64_t(max(hi - lo, 0)) * n_kt;
+  for (int64_t blk = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) / 32; blk < n_blocks;
+       blk += int64_t(gridDim.x) * blockDim.x / 32) {
+    const int row = lo + int(blk / n_kt), kt = int(blk % n_kt);
+    const uint4 v = *reinterpret_cast<const uint4*>(src + row * src_stride + int64_t(kt) * kIq2KTile + lane * 8);
+    float f[8];
+    const __half2* hv = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 t = __half22float2(hv[i]);
+      f[2 * i] = t.x;
+      f[2 * i + 1] = t.y;
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float inv = amax > 0.f ? __fdiv_rn(127.f, amax) : 0.f;
+    const float sx = amax / 127.f;
+    uint32_t w1[2] = {0, 0}, w2[2] = {0, 0};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int q1 = max(-127, min(127, __float2int_rn(__fmul_rn(f[i], inv))));
+      const float res = fmaf(-float(q1), sx, f[i]);
+      const int q2 = max(-127, min(127, __float2int_rn(__fmul_rn(__fmul_rn(res, inv), 254.f))));
+      w1[i >> 2] |= uint32_t(q1 & 255) << (8 * (i & 3));
+      w2[i >> 2] |= uint32_t(q2 & 255) << (8 * (i & 3));
+    }
+    uint8_t* out = dst + (int64_t(row) * n_kt + kt) * kIq2XBlockBytes;
+    *reinterpret_cast<uint2*>(out + lane * 8) = make_uint2(w1[0], w1[1]);
+    *reinterpret_cast<uint2*>(out + 256 + lane * 8) = make_uint2(w2[0], w2[1]);
+    if (lane < 4) reinterpret_cast<uint32_t*>(out + 512)[lane] = lane == 0 ? __float_as_uint(sx) : 0u;
+  }
+}
+
+int launch_quant_s8(cudaStream_t s, const __half* src, int64_t src_stride, int K, int rows, const int32_t* range,
+                    uint8_t* dst) {
+  if (rows <= 0) return 0;
+  const int64_t warps = int64_t(rows) * (K / kIq2KTile);
+  const int64_t blocks = std::min<int64_t>((warps + 7) / 8, 148 * 16);
+  quant_s8_kernel<<<int(blocks), 256, 0, s>>>(src, src_stride, K, rows, range, dst);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 // One kernel per format and epilogue; the split-K is read from the device

@@ -1,6 +1,7 @@
 // Internal launchers shared between the library's translation units.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -61,6 +62,7 @@ struct PlanArgs {
   // GEMV of bank b runs with (16 / rc for a fixed rc)
   KsModel ks_model[2];
   int32_t* ks_sel;
+  int32_t* bank_range;  // optional [2][2]: sorted positions [begin, end) of each bank's routes
   const float* w_in;    // [n] router weights (product)
   float* w_eff;         // [n] weight used by the combine (0 for a route without an expert)
   // product: a route without an expert gets a zero y2 row and its completion
@@ -80,6 +82,9 @@ struct PlanArgs {
 };
 
 size_t plan_smem_bytes(int n_keys);
+// fp16 rows -> int8 blocks of kIq2XBlockBytes per 256-wide K tile (IQ2 activations)
+int launch_quant_s8(cudaStream_t s, const __half* src, int64_t src_stride, int K, int rows, const int32_t* range,
+                    uint8_t* dst);
 int launch_plan(cudaStream_t s, const PlanArgs& a);
 int launch_gating(cudaStream_t s, const float* logits, int T, int E, int k, int32_t* ids, float* w,
                   uint32_t* err);
@@ -115,7 +120,7 @@ struct GemvArgs {
   int32_t* counters;          // [tokens][H/32]
   float* out;                 // [tokens][H]
   int H;
-  const uint32_t* iq2_tables; // grid f16 [256][8] then sign masks [128][4]
+  const uint32_t* iq2_tables; // kIq2TableWords: grid magnitude codes [256], sign nibbles [128]
   uint32_t* err;
   int grid;                   // persistent CTAs
 };

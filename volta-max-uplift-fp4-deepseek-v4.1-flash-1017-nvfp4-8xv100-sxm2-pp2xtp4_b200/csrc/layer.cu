@@ -43,7 +43,10 @@ struct b200moe_layer {
   int max_chunks = 0;
   int32_t* n_chunks = nullptr;
   int32_t* ks_sel = nullptr;  // [2] split-K per bank, written by the route plan
+  int32_t* bank_range = nullptr;  // [2][2] sorted positions of each bank's routes, written by the route plan
   __half* x16 = nullptr;
+  uint8_t* xq = nullptr;      // IQ2 int8 activation blocks of the token rows
+  uint8_t* interq = nullptr;  // IQ2 int8 activation blocks of the SwiGLU rows (by sorted position)
   __half* inter = nullptr;
   __half* y2 = nullptr;
   int32_t* counters = nullptr;
@@ -90,7 +93,7 @@ int dalloc(T** p, size_t count) {
 void free_layer(b200moe_layer* L) {
   void* ptrs[] = {L->bank[0], L->bank[1], L->globals, L->span, L->iq2_tables, L->key_of_expert, L->perm,
                   L->w_eff, L->chunks[0], L->chunks[1], L->n_chunks, L->x16, L->inter, L->y2,
-                  L->counters, L->err, L->xperm, L->ks_sel};
+                  L->counters, L->err, L->xperm, L->ks_sel, L->bank_range, L->xq, L->interq};
   for (void* p : ptrs)
     if (p) cudaFree(p);
 }
@@ -130,6 +133,45 @@ KsModel ks_model(const b200moe_layer* L, int bank) {
   return m;
 }
 
+// Per-call intermediates of a forward: the layer's own (allocated at create)
+// or the library's static array (b200moe_forward_static).
+struct Workspace {
+  int32_t* perm;
+  float* w_eff;
+  Chunk* chunks[2];
+  int max_chunks;
+  int32_t* n_chunks;
+  int32_t* ks_sel;
+  int32_t* bank_range;
+  __half* x16;
+  __half* inter;
+  __half* y2;
+  int32_t* counters;
+  uint8_t* xq;
+  uint8_t* interq;
+  void* dbg_y13;
+};
+
+Workspace layer_workspace(b200moe_layer* L) {
+  Workspace w{};
+  w.perm = L->perm;
+  w.w_eff = L->w_eff;
+  w.chunks[0] = L->chunks[0];
+  w.chunks[1] = L->chunks[1];
+  w.max_chunks = L->max_chunks;
+  w.n_chunks = L->n_chunks;
+  w.ks_sel = L->ks_sel;
+  w.bank_range = L->bank_range;
+  w.x16 = L->x16;
+  w.inter = L->inter;
+  w.y2 = L->y2;
+  w.counters = L->counters;
+  w.xq = L->xq;
+  w.interq = L->interq;
+  w.dbg_y13 = L->dbg_y13;
+  return w;
+}
+
 struct Marks {
   const b200moe_layer* L;
   cudaStream_t s;
@@ -140,8 +182,8 @@ struct Marks {
   }
 };
 
-int run_forward(b200moe_layer* L, cudaStream_t s, const void* x, int x_dtype, const int32_t* ids,
-                const float* w, float* out, int m, bool prefill = false) {
+int run_forward(b200moe_layer* L, const Workspace& ws, cudaStream_t s, const void* x, int x_dtype,
+                const int32_t* ids, const float* w, float* out, int m, bool prefill = false) {
   const auto& c = L->cfg;
   Marks marks{L, s};
   if (!L->maps_set) return B200MOE_ERR_STATE;
@@ -153,10 +195,14 @@ int run_forward(b200moe_layer* L, cudaStream_t s, const void* x, int x_dtype, co
   const __half* xsrc = static_cast<const __half*>(x);
   marks.mark();
   if (x_dtype == B200MOE_BF16) {
-    if (launch_convert_bf16(s, x, int64_t(m) * c.hidden, L->x16)) return B200MOE_ERR_CUDA;
-    xsrc = L->x16;
+    if (launch_convert_bf16(s, x, int64_t(m) * c.hidden, ws.x16)) return B200MOE_ERR_CUDA;
+    xsrc = ws.x16;
   }
   marks.mark();  // after the bf16 conversion (or none): the event layout does not depend on x's dtype
+  if (c.n_iq2 > 0) {  // int8 blocks of the token rows for the IQ2 bank's W13
+    if (launch_quant_s8(s, xsrc, c.hidden, c.hidden, m, nullptr, ws.xq)) return B200MOE_ERR_CUDA;
+    marks.mark();
+  }
   // prefill with the tcgen05 GEMM: the FP4 bank's chunks are 128-route token tiles
   const bool tc = prefill && c.prefill_gemm && c.n_fp4 > 0 && L->xperm;
   PlanArgs p{};
@@ -165,7 +211,7 @@ int run_forward(b200moe_layer* L, cudaStream_t s, const void* x, int x_dtype, co
   p.num_experts = c.num_experts;
   p.key_of_expert = L->key_of_expert;
   p.n_keys = c.n_fp4 + c.n_iq2;
-  p.perm = L->perm;
+  p.perm = ws.perm;
   p.n_banks = 2;
   p.key_lo[0] = 0;
   p.key_hi[0] = c.n_fp4;
@@ -174,27 +220,32 @@ int run_forward(b200moe_layer* L, cudaStream_t s, const void* x, int x_dtype, co
   for (int b = 0; b < 2; ++b) {
     p.rc[b] = (tc && b == 0) ? kTcTokenTile : fixed_rc(L, b);
     p.ks_model[b] = ks_model(L, b);
-    p.max_chunks[b] = L->max_chunks;
-    p.chunks[b] = L->chunks[b];
+    p.max_chunks[b] = ws.max_chunks;
+    p.chunks[b] = ws.chunks[b];
   }
-  p.n_chunks = L->n_chunks;
+  p.n_chunks = ws.n_chunks;
   p.w_in = w;
-  p.w_eff = L->w_eff;
-  p.y2 = L->y2;
-  p.counters = L->counters;
+  p.w_eff = ws.w_eff;
+  p.y2 = ws.y2;
+  p.counters = ws.counters;
   p.out = out;
   p.H = c.hidden;
   p.top_k = c.top_k;
-  p.ks_sel = L->ks_sel;
+  p.ks_sel = ws.ks_sel;
+  p.bank_range = ws.bank_range;
   p.err = L->err;
   if (launch_plan(s, p)) return B200MOE_ERR_CUDA;
   marks.mark();
   if (tc) {
-    if (launch_gather_rows(s, x, x_dtype == B200MOE_BF16, L->perm, S, c.top_k, c.hidden, L->xperm))
+    if (launch_gather_rows(s, x, x_dtype == B200MOE_BF16, ws.perm, S, c.top_k, c.hidden, L->xperm))
       return B200MOE_ERR_CUDA;
     marks.mark();
   }
   for (int epi = 0; epi < 2; ++epi) {
+    if (epi == 1 && c.n_iq2 > 0) {  // int8 blocks of the IQ2 routes' SwiGLU rows for the IQ2 bank's W2
+      if (launch_quant_s8(s, ws.inter, c.inter, c.inter, S, ws.bank_range + 2, ws.interq)) return B200MOE_ERR_CUDA;
+      marks.mark();
+    }
     for (int b = 0; b < 2; ++b) {
       const int n_slots = b == 0 ? c.n_fp4 : c.n_iq2;
       if (n_slots == 0) continue;
@@ -206,18 +257,18 @@ int run_forward(b200moe_layer* L, cudaStream_t s, const void* x, int x_dtype, co
         t.globals = L->globals;
         t.K = epi == 0 ? c.hidden : c.inter;
         t.n_rt = epi == 0 ? c.inter / 128 : c.hidden / 256;
-        t.chunks = L->chunks[0];
-        t.n_chunks = L->n_chunks;
+        t.chunks = ws.chunks[0];
+        t.n_chunks = ws.n_chunks;
         t.bank = 0;
-        t.perm = L->perm;
+        t.perm = ws.perm;
         t.S = S;
         t.top_k = c.top_k;
-        t.inter = L->inter;
+        t.inter = ws.inter;
         t.inter_stride = c.inter;
         t.limit = c.swiglu_limit;
-        t.w_eff = L->w_eff;
-        t.y2 = L->y2;
-        t.counters = L->counters;
+        t.w_eff = ws.w_eff;
+        t.y2 = ws.y2;
+        t.counters = ws.counters;
         t.out = out;
         t.H = c.hidden;
         t.err = L->err;
@@ -229,30 +280,31 @@ int run_forward(b200moe_layer* L, cudaStream_t s, const void* x, int x_dtype, co
       GemvArgs g{};
       g.fmt = b == 0 ? c.fp4_format : 2;
       g.epi = epi;
-      g.ks_sel = L->ks_sel;
+      g.ks_sel = ws.ks_sel;
       g.region = L->bank[b] + (epi == 0 ? 0 : L->geom[b].w13_bytes);
       g.slot_stride = L->geom[b].slot_bytes;
       g.n_slots = n_slots;
       g.globals = b == 0 ? L->globals : nullptr;
       g.K = epi == 0 ? c.hidden : c.inter;
       g.n_tp = epi == 0 ? c.inter / 16 : c.hidden / 32;
-      g.chunks = L->chunks[b];
-      g.n_chunks = L->n_chunks;
+      g.chunks = ws.chunks[b];
+      g.n_chunks = ws.n_chunks;
       g.bank = b;
-      g.perm = L->perm;
+      g.perm = ws.perm;
       g.S = S;
       g.top_k = c.top_k;
-      g.xsrc = epi == 0 ? static_cast<const void*>(xsrc) : static_cast<const void*>(L->inter);
+      if (b == 0) g.xsrc = epi == 0 ? static_cast<const void*>(xsrc) : static_cast<const void*>(ws.inter);
+      else g.xsrc = epi == 0 ? static_cast<const void*>(ws.xq) : static_cast<const void*>(ws.interq);
       g.x_by_token = epi == 0;
       g.x_row_stride = epi == 0 ? c.hidden : c.inter;
       g.n_x_rows = epi == 0 ? m : S;
-      g.inter = L->inter;
+      g.inter = ws.inter;
       g.inter_stride = c.inter;
-      g.dbg_y13 = L->dbg_y13;
+      g.dbg_y13 = ws.dbg_y13;
       g.limit = c.swiglu_limit;
-      g.w_eff = L->w_eff;
-      g.y2 = L->y2;
-      g.counters = L->counters;
+      g.w_eff = ws.w_eff;
+      g.y2 = ws.y2;
+      g.counters = ws.counters;
       g.out = out;
       g.H = c.hidden;
       g.iq2_tables = L->iq2_tables;
@@ -321,7 +373,7 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
   take(dalloc(&L->bank[1], size_t(c.n_iq2) * L->geom[1].slot_bytes));
   take(dalloc(&L->globals, size_t(std::max(c.n_fp4, 1)) * 3));
   take(dalloc(&L->span, size_t(std::max(c.n_fp4, 1)) * 6));
-  take(dalloc(&L->iq2_tables, 256 * 4 + 128 * 4 + 16));
+  take(dalloc(&L->iq2_tables, size_t(kIq2TableWords)));
   take(dalloc(&L->key_of_expert, size_t(c.num_experts)));
   take(dalloc(&L->perm, size_t(L->s_max)));
   take(dalloc(&L->w_eff, size_t(L->s_max)));
@@ -334,6 +386,11 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
   take(dalloc(&L->counters, size_t(L->t_max) * (c.hidden / 32)));
   take(dalloc(&L->err, 1));
   take(dalloc(&L->ks_sel, 2));
+  take(dalloc(&L->bank_range, 4));
+  if (c.n_iq2 > 0) {
+    take(dalloc(&L->xq, size_t(L->t_max) * (c.hidden / kIq2KTile) * kIq2XBlockBytes));
+    take(dalloc(&L->interq, size_t(L->s_max) * (c.inter / kIq2KTile) * kIq2XBlockBytes));
+  }
   if (c.prefill_gemm && c.max_prefill_tokens > 0 && c.n_fp4 > 0) {
     take(dalloc(&L->xperm, size_t(L->s_max) * c.hidden));
     if (st == B200MOE_OK && (make_token_map(L->map_x, L->xperm, L->s_max, c.hidden) ||
@@ -396,23 +453,17 @@ int b200moe_set_slot_maps(b200moe_layer* L, const int32_t* fp4_slot, const int32
 
 int b200moe_set_iq2_tables(b200moe_layer* L, const int8_t* grid, const uint8_t* ksigns) {
   if (!L || !grid || !ksigns) return B200MOE_ERR_INVALID_ARG;
-  std::vector<uint32_t> t(256 * 4 + 128 * 4 + 16);
-  auto h = [](float v) {
-    __half x = __float2half_rn(v);
-    return uint32_t(*reinterpret_cast<uint16_t*>(&x));
-  };
+  // magnitude code per grid value (ggml's IQ2_XXS grid holds 8, 25 and 43 only)
+  std::vector<uint32_t> t(kIq2TableWords, 0u);
   for (int e = 0; e < 256; ++e)
-    for (int p = 0; p < 4; ++p) {
-      const int8_t g0 = grid[e * 8 + 2 * p], g1 = grid[e * 8 + 2 * p + 1];
-      if (g0 < 0 || g1 < 0) return B200MOE_ERR_INVALID_ARG;  // ggml's grid values are positive
-      t[e * 4 + p] = h(float(g0)) | (h(float(g1)) << 16);
+    for (int j = 0; j < 8; ++j) {
+      const int8_t g = grid[e * 8 + j];
+      const int code = g == 8 ? 0 : g == 25 ? 1 : g == 43 ? 2 : -1;
+      if (code < 0) return B200MOE_ERR_INVALID_ARG;
+      t[e] |= uint32_t(code) << (4 * j);
     }
-  for (int si = 0; si < 128; ++si) {
-    const uint32_t sb = ksigns[si];
-    for (int p = 0; p < 4; ++p)
-      t[1024 + si * 4 + p] = (((sb >> (2 * p)) & 1u) << 15) | (((sb >> (2 * p + 1)) & 1u) << 31);
-  }
-  for (int s = 0; s < 16; ++s) t[1024 + 512 + s] = h(0.5f + s) * 0x10001u;
+  for (int si = 0; si < 128; ++si)
+    for (int j = 0; j < 8; ++j) t[256 + si] |= ((uint32_t(ksigns[si]) >> j) & 1u) << (4 * j + 2);
   DeviceGuard guard(L->device);
   if (cudaMemcpy(L->iq2_tables, t.data(), t.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
     return B200MOE_ERR_CUDA;
@@ -465,14 +516,14 @@ int b200moe_forward(b200moe_layer* L, void* stream, const void* x, int x_dtype, 
                     const float* w, float* out, int M) {
   if (!L || M < 1 || M > L->cfg.max_tokens) return B200MOE_ERR_INVALID_ARG;
   DeviceGuard guard(L->device);
-  return run_forward(L, static_cast<cudaStream_t>(stream), x, x_dtype, ids, w, out, M);
+  return run_forward(L, layer_workspace(L), static_cast<cudaStream_t>(stream), x, x_dtype, ids, w, out, M);
 }
 
 int b200moe_forward_prefill(b200moe_layer* L, void* stream, const void* x, int x_dtype, const int32_t* ids,
                             const float* w, float* out, int T) {
   if (!L || T < 1 || T > L->t_max) return B200MOE_ERR_INVALID_ARG;
   DeviceGuard guard(L->device);
-  return run_forward(L, static_cast<cudaStream_t>(stream), x, x_dtype, ids, w, out, T, true);
+  return run_forward(L, layer_workspace(L), static_cast<cudaStream_t>(stream), x, x_dtype, ids, w, out, T, true);
 }
 
 int b200moe_check_errors(b200moe_layer* L, void* stream, uint32_t* bits) {
@@ -604,13 +655,18 @@ constexpr size_t kOffChunks0 = kOffWeff + align256(kStaticRoutes * 4);
 constexpr size_t kOffChunks1 = kOffChunks0 + align256(kStaticMaxChunks * sizeof(Chunk));
 constexpr size_t kOffNChunks = kOffChunks1 + align256(kStaticMaxChunks * sizeof(Chunk));
 constexpr size_t kOffKsSel = kOffNChunks + 64;
+constexpr size_t kOffBankRange = kOffNChunks + 128;
 constexpr size_t kOffX16 = kOffNChunks + 256;
 constexpr size_t kOffInter = kOffX16 + align256(size_t(kStaticMaxTokens) * kStaticMaxHidden * 2);
 constexpr size_t kOffYw = kOffInter + align256(size_t(kStaticRoutes) * kStaticMaxInter * 2);
 constexpr size_t kOffCounters = kOffYw + align256(size_t(kStaticRoutes) * kStaticMaxHidden * 2);
-constexpr size_t kStaticScratchBytes = kOffCounters + align256(size_t(kStaticMaxTokens) * (kStaticMaxHidden / 32) * 4);
+constexpr size_t kOffXq = kOffCounters + align256(size_t(kStaticMaxTokens) * (kStaticMaxHidden / 32) * 4);
+constexpr size_t kOffInterq =
+    kOffXq + align256(size_t(kStaticMaxTokens) * (kStaticMaxHidden / kIq2KTile) * kIq2XBlockBytes);
+constexpr size_t kStaticScratchBytes =
+    kOffInterq + align256(size_t(kStaticRoutes) * (kStaticMaxInter / kIq2KTile) * kIq2XBlockBytes);
 
-// About 1.7 MB per GPU (see the limits above).
+// About 2 MB per GPU (see the limits above).
 static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
 
 // Device address of g_static_scratch per device, looked up on the first call
@@ -652,91 +708,24 @@ extern "C" int b200moe_forward_static(b200moe_layer* L, void* stream, const void
   uint8_t* ws = nullptr;
   if (int st = static_scratch(L->device, &ws)) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int32_t* perm = reinterpret_cast<int32_t*>(ws + kOffPerm);
-  float* w_eff = reinterpret_cast<float*>(ws + kOffWeff);
-  Chunk* chunks[2] = {reinterpret_cast<Chunk*>(ws + kOffChunks0), reinterpret_cast<Chunk*>(ws + kOffChunks1)};
-  int32_t* n_chunks = reinterpret_cast<int32_t*>(ws + kOffNChunks);
-  __half* x16 = reinterpret_cast<__half*>(ws + kOffX16);
-  __half* inter = reinterpret_cast<__half*>(ws + kOffInter);
-  __half* y2 = reinterpret_cast<__half*>(ws + kOffYw);
-  int32_t* counters = reinterpret_cast<int32_t*>(ws + kOffCounters);
+  Workspace w_{};
+  w_.perm = reinterpret_cast<int32_t*>(ws + kOffPerm);
+  w_.w_eff = reinterpret_cast<float*>(ws + kOffWeff);
+  w_.chunks[0] = reinterpret_cast<Chunk*>(ws + kOffChunks0);
+  w_.chunks[1] = reinterpret_cast<Chunk*>(ws + kOffChunks1);
+  w_.max_chunks = int(kStaticMaxChunks);
+  w_.n_chunks = reinterpret_cast<int32_t*>(ws + kOffNChunks);
+  w_.ks_sel = reinterpret_cast<int32_t*>(ws + kOffKsSel);
+  w_.bank_range = reinterpret_cast<int32_t*>(ws + kOffBankRange);
+  w_.x16 = reinterpret_cast<__half*>(ws + kOffX16);
+  w_.inter = reinterpret_cast<__half*>(ws + kOffInter);
+  w_.y2 = reinterpret_cast<__half*>(ws + kOffYw);
+  w_.counters = reinterpret_cast<int32_t*>(ws + kOffCounters);
+  w_.xq = ws + kOffXq;
+  w_.interq = ws + kOffInterq;
+  w_.dbg_y13 = nullptr;
   // The array keeps the previous call's contents: the combine counters must
-  // start at zero, and the SwiGLU rows are read whole by the W2 launch.
-  if (cudaMemsetAsync(counters, 0, size_t(M) * (c.hidden / 32) * 4, s) != cudaSuccess) return B200MOE_ERR_CUDA;
-  const int S = M * c.top_k;
-  const __half* xsrc = static_cast<const __half*>(x);
-  if (x_dtype == B200MOE_BF16) {
-    if (launch_convert_bf16(s, x, int64_t(M) * c.hidden, x16)) return B200MOE_ERR_CUDA;
-    xsrc = x16;
-  }
-  int32_t* ks_sel = reinterpret_cast<int32_t*>(ws + kOffKsSel);
-  PlanArgs p{};
-  p.ids = ids;
-  p.n = S;
-  p.num_experts = c.num_experts;
-  p.key_of_expert = L->key_of_expert;
-  p.n_keys = c.n_fp4 + c.n_iq2;
-  p.perm = perm;
-  p.n_banks = 2;
-  p.key_lo[0] = 0;
-  p.key_hi[0] = c.n_fp4;
-  p.key_lo[1] = c.n_fp4;
-  p.key_hi[1] = c.n_fp4 + c.n_iq2;
-  for (int b = 0; b < 2; ++b) {
-    p.rc[b] = fixed_rc(L, b);
-    p.ks_model[b] = ks_model(L, b);
-    p.max_chunks[b] = int(kStaticMaxChunks);
-    p.chunks[b] = chunks[b];
-  }
-  p.n_chunks = n_chunks;
-  p.w_in = w;
-  p.w_eff = w_eff;
-  p.y2 = y2;
-  p.counters = counters;
-  p.out = out;
-  p.H = c.hidden;
-  p.top_k = c.top_k;
-  p.ks_sel = ks_sel;
-  p.err = L->err;
-  if (launch_plan(s, p)) return B200MOE_ERR_CUDA;
-  for (int epi = 0; epi < 2; ++epi) {
-    for (int b = 0; b < 2; ++b) {
-      const int n_slots = b == 0 ? c.n_fp4 : c.n_iq2;
-      if (n_slots == 0) continue;
-      GemvArgs g{};
-      g.fmt = b == 0 ? c.fp4_format : 2;
-      g.epi = epi;
-      g.ks_sel = ks_sel;
-      g.region = L->bank[b] + (epi == 0 ? 0 : L->geom[b].w13_bytes);
-      g.slot_stride = L->geom[b].slot_bytes;
-      g.n_slots = n_slots;
-      g.globals = b == 0 ? L->globals : nullptr;
-      g.K = epi == 0 ? c.hidden : c.inter;
-      g.n_tp = epi == 0 ? c.inter / 16 : c.hidden / 32;
-      g.chunks = chunks[b];
-      g.n_chunks = n_chunks;
-      g.bank = b;
-      g.perm = perm;
-      g.S = S;
-      g.top_k = c.top_k;
-      g.xsrc = epi == 0 ? static_cast<const void*>(xsrc) : static_cast<const void*>(inter);
-      g.x_by_token = epi == 0;
-      g.x_row_stride = epi == 0 ? c.hidden : c.inter;
-      g.n_x_rows = epi == 0 ? M : S;
-      g.inter = inter;
-      g.inter_stride = c.inter;
-      g.dbg_y13 = nullptr;
-      g.limit = c.swiglu_limit;
-      g.w_eff = w_eff;
-      g.y2 = y2;
-      g.counters = counters;
-      g.out = out;
-      g.H = c.hidden;
-      g.iq2_tables = L->iq2_tables;
-      g.err = L->err;
-      g.grid = L->grid * gemv_ctas_per_sm(g.fmt);
-      if (launch_gemv(s, g)) return B200MOE_ERR_CUDA;
-    }
-  }
-  return B200MOE_OK;
+  // start at zero (the SwiGLU rows and int8 blocks are rewritten before use).
+  if (cudaMemsetAsync(w_.counters, 0, size_t(M) * (c.hidden / 32) * 4, s) != cudaSuccess) return B200MOE_ERR_CUDA;
+  return run_forward(L, w_, s, x, x_dtype, ids, w, out, M);
 }

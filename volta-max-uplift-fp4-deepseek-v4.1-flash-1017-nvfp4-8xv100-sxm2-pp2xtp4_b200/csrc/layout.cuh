@@ -27,6 +27,18 @@ namespace b200moe {
 
 constexpr int kFp4KTile = 128;   // K elements per FP4 unit
 constexpr int kIq2KTile = 256;   // K elements per IQ2 unit
+// The IQ2 op multiplies int8 weights by int8 activations on the tensor cores
+// (the reference's IQ2 dot products are int8 too, ggml's with Q8_K blocks).
+// One int8 plane per 256-wide block misses 1e-2 on SwiGLU rows (amax ~7x
+// their RMS), so an activation block holds two planes: x ~ s * (q1 + q2/254),
+// s = amax / 127, q2 the rounded residual (error <= amax / 64,516).  Layout
+// per row and 256-wide K tile: q1 [256], q2 [256], s (f32), 12 bytes padding.
+constexpr int kIq2XBlockBytes = 528;
+// IQ2 decode tables (32-bit words): per grid entry the 2-bit magnitude codes
+// of its 8 values in nibbles (8 -> 0, 25 -> 1, 43 -> 2), then per 7-bit sign
+// index the 8 signs in bit 2 of each nibble; nibble j | sign j is a byte index
+// into {8, 25, 43, -, -8, -25, -43, -}.
+constexpr int kIq2TableWords = 256 + 128;
 constexpr int kCodesPerTile = 1024;
 
 __host__ __device__ constexpr int fp4_scale_bytes(int fmt) { return fmt == 0 ? 128 : 64; }

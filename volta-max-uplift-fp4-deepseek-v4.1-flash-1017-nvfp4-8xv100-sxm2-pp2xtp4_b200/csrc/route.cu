@@ -211,6 +211,10 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanArgs a) {
       }
       rc_sel[b] = rc;
       if (a.ks_sel) a.ks_sel[b] = max(1, kRouteSlotsPerChunk / rc);
+      if (a.bank_range) {
+        a.bank_range[2 * b] = start[a.key_lo[b]];
+        a.bank_range[2 * b + 1] = start[a.key_hi[b]];
+      }
     }
     __syncthreads();
   }
