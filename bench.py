@@ -82,6 +82,8 @@ def parse():
                     help="decode tokens per step (c1 default 64, c2 default 32)")
     ap.add_argument("--tokens", type=int, default=4096, choices=[4096, 16384], help="c3 prefill tokens")
     ap.add_argument("--eager", action="store_true", help="decode: launch each kernel instead of a graph replay")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="multi-GPU: the library's NVLink peer-memory exchange (default) or NCCL all-to-all")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--experts", type=int, default=E,
                     help="routed experts (384 = configs[1]; fewer only for a small ncu capture)")
@@ -676,7 +678,8 @@ def run_expert_parallel(job) -> None:
 
     args, dev, rank, world, m = job.args, job.dev, job.rank, job.world, job.args.m
     tier = np.zeros(E, np.int8)
-    layer = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, tokens=m, tier=tier, device=dev)
+    layer = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, tokens=m, tier=tier, device=dev,
+                                 exchange=args.exchange)
     n_local = int((layer.layer.fp4_slot >= 0).sum())
     bank = synth.make_fp4_bank(n_local, H, I, "nvfp4", 1000 + rank, dev)
     synth.load_bank(layer.layer, bank)
@@ -690,19 +693,23 @@ def run_expert_parallel(job) -> None:
                           f"expert parallel over {world} GPUs, {m} tokens per GPU",
               "tokens_per_step": m * world, "experts_per_gpu": n_local, "format": "nvfp4",
               "l2": "inputs larger than L2 (expert weights streamed per step)",
-              "launch": "eager (the exchange sizes come from a host read of the route counts)",
-              "parallelism": f"expert parallel x{world} (NCCL all-to-all)"}
+              "launch": "one CUDA graph replay per step" if args.exchange == "p2p" and not args.eager else
+                        "eager" + (" (the exchange sizes come from a host read of the route counts)"
+                                   if args.exchange == "nccl" else ""),
+              "parallelism": f"expert parallel x{world} ("
+                             + ("NVLink peer-memory exchange kernels" if args.exchange == "p2p" else "NCCL all-to-all")
+                             + ")"}
 
     def step():
         ids, w = layer.route(logits)
         return layer.forward(x, ids, w, out=out)
 
-    for _ in range(max(3, args.warmup)):
-        step()
+    run, graph = graphed(step, args.exchange == "p2p" and not args.eager, args.warmup)
     layer.check_errors()
-    ms, clk = job.timed(step, args.steps)
+    ms, clk = job.timed(run, args.steps)
     layer.check_errors()
     value = world * m / (ms / 1e3)
+    del graph
 
     # exposed communication and the local W13 launch (separate pass: these read events every step)
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
@@ -748,8 +755,9 @@ def run_expert_parallel(job) -> None:
             "e2e": {"value": world * m / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": int(hx.numel() * hx.element_size() + hl.numel() * hl.element_size()),
                     "d2h_bytes_per_step": int(hout.numel() * hout.element_size())},
-            # gating; dispatch plan, row gather, metadata; local convert, plan, W13, W2; f32->f16; combine
-            "gpu_launches": 10 * args.steps,
+            # p2p: gating; owner plan, push, receive; local plan, W13, W2; return; combine
+            # nccl: gating; owner plan, row gather, metadata; local plan, W13, W2, f32->f16; combine
+            "gpu_launches": (9 if args.exchange == "p2p" else 9) * args.steps,
             "cpu_baseline": None,
             "clocks": clk,
         })

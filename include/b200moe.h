@@ -216,6 +216,44 @@ int b200moe_ep_dispatch(void* stream, const void* x, int x_dtype, const int32_t*
 int b200moe_ep_combine(void* stream, const void* y2, const int32_t* route_pos, const float* topk_weights, int T,
                        int k, int H, const float* residual, float* out);
 
+/* Expert-parallel exchange over NVLink peer memory (no NCCL, no host sync:
+ * the whole step can be captured in one CUDA graph).  Each rank creates one
+ * exchange object whose shared buffers all ranks map through CUDA IPC:
+ * create -> ipc_handle (64 bytes) -> exchange the handles among the ranks on
+ * the host -> connect (world x 64 bytes, rank order).  A step, on every rank
+ * in the same order: ep_push (owner plan of this rank's T*k routes, rows and
+ * expert ids stored into the owners' buffers), b200moe_forward_rows of the
+ * local top-1 layer on the buffers of ep_recv_buffers, ep_return (y2 rows
+ * back to their home ranks), ep_combine_p2p (slot-order combine + residual).
+ * Waits are bounded (B200MOE_ERR_TIMEOUT through ep_check_errors).  All ranks
+ * must be alive at destroy (call it after a host barrier).  No reference
+ * counterpart: the reference refuses expert parallelism
+ * (engine/patches/gguf_moe.patch:57-58). */
+typedef struct b200moe_ep b200moe_ep;
+int b200moe_ep_create(int device, int world, int rank, int hidden, int max_routes, b200moe_ep** out);
+int b200moe_ep_ipc_handle(b200moe_ep* ep, void* handle);
+int b200moe_ep_connect(b200moe_ep* ep, const void* handles);
+int b200moe_ep_destroy(b200moe_ep* ep);
+int b200moe_ep_recv_buffers(b200moe_ep* ep, void** rows, int32_t** expert_ids, int32_t** n_valid,
+                            int32_t** row_range, void** y2, int* max_rows);
+int b200moe_ep_push(b200moe_ep* ep, void* stream, const void* x, int x_dtype, const int32_t* topk_ids, int T,
+                    int k, int num_experts, const int32_t* owner_of_expert);
+int b200moe_ep_return(b200moe_ep* ep, void* stream);
+int b200moe_ep_combine_p2p(b200moe_ep* ep, void* stream, const int32_t* topk_ids, const float* topk_weights,
+                           int T, int k, int num_experts, const int32_t* owner_of_expert, const float* residual,
+                           float* out);
+int b200moe_ep_check_errors(b200moe_ep* ep, void* stream, uint32_t* bits);
+/* Synchronize; the routes received in the last step and up to max of their
+ * expert ids (host memory). */
+int b200moe_ep_received(b200moe_ep* ep, void* stream, int32_t* n, int32_t* expert_ids, int max);
+
+/* Top-1 layer forward on rows that are routes (expert parallel owners): the
+ * device int *n_valid (<= max_rows) says how many rows this call has,
+ * row_range = {0, *n_valid}; writes the fp16 y2 row of every route (the
+ * reference's y2, before any weighting) into y2 [max_rows][H].  No host sync. */
+int b200moe_forward_rows(b200moe_layer* layer, void* stream, const void* rows, const int32_t* expert_ids,
+                         const int32_t* n_valid, const int32_t* row_range, int max_rows, void* y2);
+
 /* fp32 -> fp16 copy of n values (n % 4 == 0), round to nearest. */
 int b200moe_f32_to_f16(void* stream, const float* x, int64_t n, void* y);
 

@@ -23,7 +23,7 @@ __graft_entry__.load_package()
 from b200moe import ep, moe, synth, tiers  # noqa: E402
 
 
-def main(out_path: str) -> None:
+def main(out_path: str, exchange: str) -> None:
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
     dev = torch.device("cuda", torch.cuda.current_device())
@@ -37,9 +37,10 @@ def main(out_path: str) -> None:
     synth.load_bank(full, fp4)
     full.set_iq2_tables()
     synth.load_bank(full, iq2)
-    sharded = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K, tokens=T, tier=tier, device=dev)
+    sharded = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K, tokens=T, tier=tier, device=dev,
+                                   exchange=exchange)
     exact = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K, tokens=T, tier=tier, device=dev,
-                                 split_k=(2, 2))
+                                 split_k=(2, 2), exchange=exchange)
     sharded.set_iq2_tables()
     synth.load_local(sharded.layer, tier, fp4, iq2)
     exact.set_iq2_tables()
@@ -67,7 +68,9 @@ def main(out_path: str) -> None:
         d = (y - resid - ref).norm() / ref.norm()
         res[name] = float(d)
         res[name + "_comm_ms"] = sharded.comm_ms()
-        res[name + "_owner_counts"] = sharded.send_counts.cpu().tolist()
+        got = sharded.received()
+        res[name + "_routes_in"] = int(got.size)
+        res[name + "_foreign_ids"] = int(((got < 0) | (got >= E) | (sharded.owner.cpu().numpy()[np.clip(got, 0, E - 1)] != rank)).sum())
         # fixed split-K on both sides: the sharded layer equals the single-GPU one bit for bit
         y_exact = exact.forward(x, ids, w)
         ref_exact = full2.forward(x, ids, w).clone()
@@ -84,4 +87,4 @@ def main(out_path: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1])
+    main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else "p2p")

@@ -26,7 +26,8 @@ def dev():
     return torch.device("cuda", 0)
 
 
-def test_ep_world1_matches_layer(dev, pkg):
+@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
+def test_ep_world1_matches_layer(dev, pkg, exchange):
     from b200moe import ep, moe, synth, tiers
 
     H, I, E, K, T = 1024, 512, 64, 6, 48
@@ -38,7 +39,8 @@ def test_ep_world1_matches_layer(dev, pkg):
     synth.load_bank(full, fp4)
     full.set_iq2_tables()
     synth.load_bank(full, iq2)
-    sharded = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K, tokens=T, tier=tier, device=dev)
+    sharded = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K, tokens=T, tier=tier, device=dev,
+                                   exchange=exchange)
     sharded.set_iq2_tables()
     synth.load_local(sharded.layer, tier, fp4, iq2)
     g = torch.Generator(device=dev).manual_seed(5)
@@ -54,7 +56,7 @@ def test_ep_world1_matches_layer(dev, pkg):
     resid = torch.randn((T, H), generator=g, device=dev)
     y_r = sharded.forward(x, ids, w, residual=resid)
     assert torch.equal(y_r, y + resid)
-    assert torch.equal(sharded.send_counts.cpu(), torch.tensor([T * K], dtype=torch.int32))
+    assert sharded.received().size == T * K
     # a route without an expert: flagged, contributes nothing, the layer recovers
     bad = ids.clone()
     bad[3, 2] = E + 7
@@ -70,6 +72,22 @@ def test_ep_world1_matches_layer(dev, pkg):
     sharded.check_errors()
     assert float((y_b[3] - y_z[3]).norm() / y_z[3].norm()) < TOL
     assert torch.equal(sharded.forward(x, ids, w), y)
+    if exchange == "p2p":  # the step holds no host sync: replay it from a CUDA graph
+        out = torch.empty_like(y)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            sharded.forward(x, ids, w, out=out)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                sharded.forward(x, ids, w, out=out)
+        torch.cuda.current_stream().wait_stream(s)
+        out.zero_()
+        g.replay()
+        g.replay()
+        sharded.check_errors()
+        assert torch.equal(out, y)
+        del g
     # same fixed split-K on both sides: bit-equal to the single-GPU layer
     full.set_split_k(2, 2)
     sharded.layer.set_split_k(2, 2)
@@ -81,7 +99,8 @@ def test_ep_world1_matches_layer(dev, pkg):
     full.close()
 
 
-def test_ep_two_gpus_nccl(tmp_path):
+@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
+def test_ep_two_gpus(tmp_path, exchange):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     with socket.socket() as s:
@@ -91,7 +110,7 @@ def test_ep_two_gpus_nccl(tmp_path):
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={port}",
-           str(Path(__file__).with_name("ep_worker.py")), str(out)]
+           str(Path(__file__).with_name("ep_worker.py")), str(out), exchange]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     for rank in range(2):
@@ -99,5 +118,8 @@ def test_ep_two_gpus_nccl(tmp_path):
         for case in ("zipf", "ragged", "one_owner"):
             assert res[case] < TOL, (rank, case, res)
             assert res[case + "_bitequal"], (rank, case)
-        assert res["one_owner_owner_counts"][1] == 0
+        for case in ("zipf", "ragged", "one_owner"):
+            assert res[case + "_foreign_ids"] == 0, (rank, case)
+        # every route goes to rank 0's experts: rank 1 receives none
+        assert res["one_owner_routes_in"] == 0 if rank == 1 else res["one_owner_routes_in"] > 0
         assert res["zipf_comm_ms"] > 0

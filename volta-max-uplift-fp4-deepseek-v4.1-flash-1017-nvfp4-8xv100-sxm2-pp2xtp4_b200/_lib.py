@@ -69,6 +69,17 @@ SIGNATURES = {
     "b200moe_ep_workspace_bytes": ([I32, I32], ctypes.c_size_t),
     "b200moe_ep_dispatch": ([P, P, I32, P, I32, I32, I32, I32, P, I32, P, P, P, P, P, ctypes.c_size_t, P], I32),
     "b200moe_ep_combine": ([P, P, P, P, I32, I32, I32, P, P], I32),
+    "b200moe_ep_create": ([I32, I32, I32, I32, I32, P], I32),
+    "b200moe_ep_ipc_handle": ([P, P], I32),
+    "b200moe_ep_connect": ([P, P], I32),
+    "b200moe_ep_destroy": ([P], I32),
+    "b200moe_ep_recv_buffers": ([P, P, P, P, P, P, P], I32),
+    "b200moe_ep_push": ([P, P, P, I32, P, I32, I32, I32, P], I32),
+    "b200moe_ep_return": ([P, P], I32),
+    "b200moe_ep_combine_p2p": ([P, P, P, P, I32, I32, I32, P, P, P], I32),
+    "b200moe_ep_check_errors": ([P, P, P], I32),
+    "b200moe_ep_received": ([P, P, P, P, I32], I32),
+    "b200moe_forward_rows": ([P, P, P, P, P, P, I32, P], I32),
     "b200moe_f32_to_f16": ([P, P, ctypes.c_int64, P], I32),
 }
 

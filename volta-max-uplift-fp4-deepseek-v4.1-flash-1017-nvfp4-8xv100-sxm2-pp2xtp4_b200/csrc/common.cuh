@@ -38,6 +38,33 @@ __device__ __forceinline__ void set_error(uint32_t* err, uint32_t bits) {
   if (err) atomicOr(err, bits);
 }
 
+// System-scope acquire load / release store (flags written over NVLink by peer GPUs).
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Wait until flags[0..n) have all reached epoch e (monotonic counters), at
+// most kWaitLimitNs; false (and kErrTimeout) when the bound runs out.
+__device__ __forceinline__ bool wait_flags(const int* flags, int n, int e, uint32_t* err) {
+  const uint64_t t0 = global_timer_ns();
+  for (;;) {
+    bool ok = true;
+    for (int i = 0; i < n; ++i) ok = ok && (ld_acquire_sys(flags + i) - e) >= 0;
+    if (ok) return true;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      set_error(err, kErrTimeout);
+      return false;
+    }
+    __nanosleep(128);
+  }
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

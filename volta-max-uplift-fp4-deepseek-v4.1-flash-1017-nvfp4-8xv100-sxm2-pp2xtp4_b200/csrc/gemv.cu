@@ -433,7 +433,7 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, uint8_t* smem) {
             }
         }
       }
-      if (EPI == 1) {
+      if (EPI == 1 && a.counters) {  // (no counters: the caller combines the y2 rows itself)
         // completion count per (token, 32-row tile); the last route sums in slot order
         __threadfence();
         named_bar(1, kConsumerWarps * 32);

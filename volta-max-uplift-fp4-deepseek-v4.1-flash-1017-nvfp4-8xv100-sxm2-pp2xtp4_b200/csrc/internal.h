@@ -40,6 +40,7 @@ struct KsModel {
 struct PlanArgs {
   const int32_t* ids;  // [n] expert id per route (flat t*k + slot)
   int n;
+  const int32_t* n_valid;  // optional (device): routes of this call, <= n
   int num_experts;
   // product keys: key_of_expert[e] in [0, n_keys) or -1 (not on this GPU / invalid)
   const int32_t* key_of_expert;

@@ -172,6 +172,15 @@ Workspace layer_workspace(b200moe_layer* L) {
   return w;
 }
 
+// Rows mode (b200moe_forward_rows): every row is one route of a top-1 layer,
+// the number of rows of this call is on the device, and the fp16 y2 rows are
+// the output (no weighted combine).
+struct RowsMode {
+  const int32_t* n_valid;    // device: rows of this call
+  const int32_t* row_range;  // device [2]: {0, rows of this call}
+  __half* y2;                // fp16 [max rows][H]
+};
+
 struct Marks {
   const b200moe_layer* L;
   cudaStream_t s;
@@ -182,15 +191,23 @@ struct Marks {
   }
 };
 
-int run_forward(b200moe_layer* L, const Workspace& ws, cudaStream_t s, const void* x, int x_dtype,
-                const int32_t* ids, const float* w, float* out, int m, bool prefill = false) {
+int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const void* x, int x_dtype,
+                const int32_t* ids, const float* w, float* out, int m, bool prefill = false,
+                const RowsMode* rows = nullptr) {
   const auto& c = L->cfg;
   Marks marks{L, s};
   if (!L->maps_set) return B200MOE_ERR_STATE;
   if (c.n_iq2 > 0 && !L->tables_set) return B200MOE_ERR_STATE;
-  if (!x || !ids || !w || !out) return B200MOE_ERR_INVALID_ARG;
+  if (!x || !ids || (!rows && (!w || !out))) return B200MOE_ERR_INVALID_ARG;
   if (x_dtype != B200MOE_F16 && x_dtype != B200MOE_BF16) return B200MOE_ERR_DTYPE;
-  if (!aligned(x, 16) || !aligned(out, 16)) return B200MOE_ERR_ALIGN;
+  if (!aligned(x, 16) || (out && !aligned(out, 16))) return B200MOE_ERR_ALIGN;
+  Workspace ws = ws_in;
+  if (rows) {
+    ws.y2 = rows->y2;
+    ws.counters = nullptr;
+    ws.w_eff = nullptr;
+    out = nullptr;
+  }
   const int S = m * c.top_k;
   const __half* xsrc = static_cast<const __half*>(x);
   marks.mark();
@@ -200,14 +217,16 @@ int run_forward(b200moe_layer* L, const Workspace& ws, cudaStream_t s, const voi
   }
   marks.mark();  // after the bf16 conversion (or none): the event layout does not depend on x's dtype
   if (c.n_iq2 > 0) {  // int8 blocks of the token rows for the IQ2 bank's W13
-    if (launch_quant_s8(s, xsrc, c.hidden, c.hidden, m, nullptr, ws.xq)) return B200MOE_ERR_CUDA;
+    if (launch_quant_s8(s, xsrc, c.hidden, c.hidden, m, rows ? rows->row_range : nullptr, ws.xq))
+      return B200MOE_ERR_CUDA;
     marks.mark();
   }
   // prefill with the tcgen05 GEMM: the FP4 bank's chunks are 128-route token tiles
-  const bool tc = prefill && c.prefill_gemm && c.n_fp4 > 0 && L->xperm;
+  const bool tc = !rows && prefill && c.prefill_gemm && c.n_fp4 > 0 && L->xperm;
   PlanArgs p{};
   p.ids = ids;
   p.n = S;
+  p.n_valid = rows ? rows->n_valid : nullptr;
   p.num_experts = c.num_experts;
   p.key_of_expert = L->key_of_expert;
   p.n_keys = c.n_fp4 + c.n_iq2;
@@ -524,6 +543,18 @@ int b200moe_forward_prefill(b200moe_layer* L, void* stream, const void* x, int x
   if (!L || T < 1 || T > L->t_max) return B200MOE_ERR_INVALID_ARG;
   DeviceGuard guard(L->device);
   return run_forward(L, layer_workspace(L), static_cast<cudaStream_t>(stream), x, x_dtype, ids, w, out, T, true);
+}
+
+int b200moe_forward_rows(b200moe_layer* L, void* stream, const void* rows, const int32_t* expert_ids,
+                         const int32_t* n_valid, const int32_t* row_range, int max_rows, void* y2) {
+  if (!L || !rows || !expert_ids || !n_valid || !row_range || !y2 || max_rows < 1 || max_rows > L->t_max)
+    return B200MOE_ERR_INVALID_ARG;
+  if (L->cfg.top_k != 1) return B200MOE_ERR_INVALID_ARG;
+  if (!aligned(y2, 16)) return B200MOE_ERR_ALIGN;
+  DeviceGuard guard(L->device);
+  RowsMode rm{n_valid, row_range, static_cast<__half*>(y2)};
+  return run_forward(L, layer_workspace(L), static_cast<cudaStream_t>(stream), rows, B200MOE_F16, expert_ids,
+                     nullptr, nullptr, max_rows, true, &rm);
 }
 
 int b200moe_check_errors(b200moe_layer* L, void* stream, uint32_t* bits) {

@@ -98,7 +98,8 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanArgs a) {
   int* start = hist + 32 * nk;  // [nk]
   int* aux = start + nk;        // [nk]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int n = a.n;
+  // a.n_valid (device) bounds the routes of this call below the launch's a.n
+  const int n = a.n_valid ? min(a.n, max(0, *a.n_valid)) : a.n;
   for (int i = tid; i < 32 * nk; i += kPlanThreads) hist[i] = 0;
   __syncthreads();
   const int per_warp = ((n + 31) / 32 + 31) / 32 * 32;
@@ -143,7 +144,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanArgs a) {
   }
   __syncthreads();
 
-  if (product && aux[nk - 1] > 0 && a.y2) {
+  if (product && aux[nk - 1] > 0 && a.y2 && a.counters) {
     // routes without an expert (sorted last): zero their rows, count them done
     const int first = start[nk - 1], cnt = aux[nk - 1];
     const int tiles = a.H / 32;

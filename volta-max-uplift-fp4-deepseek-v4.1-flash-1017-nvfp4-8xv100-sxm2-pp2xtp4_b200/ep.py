@@ -5,19 +5,30 @@ parallelism (engine/patches/gguf_moe.patch:57-58); its tier placement
 (engine/.../experts/nvfp4_8r_tiers.py) becomes ownership here: rank r owns the
 contiguous expert ids ``tiers.owner_ranges(E, world)[r]``, in either format.
 
-One forward (per rank: its own T tokens, all ranks call in the same order):
-  1. ``b200moe_ep_dispatch``: stable sort of the T*k routes by owner rank,
-     per-rank counts, fp16 row + expert id + sorted position per route;
-  2. counts exchange (one host sync), then NCCL all-to-all of rows and ids;
-  3. the owner runs its experts on the received routes with k = 1 and weight
-     1.0, which yields exactly the fp16 y2 rows, and all-to-all returns them;
-  4. ``b200moe_ep_combine``: slot-order sum of fma(y2, w) per token (the
-     single-GPU combine's arithmetic) plus the residual.
+Two exchanges, the same arithmetic (per rank: its own T tokens, all ranks
+call in the same order):
+
+``exchange="p2p"`` (default): the library's own kernels over NVLink peer
+memory (CUDA IPC, no multicast): ``b200moe_ep_push`` sorts this rank's routes
+by owner and stores each route's fp16 row and expert id straight into its
+owner's receive buffer; the owner runs its experts on what it received
+(``b200moe_forward_rows``, top-1, y2 rows out); ``b200moe_ep_return`` stores
+the y2 rows back into their home ranks; ``b200moe_ep_combine_p2p`` sums them
+per token in slot order and adds the residual.  Counts, offsets and the
+hand-offs live on the device (bounded flag waits), so a step needs no host
+sync and can be captured in a CUDA graph.
+
+``exchange="nccl"``: ``b200moe_ep_dispatch`` + one host read of the counts +
+NCCL all-to-all out and back + ``b200moe_ep_combine``.
+
 Communication is timed with CUDA events on the launching stream
-(``comm_ms()``: the exposed, non-overlapped exchange time of the last call).
+(``comm_ms()``: the exposed, non-overlapped exchange time of the last call,
+waits for slower ranks included).
 """
 
 from __future__ import annotations
+
+import ctypes
 
 import numpy as np
 import torch
@@ -87,7 +98,10 @@ class ExpertParallelMoe:
 
     def __init__(self, *, hidden: int, inter: int, num_experts: int, top_k: int, tokens: int, tier,
                  fp4_format: str = "nvfp4", group=None, device: torch.device | None = None,
-                 split_k: tuple[int, int] | None = None):
+                 split_k: tuple[int, int] | None = None, exchange: str = "p2p"):
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError("exchange is 'p2p' or 'nccl'")
+        self.exchange = exchange
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -122,6 +136,32 @@ class ExpertParallelMoe:
         self._ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
         self._timed = False
         self.last_routes_in = 0
+        self._ep = None
+        if exchange == "p2p":
+            self._open_p2p(S)
+
+    def _open_p2p(self, S: int) -> None:
+        L = _lib.lib()
+        ep = ctypes.c_void_p()
+        _lib.check("b200moe_ep_create", L.b200moe_ep_create(self.device.index, self.world, self.rank, self.hidden,
+                                                            S, ctypes.byref(ep)))
+        self._ep = ep
+        h = (ctypes.c_uint8 * 64)()
+        _lib.check("b200moe_ep_ipc_handle", L.b200moe_ep_ipc_handle(ep, h))
+        handles = [bytes(h)]
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(h), group=self.group)
+        blob = b"".join(handles)
+        _lib.check("b200moe_ep_connect", L.b200moe_ep_connect(ep, ctypes.c_char_p(blob)))
+        ptrs = [ctypes.c_void_p() for _ in range(5)]
+        max_rows = ctypes.c_int()
+        _lib.check("b200moe_ep_recv_buffers", L.b200moe_ep_recv_buffers(ep, *(ctypes.byref(p) for p in ptrs),
+                                                                       ctypes.byref(max_rows)))
+        self._rows, self._eids, self._n_valid, self._row_range, self._y2 = (p.value for p in ptrs)
+        self._max_rows = max_rows.value
+        if self.world > 1:
+            dist.barrier(group=self.group)  # every rank mapped every buffer before the first push
 
     # weights go to the local layer (slots = this rank's experts of each format, ascending id)
     def load_fp4(self, *args, **kw):
@@ -147,6 +187,12 @@ class ExpertParallelMoe:
         S = T * k
         dt = _lib.F16 if x.dtype == torch.float16 else _lib.BF16
         L = _lib.lib()
+        if out is None:
+            out = torch.empty((T, self.hidden), dtype=torch.float32, device=self.device)
+        if residual is not None and (residual.shape != (T, self.hidden) or residual.dtype != torch.float32):
+            raise ValueError("residual must be fp32 [T, hidden]")
+        if self.exchange == "p2p":
+            return self._forward_p2p(x, dt, ids, w, T, k, residual, out)
         _lib.check("b200moe_ep_dispatch", L.b200moe_ep_dispatch(
             _stream(), x.data_ptr(), dt, ids.data_ptr(), T, k, self.num_experts, self.world, self.owner.data_ptr(),
             self.hidden, self.send_rows.data_ptr(), self.send_eid.data_ptr(), self.route_pos.data_ptr(),
@@ -177,24 +223,54 @@ class ExpertParallelMoe:
             y2 = self.y2_home
         else:
             y2 = self.y2_local
-        if out is None:
-            out = torch.empty((T, self.hidden), dtype=torch.float32, device=self.device)
         _lib.check("b200moe_ep_combine", L.b200moe_ep_combine(
             _stream(), y2.data_ptr(), self.route_pos.data_ptr(), w.data_ptr(), T, k, self.hidden,
             _lib.ptr(residual), out.data_ptr()))
         self._timed = self.world > 1
         return out
 
+    def _forward_p2p(self, x, dt, ids, w, T, k, residual, out):
+        L, st, ev = _lib.lib(), _stream(), self._ev
+        timed = torch.cuda.is_current_stream_capturing() is False
+        if timed:
+            ev[0].record()
+        _lib.check("b200moe_ep_push", L.b200moe_ep_push(self._ep, st, x.data_ptr(), dt, ids.data_ptr(), T, k,
+                                                        self.num_experts, self.owner.data_ptr()))
+        if timed:
+            ev[1].record()
+        _lib.check("b200moe_forward_rows", L.b200moe_forward_rows(
+            self.layer._h, st, self._rows, self._eids, self._n_valid, self._row_range, self._max_rows, self._y2))
+        if timed:
+            ev[2].record()
+        _lib.check("b200moe_ep_return", L.b200moe_ep_return(self._ep, st))
+        _lib.check("b200moe_ep_combine_p2p", L.b200moe_ep_combine_p2p(
+            self._ep, st, ids.data_ptr(), w.data_ptr(), T, k, self.num_experts, self.owner.data_ptr(),
+            _lib.ptr(residual), out.data_ptr()))
+        if timed:
+            ev[3].record()
+        self._timed = timed
+        self.last_routes_in = -1  # on the device: read by local_experts_used()
+        return out
+
+    def received(self) -> np.ndarray:
+        """Expert ids of the routes this rank's experts ran in the last forward (host sync)."""
+        if self.exchange == "p2p":
+            n = ctypes.c_int()
+            ids = np.empty(self._max_rows, np.int32)
+            _lib.check("b200moe_ep_received", _lib.lib().b200moe_ep_received(
+                self._ep, _stream(), ctypes.byref(n), ids.ctypes.data_as(ctypes.c_void_p), ids.size))
+            return ids[:n.value]
+        R = self.last_routes_in
+        return (self.recv_eid if self.world > 1 else self.send_eid)[:R].cpu().numpy()
+
     def local_experts_used(self) -> int:
         """Distinct local experts the last forward ran (host sync)."""
-        if self.last_routes_in == 0:
-            return 0
-        eid = (self.recv_eid if self.world > 1 else self.send_eid)[:self.last_routes_in]
-        return int(torch.unique(eid).numel())
+        return int(np.unique(self.received()).size)
 
     def comm_ms(self) -> float:
-        """Exchange time (counts + rows + ids out, y2 back) of the last forward;
-        waits for those events."""
+        """Exchange time of the last forward (NCCL: counts + rows + ids out, y2
+        back; p2p: push + receive, return + combine, waits for the slower
+        ranks included); waits for those events."""
         if not self._timed:
             return 0.0
         ev = self._ev
@@ -202,14 +278,26 @@ class ExpertParallelMoe:
         return ev[0].elapsed_time(ev[1]) + ev[2].elapsed_time(ev[3])
 
     def check_errors(self) -> None:
-        """Synchronize; raise if the dispatch (a route id without an owner) or
-        the local layer recorded an error since the last check."""
+        """Synchronize; raise if the dispatch (a route id without an owner), the
+        exchange (a wait that ran out) or the local layer recorded an error
+        since the last check."""
         bits = int(self.err.item())
         if bits:
             self.err.zero_()
+        status = 0
+        if self._ep is not None:
+            status = _lib.lib().b200moe_ep_check_errors(self._ep, _stream(), None)
         self.layer.check_errors()
         if bits:
             raise _lib.B200MoeError("expert-parallel dispatch", 5)
+        _lib.check("expert-parallel exchange", status)
 
     def close(self) -> None:
+        """Free the layer and the exchange; a collective (every rank must call it)."""
+        if self._ep is not None:
+            torch.cuda.synchronize(self.device)
+            if self.world > 1:
+                dist.barrier(group=self.group)  # no rank still writes into another's buffers
+            _lib.lib().b200moe_ep_destroy(self._ep)
+            self._ep = None
         self.layer.close()
