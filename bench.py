@@ -16,6 +16,12 @@ random-init and packed by the library's own quantizers):
     device from a grid so that about 80 % of routes reach the NVFP4 experts.
 ``c3`` configs[3], prefill: T = 4096 tokens (``--tokens 16384``), MXFP4
     experts, logits ~U(0,1); the W13/W2 launches are the tcgen05 grouped GEMM.
+``c4`` configs[4], a 40-layer stack of c2 layers (own seeded tier map and
+    experts per layer), one decode batch of 256 tokens for the whole box
+    (256 / N per GPU: strong scaling), Zipf routing, residual add between
+    layers; experts sharded by id over the N GPUs (peer-memory exchange); the
+    whole 40-layer step is one CUDA graph.  Reports box tokens/s and the
+    exposed exchange time summed over the layers.
 
 A step = gating (router logits -> top-8) + the layer forward, all on the GPU.
 Decode steps (c1, c2) replay one CUDA graph per step (the reference captures
@@ -77,7 +83,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c1", "c2", "c3"], default="c1")
+    ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4"], default="c1")
+    ap.add_argument("--layers", type=int, default=40, help="c4: layers in the stack")
+    ap.add_argument("--batch", type=int, default=256, help="c4: decode tokens of the whole box per step")
     ap.add_argument("--m", type=int, default=None, choices=[1, 8, 32, 64],
                     help="decode tokens per step (c1 default 64, c2 default 32)")
     ap.add_argument("--tokens", type=int, default=4096, choices=[4096, 16384], help="c3 prefill tokens")
@@ -669,6 +677,166 @@ def run_c3(job) -> None:
     layer.close()
 
 
+# --------------------------------------------------------------------------- c4
+def run_c4(job) -> None:
+    import torch
+
+    from b200moe import ep, moe, synth, tiers
+
+    args, dev, rank, world = job.args, job.dev, job.rank, job.world
+    n_layers, batch = args.layers, args.batch
+    if batch % world:
+        raise SystemExit(f"--batch {batch} must divide over {world} GPUs")
+    T = batch // world
+    peer = ep.PeerExchange(H, T * K_TOP, None, dev) if world > 1 else None
+    layers = []
+    alpha = None
+    for li in range(n_layers):
+        tier, trank = tiers.zipf_tier(E, C2_HOT, seed=4000 + li)
+        if world == 1:
+            lay = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, max_tokens=min(T, 64),
+                                    max_prefill_tokens=T, tier=tier, device=dev, prefill_gemm="skinny")
+            local = lay
+        else:
+            lay = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, tokens=T, tier=tier,
+                                       device=dev, peer=peer)
+            local = lay.layer
+        n_hot, n_iq = int((local.fp4_slot >= 0).sum()), int((local.iq2_slot >= 0).sum())
+        if n_hot:
+            synth.load_bank(local, synth.make_fp4_bank(n_hot, H, I, "nvfp4", 4000 + 131 * li + rank, dev))
+        local.set_iq2_tables()
+        if n_iq:
+            synth.load_bank(local, synth.make_iq2_bank(n_iq, H, I, 9000 + 131 * li + rank, dev))
+        if alpha is None:  # the routing bias of configs[2], chosen once on a whole-layer tier map
+            probe = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, max_tokens=min(T, 64),
+                                      max_prefill_tokens=T, tier=tier, device=dev)
+            alpha = c2_inputs(probe, trank, T, dev)[0]
+            probe.close()
+        logits = synth.zipf_logits(T, trank, alpha, 1.1, 4000 + li + 7919 * rank, dev)
+        layers.append((lay, logits))
+        torch.cuda.empty_cache()
+    g = torch.Generator(device=dev).manual_seed(4000 + rank)
+    x0 = torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
+    h = torch.empty((T, H), dtype=torch.float32, device=dev)
+    xb = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    routes = [lay.route(lg) for lay, lg in layers]
+
+    def single(lay, ids, w):  # world 1: the whole layer on this GPU, fused combine
+        return lay.forward(xb, ids, w) if T <= 64 else lay.forward_prefill(xb, ids, w)
+
+    def step():
+        h.copy_(x0)
+        xb.copy_(x0)
+        for (lay, _), (ids, w) in zip(layers, routes):
+            if world == 1:
+                h.add_(single(lay, ids, w))
+            else:
+                lay.forward(xb, ids, w, residual=h, out=h)
+            xb.copy_(h)
+
+    def step_with_gating():
+        h.copy_(x0)
+        xb.copy_(x0)
+        for lay, lg in layers:
+            ids, w = lay.route(lg)
+            if world == 1:
+                h.add_(single(lay, ids, w))
+            else:
+                lay.forward(xb, ids, w, residual=h, out=h)
+            xb.copy_(h)
+
+    run, graph = graphed(step_with_gating, not args.eager, args.warmup)
+    for lay, _ in layers:
+        lay.check_errors()
+    steps = max(3, args.steps // 10)
+    ms, clk = job.timed(run, steps)
+    for lay, _ in layers:
+        lay.check_errors()
+    del graph
+    value = batch / (ms / 1e3)
+
+    # bytes this GPU streams per step (distinct local experts per layer) and exposed exchange time
+    comm, local_bytes = 0.0, 0
+    step()
+    torch.cuda.synchronize()
+    for (lay, _), (ids, w) in zip(layers, routes):
+        local = lay if world == 1 else lay.layer
+        if world == 1:
+            used = np.unique(ids.cpu().numpy())
+        else:
+            lay.forward(xb, ids, w, residual=h, out=h)
+            torch.cuda.synchronize()
+            comm += lay.comm_ms()
+            used = np.unique(lay.received())
+        local_bytes += int((local.fp4_slot[used] >= 0).sum()) * EXPERT_BYTES + \
+            int((local.iq2_slot[used] >= 0).sum()) * (IQ_W13_BYTES + IQ_W2_BYTES)
+    comm_max = job.maxall(comm)
+    # this library's launches per layer: gating; world 1: bf16 copy, x int8 blocks, plan, W13 and W2 per bank,
+    # SwiGLU int8 blocks; world > 1 adds owner plan, push, receive, return, combine (no bf16 copy)
+    launches_per_step = 0
+    for lay, _ in layers:
+        local = lay if world == 1 else lay.layer
+        banks = int((local.fp4_slot >= 0).any()) + int((local.iq2_slot >= 0).any())
+        launches_per_step += 1 + 2 * banks + (3 if world == 1 else 2) + (5 if world > 1 else 0)
+    pk = peaks()
+    achieved = local_bytes / (ms / 1e3) / 1e9
+    frac_min = -job.maxall(-achieved / pk["hbm_gbs"])
+
+    hx = x0.cpu().pin_memory()
+    hout = torch.empty((T, H), dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        x0.copy_(hx, non_blocking=True)
+        step_with_gating()
+        hout.copy_(h, non_blocking=True)
+
+    run2, graph2 = graphed(e2e_step, not args.eager, 1)
+    e2e_ms, _ = job.timed(run2, steps, clocks=False)
+    del graph2
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        # one layer on the host cores, scaled by the layer count
+        lay0, _ = layers[0]
+        ids0, w0 = routes[0]
+        hot0 = synth.make_fp4_bank(C2_HOT, H, I, "nvfp4", 4000, dev)
+        iq0 = synth.make_iq2_bank(E - C2_HOT, H, I, 9000, dev)
+        one = cpu_c2(hot0, iq0, lay0, ids0.cpu().numpy(), w0.cpu().numpy(), x0.float().cpu().numpy(), T)
+        one["value"] /= n_layers
+        one["sample"] = f"one layer of the stack ({one['sample']}), time x {n_layers} layers"
+        cpu = one
+    if rank == 0:
+        config = {"workload": f"configs[4] {n_layers}-layer stack of configs[2] layers ({C2_HOT} NVFP4 + "
+                              f"{E - C2_HOT} IQ2_XXS experts each), decode batch {batch} tokens per box, "
+                              f"{T} per GPU, residual add between layers",
+                  "layers": n_layers, "batch": batch, "tokens_per_gpu": T, "alpha": alpha,
+                  "experts_per_gpu_per_layer": E // world,
+                  "l2": "inputs larger than L2 (GBs of expert weights per step)",
+                  "launch": "one CUDA graph replay per step" if not args.eager else "eager",
+                  "parallelism": f"expert parallel x{world} (NVLink peer-memory exchange kernels)" if world > 1
+                                 else "single GPU"}
+        line = line_base(job, args, f"MoE-stack tokens/s ({n_layers} layers, decode batch {batch}) & % HBM roofline",
+                         value, ms, config)
+        line["steps"] = steps
+        line["scaling"] = "strong"
+        line.update({
+            "roofline": {"bound": "hbm", "kernel": "all GEMV launches of the stack on rank 0 (whole step)",
+                         "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / pk["hbm_gbs"], "min_frac_over_ranks": frac_min,
+                         "peak_source": pk["source"], "traffic": None, "algorithmic_bytes_per_step": local_bytes},
+            "exposed_comm_ms": comm_max,
+            "e2e": {"value": batch / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": int(hx.numel() * 2), "d2h_bytes_per_step": int(hout.numel() * 4)},
+            "gpu_launches": launches_per_step * steps,
+            "cpu_baseline": cpu,
+            "clocks": clk,
+        })
+        print(json.dumps(line), flush=True)
+    for lay, _ in layers:
+        lay.close()
+    if peer is not None:
+        peer.close()
+
+
 # ------------------------------------------------------------- expert parallel
 def run_expert_parallel(job) -> None:
     """N ranks, expert parallel over NCCL (see the module docstring)."""
@@ -842,6 +1010,8 @@ def main() -> None:
     __graft_entry__.load_package()
     if args.impl == "reference":
         run_reference(job)
+    elif args.workload == "c4":
+        run_c4(job)
     elif job.world > 1:
         run_expert_parallel(job)
     elif args.workload == "c2":

@@ -88,6 +88,60 @@ def exchange_counts(send_counts: torch.Tensor, world: int, group=None) -> tuple[
     return mat[rank].tolist(), mat[:, rank].tolist()
 
 
+class PeerExchange:
+    """The NVLink peer-memory exchange of one process group: receive buffers
+    every rank maps through CUDA IPC (``b200moe_ep_*``).  Layers that run one
+    after another on the same stream may share one (``ExpertParallelMoe(peer=)``);
+    ``max_routes`` bounds the routes one rank sends in a step (tokens * top_k).
+    Creating and closing it are collectives."""
+
+    def __init__(self, hidden: int, max_routes: int, group=None, device: torch.device | None = None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.hidden, self.max_routes = hidden, max_routes
+        L = _lib.lib()
+        ep = ctypes.c_void_p()
+        _lib.check("b200moe_ep_create", L.b200moe_ep_create(self.device.index, self.world, self.rank, hidden,
+                                                            max_routes, ctypes.byref(ep)))
+        self.handle = ep
+        h = (ctypes.c_uint8 * 64)()
+        _lib.check("b200moe_ep_ipc_handle", L.b200moe_ep_ipc_handle(ep, h))
+        handles = [bytes(h)]
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(h), group=group)
+        _lib.check("b200moe_ep_connect", L.b200moe_ep_connect(ep, ctypes.c_char_p(b"".join(handles))))
+        ptrs = [ctypes.c_void_p() for _ in range(5)]
+        max_rows = ctypes.c_int()
+        _lib.check("b200moe_ep_recv_buffers", L.b200moe_ep_recv_buffers(ep, *(ctypes.byref(p) for p in ptrs),
+                                                                       ctypes.byref(max_rows)))
+        self.rows, self.eids, self.n_valid, self.row_range, self.y2 = (p.value for p in ptrs)
+        self.max_rows = max_rows.value
+        if self.world > 1:
+            dist.barrier(group=group)  # every rank mapped every buffer before the first push
+
+    def check(self) -> int:
+        return _lib.lib().b200moe_ep_check_errors(self.handle, _stream(), None)
+
+    def received(self) -> np.ndarray:
+        n = ctypes.c_int()
+        ids = np.empty(self.max_rows, np.int32)
+        _lib.check("b200moe_ep_received", _lib.lib().b200moe_ep_received(
+            self.handle, _stream(), ctypes.byref(n), ids.ctypes.data_as(ctypes.c_void_p), ids.size))
+        return ids[:n.value]
+
+    def close(self) -> None:
+        if self.handle is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)  # no rank still writes into another's buffers
+        _lib.lib().b200moe_ep_destroy(self.handle)
+        self.handle = None
+
+
 class ExpertParallelMoe:
     """One routed-MoE layer with its experts sharded over a process group.
 
@@ -98,7 +152,7 @@ class ExpertParallelMoe:
 
     def __init__(self, *, hidden: int, inter: int, num_experts: int, top_k: int, tokens: int, tier,
                  fp4_format: str = "nvfp4", group=None, device: torch.device | None = None,
-                 split_k: tuple[int, int] | None = None, exchange: str = "p2p"):
+                 split_k: tuple[int, int] | None = None, exchange: str = "p2p", peer: PeerExchange | None = None):
         if exchange not in ("p2p", "nccl"):
             raise ValueError("exchange is 'p2p' or 'nccl'")
         self.exchange = exchange
@@ -121,6 +175,18 @@ class ExpertParallelMoe:
         self.owner = torch.from_numpy(owner_of_expert(num_experts, self.world)).to(dev)
         f16 = dict(dtype=torch.float16, device=dev)
         i32 = dict(dtype=torch.int32, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        self._timed = False
+        self.last_routes_in = 0
+        self._peer, self._own_peer = None, False
+        if exchange == "p2p":
+            if peer is None:
+                peer, self._own_peer = PeerExchange(hidden, S, group, dev), True
+            elif peer.hidden != hidden or peer.max_routes < S or peer.world != self.world:
+                raise ValueError("the shared exchange does not fit this layer")
+            self._peer = peer
+            return
         self.send_rows = torch.empty((S, hidden), **f16)
         self.send_eid = torch.empty(S, **i32)
         self.route_pos = torch.empty(S, **i32)
@@ -132,36 +198,6 @@ class ExpertParallelMoe:
         self.y2_home = torch.empty((S, hidden), **f16) if self.world > 1 else None
         nbytes = int(_lib.lib().b200moe_ep_workspace_bytes(S, self.world))
         self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
-        self._ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-        self._timed = False
-        self.last_routes_in = 0
-        self._ep = None
-        if exchange == "p2p":
-            self._open_p2p(S)
-
-    def _open_p2p(self, S: int) -> None:
-        L = _lib.lib()
-        ep = ctypes.c_void_p()
-        _lib.check("b200moe_ep_create", L.b200moe_ep_create(self.device.index, self.world, self.rank, self.hidden,
-                                                            S, ctypes.byref(ep)))
-        self._ep = ep
-        h = (ctypes.c_uint8 * 64)()
-        _lib.check("b200moe_ep_ipc_handle", L.b200moe_ep_ipc_handle(ep, h))
-        handles = [bytes(h)]
-        if self.world > 1:
-            handles = [None] * self.world
-            dist.all_gather_object(handles, bytes(h), group=self.group)
-        blob = b"".join(handles)
-        _lib.check("b200moe_ep_connect", L.b200moe_ep_connect(ep, ctypes.c_char_p(blob)))
-        ptrs = [ctypes.c_void_p() for _ in range(5)]
-        max_rows = ctypes.c_int()
-        _lib.check("b200moe_ep_recv_buffers", L.b200moe_ep_recv_buffers(ep, *(ctypes.byref(p) for p in ptrs),
-                                                                       ctypes.byref(max_rows)))
-        self._rows, self._eids, self._n_valid, self._row_range, self._y2 = (p.value for p in ptrs)
-        self._max_rows = max_rows.value
-        if self.world > 1:
-            dist.barrier(group=self.group)  # every rank mapped every buffer before the first push
 
     # weights go to the local layer (slots = this rank's experts of each format, ascending id)
     def load_fp4(self, *args, **kw):
@@ -234,17 +270,18 @@ class ExpertParallelMoe:
         timed = torch.cuda.is_current_stream_capturing() is False
         if timed:
             ev[0].record()
-        _lib.check("b200moe_ep_push", L.b200moe_ep_push(self._ep, st, x.data_ptr(), dt, ids.data_ptr(), T, k,
+        pe = self._peer
+        _lib.check("b200moe_ep_push", L.b200moe_ep_push(pe.handle, st, x.data_ptr(), dt, ids.data_ptr(), T, k,
                                                         self.num_experts, self.owner.data_ptr()))
         if timed:
             ev[1].record()
         _lib.check("b200moe_forward_rows", L.b200moe_forward_rows(
-            self.layer._h, st, self._rows, self._eids, self._n_valid, self._row_range, self._max_rows, self._y2))
+            self.layer._h, st, pe.rows, pe.eids, pe.n_valid, pe.row_range, pe.max_rows, pe.y2))
         if timed:
             ev[2].record()
-        _lib.check("b200moe_ep_return", L.b200moe_ep_return(self._ep, st))
+        _lib.check("b200moe_ep_return", L.b200moe_ep_return(pe.handle, st))
         _lib.check("b200moe_ep_combine_p2p", L.b200moe_ep_combine_p2p(
-            self._ep, st, ids.data_ptr(), w.data_ptr(), T, k, self.num_experts, self.owner.data_ptr(),
+            pe.handle, st, ids.data_ptr(), w.data_ptr(), T, k, self.num_experts, self.owner.data_ptr(),
             _lib.ptr(residual), out.data_ptr()))
         if timed:
             ev[3].record()
@@ -255,11 +292,7 @@ class ExpertParallelMoe:
     def received(self) -> np.ndarray:
         """Expert ids of the routes this rank's experts ran in the last forward (host sync)."""
         if self.exchange == "p2p":
-            n = ctypes.c_int()
-            ids = np.empty(self._max_rows, np.int32)
-            _lib.check("b200moe_ep_received", _lib.lib().b200moe_ep_received(
-                self._ep, _stream(), ctypes.byref(n), ids.ctypes.data_as(ctypes.c_void_p), ids.size))
-            return ids[:n.value]
+            return self._peer.received()
         R = self.last_routes_in
         return (self.recv_eid if self.world > 1 else self.send_eid)[:R].cpu().numpy()
 
@@ -284,9 +317,7 @@ class ExpertParallelMoe:
         bits = int(self.err.item())
         if bits:
             self.err.zero_()
-        status = 0
-        if self._ep is not None:
-            status = _lib.lib().b200moe_ep_check_errors(self._ep, _stream(), None)
+        status = self._peer.check() if self._peer is not None else 0
         self.layer.check_errors()
         if bits:
             raise _lib.B200MoeError("expert-parallel dispatch", 5)
@@ -294,10 +325,7 @@ class ExpertParallelMoe:
 
     def close(self) -> None:
         """Free the layer and the exchange; a collective (every rank must call it)."""
-        if self._ep is not None:
-            torch.cuda.synchronize(self.device)
-            if self.world > 1:
-                dist.barrier(group=self.group)  # no rank still writes into another's buffers
-            _lib.lib().b200moe_ep_destroy(self._ep)
-            self._ep = None
+        if self._peer is not None and self._own_peer:
+            self._peer.close()
+        self._peer = None
         self.layer.close()
