@@ -289,8 +289,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < kEpiWarp0) {
     // ------------------------------------------------------------ dequant
-    const int t = threadIdx.x - 64;   // 0..255
-    const int u = t >> 5;              // unit (tile pair) of this warp
+    // the 16 pieces of a block (8 tile pairs x 2 m16 row tiles) spread over the dequant warps
+    const int dw = warp - 2;
     const int r = lane >> 2, q = lane & 3;
     uint32_t gk = 0, graw = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
@@ -310,11 +310,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = !*abort_ptr && mbar_wait(&w_empty[sw], pw ^ 1u, a.err);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
-        const uint8_t* unit = raw + rs * F::RAW + u * F::U;
         uint8_t* dst = wt + sw * kWBytes;
         const int half = kb & 1;
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
+        for (int pc = dw; pc < 2 * kUnits; pc += kDequantWarps) {
+          const int u = pc >> 1, mt = pc & 1;
+          const uint8_t* unit = raw + rs * F::RAW + u * F::U;
           const uint2 sc = FMT == 0 ? *reinterpret_cast<const uint2*>(unit + 2048 + mt * 128 + (r * 2 + (q >> 1)) * 8)
                                     : *reinterpret_cast<const uint2*>(unit + 2048 + mt * 64 + r * 8);
 #pragma unroll

@@ -11,6 +11,8 @@
 // for any number of routes, not just the reference's 96.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+
+#include <atomic>
 #include <float.h>
 
 #include "common.cuh"
@@ -84,6 +86,122 @@ __device__ __forceinline__ int plan_key(const PlanArgs& a, int i, int sentinel) 
   return sec >= 0 ? a.n_hot + sec : a.n_hot + a.n_second;
 }
 
+// Routes per chunk for the split-K with the least modelled time, given the
+// bank's chunk counts at 16, 8, 4 and 2 routes per chunk.
+__device__ __forceinline__ int model_rc(const KsModel& m, const int (&chunks_at)[4]) {
+  int best = 1;
+  float best_t = 3.0e38f;
+  for (int j = 0; j < 4; ++j) {
+    if (!(m.allowed >> j & 1)) continue;
+    const int ks = 1 << j;
+    const float chunks = fmaxf(1.f, float(chunks_at[j]));
+    float t = 0.f;
+    for (int p = 0; p < 2; ++p) {
+      const float items = chunks * m.tiles[p] / (8.f / ks);
+      const float bytes = (8.f / ks) * m.kdim[p] * m.bpe;
+      const float waves = ceilf(items / m.slots);
+      t += waves * (fmaxf(bytes / m.bw_cta, fminf(items, m.slots) * bytes / m.bw_hbm) + m.per_wave);
+    }
+    if (t < best_t * 0.999999f) {
+      best_t = t;
+      best = ks;
+    }
+  }
+  return kRouteSlotsPerChunk / best;
+}
+
+// Product plan of at most 32 routes by one warp (decode at M <= 4 for top-8):
+// the same outputs as the block-wide path below -- stable order by key,
+// chunk lists, split-K, bank ranges, key counts, routes without an expert --
+// from a 32-wide bitonic sort of (key, route) and warp scans.
+__device__ void plan_small(const PlanArgs& a, int n, int sentinel) {
+  const unsigned full = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  const int key = lane < n ? plan_key(a, lane, sentinel) : 0x7fff;
+  if (lane < n && a.w_eff) a.w_eff[lane] = key < a.n_keys ? a.w_in[lane] : 0.f;
+  int c = (key << 5) | lane;  // stable: ties in key keep the route order
+  for (int k = 2; k <= 32; k <<= 1)
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const int o = __shfl_xor_sync(full, c, j);
+      const bool take_min = ((lane & j) == 0) == ((lane & k) == 0);
+      c = take_min ? min(c, o) : max(c, o);
+    }
+  const int pkey = lane < n ? (c >> 5) : 0x7fff, route = c & 31;
+  if (lane < n) a.perm[lane] = route;
+  const int prev = __shfl_up_sync(full, pkey, 1);
+  const bool starts = lane < n && (lane == 0 || prev != pkey);
+  const unsigned smask = __ballot_sync(full, starts);
+  const unsigned later = smask & ~((2u << lane) - 1u);  // (2u << 31) == 0: no later start for lane 31
+  const int count = starts ? (later ? __ffs(later) - 1 : n) - lane : 0;
+  if (a.key_counts) {
+    for (int kk = lane; kk < a.n_keys; kk += 32) a.key_counts[kk] = 0;
+    __syncwarp();
+    if (starts && pkey < a.n_keys) a.key_counts[pkey] = count;
+  }
+  // routes without an expert (sorted last): zero y2 rows, count them done
+  const int n_bad = __popc(__ballot_sync(full, lane < n && pkey == a.n_keys));
+  if (n_bad > 0 && a.y2 && a.counters) {
+    const int first = n - n_bad;
+    for (int64_t idx = lane; idx < int64_t(n_bad) * a.H; idx += 32) {
+      const int r = a.perm[first + int(idx / a.H)];
+      static_cast<__half*>(a.y2)[int64_t(r) * a.H + idx % a.H] = __float2half_rn(0.f);
+    }
+    __threadfence();
+    __syncwarp();
+    const int tiles = a.H / 32;
+    for (int idx = lane; idx < n_bad * tiles; idx += 32) {
+      const int r = a.perm[first + idx / tiles], tile = idx % tiles;
+      const int tok = r / a.top_k;
+      int* cp = a.counters + int64_t(tok) * tiles + tile;
+      if (atomicAdd(cp, 1) == a.top_k - 1) {
+        for (int q = 0; q < 32; ++q) a.out[int64_t(tok) * a.H + 32 * tile + q] = 0.f;
+        *cp = 0;
+      }
+    }
+  }
+  for (int b = 0; b < a.n_banks; ++b) {
+    const bool mine = starts && pkey >= a.key_lo[b] && pkey < a.key_hi[b];
+    int at[4];
+    for (int j = 0; j < 4; ++j) {
+      int v = mine ? (count + (16 >> j) - 1) / (16 >> j) : 0;
+      for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(full, v, o);
+      at[j] = v;
+    }
+    int rc = a.rc[b];
+    if (rc == 0) rc = model_rc(a.ks_model[b], at);
+    if (lane == 0 && a.ks_sel) a.ks_sel[b] = max(1, kRouteSlotsPerChunk / rc);
+    const int lo = __popc(__ballot_sync(full, lane < n && pkey < a.key_lo[b]));
+    const int hi = __popc(__ballot_sync(full, lane < n && pkey < a.key_hi[b]));
+    if (a.bank_range && lane == 0) {
+      a.bank_range[2 * b] = lo;
+      a.bank_range[2 * b + 1] = hi;
+    }
+    // chunks: ceil(count / rc) per run of this bank, in key order
+    const int nch = mine ? (count + rc - 1) / rc : 0;
+    int incl = nch;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(full, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const int total = __shfl_sync(full, incl, 31);
+    int ci = incl - nch;
+    for (int off = 0; off < count && mine; off += rc, ++ci) {
+      if (ci < a.max_chunks[b]) {
+        Chunk ch;
+        ch.slot = pkey - a.key_lo[b];
+        ch.begin = lane + off;
+        ch.count = min(rc, count - off);
+        ch.pad = 0;
+        a.chunks[b][ci] = ch;
+      }
+    }
+    if (lane == 0) {
+      if (total > a.max_chunks[b]) set_error(a.err, kErrRange);
+      a.n_chunks[b] = min(total, a.max_chunks[b]);
+    }
+  }
+}
+
 // Keys: product mode [0, n_keys) plus one sentinel bucket n_keys for a route
 // without an expert; reference mode [0, n_hot) (resident) or
 // [0, n_hot + n_second] (split, the last key being the WARM sentinel).
@@ -100,6 +218,10 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanArgs a) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // a.n_valid (device) bounds the routes of this call below the launch's a.n
   const int n = a.n_valid ? min(a.n, max(0, *a.n_valid)) : a.n;
+  if (product && n <= 32) {  // decode-sized plans: one warp, no block-wide phases
+    if (warp == 0) plan_small(a, n, sentinel);
+    return;
+  }
   for (int i = tid; i < 32 * nk; i += kPlanThreads) hist[i] = 0;
   __syncthreads();
   const int per_warp = ((n + 31) / 32 + 31) / 32 * 32;
@@ -188,28 +310,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanArgs a) {
     if (tid < a.n_banks) {
       const int b = tid;
       int rc = a.rc[b];
-      if (rc == 0) {  // split-K of this bank from the model over this plan's chunk counts
-        const KsModel& m = a.ks_model[b];
-        int best = 1;
-        float best_t = 3.0e38f;
-        for (int j = 0; j < 4; ++j) {
-          if (!(m.allowed >> j & 1)) continue;
-          const int ks = 1 << j;
-          const float chunks = fmaxf(1.f, float(st[b][j]));
-          float t = 0.f;
-          for (int p = 0; p < 2; ++p) {
-            const float items = chunks * m.tiles[p] / (8.f / ks);
-            const float bytes = (8.f / ks) * m.kdim[p] * m.bpe;
-            const float waves = ceilf(items / m.slots);
-            t += waves * (fmaxf(bytes / m.bw_cta, fminf(items, m.slots) * bytes / m.bw_hbm) + m.per_wave);
-          }
-          if (t < best_t * 0.999999f) {
-            best_t = t;
-            best = ks;
-          }
-        }
-        rc = kRouteSlotsPerChunk / best;
-      }
+      if (rc == 0) rc = model_rc(a.ks_model[b], st[b]);  // split-K of this bank from this plan's chunk counts
       rc_sel[b] = rc;
       if (a.ks_sel) a.ks_sel[b] = max(1, kRouteSlotsPerChunk / rc);
       if (a.bank_range) {
@@ -303,10 +404,17 @@ int launch_plan(cudaStream_t s, const PlanArgs& a) {
   const int nk = product ? a.n_keys + 1 : (a.split ? a.n_hot + a.n_second + 1 : a.n_hot + 1);
   const size_t smem = plan_smem_bytes(nk);
   if (smem > 200 * 1024) return -1;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr_set = true;
+  if (product && a.n <= 32) {  // the one-warp path needs neither the block nor the shared histograms
+    plan_kernel<<<1, 32, 0, s>>>(a);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  }
+  static std::atomic<uint64_t> attr_set{0};  // devices whose attribute is set
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return -1;
+  if (!(attr_set.load() >> dev & 1)) {
+    if (cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess)
+      return -1;
+    attr_set.fetch_or(uint64_t(1) << dev);
   }
   plan_kernel<<<1, kPlanThreads, smem, s>>>(a);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
@@ -333,8 +441,10 @@ __global__ void gating_kernel(const float* __restrict__ logits, int T, int E, in
         v[j] = -FLT_MAX;
       }
     }
-    float sel_v[16];
-    int sel_i[16];
+    // k rounds: warp argmax (larger value, then smaller id), the winner leaves.
+    // Lane r keeps the r-th winner (value, id), so the exps below run in parallel.
+    float my_v = 0.f;
+    int my_i = 0;
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
       if (r >= k) break;
@@ -357,27 +467,28 @@ __global__ void gating_kernel(const float* __restrict__ logits, int T, int E, in
           bi = oi;
         }
       }
-      sel_v[r] = best;
-      sel_i[r] = bi;
+      if (lane == r) {
+        my_v = best;
+        my_i = bi;
+      }
+      if ((bi & 31) == lane) {  // only the owner lane drops it (static indices keep v in registers)
 #pragma unroll
-      for (int j = 0; j < MAXV; ++j)
-        if (lane + 32 * j == bi) v[j] = -INFINITY;
+        for (int j = 0; j < MAXV; ++j)
+          if (j == (bi >> 5)) v[j] = -INFINITY;
+      }
     }
-    if (lane == 0) {
-      double ex[16];
-      double total = 0.0;
+    // weights: exp(l - l_max) in double, summed in rank order, divided, rounded once
+    const float vmax = __shfl_sync(0xffffffffu, my_v, 0);
+    const double ex = lane < k ? exp(double(my_v) - double(vmax)) : 0.0;
+    double total = 0.0;
 #pragma unroll
-      for (int r = 0; r < 16; ++r) {
-        if (r >= k) break;
-        ex[r] = exp(double(sel_v[r]) - double(sel_v[0]));
-        total = total + ex[r];
-      }
-#pragma unroll
-      for (int r = 0; r < 16; ++r) {
-        if (r >= k) break;
-        ids[int64_t(t) * k + r] = sel_i[r];
-        w[int64_t(t) * k + r] = float(ex[r] / total);
-      }
+    for (int r = 0; r < 16; ++r) {
+      if (r >= k) break;
+      total = total + __shfl_sync(0xffffffffu, ex, r);
+    }
+    if (lane < k) {
+      ids[int64_t(t) * k + lane] = my_i;
+      w[int64_t(t) * k + lane] = float(ex / total);
     }
   }
 }
