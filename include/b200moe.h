@@ -80,8 +80,13 @@ typedef struct {
   int32_t n_fp4;              /* slots in bank 0 */
   int32_t n_iq2;              /* slots in bank 1 */
   float swiglu_limit;         /* limited SwiGLU bound (reference: 10.0) */
-  int32_t prefill_gemm;       /* forward_prefill's FP4 bank: 0 = the skinny decode kernels,
-                                 1 = the tcgen05 grouped GEMM (route tiles of 128) */
+  int32_t prefill_gemm;       /* FP4 bank kernels: 0 = the skinny decode kernels for every call,
+                                 1 = forward_prefill on the tcgen05 grouped GEMM (f16 dequantized
+                                 weight tiles, route tiles of 128), decode on the skinny kernels,
+                                 2 = NVFP4 only: every call on the block-scaled FP4 tensor cores
+                                 (tcgen05.mma.kind::mxf4nvf4, activations as four E2M1 planes);
+                                 the bank is stored in natural order, so b200moe_forward_static
+                                 and b200moe_forward_rows return B200MOE_ERR_STATE */
 } b200moe_config;
 
 typedef struct b200moe_layer b200moe_layer;

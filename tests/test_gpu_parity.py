@@ -164,12 +164,12 @@ def _fp4_dequant(bank, fmt, inter):
     return dq
 
 
-def _make_layer(dev, H, I, E, K, max_tokens, fmt="nvfp4", tier=None, seed=0, max_prefill=0):
+def _make_layer(dev, H, I, E, K, max_tokens, fmt="nvfp4", tier=None, seed=0, max_prefill=0, gemm="tcgen05"):
     from b200moe import moe, synth, tiers
 
     tier = np.zeros(E, np.int8) if tier is None else tier
     layer = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K, max_tokens=max_tokens, tier=tier,
-                              fp4_format=fmt, device=dev, max_prefill_tokens=max_prefill)
+                              fp4_format=fmt, device=dev, max_prefill_tokens=max_prefill, prefill_gemm=gemm)
     n_hot, n_iq = int((tier == tiers.HOT).sum()), int((tier == tiers.WARM).sum())
     fp4 = synth.make_fp4_bank(n_hot, H, I, fmt, seed, dev) if n_hot else None
     iq2 = synth.make_iq2_bank(n_iq, H, I, seed + 1, dev) if n_iq else None
@@ -341,6 +341,29 @@ def test_all_iq2_layer(dev, pkg, m):
     layer.check_errors()
     err = tr.rel_l2(out, tr.layer_forward(x, ids.long(), w, dequant))
     assert err < 2e-3, err
+    layer.close()
+
+
+@pytest.mark.parametrize("m,mixed", [(1, False), (8, False), (64, False), (300, False), (32, True)])
+def test_block_scaled_fp4_path(dev, pkg, m, mixed):
+    """prefill_gemm="fp4": the NVFP4 bank on tcgen05.mma.kind::mxf4nvf4 (E2M1 x E2M1
+    with E4M3 block scales, activations as four E2M1 planes), decode and
+    prefill, against the fp32 dequant-then-matmul reference."""
+    from b200moe import tiers
+
+    H, I, E, K = 2048, 1024, 64, 8
+    tier = tiers.zipf_tier(E, 40, seed=5)[0] if mixed else np.zeros(E, np.int8)
+    layer, dequant, _, _ = _make_layer(dev, H, I, E, K, 64, tier=tier, seed=13, max_prefill=300, gemm="fp4")
+    g = torch.Generator(device=dev).manual_seed(130 + m)
+    x = torch.randn((m, H), generator=g, device=dev).to(torch.bfloat16)
+    ids, w = layer.route(torch.randn((m, E), generator=g, device=dev))
+    out = (layer.forward(x, ids, w) if m <= 64 else layer.forward_prefill(x, ids, w)).clone()
+    layer.check_errors()
+    err = tr.rel_l2(out, tr.layer_forward(x, ids.long(), w, dequant))
+    assert err < 2e-3, err
+    again = (layer.forward(x, ids, w) if m <= 64 else layer.forward_prefill(x, ids, w)).clone()
+    layer.check_errors()
+    assert torch.equal(again, out)  # deterministic
     layer.close()
 
 

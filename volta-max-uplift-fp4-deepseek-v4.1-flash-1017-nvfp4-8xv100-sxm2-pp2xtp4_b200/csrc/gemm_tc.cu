@@ -526,6 +526,20 @@ static int launch_tc_one(cudaStream_t s, const TcArgs& a, const void* map, int g
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
+int make_u8_tile_map(void* map_out, const void* base, int64_t rows, int64_t row_bytes, int box_bytes, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn || row_bytes % 16 || box_bytes > 128 || (reinterpret_cast<uintptr_t>(base) & 15)) return -1;
+  CUtensorMap* m = static_cast<CUtensorMap*>(map_out);
+  cuuint64_t dims[2] = {cuuint64_t(row_bytes), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(row_bytes)};
+  cuuint32_t box[2] = {cuuint32_t(box_bytes), cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -1;
+}
+
 int launch_tc_gemm(cudaStream_t s, int fmt, int epi, const TcArgs& a, const void* map, int grid) {
   if (fmt == 0) return epi == 0 ? launch_tc_one<0, 0>(s, a, map, grid) : launch_tc_one<0, 1>(s, a, map, grid);
   if (fmt == 1) return epi == 0 ? launch_tc_one<1, 0>(s, a, map, grid) : launch_tc_one<1, 1>(s, a, map, grid);

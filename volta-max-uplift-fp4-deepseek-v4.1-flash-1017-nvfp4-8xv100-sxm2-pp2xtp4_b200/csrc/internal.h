@@ -10,6 +10,10 @@ namespace b200moe {
 // Activation rows staged per GEMV stage: a chunk holds 16 / ks routes.
 constexpr int kRouteSlotsPerChunk = 16;
 
+// Block-scaled FP4 tensor path: activation planes and routes per chunk.
+constexpr int kFp4Planes = 4;
+constexpr int kFp4TcRoutes = 16;
+
 // ---- packing (pack.cu)
 int launch_fp4_prepack(cudaStream_t s, int fmt, int hidden, int inter, int n, const uint8_t* w13c,
                        const uint8_t* w13s, const uint8_t* w2c, const uint8_t* w2s, float* slot_globals,
@@ -81,6 +85,44 @@ struct PlanArgs {
   int32_t* iq_out;
   uint32_t* err;
 };
+
+// Block-scaled FP4 GEMM (tcgen05.mma.kind::mxf4nvf4) of the FP4 bank.
+struct Fp4Args {
+  const uint8_t* sfa;     // weight scales blocked: [slot][row block][K/64][512]
+  int rows_per_slot;      // W13: 2I, W2: H
+  int rb_per_slot;        // rows_per_slot / 128
+  int up_rb;              // W13: I / 128 (row blocks from a gate tile to its up tile), W2: 0
+  const float* globals;   // [slot][3] FP32 global scales (NVFP4)
+  int K;
+  int n_rt;               // 128-row tiles per item list entry: W13 I/128, W2 H/128
+  const uint8_t* sfb;     // activation plane scales blocked: [chunk][K/64][512]
+  const float* gx;        // [plane][plane_rows] per-row plane factors
+  int plane_rows;
+  const Chunk* chunks;
+  const int32_t* n_chunks;
+  int bank;
+  int n_slots;
+  const int32_t* perm;
+  int S;
+  int top_k;
+  __half* inter;
+  int inter_stride;
+  float limit;
+  const float* w_eff;
+  void* y2;
+  int32_t* counters;
+  float* out;
+  int H;
+  uint32_t* err;
+};
+int launch_fp4_gemm(cudaStream_t s, int epi, const Fp4Args& a, const void* map_w, const void* map_x, int grid);
+int launch_fp4_planes(cudaStream_t s, bool by_token, const __half* src, int64_t src_stride, int K,
+                      const int32_t* perm, int top_k, const Chunk* chunks, const int32_t* n_chunks, int bank,
+                      const int32_t* bank_range, int max_rows, uint8_t* planes, int plane_rows, uint8_t* sfb,
+                      float* gx);
+int launch_fp4_block_scales(cudaStream_t s, const uint8_t* scales, int64_t n_rows, int K, uint8_t* out);
+// 2D uint8 TMA map with 128-byte swizzle: rows x row_bytes, box box_bytes x box_rows, zero fill out of range
+int make_u8_tile_map(void* map_out, const void* base, int64_t rows, int64_t row_bytes, int box_bytes, int box_rows);
 
 size_t plan_smem_bytes(int n_keys);
 // fp16 rows -> int8 blocks of kIq2XBlockBytes per 256-wide K tile (IQ2 activations)

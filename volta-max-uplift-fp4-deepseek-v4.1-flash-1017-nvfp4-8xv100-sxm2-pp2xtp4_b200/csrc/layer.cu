@@ -52,6 +52,16 @@ struct b200moe_layer {
   int32_t* counters = nullptr;
   uint32_t* err = nullptr;
   void* dbg_y13 = nullptr;
+  // FP4 bank on the block-scaled tensor path (prefill_gemm = 2): natural NVFP4 codes and
+  // blocked scales per projection, the activation planes, their blocked scales and factors
+  uint8_t* f4_codes[2] = {nullptr, nullptr};  // W13 [n][2I][H/2], W2 [n][H][I/2]
+  uint8_t* f4_sf[2] = {nullptr, nullptr};     // [n][rows/128][K/64][512]
+  uint8_t* f4_planes[2] = {nullptr, nullptr}; // [P][plane_rows][K/2]
+  uint8_t* f4_sfb[2] = {nullptr, nullptr};    // [f4_max_chunks][K/64][512]
+  float* f4_gx[2] = {nullptr, nullptr};       // [P][plane_rows]
+  int f4_plane_rows = 0, f4_max_chunks = 0;
+  alignas(128) unsigned char f4_map_w[2][128] = {};
+  alignas(128) unsigned char f4_map_x[2][128] = {};
   // prefill on tcgen05: permuted fp16 token rows and the TMA maps of the two B operands
   __half* xperm = nullptr;
   alignas(128) unsigned char map_x[128] = {};
@@ -93,7 +103,9 @@ int dalloc(T** p, size_t count) {
 void free_layer(b200moe_layer* L) {
   void* ptrs[] = {L->bank[0], L->bank[1], L->globals, L->span, L->iq2_tables, L->key_of_expert, L->perm,
                   L->w_eff, L->chunks[0], L->chunks[1], L->n_chunks, L->x16, L->inter, L->y2,
-                  L->counters, L->err, L->xperm, L->ks_sel, L->bank_range, L->xq, L->interq};
+                  L->counters, L->err, L->xperm, L->ks_sel, L->bank_range, L->xq, L->interq,
+                  L->f4_codes[0], L->f4_codes[1], L->f4_sf[0], L->f4_sf[1], L->f4_planes[0], L->f4_planes[1],
+                  L->f4_sfb[0], L->f4_sfb[1], L->f4_gx[0], L->f4_gx[1]};
   for (void* p : ptrs)
     if (p) cudaFree(p);
 }
@@ -222,7 +234,9 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
     marks.mark();
   }
   // prefill with the tcgen05 GEMM: the FP4 bank's chunks are 128-route token tiles
-  const bool tc = !rows && prefill && c.prefill_gemm && c.n_fp4 > 0 && L->xperm;
+  const bool tc = !rows && prefill && c.prefill_gemm == 1 && c.n_fp4 > 0 && L->xperm;
+  const bool f4 = c.prefill_gemm == 2 && c.n_fp4 > 0;
+  if (f4 && (rows || ws.y2 != L->y2)) return B200MOE_ERR_STATE;  // rows mode and the static array: GEMV banks only
   PlanArgs p{};
   p.ids = ids;
   p.n = S;
@@ -237,9 +251,9 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   p.key_lo[1] = c.n_fp4;
   p.key_hi[1] = c.n_fp4 + c.n_iq2;
   for (int b = 0; b < 2; ++b) {
-    p.rc[b] = (tc && b == 0) ? kTcTokenTile : fixed_rc(L, b);
+    p.rc[b] = (tc && b == 0) ? kTcTokenTile : (f4 && b == 0) ? kFp4TcRoutes : fixed_rc(L, b);
     p.ks_model[b] = ks_model(L, b);
-    p.max_chunks[b] = ws.max_chunks;
+    p.max_chunks[b] = (f4 && b == 0) ? std::min(ws.max_chunks, L->f4_max_chunks) : ws.max_chunks;
     p.chunks[b] = ws.chunks[b];
   }
   p.n_chunks = ws.n_chunks;
@@ -261,6 +275,13 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
     marks.mark();
   }
   for (int epi = 0; epi < 2; ++epi) {
+    if (f4) {  // the FP4 bank's activation rows as E2M1 planes for its block-scaled GEMM
+      if (launch_fp4_planes(s, epi == 0, epi == 0 ? xsrc : ws.inter, epi == 0 ? c.hidden : c.inter,
+                            epi == 0 ? c.hidden : c.inter, ws.perm, c.top_k, ws.chunks[0], ws.n_chunks, 0,
+                            ws.bank_range, S, L->f4_planes[epi], L->f4_plane_rows, L->f4_sfb[epi], L->f4_gx[epi]))
+        return B200MOE_ERR_CUDA;
+      marks.mark();
+    }
     if (epi == 1 && c.n_iq2 > 0) {  // int8 blocks of the IQ2 routes' SwiGLU rows for the IQ2 bank's W2
       if (launch_quant_s8(s, ws.inter, c.inter, c.inter, S, ws.bank_range + 2, ws.interq)) return B200MOE_ERR_CUDA;
       marks.mark();
@@ -268,6 +289,38 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
     for (int b = 0; b < 2; ++b) {
       const int n_slots = b == 0 ? c.n_fp4 : c.n_iq2;
       if (n_slots == 0) continue;
+      if (f4 && b == 0) {
+        Fp4Args f{};
+        f.sfa = L->f4_sf[epi];
+        f.rows_per_slot = epi == 0 ? 2 * c.inter : c.hidden;
+        f.rb_per_slot = f.rows_per_slot / 128;
+        f.up_rb = epi == 0 ? c.inter / 128 : 0;
+        f.globals = L->globals;
+        f.K = epi == 0 ? c.hidden : c.inter;
+        f.n_rt = epi == 0 ? c.inter / 128 : c.hidden / 128;
+        f.sfb = L->f4_sfb[epi];
+        f.gx = L->f4_gx[epi];
+        f.plane_rows = L->f4_plane_rows;
+        f.chunks = ws.chunks[0];
+        f.n_chunks = ws.n_chunks;
+        f.bank = 0;
+        f.n_slots = n_slots;
+        f.perm = ws.perm;
+        f.S = S;
+        f.top_k = c.top_k;
+        f.inter = ws.inter;
+        f.inter_stride = c.inter;
+        f.limit = c.swiglu_limit;
+        f.w_eff = ws.w_eff;
+        f.y2 = ws.y2;
+        f.counters = ws.counters;
+        f.out = out;
+        f.H = c.hidden;
+        f.err = L->err;
+        if (launch_fp4_gemm(s, epi, f, L->f4_map_w[epi], L->f4_map_x[epi], L->grid)) return B200MOE_ERR_CUDA;
+        marks.mark();
+        continue;
+      }
       if (tc && b == 0) {
         TcArgs t{};
         t.region = L->bank[0] + (epi == 0 ? 0 : L->geom[0].w13_bytes);
@@ -370,7 +423,10 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
     return B200MOE_ERR_INVALID_ARG;
   if (c.fp4_format != B200MOE_NVFP4 && c.fp4_format != B200MOE_MXFP4) return B200MOE_ERR_INVALID_ARG;
   if (c.n_iq2 > 0 && c.inter % 256) return B200MOE_ERR_INVALID_ARG;
-  if (c.prefill_gemm != 0 && c.prefill_gemm != 1) return B200MOE_ERR_INVALID_ARG;
+  if (c.prefill_gemm < 0 || c.prefill_gemm > 2) return B200MOE_ERR_INVALID_ARG;
+  // the block-scaled FP4 path: NVFP4 (E4M3 scales per 16), K tiles of 256 on both projections
+  if (c.prefill_gemm == 2 && (c.fp4_format != B200MOE_NVFP4 || c.hidden % 256 || c.inter % 256))
+    return B200MOE_ERR_INVALID_ARG;
   DeviceGuard guard(device);
   cudaDeviceProp prop;
   if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return B200MOE_ERR_CUDA;
@@ -388,7 +444,15 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
   auto take = [&](int r) {
     if (st == B200MOE_OK) st = r;
   };
-  take(dalloc(&L->bank[0], size_t(c.n_fp4) * L->geom[0].slot_bytes));
+  const bool f4 = c.prefill_gemm == 2;
+  take(dalloc(&L->bank[0], f4 ? size_t(0) : size_t(c.n_fp4) * L->geom[0].slot_bytes));
+  if (f4 && c.n_fp4 > 0) {
+    const size_t H = c.hidden, I = c.inter, n = c.n_fp4;
+    take(dalloc(&L->f4_codes[0], n * 2 * I * H / 2));
+    take(dalloc(&L->f4_codes[1], n * H * I / 2));
+    take(dalloc(&L->f4_sf[0], n * 2 * I * H / 16));
+    take(dalloc(&L->f4_sf[1], n * H * I / 16));
+  }
   take(dalloc(&L->bank[1], size_t(c.n_iq2) * L->geom[1].slot_bytes));
   take(dalloc(&L->globals, size_t(std::max(c.n_fp4, 1)) * 3));
   take(dalloc(&L->span, size_t(std::max(c.n_fp4, 1)) * 6));
@@ -410,7 +474,24 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
     take(dalloc(&L->xq, size_t(L->t_max) * (c.hidden / kIq2KTile) * kIq2XBlockBytes));
     take(dalloc(&L->interq, size_t(L->s_max) * (c.inter / kIq2KTile) * kIq2XBlockBytes));
   }
-  if (c.prefill_gemm && c.max_prefill_tokens > 0 && c.n_fp4 > 0) {
+  if (f4 && c.n_fp4 > 0) {
+    L->f4_plane_rows = L->s_max + kFp4TcRoutes;
+    L->f4_max_chunks = (L->s_max + kFp4TcRoutes - 1) / kFp4TcRoutes + c.n_fp4;
+    const size_t P = kFp4Planes, R = L->f4_plane_rows, H = c.hidden, I = c.inter;
+    take(dalloc(&L->f4_planes[0], P * R * H / 2));
+    take(dalloc(&L->f4_planes[1], P * R * I / 2));
+    take(dalloc(&L->f4_sfb[0], size_t(L->f4_max_chunks) * (H / 64) * 512));
+    take(dalloc(&L->f4_sfb[1], size_t(L->f4_max_chunks) * (I / 64) * 512));
+    take(dalloc(&L->f4_gx[0], P * R));
+    take(dalloc(&L->f4_gx[1], P * R));
+    if (st == B200MOE_OK &&
+        (make_u8_tile_map(L->f4_map_w[0], L->f4_codes[0], int64_t(c.n_fp4) * 2 * I, H / 2, 128, 128) ||
+         make_u8_tile_map(L->f4_map_w[1], L->f4_codes[1], int64_t(c.n_fp4) * H, I / 2, 128, 128) ||
+         make_u8_tile_map(L->f4_map_x[0], L->f4_planes[0], int64_t(P * R), H / 2, 128, kFp4TcRoutes) ||
+         make_u8_tile_map(L->f4_map_x[1], L->f4_planes[1], int64_t(P * R), I / 2, 128, kFp4TcRoutes)))
+      st = B200MOE_ERR_CUDA;
+  }
+  if (c.prefill_gemm == 1 && c.max_prefill_tokens > 0 && c.n_fp4 > 0) {
     take(dalloc(&L->xperm, size_t(L->s_max) * c.hidden));
     if (st == B200MOE_OK && (make_token_map(L->map_x, L->xperm, L->s_max, c.hidden) ||
                              make_token_map(L->map_inter, L->inter, L->s_max, c.inter)))
@@ -421,6 +502,8 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
         cudaMemset(L->err, 0, 4) != cudaSuccess || cudaMemset(L->n_chunks, 0, 8) != cudaSuccess ||
         cudaMemset(L->inter, 0, size_t(L->s_max) * c.inter * 2) != cudaSuccess ||
         cudaMemset(L->globals, 0, size_t(std::max(c.n_fp4, 1)) * 12) != cudaSuccess ||
+        (L->f4_sfb[0] && cudaMemset(L->f4_sfb[0], 0, size_t(L->f4_max_chunks) * (c.hidden / 64) * 512) != cudaSuccess) ||
+        (L->f4_sfb[1] && cudaMemset(L->f4_sfb[1], 0, size_t(L->f4_max_chunks) * (c.inter / 64) * 512) != cudaSuccess) ||
         cudaDeviceSynchronize() != cudaSuccess)
       st = B200MOE_ERR_CUDA;
   }
@@ -503,6 +586,18 @@ int b200moe_load_fp4(b200moe_layer* L, void* stream, int slot_begin, int n, cons
   if (c.fp4_format == B200MOE_NVFP4 &&
       cudaMemcpyAsync(gdst, globals, size_t(n) * 12, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
     return B200MOE_ERR_CUDA;
+  if (c.prefill_gemm == 2) {  // natural codes, scales re-blocked for tcgen05.cp
+    const size_t H = c.hidden, I = c.inter, b = size_t(slot_begin);
+    if (cudaMemcpyAsync(L->f4_codes[0] + b * 2 * I * H / 2, w13c, size_t(n) * 2 * I * H / 2, cudaMemcpyDeviceToDevice,
+                        s) != cudaSuccess ||
+        cudaMemcpyAsync(L->f4_codes[1] + b * H * I / 2, w2c, size_t(n) * H * I / 2, cudaMemcpyDeviceToDevice, s) !=
+            cudaSuccess)
+      return B200MOE_ERR_CUDA;
+    if (launch_fp4_block_scales(s, w13s, int64_t(n) * 2 * I, int(H), L->f4_sf[0] + b * 2 * I * H / 16) ||
+        launch_fp4_block_scales(s, w2s, int64_t(n) * H, int(I), L->f4_sf[1] + b * H * I / 16))
+      return B200MOE_ERR_CUDA;
+    return B200MOE_OK;
+  }
   uint8_t* dst = L->bank[0] + size_t(slot_begin) * L->geom[0].slot_bytes;
   if (launch_fp4_prepack(s, c.fp4_format, c.hidden, c.inter, n, w13c, w13s, w2c, w2s, gdst, L->span, dst,
                          L->geom[0].slot_bytes, L->geom[0].w13_bytes, L->err))

@@ -42,9 +42,14 @@ class B200NativeMoe:
     expert is local.  Buffers are fixed at construction (``max_tokens`` for the
     graph-capturable decode ``forward``, ``max_prefill_tokens`` for
     ``forward_prefill``); forward never allocates or syncs with the host.
-    ``prefill_gemm`` picks forward_prefill's kernel for the FP4 bank:
-    "tcgen05" (the tensor-core grouped GEMM, 128-route tiles) or "skinny"
-    (the decode kernels, 16-route chunks); IQ2_XXS experts always use the latter.
+    ``prefill_gemm`` picks the FP4 bank's kernels: "tcgen05" (forward_prefill
+    on the tensor-core grouped GEMM over dequantized f16 tiles, 128-route
+    tiles; decode on the skinny kernels), "skinny" (the skinny kernels for
+    both) or "fp4" (NVFP4 only: every FP4-bank launch, decode and prefill, on
+    the block-scaled FP4 tensor cores, tcgen05.mma.kind::mxf4nvf4, with the
+    activations as four E2M1 planes; the bank is stored in natural order with
+    re-blocked scales, so forward_static and the expert-parallel rows forward
+    refuse such a layer).  IQ2_XXS experts always use their int8 kernel.
     """
 
     def __init__(self, *, hidden: int, inter: int, num_experts: int, top_k: int, max_tokens: int,
@@ -53,8 +58,8 @@ class B200NativeMoe:
                  rank: int = 0, world: int = 1, prefill_gemm: str = "tcgen05"):
         if fp4_format not in ("nvfp4", "mxfp4"):
             raise ValueError(f"fp4_format must be nvfp4 or mxfp4, got {fp4_format!r}")
-        if prefill_gemm not in ("tcgen05", "skinny"):
-            raise ValueError(f"prefill_gemm must be tcgen05 or skinny, got {prefill_gemm!r}")
+        if prefill_gemm not in ("tcgen05", "skinny", "fp4"):
+            raise ValueError(f"prefill_gemm must be tcgen05, skinny or fp4, got {prefill_gemm!r}")
         self.prefill_gemm = prefill_gemm
         dev = torch.device("cuda", torch.cuda.current_device() if device is None else
                            (device if isinstance(device, int) else device.index))
@@ -71,7 +76,7 @@ class B200NativeMoe:
         self.fp4_slot, self.iq2_slot = fp4_map, iq2_map
         cfg = _lib.Config(hidden, inter, num_experts, top_k, max_tokens, max_prefill_tokens,
                           _lib.NVFP4 if fp4_format == "nvfp4" else _lib.MXFP4, self.n_fp4, self.n_iq2,
-                          float(swiglu_limit), 1 if prefill_gemm == "tcgen05" else 0)
+                          float(swiglu_limit), {"skinny": 0, "tcgen05": 1, "fp4": 2}[prefill_gemm])
         handle = ctypes.c_void_p()
         L = _lib.lib()
         _lib.check("b200moe_layer_create", L.b200moe_layer_create(ctypes.byref(cfg), dev.index, ctypes.byref(handle)))
