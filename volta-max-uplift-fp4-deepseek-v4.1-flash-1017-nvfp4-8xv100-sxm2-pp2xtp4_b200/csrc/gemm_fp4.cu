@@ -9,15 +9,16 @@
 // weighted reduce, as the other expert kernels here do.
 //
 // Activations.  The block-scaled FP4 kind takes FP4 on both sides, so each
-// activation row x is written as four E2M1 planes, x ~ sum_p g_p * s_pb * q_p:
+// activation row x is written as four E2M1 planes, x ~ g * sum_p s_pb * q_p:
 // plane p quantizes the residual of the planes before it, with an E4M3 scale
-// s_pb per 16 elements and an FP32 factor g_p per row and plane (its amax over
-// 6 * 448, so the block scales use E4M3's range).  Each plane cuts the error
-// about ten times; four planes leave ~1e-4 relative on the layer's inputs
-// (the fp16 activations of the reference are ~5e-4).  The planes are four
-// groups of 16 rows of the MMA's B operand (N = 64): one MMA per 64-wide K
-// step covers every plane of every route of the chunk, and the epilogue sums
-// the four columns of a route with their g_p.
+// s_pb per 16 elements and one FP32 factor g per row (its amax over 6 * 448,
+// so plane 0's block scales use E4M3's range and the later ones stay inside
+// it).  Each plane cuts the error about ten times; four planes leave ~1e-4
+// relative on the layer's inputs (the fp16 activations of the reference are
+// ~5e-4).  The planes are stored route-major (row 4 * position + p), so the
+// 16 routes of a chunk are 64 consecutive rows: one TMA box is the MMA's B
+// operand (N = 64, column 4n + p), one MMA per 64-wide K step covers every
+// plane of every route, and the epilogue sums a route's four columns times g.
 //
 // Tiles.  An item is a chunk of <= 16 routes of one expert x a tile of 128
 // weight rows (W13: 128 gate rows and the 128 matching up rows, two MMAs into
@@ -48,15 +49,34 @@ constexpr int kN = kP * kRC;               // MMA N = 64
 constexpr int kATile = 128 * 128;          // weight tile: 128 rows x 256 FP4 = 16 KB
 constexpr int kBTile = kN * 128;           // activation tile: 64 rows x 256 FP4 = 8 KB
 constexpr int kSFBytes = 4 * 512;          // the scale blocks of one 256-wide K tile
-constexpr int kOffAG = 0, kOffAU = kATile, kOffB = 2 * kATile;
-constexpr int kOffSFG = 2 * kATile + kBTile, kOffSFU = kOffSFG + kSFBytes, kOffSFB = kOffSFU + kSFBytes;
-constexpr int kStage = kOffSFB + kSFBytes;  // 46 KB
-constexpr int kStages = 4;
 constexpr int kThreads = 6 * 32;           // producer, MMA, 4 epilogue warps
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kSfCol = 256;           // per stage: SFA gate 16, SFA up 16, SFB 16 columns
-constexpr uint32_t kSfStageCols = 48;      // own columns per stage: a copy never lands under an MMA in flight
-static_assert(kSfCol + kStages * kSfStageCols <= kTmemCols, "TMEM columns");
+constexpr uint32_t kSfCol = 256;           // scale columns start after the two accumulator buffers
+
+// Stage layout by weight tiles per unit.  Two tiles (W13: the gate and up
+// tiles; W2: two adjacent 128-row tiles) make 46 KB stages, 4 of them; one
+// tile 28 KB, 7 stages.  Each stage has its own TMEM scale columns: a scale
+// copy never lands under an MMA still in flight.
+template <int TILES>
+struct Fp4Stage {
+  static constexpr int kTiles = TILES;  // weight tiles per unit
+  static constexpr int kUnit = kTiles * (kATile + kSFBytes);  // one weight unit, one bulk copy
+  static constexpr int kOffAG = 0;
+  static constexpr int kOffAU = kATile;  // W13 only
+  static constexpr int kOffSFG = kTiles * kATile;
+  static constexpr int kOffSFU = kOffSFG + kSFBytes;  // W13 only
+  static constexpr int kOffB = kUnit;
+  static constexpr int kOffSFB = kOffB + kBTile;
+  static constexpr int kBytes = kOffSFB + kSFBytes;  // 46 KB / 28 KB
+  static constexpr int kStages = TILES == 2 ? 4 : 7;
+  static constexpr uint32_t kSfCols = TILES == 2 ? 48 : 32;  // tile 0 (, tile 1), activations: 16 each
+  static constexpr uint32_t kSfB = TILES == 2 ? 32 : 16;
+  static constexpr size_t kSmem = 1024 + size_t(kStages) * kBytes + 64 * 8;
+  static_assert(kBytes % 1024 == 0, "128-byte swizzled tiles need 1024-byte aligned stages");
+  static_assert(kSfCol + kStages * kSfCols <= kTmemCols, "TMEM columns");
+  static_assert(kSmem <= 227 * 1024, "shared memory");
+};
+
 // kind::mxf4nvf4 block16: A and B E2M1 (1), K-major, N = 64, M = 128, scales UE4M3
 constexpr uint32_t kIdesc = (1u << 7) | (1u << 10) | (uint32_t(kN >> 3) << 17) | (uint32_t(128 >> 4) << 24);
 
@@ -115,9 +135,12 @@ __device__ __forceinline__ __half swiglu1(float g, float u, float limit) {
   return __float2half_rn(__fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), u));
 }
 
-template <int EPI>
+template <int EPI, int TILES>
 __global__ void __launch_bounds__(kThreads, 1)
-    fp4_gemm_kernel(const Fp4Args a, const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x) {
+    fp4_gemm_kernel(const Fp4Args a, const __grid_constant__ CUtensorMap map_x) {
+  static_assert(EPI == 1 || TILES == 2, "W13 items pair a gate tile with its up tile");
+  using St = Fp4Stage<TILES>;
+  constexpr int kStages = St::kStages, kStage = St::kBytes;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base_u32 = (smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t* stages = smem_raw + (base_u32 - smem_u32(smem_raw));
@@ -154,6 +177,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_kt = a.K / 256;
   const int n_ks = a.K / 64;
   const int n_items = a.n_chunks[a.bank] * a.n_rt;
+  // the next item's chunk is loaded one item ahead: its latency never stalls a role
+  auto chunk_of_item = [&](int item) {
+    Chunk c{};
+    c.slot = -1;
+    if (item < n_items) c = a.chunks[item / a.n_rt];
+    return c;
+  };
   auto item_ok = [&](const Chunk& ch) {
     return ch.slot >= 0 && ch.slot < a.n_slots && ch.count >= 1 && ch.count <= kRC && ch.begin >= 0 &&
            ch.begin + ch.count <= a.S;
@@ -163,18 +193,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_x)) : "memory");
       uint32_t g = 0, issued = 0, parity = 0;
+      Chunk next = chunk_of_item(blockIdx.x);
       for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
         const int ci = item / a.n_rt;
-        const Chunk ch = a.chunks[ci];
+        const Chunk ch = next;
+        next = chunk_of_item(item + gridDim.x);
         if (!item_ok(ch)) {
           set_error(a.err, kErrBounds);
           continue;
         }
         const int rt = item % a.n_rt;
-        const int row_g = ch.slot * a.rows_per_slot + rt * 128;
-        const uint8_t* sf_g = a.sfa + (int64_t(ch.slot) * a.rb_per_slot + rt) * n_ks * 512;
-        const uint8_t* sf_u = sf_g + int64_t(a.up_rb) * n_ks * 512;
+        const uint8_t* wu = a.wt + (int64_t(ch.slot) * a.n_rt + rt) * n_kt * St::kUnit;
         const uint8_t* sf_b = a.sfb + int64_t(ci) * n_ks * 512;
         for (int kt = 0; kt < n_kt; ++kt, ++g) {
           const int s = g % kStages;
@@ -184,17 +215,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           uint8_t* st = stages + s * kStage;
-          const uint32_t bytes = uint32_t((EPI == 0 ? 2 : 1) * (kATile + kSFBytes) + kBTile + kSFBytes);
+          const uint32_t bytes = uint32_t(kStage);
           mbar_arrive_expect_tx(&full[s], bytes);
-          tma_2d(st + kOffAG, &map_w, kt * 128, row_g, &full[s]);
-          bulk_g2s_hint(st + kOffSFG, sf_g + kt * kSFBytes, kSFBytes, &full[s], pol);
-          if (EPI == 0) {
-            tma_2d(st + kOffAU, &map_w, kt * 128, row_g + a.up_rb * 128, &full[s]);
-            bulk_g2s_hint(st + kOffSFU, sf_u + kt * kSFBytes, kSFBytes, &full[s], pol);
-          }
-#pragma unroll
-          for (int p = 0; p < kP; ++p) tma_2d(st + kOffB + p * kRC * 128, &map_x, kt * 128, p * a.plane_rows + ch.begin, &full[s]);
-          bulk_g2s(st + kOffSFB, sf_b + kt * kSFBytes, kSFBytes, &full[s]);
+          bulk_g2s_hint(st, wu + int64_t(kt) * St::kUnit, St::kUnit, &full[s], pol);  // codes + scales
+          tma_2d(st + St::kOffB, &map_x, kt * 128, ch.begin * kP, &full[s]);  // the chunk's routes x planes
+          bulk_g2s(st + St::kOffSFB, sf_b + kt * kSFBytes, kSFBytes, &full[s]);
           issued |= 1u << s;
           parity = (parity & ~(1u << s)) | (ph << s);
         }
@@ -209,8 +234,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       uint32_t g = 0, acc_i = 0, last_b = 0, last_ph = 0;
       bool committed = false;
+      Chunk next = chunk_of_item(blockIdx.x);
       for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-        const Chunk ch = a.chunks[item / a.n_rt];
+        const Chunk ch = next;
+        next = chunk_of_item(item + gridDim.x);
         if (!item_ok(ch)) continue;
         const uint32_t b = acc_i & 1u, bph = (acc_i >> 1) & 1u;
         if (*abort_ptr || !mbar_wait(&acc_empty[b], bph ^ 1u, a.err)) {
@@ -229,20 +256,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           fence_after();
           const uint32_t st = smem_u32(stages + s * kStage);
-          const uint32_t sfg = tmem + kSfCol + s * kSfStageCols, sfu = sfg + 16, sfb = sfg + 32;
+          const uint32_t sfg = tmem + kSfCol + s * St::kSfCols, sfu = sfg + 16, sfb = sfg + St::kSfB;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            sf_copy(sfg + 4 * j, st + kOffSFG + 512 * j);
-            if (EPI == 0) sf_copy(sfu + 4 * j, st + kOffSFU + 512 * j);
-            sf_copy(sfb + 4 * j, st + kOffSFB + 512 * j);
+            sf_copy(sfg + 4 * j, st + St::kOffSFG + 512 * j);
+            if (TILES == 2) sf_copy(sfu + 4 * j, st + St::kOffSFU + 512 * j);
+            sf_copy(sfb + 4 * j, st + St::kOffSFB + 512 * j);
           }
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const uint32_t acc = (kt | j) != 0;
-            mma_fp4(dg, desc_sw128(st + kOffAG + 32 * j), desc_sw128(st + kOffB + 32 * j), sfg + 4 * j, sfb + 4 * j, acc);
-            if (EPI == 0)
-              mma_fp4(du, desc_sw128(st + kOffAU + 32 * j), desc_sw128(st + kOffB + 32 * j), sfu + 4 * j, sfb + 4 * j,
-                      acc);
+            const uint64_t bdesc = desc_sw128(st + St::kOffB + 32 * j);
+            mma_fp4(dg, desc_sw128(st + St::kOffAG + 32 * j), bdesc, sfg + 4 * j, sfb + 4 * j, acc);
+            if (TILES == 2) mma_fp4(du, desc_sw128(st + St::kOffAU + 32 * j), bdesc, sfu + 4 * j, sfb + 4 * j, acc);
           }
           commit_to(&empty[s]);
         }
@@ -263,10 +289,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;  // TMEM lanes 32 * quarter .. : weight rows of this warp
     const int row = quarter * 32 + lane;
     uint32_t acc_i = 0;
+    Chunk next = chunk_of_item(blockIdx.x);
     for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-      const Chunk ch = a.chunks[item / a.n_rt];
+      const Chunk ch = next;
+      next = chunk_of_item(item + gridDim.x);
       if (!item_ok(ch)) continue;
       const int rt = item % a.n_rt;
+      // per-route data and scales, loaded while the MMAs run: lane n holds route n's
+      const float* gl = a.globals ? a.globals + ch.slot * 3 : nullptr;
+      const float gw0 = gl ? gl[EPI == 0 ? 0 : 2] : 1.f, gw1 = (gl && EPI == 0) ? gl[1] : 1.f;
+      float gx_l = 0.f;
+      int route_l = 0;
+      if (lane < ch.count) {
+        gx_l = __ldg(a.gx + ch.begin + lane);
+        if (EPI == 1) route_l = a.perm[ch.begin + lane];
+      }
       const uint32_t b = acc_i & 1u, bph = (acc_i >> 1) & 1u;
       bool ok = !*abort_ptr && mbar_wait(&acc_full[b], bph, a.err);
       ok = __all_sync(0xffffffffu, ok);
@@ -276,11 +313,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_after();
       const uint32_t lanes = uint32_t(quarter * 32) << 16;
-      const float* gl = a.globals ? a.globals + ch.slot * 3 : nullptr;
-      float d0[kN], d1[EPI == 0 ? kN : 1];
+      float d0[kN], d1[TILES == 2 ? kN : 1];
 #pragma unroll
       for (int c = 0; c < kN; c += 16) tmem_ld16(tmem + lanes + b * 128 + c, d0 + c);
-      if (EPI == 0) {
+      if (TILES == 2) {
 #pragma unroll
         for (int c = 0; c < kN; c += 16) tmem_ld16(tmem + lanes + b * 128 + 64 + c, d1 + c);
       }
@@ -288,7 +324,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);  // the accumulator is in registers now
       if (EPI == 0) {
-        const float g1 = gl ? gl[0] : 1.f, g3 = gl ? gl[1] : 1.f;
 #pragma unroll
         for (int n = 0; n < kRC; ++n) {
           if (n >= ch.count) break;
@@ -296,50 +331,37 @@ __global__ void __launch_bounds__(kThreads, 1)
           float gs = 0.f, us = 0.f;
 #pragma unroll
           for (int p = 0; p < kP; ++p) {
-            const float gx = __ldg(a.gx + int64_t(p) * a.plane_rows + pos);
-            gs = fmaf(d0[p * kRC + n], gx, gs);
-            us = fmaf(d1[p * kRC + n], gx, us);
+            gs += d0[n * kP + p];
+            us += d1[n * kP + p];
           }
-          const float gh = __half2float(__float2half_rn(gs * g1));
-          const float uh = __half2float(__float2half_rn(us * g3));
-          a.inter[int64_t(pos) * a.inter_stride + rt * 128 + row] = swiglu1(gh, uh, a.limit);
+          const float gx = __shfl_sync(0xffffffffu, gx_l, n);
+          const float gh = __half2float(__float2half_rn(gs * gx * gw0));
+          const float uh = __half2float(__float2half_rn(us * gx * gw1));
+          const __half h = swiglu1(gh, uh, a.limit);
+          a.inter[int64_t(pos) * a.inter_stride + rt * 128 + row] = h;
+          float hm = fabsf(__half2float(h));  // the row's amax for its W2 planes
+#pragma unroll
+          for (int o = 16; o; o >>= 1) hm = fmaxf(hm, __shfl_xor_sync(0xffffffffu, hm, o));
+          if (lane == 0) atomicMax(a.rowmax + pos, __float_as_uint(hm));
         }
       } else {
-        const float g2 = gl ? gl[2] : 1.f;
-        const int tile = rt * 4 + quarter;  // 32-row tile of the output row
+        // fp16 y2 rows (unweighted, by route index); the slot-order combine
+        // runs after the W2 launches of both banks
 #pragma unroll
         for (int n = 0; n < kRC; ++n) {
           if (n >= ch.count) break;
-          const int pos = ch.begin + n;
+          const int route = __shfl_sync(0xffffffffu, route_l, n);
+          const float gx = __shfl_sync(0xffffffffu, gx_l, n);
+          __half* yrow = reinterpret_cast<__half*>(a.y2) + int64_t(route) * a.H + rt * (128 * TILES) + row;
           float v = 0.f;
 #pragma unroll
-          for (int p = 0; p < kP; ++p) v = fmaf(d0[p * kRC + n], __ldg(a.gx + int64_t(p) * a.plane_rows + pos), v);
-          const int route = a.perm[pos];
-          reinterpret_cast<__half*>(a.y2)[int64_t(route) * a.H + rt * 128 + row] = __float2half_rn(v * g2);
-        }
-        if (a.counters) {
-          __threadfence();
-          __syncwarp();
-          for (int n = 0; n < ch.count; ++n) {
-            const int route = a.perm[ch.begin + n];
-            const int tok = route / a.top_k;
-            int* cnt = a.counters + int64_t(tok) * (a.H / 32) + tile;
-            int old = 0;
-            if (lane == 0) old = atomicAdd(cnt, 1);
-            old = __shfl_sync(0xffffffffu, old, 0);
-            if (old == a.top_k - 1) {  // the last route of (token, tile): slot-order sum
-              __threadfence();
-              const unsigned short* y2 = reinterpret_cast<const unsigned short*>(a.y2);
-              const int orow = rt * 128 + row;
-              float sum = 0.f;
-              for (int slot = 0; slot < a.top_k; ++slot) {
-                const int r2 = tok * a.top_k + slot;
-                const float y = __half2float(__ushort_as_half(__ldcg(y2 + int64_t(r2) * a.H + orow)));
-                sum = __fmaf_rn(y, __ldcg(a.w_eff + r2), sum);
-              }
-              a.out[int64_t(tok) * a.H + orow] = sum;
-              if (lane == 0) *cnt = 0;
-            }
+          for (int p = 0; p < kP; ++p) v += d0[n * kP + p];
+          yrow[0] = __float2half_rn(v * gx * gw0);
+          if (TILES == 2) {
+            float v1 = 0.f;
+#pragma unroll
+            for (int p = 0; p < kP; ++p) v1 += d1[n * kP + p];
+            yrow[128] = __float2half_rn(v1 * gx * gw0);
           }
         }
       }
@@ -352,149 +374,275 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------- planes
-// One CTA per sorted route position of the FP4 bank: the row (a token's x
-// for W13, the route's SwiGLU row for W2) as kP E2M1 planes, their blocked
-// scales in the chunk's SFB blocks (MMA row p * 16 + n) and g_p.
-template <int SRC_TOKEN>
-__global__ void __launch_bounds__(128) fp4_planes_kernel(const __half* __restrict__ src, int64_t src_stride, int K,
-                                                         const int32_t* __restrict__ perm, int top_k,
-                                                         const Chunk* __restrict__ chunks,
-                                                         const int32_t* __restrict__ n_chunks, int bank,
-                                                         const int32_t* __restrict__ bank_range, uint8_t* planes,
-                                                         int plane_rows, uint8_t* sfb, float* gx) {
-  constexpr int kMaxBlk = 4;  // 16-wide blocks per thread: K <= 128 * 16 * kMaxBlk
-  __shared__ float red[4];
+// Nearest E2M1 value (ties to even) of v >= 0, and its 3-bit magnitude code:
+// step 0.5 below 2, 1 below 4, 2 above, saturating at 6.
+__device__ __forceinline__ float e2m1_round(float v) {
+  const float q = v < 2.f ? rintf(v * 2.f) * 0.5f : v < 4.f ? rintf(v) : rintf(v * 0.5f) * 2.f;
+  return fminf(q, 6.f);
+}
+__device__ __forceinline__ uint32_t e2m1_code_of(float q) {  // q on the E2M1 grid
+  return q < 2.f ? uint32_t(q * 2.f) : q < 4.f ? uint32_t(q) + 2u : uint32_t(q * 0.5f) + 4u;
+}
+// Nearest E4M3 byte of x >= 0 (ties to even, saturating at 448) by the
+// hardware conversion; both halves of the pair convert x.
+__device__ __forceinline__ uint32_t e4m3_rn(float x) {
+  uint16_t pair;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %1;" : "=h"(pair) : "f"(x));
+  return pair & 0xFFu;
+}
+
+// The activation rows of the FP4 bank as kP E2M1 planes with their blocked
+// scales in the chunk's SFB blocks (MMA row n * kP + p) and one FP32 factor g
+// per row (its amax over 6 * 448: plane 0's block scales use E4M3's range and
+// the later planes, each ~10x smaller, stay inside it).  With g fixed per row
+// the planes are block-local: a CTA takes a 1024-wide slice of a row, a
+// thread one half-block of 8 elements through all planes.
+// BY_TOKEN (W13): a token row of x, written to every FP4-bank route of the
+// token (found through the plan's inverse permutation), so a token is
+// quantized once for its top_k routes; the CTA finds the row amax itself and
+// clears the W2 row maxima of those positions.  Otherwise (W2): the SwiGLU row
+// of one sorted position, its amax taken by the W13 epilogue (rowmax).
+constexpr int kPlaneThreads = 128;
+constexpr int kSlice = kPlaneThreads * 8;
+template <int BY_TOKEN>
+__global__ void __launch_bounds__(kPlaneThreads) fp4_planes_kernel(
+    const __half* __restrict__ src, int64_t src_stride, int K, const int32_t* __restrict__ inv, int top_k,
+    const int32_t* __restrict__ chunk_of, int bank, const int32_t* __restrict__ bank_range, int n_tokens,
+    uint32_t* rowmax, uint8_t* planes, int plane_rows, uint8_t* sfb, float* gx) {
+  __shared__ float red[kPlaneThreads / 32];
+  __shared__ int dst_pos[32], dst_sf[32], dst_n[32];
+  __shared__ int n_dst;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  const int nb = K / 16, n_ks = K / 64;
-  const int nch = n_chunks[bank];
-  for (int pos = bank_range[2 * bank] + blockIdx.x; pos < bank_range[2 * bank + 1]; pos += gridDim.x) {
-    // the chunk holding pos: chunks are in position order
-    int lo = 0, hi = nch - 1;
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (chunks[mid].begin <= pos) lo = mid;
-      else hi = mid - 1;
+  const int nhb = K / 8, n_ks = K / 64;
+  const int hb = blockIdx.y * kPlaneThreads + t, blk = hb >> 1;  // this thread's half-block
+  const bool own = hb < nhb;
+  const int lo = bank_range[2 * bank], hi = bank_range[2 * bank + 1];
+  const int rows = BY_TOKEN ? n_tokens : hi - lo;
+  for (int ri = blockIdx.x; ri < rows; ri += gridDim.x) {
+    __syncthreads();  // the previous row's destinations are read
+    if (warp == 0) {
+      int pos = -1;
+      if (BY_TOKEN) {
+        if (lane < top_k) {
+          const int q = inv[int64_t(ri) * top_k + lane];
+          if (q >= lo && q < hi) pos = q;
+        }
+      } else if (lane == 0) {
+        pos = lo + ri;
+      }
+      const int cn = pos >= 0 ? chunk_of[pos] : 0;
+      const unsigned have = __ballot_sync(0xffffffffu, pos >= 0);
+      if (pos >= 0) {
+        const int i = __popc(have & ((1u << lane) - 1u));
+        dst_pos[i] = pos;
+        dst_sf[i] = (cn >> 8) * n_ks * 512;
+        dst_n[i] = cn & 255;
+      }
+      if (lane == 0) n_dst = __popc(have);
     }
-    const int c = lo, n = pos - chunks[c].begin;
-    const __half* row = src + (SRC_TOKEN ? int64_t(perm[pos] / top_k) : int64_t(pos)) * src_stride;
-    float r[kMaxBlk][16];
+    const __half* row = src + (BY_TOKEN ? int64_t(ri) : int64_t(lo + ri)) * src_stride;
+    float r[8];
+    {
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (own) v = *reinterpret_cast<const uint4*>(row + hb * 8);
+      const __half2* hv = reinterpret_cast<const __half2*>(&v);
 #pragma unroll
-    for (int i = 0; i < kMaxBlk; ++i) {
-      const int blk = t + 128 * i;
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (blk < nb) v = *reinterpret_cast<const uint4*>(row + blk * 16 + h * 8);
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(hv[e]);
+        r[2 * e] = f.x;
+        r[2 * e + 1] = f.y;
+      }
+    }
+    float amax = 0.f;
+    if (BY_TOKEN) {  // the whole row's amax (every slice's CTA reads the row: it is L2-resident)
+      for (int j = t; j < nhb; j += kPlaneThreads) {
+        const uint4 v = *reinterpret_cast<const uint4*>(row + j * 8);
         const __half2* hv = reinterpret_cast<const __half2*>(&v);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 f = __half22float2(hv[e]);
-          r[i][h * 8 + 2 * e] = f.x;
-          r[i][h * 8 + 2 * e + 1] = f.y;
+          amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
         }
       }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      if (lane == 0) red[warp] = amax;
     }
-#pragma unroll 1
+    __syncthreads();
+    const int nd = n_dst;
+    if (nd == 0) continue;
+    if (BY_TOKEN) {
+      amax = red[0];
+#pragma unroll
+      for (int w = 1; w < kPlaneThreads / 32; ++w) amax = fmaxf(amax, red[w]);
+    } else {
+      amax = __uint_as_float(rowmax[dst_pos[0]]);
+    }
+    const float g = amax / (6.f * 448.f);
+    const float inv_g = g > 0.f ? 1.f / g : 0.f;
+#pragma unroll
     for (int p = 0; p < kP; ++p) {
-      float m = 0.f;
+      float bm = 0.f;
 #pragma unroll
-      for (int i = 0; i < kMaxBlk; ++i)
+      for (int e = 0; e < 8; ++e) bm = fmaxf(bm, fabsf(r[e]));
+      bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 1));  // the other half of the block
+      const uint32_t sc = own ? e4m3_rn(bm / 6.f * inv_g) : 0u;
+      const float scale = e4m3_value(sc) * g;
+      const float rs = scale > 0.f ? 1.f / scale : 0.f;
+      uint32_t w = 0u;
 #pragma unroll
-        for (int e = 0; e < 16; ++e) m = fmaxf(m, fabsf(r[i][e]));
-#pragma unroll
-      for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      if (lane == 0) red[warp] = m;
-      __syncthreads();
-      const float amax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-      __syncthreads();
-      const float g = amax / (6.f * 448.f);
-      const float inv_g = g > 0.f ? 1.f / g : 0.f;
-      const int mrow = p * kRC + n, m0 = mrow & 31, m1 = mrow >> 5;
-#pragma unroll
-      for (int i = 0; i < kMaxBlk; ++i) {
-        const int blk = t + 128 * i;
-        if (blk >= nb) continue;
-        float bm = 0.f;
-#pragma unroll
-        for (int e = 0; e < 16; ++e) bm = fmaxf(bm, fabsf(r[i][e]));
-        const uint32_t sc = e4m3_encode(bm / 6.f * inv_g);
-        const float scale = e4m3_value(sc) * g;
-        const float inv = scale > 0.f ? 1.f / scale : 0.f;
-        uint32_t w[2] = {0u, 0u};
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float v = r[i][e] * inv;
-          const uint32_t code = e2m1_code(fabsf(v)) | (v < 0.f ? 8u : 0u);
-          const float dq = (code & 8u ? -1.f : 1.f) * e2m1_mag(code) * scale;
-          r[i][e] -= dq;
-          w[e >> 3] |= code << (4 * (e & 7));
-        }
-        *reinterpret_cast<uint2*>(planes + (int64_t(p) * plane_rows + pos) * (K / 2) + blk * 8) = make_uint2(w[0], w[1]);
-        sfb[(int64_t(c) * n_ks + (blk >> 2)) * 512 + m0 * 16 + m1 * 4 + (blk & 3)] = uint8_t(sc);
+      for (int e = 0; e < 8; ++e) {
+        const float v = r[e] * rs;
+        const float q = e2m1_round(fabsf(v));
+        r[e] -= copysignf(q, v) * scale;
+        w |= (e2m1_code_of(q) | (v < 0.f ? 8u : 0u)) << (4 * e);
       }
-      if (t == 0) gx[int64_t(p) * plane_rows + pos] = g;
+      // the four scale bytes of blocks 4j .. 4j + 3 as one word from lane 8j
+      uint32_t word = sc;
+      word |= __shfl_down_sync(0xffffffffu, sc, 2) << 8;
+      word |= __shfl_down_sync(0xffffffffu, sc, 4) << 16;
+      word |= __shfl_down_sync(0xffffffffu, sc, 6) << 24;
+      if (own) {
+        for (int d = 0; d < nd; ++d) {
+          const int pos = dst_pos[d];
+          *reinterpret_cast<uint32_t*>(planes + (int64_t(pos) * kP + p) * (K / 2) + hb * 4) = w;
+          if ((hb & 7) == 0) {
+            const int mr = dst_n[d] * kP + p;
+            *reinterpret_cast<uint32_t*>(sfb + dst_sf[d] + (blk >> 2) * 512 + (mr & 31) * 16 + (mr >> 5) * 4) = word;
+          }
+        }
+      }
     }
+    if (blockIdx.y == 0 && t < nd) {
+      gx[dst_pos[t]] = g;
+      if (BY_TOKEN) rowmax[dst_pos[t]] = 0u;  // the W13 epilogue takes the W2 row maxima afresh
+    }
+  }
+}
+
+// --------------------------------------------------------------- combine
+// out[t] = sum over slots, in slot order, of fma(f32(y2[route]), w[route]):
+// the fused combine's arithmetic, with a route that has no expert (sorted
+// past the last bank, inv[route] >= end) taken as a zero row.  Thread: 4
+// consecutive columns of a token.
+__global__ void fp4_combine_kernel(const __half* __restrict__ y2, const int32_t* __restrict__ inv,
+                                   const int32_t* __restrict__ bank_range, int n_banks, const float* __restrict__ w,
+                                   int T, int k, int H, float* __restrict__ out) {
+  const int per_row = H / 4;
+  const int end = bank_range[2 * (n_banks - 1) + 1];
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < int64_t(T) * per_row;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int t = int(i / per_row), c = int(i % per_row) * 4;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    for (int slot = 0; slot < k; ++slot) {
+      const int route = t * k + slot;
+      const float wr = w[route];
+      uint2 v = make_uint2(0u, 0u);
+      if (inv[route] < end) v = *reinterpret_cast<const uint2*>(y2 + int64_t(route) * H + c);
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+      s0 = __fmaf_rn(a.x, wr, s0);
+      s1 = __fmaf_rn(a.y, wr, s1);
+      s2 = __fmaf_rn(b.x, wr, s2);
+      s3 = __fmaf_rn(b.y, wr, s3);
+    }
+    *reinterpret_cast<float4*>(out + int64_t(t) * H + c) = make_float4(s0, s1, s2, s3);
   }
 }
 
 // --------------------------------------------------------------- prepack
-// NVFP4 scales [slot][rows][K/16] -> blocked [slot][rows/128][K/64][512]:
-// byte m0 * 16 + m1 * 4 + s of block (rb, ks) = scale of row rb * 128 + m1 * 32 + m0, K block 4 ks + s.
-__global__ void fp4_block_scales_kernel(const uint8_t* __restrict__ sc, int64_t n_rows, int K, uint8_t* __restrict__ out) {
-  const int kb16 = K / 16, n_ks = K / 64;
-  const int64_t total = n_rows * kb16;
-  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
-    const int64_t r = i / kb16;
-    const int kb = int(i % kb16);
-    const int64_t rb = r >> 7;
-    const int m = int(r & 127), m0 = m & 31, m1 = m >> 5;
-    out[(rb * n_ks + (kb >> 2)) * 512 + m0 * 16 + m1 * 4 + (kb & 3)] = sc[i];
+// NVFP4 codes [slot][rows][K/2] and E4M3 scales [slot][rows][K/16] -> weight
+// units [slot][rt][kt], one bulk copy each: the unit's tiles (W13: the gate
+// tile, rows rt * 128 .. of W1, then the up tile, the same rows of W3; W2:
+// rows rt * 256 .. and rt * 256 + 128 ..) of
+// 128 rows x 128 bytes of codes in the 128-byte swizzled order the MMA reads
+// (16-byte chunk c of row r at r * 128 + ((c ^ (r & 7)) << 4)), then per tile
+// its four 512-byte scale blocks (byte m0 * 16 + m1 * 4 + s of block q = the
+// scale of row m1 * 32 + m0, 16-wide K block 4 q + s of the tile).
+__global__ void fp4_tile_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ scales, int n_slots,
+                                int rows_per_slot, int K, int n_tiles, int n_rt, int rt_rows, int tile_rows,
+                                uint8_t* __restrict__ out) {
+  const int n_kt = K / 256;
+  const int64_t unit_bytes = int64_t(n_tiles) * (kATile + kSFBytes);
+  const int64_t n_units = int64_t(n_slots) * n_rt * n_kt;
+  for (int64_t u = blockIdx.x; u < n_units; u += gridDim.x) {
+    const int kt = int(u % n_kt), rt = int((u / n_kt) % n_rt);
+    const int64_t slot = u / (int64_t(n_kt) * n_rt);
+    uint8_t* dst = out + u * unit_bytes;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int64_t row0 = slot * rows_per_slot + int64_t(rt) * rt_rows + int64_t(j) * tile_rows;
+      for (int i = threadIdx.x; i < 128 * 8; i += blockDim.x) {
+        const int r = i >> 3, c = i & 7;
+        const uint4 v = *reinterpret_cast<const uint4*>(codes + (row0 + r) * (K / 2) + kt * 128 + c * 16);
+        *reinterpret_cast<uint4*>(dst + j * kATile + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+      }
+      for (int i = threadIdx.x; i < 128 * 4; i += blockDim.x) {
+        const int r = i >> 2, q = i & 3;
+        const uint32_t v = *reinterpret_cast<const uint32_t*>(scales + (row0 + r) * (K / 16) + kt * 16 + q * 4);
+        *reinterpret_cast<uint32_t*>(dst + n_tiles * kATile + j * kSFBytes + q * 512 + (r & 31) * 16 + (r >> 5) * 4) = v;
+      }
+    }
   }
 }
 
-template <int EPI>
-int launch_fp4_one(cudaStream_t s, const Fp4Args& a, const void* map_w, const void* map_x, int grid) {
-  const size_t smem = 1024 + size_t(kStages) * kStage + 64 * 8;
+template <int EPI, int TILES>
+int launch_fp4_one(cudaStream_t s, const Fp4Args& a, const void* map_x, int grid) {
+  const size_t smem = Fp4Stage<TILES>::kSmem;
   static std::atomic<uint64_t> attr_set{0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return -1;
   if (!(attr_set.load() >> dev & 1)) {
-    if (cudaFuncSetAttribute(fp4_gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
+    if (cudaFuncSetAttribute(fp4_gemm_kernel<EPI, TILES>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
         cudaSuccess)
       return -1;
     attr_set.fetch_or(uint64_t(1) << dev);
   }
-  fp4_gemm_kernel<EPI><<<grid, kThreads, smem, s>>>(a, *static_cast<const CUtensorMap*>(map_w),
-                                                    *static_cast<const CUtensorMap*>(map_x));
+  fp4_gemm_kernel<EPI, TILES><<<grid, kThreads, smem, s>>>(a, *static_cast<const CUtensorMap*>(map_x));
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 }  // namespace
 
-int launch_fp4_gemm(cudaStream_t s, int epi, const Fp4Args& a, const void* map_w, const void* map_x, int grid) {
-  return epi == 0 ? launch_fp4_one<0>(s, a, map_w, map_x, grid) : launch_fp4_one<1>(s, a, map_w, map_x, grid);
+int launch_fp4_gemm(cudaStream_t s, int epi, const Fp4Args& a, const void* map_x, int grid) {
+  // W2 items take two adjacent 128-row tiles, as W13 items take a gate and an up tile
+  return epi == 0 ? launch_fp4_one<0, 2>(s, a, map_x, grid) : launch_fp4_one<1, 2>(s, a, map_x, grid);
 }
 
 int launch_fp4_planes(cudaStream_t s, bool by_token, const __half* src, int64_t src_stride, int K,
-                      const int32_t* perm, int top_k, const Chunk* chunks, const int32_t* n_chunks, int bank,
-                      const int32_t* bank_range, int max_rows, uint8_t* planes, int plane_rows, uint8_t* sfb,
-                      float* gx) {
-  if (K % 256 || K > 128 * 16 * 4) return -1;
-  const int blocks = std::max(1, std::min(max_rows, 148 * 16));
+                      const int32_t* inv, int top_k, const int32_t* chunk_of, int bank,
+                      const int32_t* bank_range, int max_rows, uint32_t* rowmax, uint8_t* planes, int plane_rows,
+                      uint8_t* sfb, float* gx) {
+  // max_rows: the token rows (by_token) or the bound on the bank's positions
+  if (K % 256 || top_k > 32) return -1;
+  const dim3 grid(std::max(1, std::min(max_rows, 148 * 8)), (K + kSlice - 1) / kSlice);
   if (by_token)
-    fp4_planes_kernel<1><<<blocks, 128, 0, s>>>(src, src_stride, K, perm, top_k, chunks, n_chunks, bank, bank_range,
-                                                planes, plane_rows, sfb, gx);
+    fp4_planes_kernel<1><<<grid, kPlaneThreads, 0, s>>>(src, src_stride, K, inv, top_k, chunk_of, bank, bank_range,
+                                                        max_rows, rowmax, planes, plane_rows, sfb, gx);
   else
-    fp4_planes_kernel<0><<<blocks, 128, 0, s>>>(src, src_stride, K, perm, top_k, chunks, n_chunks, bank, bank_range,
-                                                planes, plane_rows, sfb, gx);
+    fp4_planes_kernel<0><<<grid, kPlaneThreads, 0, s>>>(src, src_stride, K, inv, top_k, chunk_of, bank, bank_range,
+                                                        0, rowmax, planes, plane_rows, sfb, gx);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
-int launch_fp4_block_scales(cudaStream_t s, const uint8_t* scales, int64_t n_rows, int K, uint8_t* out) {
-  if (n_rows % 128 || K % 64) return -1;
-  const int64_t total = n_rows * (K / 16);
-  const int blocks = int(std::min<int64_t>((total + 255) / 256, 148 * 32));
-  fp4_block_scales_kernel<<<std::max(blocks, 1), 256, 0, s>>>(scales, n_rows, K, out);
+int launch_fp4_combine(cudaStream_t s, const __half* y2, const int32_t* inv, const int32_t* bank_range, int n_banks,
+                       const float* w, int T, int k, int H, float* out) {
+  if (H % 4 || T < 1) return -1;
+  const int64_t n = int64_t(T) * (H / 4);
+  const int blocks = int(std::min<int64_t>((n + 255) / 256, 148 * 16));
+  fp4_combine_kernel<<<std::max(blocks, 1), 256, 0, s>>>(y2, inv, bank_range, n_banks, w, T, k, H, out);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int launch_fp4_tile(cudaStream_t s, const uint8_t* codes, const uint8_t* scales, int n_slots, int rows_per_slot,
+                    int K, bool gate_up, uint8_t* out) {
+  // W13 (gate_up): tile 0 = rows rt * 128 .. of W1, tile 1 the same rows of W3;
+  // W2: tiles 0 and 1 = rows rt * 256 .. and rt * 256 + 128 ..
+  if (K % 256 || rows_per_slot % 256 || n_slots < 1) return -1;
+  const int n_rt = rows_per_slot / 256;
+  const int64_t units = int64_t(n_slots) * n_rt * (K / 256);
+  const int blocks = int(std::min<int64_t>(units, 148 * 8));
+  fp4_tile_kernel<<<blocks, 256, 0, s>>>(codes, scales, n_slots, rows_per_slot, K, 2, n_rt, gate_up ? 128 : 256,
+                                         gate_up ? rows_per_slot / 2 : 128, out);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

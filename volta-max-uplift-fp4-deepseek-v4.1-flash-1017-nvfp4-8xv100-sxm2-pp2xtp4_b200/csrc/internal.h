@@ -56,6 +56,8 @@ struct PlanArgs {
   const int32_t* iq_slot;
   // outputs
   int32_t* perm;        // [n]
+  int32_t* inv;         // optional [n]: sorted position of each route (perm's inverse)
+  int32_t* chunk_of;    // optional [n]: (chunk << 8) | index in chunk, for bank 0's positions
   // product: chunk lists of up to two banks (bank b = keys [key_lo[b], key_hi[b]))
   int n_banks;
   int key_lo[2], key_hi[2], rc[2], max_chunks[2];
@@ -88,15 +90,13 @@ struct PlanArgs {
 
 // Block-scaled FP4 GEMM (tcgen05.mma.kind::mxf4nvf4) of the FP4 bank.
 struct Fp4Args {
-  const uint8_t* sfa;     // weight scales blocked: [slot][row block][K/64][512]
-  int rows_per_slot;      // W13: 2I, W2: H
-  int rb_per_slot;        // rows_per_slot / 128
-  int up_rb;              // W13: I / 128 (row blocks from a gate tile to its up tile), W2: 0
+  const uint8_t* wt;      // weight units [slot][n_rt][K/256] (codes in the swizzled order + blocked scales)
   const float* globals;   // [slot][3] FP32 global scales (NVFP4)
   int K;
-  int n_rt;               // 128-row tiles per item list entry: W13 I/128, W2 H/128
+  int n_rt;               // items per chunk: W13 I/128 (gate + up tiles), W2 H/256 (two row tiles)
   const uint8_t* sfb;     // activation plane scales blocked: [chunk][K/64][512]
-  const float* gx;        // [plane][plane_rows] per-row plane factors
+  const float* gx;        // [plane_rows] per-row plane factor g
+  uint32_t* rowmax;       // W13: [plane_rows] amax (float bits) of each SwiGLU row, for the W2 planes
   int plane_rows;
   const Chunk* chunks;
   const int32_t* n_chunks;
@@ -115,12 +115,15 @@ struct Fp4Args {
   int H;
   uint32_t* err;
 };
-int launch_fp4_gemm(cudaStream_t s, int epi, const Fp4Args& a, const void* map_w, const void* map_x, int grid);
+int launch_fp4_gemm(cudaStream_t s, int epi, const Fp4Args& a, const void* map_x, int grid);
 int launch_fp4_planes(cudaStream_t s, bool by_token, const __half* src, int64_t src_stride, int K,
-                      const int32_t* perm, int top_k, const Chunk* chunks, const int32_t* n_chunks, int bank,
-                      const int32_t* bank_range, int max_rows, uint8_t* planes, int plane_rows, uint8_t* sfb,
-                      float* gx);
-int launch_fp4_block_scales(cudaStream_t s, const uint8_t* scales, int64_t n_rows, int K, uint8_t* out);
+                      const int32_t* inv, int top_k, const int32_t* chunk_of, int bank,
+                      const int32_t* bank_range, int max_rows, uint32_t* rowmax, uint8_t* planes, int plane_rows,
+                      uint8_t* sfb, float* gx);
+int launch_fp4_combine(cudaStream_t s, const __half* y2, const int32_t* inv, const int32_t* bank_range, int n_banks,
+                       const float* w, int T, int k, int H, float* out);
+int launch_fp4_tile(cudaStream_t s, const uint8_t* codes, const uint8_t* scales, int n_slots, int rows_per_slot,
+                    int K, bool gate_up, uint8_t* out);
 // 2D uint8 TMA map with 128-byte swizzle: rows x row_bytes, box box_bytes x box_rows, zero fill out of range
 int make_u8_tile_map(void* map_out, const void* base, int64_t rows, int64_t row_bytes, int box_bytes, int box_rows);
 

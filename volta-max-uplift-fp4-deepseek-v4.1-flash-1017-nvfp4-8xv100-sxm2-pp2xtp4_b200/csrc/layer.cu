@@ -54,13 +54,14 @@ struct b200moe_layer {
   void* dbg_y13 = nullptr;
   // FP4 bank on the block-scaled tensor path (prefill_gemm = 2): natural NVFP4 codes and
   // blocked scales per projection, the activation planes, their blocked scales and factors
-  uint8_t* f4_codes[2] = {nullptr, nullptr};  // W13 [n][2I][H/2], W2 [n][H][I/2]
-  uint8_t* f4_sf[2] = {nullptr, nullptr};     // [n][rows/128][K/64][512]
-  uint8_t* f4_planes[2] = {nullptr, nullptr}; // [P][plane_rows][K/2]
+  uint8_t* f4_units[2] = {nullptr, nullptr};  // weight units [n][K/256 tiles of 128 rows]: W13, W2
+  uint8_t* f4_planes[2] = {nullptr, nullptr}; // [plane_rows][P][K/2]
   uint8_t* f4_sfb[2] = {nullptr, nullptr};    // [f4_max_chunks][K/64][512]
   float* f4_gx[2] = {nullptr, nullptr};       // [P][plane_rows]
+  int32_t* f4_inv = nullptr;                   // [s_max]: sorted position of each route
+  int32_t* f4_chunk_of = nullptr;              // [s_max]: (chunk << 8) | index in chunk of an FP4-bank position
+  uint32_t* f4_rowmax = nullptr;               // [plane_rows]: amax bits of each SwiGLU row (W2 planes)
   int f4_plane_rows = 0, f4_max_chunks = 0;
-  alignas(128) unsigned char f4_map_w[2][128] = {};
   alignas(128) unsigned char f4_map_x[2][128] = {};
   // prefill on tcgen05: permuted fp16 token rows and the TMA maps of the two B operands
   __half* xperm = nullptr;
@@ -104,8 +105,9 @@ void free_layer(b200moe_layer* L) {
   void* ptrs[] = {L->bank[0], L->bank[1], L->globals, L->span, L->iq2_tables, L->key_of_expert, L->perm,
                   L->w_eff, L->chunks[0], L->chunks[1], L->n_chunks, L->x16, L->inter, L->y2,
                   L->counters, L->err, L->xperm, L->ks_sel, L->bank_range, L->xq, L->interq,
-                  L->f4_codes[0], L->f4_codes[1], L->f4_sf[0], L->f4_sf[1], L->f4_planes[0], L->f4_planes[1],
-                  L->f4_sfb[0], L->f4_sfb[1], L->f4_gx[0], L->f4_gx[1]};
+                  L->f4_units[0], L->f4_units[1], L->f4_planes[0], L->f4_planes[1],
+                  L->f4_sfb[0], L->f4_sfb[1], L->f4_gx[0], L->f4_gx[1], L->f4_inv,
+                  L->f4_chunk_of, L->f4_rowmax};
   for (void* p : ptrs)
     if (p) cudaFree(p);
 }
@@ -237,6 +239,7 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   const bool tc = !rows && prefill && c.prefill_gemm == 1 && c.n_fp4 > 0 && L->xperm;
   const bool f4 = c.prefill_gemm == 2 && c.n_fp4 > 0;
   if (f4 && (rows || ws.y2 != L->y2)) return B200MOE_ERR_STATE;  // rows mode and the static array: GEMV banks only
+  if (f4) ws.counters = nullptr;  // W2 writes y2 rows only; one combine launch follows
   PlanArgs p{};
   p.ids = ids;
   p.n = S;
@@ -245,6 +248,8 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   p.key_of_expert = L->key_of_expert;
   p.n_keys = c.n_fp4 + c.n_iq2;
   p.perm = ws.perm;
+  p.inv = f4 ? L->f4_inv : nullptr;
+  p.chunk_of = f4 ? L->f4_chunk_of : nullptr;
   p.n_banks = 2;
   p.key_lo[0] = 0;
   p.key_hi[0] = c.n_fp4;
@@ -277,8 +282,9 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   for (int epi = 0; epi < 2; ++epi) {
     if (f4) {  // the FP4 bank's activation rows as E2M1 planes for its block-scaled GEMM
       if (launch_fp4_planes(s, epi == 0, epi == 0 ? xsrc : ws.inter, epi == 0 ? c.hidden : c.inter,
-                            epi == 0 ? c.hidden : c.inter, ws.perm, c.top_k, ws.chunks[0], ws.n_chunks, 0,
-                            ws.bank_range, S, L->f4_planes[epi], L->f4_plane_rows, L->f4_sfb[epi], L->f4_gx[epi]))
+                            epi == 0 ? c.hidden : c.inter, L->f4_inv, c.top_k, L->f4_chunk_of, 0,
+                            ws.bank_range, epi == 0 ? m : S, L->f4_rowmax, L->f4_planes[epi], L->f4_plane_rows,
+                            L->f4_sfb[epi], L->f4_gx[epi]))
         return B200MOE_ERR_CUDA;
       marks.mark();
     }
@@ -291,15 +297,13 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
       if (n_slots == 0) continue;
       if (f4 && b == 0) {
         Fp4Args f{};
-        f.sfa = L->f4_sf[epi];
-        f.rows_per_slot = epi == 0 ? 2 * c.inter : c.hidden;
-        f.rb_per_slot = f.rows_per_slot / 128;
-        f.up_rb = epi == 0 ? c.inter / 128 : 0;
+        f.wt = L->f4_units[epi];
         f.globals = L->globals;
         f.K = epi == 0 ? c.hidden : c.inter;
-        f.n_rt = epi == 0 ? c.inter / 128 : c.hidden / 128;
+        f.n_rt = epi == 0 ? c.inter / 128 : c.hidden / 256;  // items of two 128-row tiles
         f.sfb = L->f4_sfb[epi];
         f.gx = L->f4_gx[epi];
+        f.rowmax = L->f4_rowmax;
         f.plane_rows = L->f4_plane_rows;
         f.chunks = ws.chunks[0];
         f.n_chunks = ws.n_chunks;
@@ -317,7 +321,7 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
         f.out = out;
         f.H = c.hidden;
         f.err = L->err;
-        if (launch_fp4_gemm(s, epi, f, L->f4_map_w[epi], L->f4_map_x[epi], L->grid)) return B200MOE_ERR_CUDA;
+        if (launch_fp4_gemm(s, epi, f, L->f4_map_x[epi], L->grid)) return B200MOE_ERR_CUDA;
         marks.mark();
         continue;
       }
@@ -386,6 +390,12 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
       marks.mark();
     }
   }
+  if (f4) {
+    if (launch_fp4_combine(s, static_cast<const __half*>(ws.y2), L->f4_inv, ws.bank_range, 2, ws.w_eff, m, c.top_k,
+                           c.hidden, out))
+      return B200MOE_ERR_CUDA;
+    marks.mark();
+  }
   return B200MOE_OK;
 }
 
@@ -448,10 +458,8 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
   take(dalloc(&L->bank[0], f4 ? size_t(0) : size_t(c.n_fp4) * L->geom[0].slot_bytes));
   if (f4 && c.n_fp4 > 0) {
     const size_t H = c.hidden, I = c.inter, n = c.n_fp4;
-    take(dalloc(&L->f4_codes[0], n * 2 * I * H / 2));
-    take(dalloc(&L->f4_codes[1], n * H * I / 2));
-    take(dalloc(&L->f4_sf[0], n * 2 * I * H / 16));
-    take(dalloc(&L->f4_sf[1], n * H * I / 16));
+    take(dalloc(&L->f4_units[0], n * 2 * I * (H / 2 + H / 16)));
+    take(dalloc(&L->f4_units[1], n * H * (I / 2 + I / 16)));
   }
   take(dalloc(&L->bank[1], size_t(c.n_iq2) * L->geom[1].slot_bytes));
   take(dalloc(&L->globals, size_t(std::max(c.n_fp4, 1)) * 3));
@@ -482,13 +490,14 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
     take(dalloc(&L->f4_planes[1], P * R * I / 2));
     take(dalloc(&L->f4_sfb[0], size_t(L->f4_max_chunks) * (H / 64) * 512));
     take(dalloc(&L->f4_sfb[1], size_t(L->f4_max_chunks) * (I / 64) * 512));
-    take(dalloc(&L->f4_gx[0], P * R));
-    take(dalloc(&L->f4_gx[1], P * R));
+    take(dalloc(&L->f4_gx[0], R));
+    take(dalloc(&L->f4_gx[1], R));
+    take(dalloc(&L->f4_inv, size_t(L->s_max)));
+    take(dalloc(&L->f4_chunk_of, size_t(L->s_max)));
+    take(dalloc(&L->f4_rowmax, R));
     if (st == B200MOE_OK &&
-        (make_u8_tile_map(L->f4_map_w[0], L->f4_codes[0], int64_t(c.n_fp4) * 2 * I, H / 2, 128, 128) ||
-         make_u8_tile_map(L->f4_map_w[1], L->f4_codes[1], int64_t(c.n_fp4) * H, I / 2, 128, 128) ||
-         make_u8_tile_map(L->f4_map_x[0], L->f4_planes[0], int64_t(P * R), H / 2, 128, kFp4TcRoutes) ||
-         make_u8_tile_map(L->f4_map_x[1], L->f4_planes[1], int64_t(P * R), I / 2, 128, kFp4TcRoutes)))
+        (make_u8_tile_map(L->f4_map_x[0], L->f4_planes[0], int64_t(P * R), H / 2, 128, kFp4TcRoutes * kFp4Planes) ||
+         make_u8_tile_map(L->f4_map_x[1], L->f4_planes[1], int64_t(P * R), I / 2, 128, kFp4TcRoutes * kFp4Planes)))
       st = B200MOE_ERR_CUDA;
   }
   if (c.prefill_gemm == 1 && c.max_prefill_tokens > 0 && c.n_fp4 > 0) {
@@ -586,15 +595,10 @@ int b200moe_load_fp4(b200moe_layer* L, void* stream, int slot_begin, int n, cons
   if (c.fp4_format == B200MOE_NVFP4 &&
       cudaMemcpyAsync(gdst, globals, size_t(n) * 12, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
     return B200MOE_ERR_CUDA;
-  if (c.prefill_gemm == 2) {  // natural codes, scales re-blocked for tcgen05.cp
+  if (c.prefill_gemm == 2) {  // weight units for the block-scaled tensor path
     const size_t H = c.hidden, I = c.inter, b = size_t(slot_begin);
-    if (cudaMemcpyAsync(L->f4_codes[0] + b * 2 * I * H / 2, w13c, size_t(n) * 2 * I * H / 2, cudaMemcpyDeviceToDevice,
-                        s) != cudaSuccess ||
-        cudaMemcpyAsync(L->f4_codes[1] + b * H * I / 2, w2c, size_t(n) * H * I / 2, cudaMemcpyDeviceToDevice, s) !=
-            cudaSuccess)
-      return B200MOE_ERR_CUDA;
-    if (launch_fp4_block_scales(s, w13s, int64_t(n) * 2 * I, int(H), L->f4_sf[0] + b * 2 * I * H / 16) ||
-        launch_fp4_block_scales(s, w2s, int64_t(n) * H, int(I), L->f4_sf[1] + b * H * I / 16))
+    if (launch_fp4_tile(s, w13c, w13s, n, int(2 * I), int(H), true, L->f4_units[0] + b * 2 * I * (H / 2 + H / 16)) ||
+        launch_fp4_tile(s, w2c, w2s, n, int(H), int(I), false, L->f4_units[1] + b * H * (I / 2 + I / 16)))
       return B200MOE_ERR_CUDA;
     return B200MOE_OK;
   }

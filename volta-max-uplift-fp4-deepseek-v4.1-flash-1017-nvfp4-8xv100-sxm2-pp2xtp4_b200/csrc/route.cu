@@ -128,6 +128,7 @@ __device__ void plan_small(const PlanArgs& a, int n, int sentinel) {
     }
   const int pkey = lane < n ? (c >> 5) : 0x7fff, route = c & 31;
   if (lane < n) a.perm[lane] = route;
+  if (lane < n && a.inv) a.inv[route] = lane;
   const int prev = __shfl_up_sync(full, pkey, 1);
   const bool starts = lane < n && (lane == 0 || prev != pkey);
   const unsigned smask = __ballot_sync(full, starts);
@@ -193,6 +194,8 @@ __device__ void plan_small(const PlanArgs& a, int n, int sentinel) {
         ch.count = min(rc, count - off);
         ch.pad = 0;
         a.chunks[b][ci] = ch;
+        if (a.chunk_of && b == 0)
+          for (int j = 0; j < ch.count; ++j) a.chunk_of[ch.begin + j] = (ci << 8) | j;
       }
     }
     if (lane == 0) {
@@ -257,6 +260,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanArgs a) {
       const int rank = __popc(mask & ((1u << lane) - 1u));
       const int pos = start[key] + hist[warp * nk + key] + rank;
       a.perm[pos] = i;
+      if (a.inv) a.inv[i] = pos;
       if (product && a.w_eff) a.w_eff[i] = key < a.n_keys ? a.w_in[i] : 0.f;
       if (a.iq_out) a.iq_out[i] = a.iq_slot[a.ids[i]];
     }
@@ -341,6 +345,8 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanArgs a) {
             ch.count = min(rc, cnt - off);
             ch.pad = 0;
             a.chunks[b][c] = ch;
+            if (a.chunk_of && b == 0)
+              for (int j = 0; j < ch.count; ++j) a.chunk_of[ch.begin + j] = (c << 8) | j;
           }
         }
       }
