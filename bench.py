@@ -98,6 +98,9 @@ def parse():
     ap.add_argument("--split-k", type=int, default=0,
                     help="fix the GEMV split-K (0 = chosen per call; set only to give a small ncu capture "
                          "the split-K of the full-size run)")
+    ap.add_argument("--gemm", choices=["fp4", "gemv"], default="fp4",
+                    help="c1, c4: the NVFP4 bank on the block-scaled FP4 tensor path (tcgen05.mma "
+                         "kind::mxf4nvf4, default) or on the skinny GEMV")
     ap.add_argument("--profile", action="store_true",
                     help="warm-up + timed steps only (no per-launch, e2e or CPU passes): the ncu command")
     a = ap.parse_args()
@@ -171,13 +174,13 @@ class Clocks:
                 "samples": len(self.samples), "source": "nvml, polled every 2 ms during the timed region"}
 
 
-def measured_traffic(distinct: int) -> dict | None:
+def measured_traffic(distinct: int, summary: str = "gemv_w13_c1_decode.md") -> dict | None:
     """DRAM bytes of one W13 launch from the committed ncu summary
     (dram__bytes_read.sum + dram__bytes_write.sum of this bench's W13 launch),
     scaled from the captured routing's distinct experts to this one's."""
     import re
 
-    p = ROOT / "profiles" / "gemv_w13_c1_decode.md"
+    p = ROOT / "profiles" / summary
     if not p.exists():
         return None
     txt = p.read_text()
@@ -187,7 +190,7 @@ def measured_traffic(distinct: int) -> dict | None:
         return None
     b, d = float(m1.group(1)), int(m2.group(1))
     return {"bytes": b * distinct / d, "captured_bytes": b, "captured_distinct_experts": d,
-            "source": "profiles/gemv_w13_c1_decode.md (ncu dram__bytes_read.sum + dram__bytes_write.sum)"}
+            "source": f"profiles/{summary} (ncu dram__bytes_read.sum + dram__bytes_write.sum)"}
 
 
 def fp4_expert(bank, j: int, fmt: int) -> dict:
@@ -373,7 +376,11 @@ def run_c1(job) -> None:
     x = torch.randn((m, H), generator=g, device=dev).to(torch.bfloat16)
     logits = torch.randn((m, E), generator=g, device=dev)
     use_graph = not args.eager
+    f4 = args.gemm == "fp4"
     config = {"workload": f"configs[1] decode layer: hidden {H}, {E} experts NVFP4, inter {I}, top-{K_TOP}, M={m}",
+              "gemm": "block-scaled FP4 tensor path (tcgen05.mma kind::mxf4nvf4, E4M3 block scales in TMEM, "
+                      "activations as four E2M1 planes)" if f4 else "skinny GEMV (mma.sync, weights dequantized "
+                                                                     "in registers)",
               "tokens_per_step": m, "hidden": H, "inter": I, "experts": E, "top_k": K_TOP, "format": "nvfp4",
               "l2": "inputs larger than L2 (expert weights streamed per step)" if m >= 32 else
                     "inputs smaller than L2 at this M: weights may stay cached across steps",
@@ -387,7 +394,7 @@ def run_c1(job) -> None:
 
     bank = synth.make_fp4_bank(n_exp, H, I, "nvfp4", 1000, dev)
     layer = moe.B200NativeMoe(hidden=H, inter=I, num_experts=n_exp, top_k=K_TOP, max_tokens=64,
-                              tier=np.zeros(n_exp, np.int8), device=dev)
+                              tier=np.zeros(n_exp, np.int8), device=dev, prefill_gemm="fp4" if f4 else "tcgen05")
     synth.load_bank(layer, bank)
     layer.check_errors()
     if args.split_k:
@@ -421,12 +428,19 @@ def run_c1(job) -> None:
     value = job.world * m / (ms / 1e3)
     del graph
 
-    per = per_launch(layer, step, args.steps, 5)  # convert, plan, W13, W2
-    t_w13_ms, t_w2_ms = float(per[2]), float(per[3])
+    if f4:  # convert, plan, x planes, W13, SwiGLU planes, W2, combine
+        per = per_launch(layer, step, args.steps, 8)
+        t_w13_ms, t_w2_ms = float(per[3]), float(per[5])
+        names = ["convert", "plan", "x_planes", "w13", "swiglu_planes", "w2", "combine"]
+    else:  # convert, plan, W13, W2
+        per = per_launch(layer, step, args.steps, 5)
+        t_w13_ms, t_w2_ms = float(per[2]), float(per[3])
+        names = ["convert", "plan", "w13", "w2"]
     pk = peaks()
     achieved = distinct * W13_BYTES / (t_w13_ms / 1e3) / 1e9
     layer_bytes = distinct * EXPERT_BYTES
-    traffic = measured_traffic(distinct) if n_exp == E else None
+    traffic = measured_traffic(distinct, "fp4_w13_c1_decode.md" if f4 else "gemv_w13_c1_decode.md") \
+        if n_exp == E else None
     e2e_ms, e2e_bytes = e2e_decode(job, layer, x, logits, layer.out[:m], args.steps, use_graph)
 
     cpu = None
@@ -436,7 +450,8 @@ def run_c1(job) -> None:
     if job.rank == 0:
         line = line_base(job, args, "MoE-layer tokens/s (decode M=%d) & %% HBM roofline" % m, value, ms, config)
         line.update({
-            "roofline": {"bound": "hbm", "kernel": "gemv_kernel W13 (+SwiGLU)", "achieved": achieved,
+            "roofline": {"bound": "hbm", "kernel": ("fp4_gemm_kernel" if f4 else "gemv_kernel") + " W13 (+SwiGLU)",
+                         "achieved": achieved,
                          "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
                          "peak_source": pk["source"], "traffic": traffic["bytes"] if traffic else None,
                          "traffic_detail": traffic,
@@ -445,11 +460,11 @@ def run_c1(job) -> None:
             "layer_roofline": {"bytes": layer_bytes, "ms": float(per.sum()),
                                "achieved_gbs": layer_bytes / (per.sum() / 1e3) / 1e9,
                                "frac": layer_bytes / (per.sum() / 1e3) / 1e9 / pk["hbm_gbs"],
-                               "launch_ms": {"convert": float(per[0]), "plan": float(per[1]), "w13": t_w13_ms,
-                                             "w2": t_w2_ms}},
+                               "launch_ms": {k: float(v) for k, v in zip(names, per)}},
             "e2e": dict({"value": job.world * m / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms},
                         **e2e_bytes),
-            "gpu_launches": 5 * args.steps,  # gating, bf16 copy, route plan, W13 (+SwiGLU), W2 (+combine)
+            # gating, bf16 copy, route plan, [x planes], W13 (+SwiGLU), [SwiGLU planes], W2 (+combine), [combine]
+            "gpu_launches": (8 if f4 else 5) * args.steps,
             "cpu_baseline": cpu,
             "clocks": clk,
         })
@@ -695,11 +710,12 @@ def run_c4(job) -> None:
         tier, trank = tiers.zipf_tier(E, C2_HOT, seed=4000 + li)
         if world == 1:
             lay = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, max_tokens=min(T, 64),
-                                    max_prefill_tokens=T, tier=tier, device=dev, prefill_gemm="skinny")
+                                    max_prefill_tokens=T, tier=tier, device=dev,
+                                    prefill_gemm="fp4" if args.gemm == "fp4" else "skinny")
             local = lay
         else:
             lay = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, tokens=T, tier=tier,
-                                       device=dev, peer=peer)
+                                       device=dev, peer=peer, gemm="fp4" if args.gemm == "fp4" else "skinny")
             local = lay.layer
         n_hot, n_iq = int((local.fp4_slot >= 0).sum()), int((local.iq2_slot >= 0).sum())
         if n_hot:
@@ -778,6 +794,8 @@ def run_c4(job) -> None:
         local = lay if world == 1 else lay.layer
         banks = int((local.fp4_slot >= 0).any()) + int((local.iq2_slot >= 0).any())
         launches_per_step += 1 + 2 * banks + (3 if world == 1 else 2) + (5 if world > 1 else 0)
+        if args.gemm == "fp4" and (local.fp4_slot >= 0).any():  # x and SwiGLU planes (+ combine at world 1)
+            launches_per_step += 3 if world == 1 else 2
     pk = peaks()
     achieved = local_bytes / (ms / 1e3) / 1e9
     frac_min = -job.maxall(-achieved / pk["hbm_gbs"])
@@ -846,8 +864,9 @@ def run_expert_parallel(job) -> None:
 
     args, dev, rank, world, m = job.args, job.dev, job.rank, job.world, job.args.m
     tier = np.zeros(E, np.int8)
+    f4 = args.gemm == "fp4"
     layer = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, tokens=m, tier=tier, device=dev,
-                                 exchange=args.exchange)
+                                 exchange=args.exchange, gemm="fp4" if f4 else "skinny")
     n_local = int((layer.layer.fp4_slot >= 0).sum())
     bank = synth.make_fp4_bank(n_local, H, I, "nvfp4", 1000 + rank, dev)
     synth.load_bank(layer.layer, bank)
@@ -880,14 +899,16 @@ def run_expert_parallel(job) -> None:
     del graph
 
     # exposed communication and the local W13 launch (separate pass: these read events every step)
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
-    layer.layer.set_timing_events(evs)  # start, convert, plan, W13, W2 of the local expert run
+    # local expert run: start, convert, plan, [x planes], W13, [SwiGLU planes], W2
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(7 if f4 else 5)]
+    i13 = 3 if f4 else 2
+    layer.layer.set_timing_events(evs)
     comm, w13_ms, used = 0.0, 0.0, 0
     for _ in range(args.steps):
         step()
         torch.cuda.synchronize()
         comm += layer.comm_ms()
-        w13_ms += evs[2].elapsed_time(evs[3])
+        w13_ms += evs[i13].elapsed_time(evs[i13 + 1])
         used += layer.local_experts_used()
     layer.layer.set_timing_events(None)
     comm, w13_ms, used = comm / args.steps, w13_ms / args.steps, used / args.steps
@@ -913,7 +934,8 @@ def run_expert_parallel(job) -> None:
     if rank == 0:
         line = line_base(job, args, "MoE-layer tokens/s (decode M=%d) & %% HBM roofline" % m, value, ms, config)
         line.update({
-            "roofline": {"bound": "hbm", "kernel": "gemv_kernel W13 (+SwiGLU) of rank 0's local experts",
+            "roofline": {"bound": "hbm", "kernel": ("fp4_gemm_kernel" if f4 else "gemv_kernel") +
+                                                   " W13 (+SwiGLU) of rank 0's local experts",
                          "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / pk["hbm_gbs"], "min_frac_over_ranks": frac_min,
                          "peak_source": pk["source"], "traffic": None,
@@ -925,7 +947,8 @@ def run_expert_parallel(job) -> None:
                     "d2h_bytes_per_step": int(hout.numel() * hout.element_size())},
             # p2p: gating; owner plan, push, receive; local plan, W13, W2; return; combine
             # nccl: gating; owner plan, row gather, metadata; local plan, W13, W2, f32->f16; combine
-            "gpu_launches": (9 if args.exchange == "p2p" else 9) * args.steps,
+            # (fp4: + the two plane launches of the local run)
+            "gpu_launches": (9 + (2 if f4 else 0)) * args.steps,
             "cpu_baseline": None,
             "clocks": clk,
         })

@@ -26,8 +26,8 @@ def dev():
     return torch.device("cuda", 0)
 
 
-@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
-def test_ep_world1_matches_layer(dev, pkg, exchange):
+@pytest.mark.parametrize("exchange,gemm", [("p2p", "skinny"), ("nccl", "skinny"), ("p2p", "fp4")])
+def test_ep_world1_matches_layer(dev, pkg, exchange, gemm):
     from b200moe import ep, moe, synth, tiers
 
     H, I, E, K, T = 1024, 512, 64, 6, 48
@@ -35,12 +35,13 @@ def test_ep_world1_matches_layer(dev, pkg, exchange):
     n_hot, n_iq = int((tier == tiers.HOT).sum()), int((tier == tiers.WARM).sum())
     fp4 = synth.make_fp4_bank(n_hot, H, I, "nvfp4", 11, dev)
     iq2 = synth.make_iq2_bank(n_iq, H, I, 12, dev)
-    full = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K, max_tokens=64, tier=tier, device=dev)
+    full = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K, max_tokens=64, tier=tier, device=dev,
+                             prefill_gemm="fp4" if gemm == "fp4" else "tcgen05")
     synth.load_bank(full, fp4)
     full.set_iq2_tables()
     synth.load_bank(full, iq2)
     sharded = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K, tokens=T, tier=tier, device=dev,
-                                   exchange=exchange)
+                                   exchange=exchange, gemm=gemm)
     sharded.set_iq2_tables()
     synth.load_local(sharded.layer, tier, fp4, iq2)
     g = torch.Generator(device=dev).manual_seed(5)

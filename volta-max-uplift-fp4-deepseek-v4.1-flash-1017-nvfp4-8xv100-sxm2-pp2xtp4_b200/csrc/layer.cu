@@ -164,6 +164,7 @@ struct Workspace {
   uint8_t* xq;
   uint8_t* interq;
   void* dbg_y13;
+  bool own = false;  // the layer's own workspace (not the static array)
 };
 
 Workspace layer_workspace(b200moe_layer* L) {
@@ -183,6 +184,7 @@ Workspace layer_workspace(b200moe_layer* L) {
   w.xq = L->xq;
   w.interq = L->interq;
   w.dbg_y13 = L->dbg_y13;
+  w.own = true;
   return w;
 }
 
@@ -238,7 +240,7 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   // prefill with the tcgen05 GEMM: the FP4 bank's chunks are 128-route token tiles
   const bool tc = !rows && prefill && c.prefill_gemm == 1 && c.n_fp4 > 0 && L->xperm;
   const bool f4 = c.prefill_gemm == 2 && c.n_fp4 > 0;
-  if (f4 && (rows || ws.y2 != L->y2)) return B200MOE_ERR_STATE;  // rows mode and the static array: GEMV banks only
+  if (f4 && !ws.own) return B200MOE_ERR_STATE;  // the static array holds no plane buffers
   if (f4) ws.counters = nullptr;  // W2 writes y2 rows only; one combine launch follows
   PlanArgs p{};
   p.ids = ids;
@@ -390,7 +392,7 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
       marks.mark();
     }
   }
-  if (f4) {
+  if (f4 && !rows) {  // (rows mode: the y2 rows are the output)
     if (launch_fp4_combine(s, static_cast<const __half*>(ws.y2), L->f4_inv, ws.bank_range, 2, ws.w_eff, m, c.top_k,
                            c.hidden, out))
       return B200MOE_ERR_CUDA;

@@ -146,13 +146,16 @@ class ExpertParallelMoe:
     """One routed-MoE layer with its experts sharded over a process group.
 
     ``tokens`` bounds the tokens one rank passes per forward.  Local experts
-    run with the skinny kernels (a rank sees few routes per expert at decode).
-    With ``split_k`` fixed here and on a single-GPU layer, the outputs of the
-    two are bit-equal (same per-route rows, same slot-order combine)."""
+    run with the skinny kernels (``gemm="skinny"``, a rank sees few routes per
+    expert at decode) or, for an NVFP4 bank, the block-scaled FP4 tensor path
+    (``gemm="fp4"``).  With ``split_k`` fixed here and on a single-GPU layer of
+    the same ``gemm``, the outputs of the two are bit-equal (same per-route
+    rows, same slot-order combine)."""
 
     def __init__(self, *, hidden: int, inter: int, num_experts: int, top_k: int, tokens: int, tier,
                  fp4_format: str = "nvfp4", group=None, device: torch.device | None = None,
-                 split_k: tuple[int, int] | None = None, exchange: str = "p2p", peer: PeerExchange | None = None):
+                 split_k: tuple[int, int] | None = None, exchange: str = "p2p", peer: PeerExchange | None = None,
+                 gemm: str = "skinny"):
         if exchange not in ("p2p", "nccl"):
             raise ValueError("exchange is 'p2p' or 'nccl'")
         self.exchange = exchange
@@ -169,7 +172,7 @@ class ExpertParallelMoe:
         self.layer = B200NativeMoe(hidden=hidden, inter=inter, num_experts=num_experts, top_k=1,
                                    max_tokens=min(64, r_max), max_prefill_tokens=r_max, tier=self.tier,
                                    fp4_format=fp4_format, device=dev, rank=self.rank, world=self.world,
-                                   prefill_gemm="skinny")
+                                   prefill_gemm=gemm)
         if split_k is not None:
             self.layer.set_split_k(*split_k)
         self.owner = torch.from_numpy(owner_of_expert(num_experts, self.world)).to(dev)
