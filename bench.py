@@ -99,7 +99,7 @@ def parse():
                     help="fix the GEMV split-K (0 = chosen per call; set only to give a small ncu capture "
                          "the split-K of the full-size run)")
     ap.add_argument("--gemm", choices=["fp4", "gemv"], default="fp4",
-                    help="c1, c4: the NVFP4 bank on the block-scaled FP4 tensor path (tcgen05.mma "
+                    help="c1, c2, c4: the NVFP4 bank on the block-scaled FP4 tensor path (tcgen05.mma "
                          "kind::mxf4nvf4, default) or on the skinny GEMV")
     ap.add_argument("--profile", action="store_true",
                     help="warm-up + timed steps only (no per-launch, e2e or CPU passes): the ncu command")
@@ -498,7 +498,9 @@ def run_c2(job) -> None:
 
     args, dev, m = job.args, job.dev, job.args.m
     tier, tier_rank = tiers.zipf_tier(E, C2_HOT, seed=2)
-    layer = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, max_tokens=64, tier=tier, device=dev)
+    f4 = args.gemm == "fp4"
+    layer = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, max_tokens=64, tier=tier, device=dev,
+                              prefill_gemm="fp4" if f4 else "tcgen05")
     fp4 = synth.make_fp4_bank(C2_HOT, H, I, "nvfp4", 2000, dev)
     synth.load_bank(layer, fp4)
     iq2 = synth.make_iq2_bank(E - C2_HOT, H, I, 2001, dev)
@@ -532,11 +534,17 @@ def run_c2(job) -> None:
     ms, clk = job.timed(run, args.steps)
     layer.check_errors()
     del graph
-    # events: start, convert, x int8 blocks, plan, W13 fp4, W13 iq2, SwiGLU int8 blocks, W2 fp4, W2 iq2
-    per = per_launch(layer, step, args.steps, 9)
+    if f4:  # start, convert, x int8 blocks, plan, x planes, W13 fp4, W13 iq2, SwiGLU planes, SwiGLU int8 blocks,
+        #     W2 fp4, W2 iq2, combine
+        per = per_launch(layer, step, args.steps, 12)
+        i13, i2, extra = (4, 5), (8, 9), {"x_planes": 3, "inter_planes": 6, "inter_int8": 7, "combine": 10}
+    else:  # start, convert, x int8 blocks, plan, W13 fp4, W13 iq2, SwiGLU int8 blocks, W2 fp4, W2 iq2
+        per = per_launch(layer, step, args.steps, 9)
+        i13, i2, extra = (3, 4), (6, 7), {"inter_int8": 5}
     pk = peaks()
-    launches = {"w13_fp4": (per[3], hot_used.size * W13_BYTES), "w13_iq2": (per[4], iq_used.size * IQ_W13_BYTES),
-                "w2_fp4": (per[6], hot_used.size * W2_BYTES), "w2_iq2": (per[7], iq_used.size * IQ_W2_BYTES)}
+    launches = {"w13_fp4": (per[i13[0]], hot_used.size * W13_BYTES),
+                "w13_iq2": (per[i13[1]], iq_used.size * IQ_W13_BYTES),
+                "w2_fp4": (per[i2[0]], hot_used.size * W2_BYTES), "w2_iq2": (per[i2[1]], iq_used.size * IQ_W2_BYTES)}
     dom = max(launches, key=lambda k: launches[k][0])
     t_dom, b_dom = launches[dom]
     achieved = b_dom / (t_dom / 1e3) / 1e9
@@ -550,7 +558,8 @@ def run_c2(job) -> None:
         line = line_base(job, args, "MoE-layer tokens/s (mixed-tier decode M=%d) & %% HBM roofline" % m,
                          job.world * m / (ms / 1e3), ms, config)
         line.update({
-            "roofline": {"bound": "hbm", "kernel": f"gemv_kernel {dom}", "achieved": achieved,
+            "roofline": {"bound": "hbm", "kernel": ("fp4_gemm_kernel " if f4 and dom.endswith("fp4") else
+                                                   "gemv_kernel ") + dom, "achieved": achieved,
                          "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
                          "peak_source": pk["source"], "traffic": None, "algorithmic_bytes_per_launch": b_dom,
                          "launch_ms": t_dom, "distinct_hot": int(hot_used.size), "distinct_iq2": int(iq_used.size)},
@@ -558,12 +567,13 @@ def run_c2(job) -> None:
                                "achieved_gbs": layer_bytes / (per.sum() / 1e3) / 1e9,
                                "frac": layer_bytes / (per.sum() / 1e3) / 1e9 / pk["hbm_gbs"],
                                "launch_ms": {"convert": float(per[0]), "x_int8": float(per[1]), "plan": float(per[2]),
-                                             "inter_int8": float(per[5]),
+                                             **{k: float(per[v]) for k, v in extra.items()},
                                              **{k: float(v[0]) for k, v in launches.items()}}},
             "e2e": dict({"value": job.world * m / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms},
                         **e2e_bytes),
             # gating, bf16 copy, x int8 blocks, plan, W13 x 2 banks, SwiGLU int8 blocks, W2 x 2 banks
-            "gpu_launches": 9 * args.steps,
+            # (fp4: + x planes, SwiGLU planes, combine)
+            "gpu_launches": (12 if f4 else 9) * args.steps,
             "cpu_baseline": cpu,
             "clocks": clk,
         })
@@ -837,7 +847,9 @@ def run_c4(job) -> None:
         line["steps"] = steps
         line["scaling"] = "strong"
         line.update({
-            "roofline": {"bound": "hbm", "kernel": "all GEMV launches of the stack on rank 0 (whole step)",
+            "roofline": {"bound": "hbm", "kernel": "all expert launches of the stack on rank 0 (whole step: " +
+                         ("fp4_gemm_kernel for the NVFP4 bank, gemv_kernel for IQ2)" if args.gemm == "fp4" else
+                          "gemv_kernel for both banks)"),
                          "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / pk["hbm_gbs"], "min_frac_over_ranks": frac_min,
                          "peak_source": pk["source"], "traffic": None, "algorithmic_bytes_per_step": local_bytes},
