@@ -650,7 +650,7 @@ def run_c3(job) -> None:
     steps = max(3, args.steps // 10)
     ms, clk = job.timed(step, steps)
     layer.check_errors()
-    per = per_launch(layer, step, steps, 6)  # convert, plan, gather, W13, W2
+    per = per_launch(layer, step, steps, 7)  # convert, plan, gather, W13, W2, combine
     pk = peaks()
     routes = T * K_TOP
     f13, f2 = 2.0 * routes * H * 2 * I, 2.0 * routes * I * H
@@ -690,11 +690,12 @@ def run_c3(job) -> None:
                                "tensor_frac": layer_flops / (per.sum() / 1e3) / 1e12 / pk["bf16_tflops"],
                                "hbm_frac": layer_bytes / (per.sum() / 1e3) / 1e9 / pk["hbm_gbs"],
                                "launch_ms": {"convert": float(per[0]), "plan": float(per[1]),
-                                             "gather": float(per[2]), "w13": t13, "w2": t2}},
+                                             "gather": float(per[2]), "w13": t13, "w2": t2,
+                                             "combine": float(per[5])}},
             "e2e": {"value": job.world * T / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": int(hx.numel() * 2 + hl.numel() * 4),
                     "d2h_bytes_per_step": int(hout.numel() * 4)},
-            "gpu_launches": 6 * steps,  # gating, bf16 copy, plan, row gather, W13, W2
+            "gpu_launches": 7 * steps,  # gating, bf16 copy, plan, row gather, W13, W2, combine
             "cpu_baseline": cpu,
             "clocks": clk,
         })

@@ -624,8 +624,8 @@ int launch_fp4_planes(cudaStream_t s, bool by_token, const __half* src, int64_t 
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
-int launch_fp4_combine(cudaStream_t s, const __half* y2, const int32_t* inv, const int32_t* bank_range, int n_banks,
-                       const float* w, int T, int k, int H, float* out) {
+int launch_route_combine(cudaStream_t s, const __half* y2, const int32_t* inv, const int32_t* bank_range,
+                         int n_banks, const float* w, int T, int k, int H, float* out) {
   if (H % 4 || T < 1) return -1;
   const int64_t n = int64_t(T) * (H / 4);
   const int blocks = int(std::min<int64_t>((n + 255) / 256, 148 * 16));

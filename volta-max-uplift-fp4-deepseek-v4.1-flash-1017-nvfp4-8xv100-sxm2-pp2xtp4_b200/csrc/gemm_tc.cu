@@ -429,7 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
       ++acc_i;
-      if (EPI == 1) {
+      if (EPI == 1 && a.counters) {
         // completion count per (token, 32-row tile) of this item's 256 rows
         int* list = lists + quarter * kListInts;
         if (lane == 0) list[0] = 0;

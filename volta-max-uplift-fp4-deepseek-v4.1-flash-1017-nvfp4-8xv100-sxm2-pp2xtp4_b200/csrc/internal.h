@@ -120,8 +120,8 @@ int launch_fp4_planes(cudaStream_t s, bool by_token, const __half* src, int64_t 
                       const int32_t* inv, int top_k, const int32_t* chunk_of, int bank,
                       const int32_t* bank_range, int max_rows, uint32_t* rowmax, uint8_t* planes, int plane_rows,
                       uint8_t* sfb, float* gx);
-int launch_fp4_combine(cudaStream_t s, const __half* y2, const int32_t* inv, const int32_t* bank_range, int n_banks,
-                       const float* w, int T, int k, int H, float* out);
+int launch_route_combine(cudaStream_t s, const __half* y2, const int32_t* inv, const int32_t* bank_range,
+                         int n_banks, const float* w, int T, int k, int H, float* out);
 int launch_fp4_tile(cudaStream_t s, const uint8_t* codes, const uint8_t* scales, int n_slots, int rows_per_slot,
                     int K, bool gate_up, uint8_t* out);
 // 2D uint8 TMA map with 128-byte swizzle: rows x row_bytes, box box_bytes x box_rows, zero fill out of range

@@ -58,7 +58,7 @@ struct b200moe_layer {
   uint8_t* f4_planes[2] = {nullptr, nullptr}; // [plane_rows][P][K/2]
   uint8_t* f4_sfb[2] = {nullptr, nullptr};    // [f4_max_chunks][K/64][512]
   float* f4_gx[2] = {nullptr, nullptr};       // [P][plane_rows]
-  int32_t* f4_inv = nullptr;                   // [s_max]: sorted position of each route
+  int32_t* route_pos = nullptr;                // [s_max]: sorted position of each route (the plan's inverse)
   int32_t* f4_chunk_of = nullptr;              // [s_max]: (chunk << 8) | index in chunk of an FP4-bank position
   uint32_t* f4_rowmax = nullptr;               // [plane_rows]: amax bits of each SwiGLU row (W2 planes)
   int f4_plane_rows = 0, f4_max_chunks = 0;
@@ -106,7 +106,7 @@ void free_layer(b200moe_layer* L) {
                   L->w_eff, L->chunks[0], L->chunks[1], L->n_chunks, L->x16, L->inter, L->y2,
                   L->counters, L->err, L->xperm, L->ks_sel, L->bank_range, L->xq, L->interq,
                   L->f4_units[0], L->f4_units[1], L->f4_planes[0], L->f4_planes[1],
-                  L->f4_sfb[0], L->f4_sfb[1], L->f4_gx[0], L->f4_gx[1], L->f4_inv,
+                  L->f4_sfb[0], L->f4_sfb[1], L->f4_gx[0], L->f4_gx[1], L->route_pos,
                   L->f4_chunk_of, L->f4_rowmax};
   for (void* p : ptrs)
     if (p) cudaFree(p);
@@ -241,7 +241,10 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   const bool tc = !rows && prefill && c.prefill_gemm == 1 && c.n_fp4 > 0 && L->xperm;
   const bool f4 = c.prefill_gemm == 2 && c.n_fp4 > 0;
   if (f4 && !ws.own) return B200MOE_ERR_STATE;  // the static array holds no plane buffers
-  if (f4) ws.counters = nullptr;  // W2 writes y2 rows only; one combine launch follows
+  // the block-scaled path and the tcgen05 prefill write y2 rows only and combine in one launch after W2
+  // (fused into their epilogues the combine's fences, atomics and re-reads stall the pipeline)
+  const bool sep_combine = !rows && (f4 || tc);
+  if (sep_combine) ws.counters = nullptr;
   PlanArgs p{};
   p.ids = ids;
   p.n = S;
@@ -250,7 +253,7 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   p.key_of_expert = L->key_of_expert;
   p.n_keys = c.n_fp4 + c.n_iq2;
   p.perm = ws.perm;
-  p.inv = f4 ? L->f4_inv : nullptr;
+  p.inv = (f4 || tc) ? L->route_pos : nullptr;
   p.chunk_of = f4 ? L->f4_chunk_of : nullptr;
   p.n_banks = 2;
   p.key_lo[0] = 0;
@@ -284,7 +287,7 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   for (int epi = 0; epi < 2; ++epi) {
     if (f4) {  // the FP4 bank's activation rows as E2M1 planes for its block-scaled GEMM
       if (launch_fp4_planes(s, epi == 0, epi == 0 ? xsrc : ws.inter, epi == 0 ? c.hidden : c.inter,
-                            epi == 0 ? c.hidden : c.inter, L->f4_inv, c.top_k, L->f4_chunk_of, 0,
+                            epi == 0 ? c.hidden : c.inter, L->route_pos, c.top_k, L->f4_chunk_of, 0,
                             ws.bank_range, epi == 0 ? m : S, L->f4_rowmax, L->f4_planes[epi], L->f4_plane_rows,
                             L->f4_sfb[epi], L->f4_gx[epi]))
         return B200MOE_ERR_CUDA;
@@ -392,9 +395,9 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
       marks.mark();
     }
   }
-  if (f4 && !rows) {  // (rows mode: the y2 rows are the output)
-    if (launch_fp4_combine(s, static_cast<const __half*>(ws.y2), L->f4_inv, ws.bank_range, 2, ws.w_eff, m, c.top_k,
-                           c.hidden, out))
+  if (sep_combine) {
+    if (launch_route_combine(s, static_cast<const __half*>(ws.y2), L->route_pos, ws.bank_range, 2, ws.w_eff, m,
+                             c.top_k, c.hidden, out))
       return B200MOE_ERR_CUDA;
     marks.mark();
   }
@@ -469,6 +472,7 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
   take(dalloc(&L->iq2_tables, size_t(kIq2TableWords)));
   take(dalloc(&L->key_of_expert, size_t(c.num_experts)));
   take(dalloc(&L->perm, size_t(L->s_max)));
+  take(dalloc(&L->route_pos, size_t(L->s_max)));
   take(dalloc(&L->w_eff, size_t(L->s_max)));
   take(dalloc(&L->chunks[0], size_t(L->max_chunks)));
   take(dalloc(&L->chunks[1], size_t(L->max_chunks)));
@@ -494,7 +498,6 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
     take(dalloc(&L->f4_sfb[1], size_t(L->f4_max_chunks) * (I / 64) * 512));
     take(dalloc(&L->f4_gx[0], R));
     take(dalloc(&L->f4_gx[1], R));
-    take(dalloc(&L->f4_inv, size_t(L->s_max)));
     take(dalloc(&L->f4_chunk_of, size_t(L->s_max)));
     take(dalloc(&L->f4_rowmax, R));
     if (st == B200MOE_OK &&
