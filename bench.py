@@ -432,10 +432,11 @@ def run_c1(job) -> None:
         per = per_launch(layer, step, args.steps, 8)
         t_w13_ms, t_w2_ms = float(per[3]), float(per[5])
         names = ["convert", "plan", "x_planes", "w13", "swiglu_planes", "w2", "combine"]
-    else:  # convert, plan, W13, W2
-        per = per_launch(layer, step, args.steps, 5)
+    else:  # convert, plan, W13, W2 (+SwiGLU or combine: fused up to 32 routes)
+        sep = m * K_TOP > 32
+        per = per_launch(layer, step, args.steps, 6 if sep else 5)
         t_w13_ms, t_w2_ms = float(per[2]), float(per[3])
-        names = ["convert", "plan", "w13", "w2"]
+        names = ["convert", "plan", "w13", "w2"] + (["combine"] if sep else [])
     pk = peaks()
     achieved = distinct * W13_BYTES / (t_w13_ms / 1e3) / 1e9
     layer_bytes = distinct * EXPERT_BYTES
@@ -463,8 +464,9 @@ def run_c1(job) -> None:
                                "launch_ms": {k: float(v) for k, v in zip(names, per)}},
             "e2e": dict({"value": job.world * m / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms},
                         **e2e_bytes),
-            # gating, bf16 copy, route plan, [x planes], W13 (+SwiGLU), [SwiGLU planes], W2 (+combine), [combine]
-            "gpu_launches": (8 if f4 else 5) * args.steps,
+            # gating, bf16 copy, route plan, [x planes], W13 (+SwiGLU), [SwiGLU planes], W2, combine
+            # (the GEMV path fuses the combine into W2 up to 32 routes)
+            "gpu_launches": (8 if f4 else 6 if m * K_TOP > 32 else 5) * args.steps,
             "cpu_baseline": cpu,
             "clocks": clk,
         })
@@ -538,9 +540,10 @@ def run_c2(job) -> None:
         #     W2 fp4, W2 iq2, combine
         per = per_launch(layer, step, args.steps, 12)
         i13, i2, extra = (4, 5), (8, 9), {"x_planes": 3, "inter_planes": 6, "inter_int8": 7, "combine": 10}
-    else:  # start, convert, x int8 blocks, plan, W13 fp4, W13 iq2, SwiGLU int8 blocks, W2 fp4, W2 iq2
-        per = per_launch(layer, step, args.steps, 9)
-        i13, i2, extra = (3, 4), (6, 7), {"inter_int8": 5}
+    else:  # start, convert, x int8 blocks, plan, W13 fp4, W13 iq2, SwiGLU int8 blocks, W2 fp4, W2 iq2, combine
+        sep = m * K_TOP > 32
+        per = per_launch(layer, step, args.steps, 10 if sep else 9)
+        i13, i2, extra = (3, 4), (6, 7), dict({"inter_int8": 5}, **({"combine": 8} if sep else {}))
     pk = peaks()
     launches = {"w13_fp4": (per[i13[0]], hot_used.size * W13_BYTES),
                 "w13_iq2": (per[i13[1]], iq_used.size * IQ_W13_BYTES),
@@ -571,9 +574,9 @@ def run_c2(job) -> None:
                                              **{k: float(v[0]) for k, v in launches.items()}}},
             "e2e": dict({"value": job.world * m / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms},
                         **e2e_bytes),
-            # gating, bf16 copy, x int8 blocks, plan, W13 x 2 banks, SwiGLU int8 blocks, W2 x 2 banks
-            # (fp4: + x planes, SwiGLU planes, combine)
-            "gpu_launches": (12 if f4 else 9) * args.steps,
+            # gating, bf16 copy, x int8 blocks, plan, W13 x 2 banks, SwiGLU int8 blocks, W2 x 2 banks, combine
+            # (fp4: + x planes, SwiGLU planes; the GEMV path fuses the combine up to 32 routes)
+            "gpu_launches": (12 if f4 else 10 if m * K_TOP > 32 else 9) * args.steps,
             "cpu_baseline": cpu,
             "clocks": clk,
         })
@@ -805,8 +808,10 @@ def run_c4(job) -> None:
         local = lay if world == 1 else lay.layer
         banks = int((local.fp4_slot >= 0).any()) + int((local.iq2_slot >= 0).any())
         launches_per_step += 1 + 2 * banks + (3 if world == 1 else 2) + (5 if world > 1 else 0)
-        if args.gemm == "fp4" and (local.fp4_slot >= 0).any():  # x and SwiGLU planes (+ combine at world 1)
-            launches_per_step += 3 if world == 1 else 2
+        if world == 1 and (args.gemm == "fp4" or T * K_TOP > 32):  # the combine launch
+            launches_per_step += 1
+        if args.gemm == "fp4" and (local.fp4_slot >= 0).any():  # x and SwiGLU planes
+            launches_per_step += 2
     pk = peaks()
     achieved = local_bytes / (ms / 1e3) / 1e9
     frac_min = -job.maxall(-achieved / pk["hbm_gbs"])

@@ -241,9 +241,12 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   const bool tc = !rows && prefill && c.prefill_gemm == 1 && c.n_fp4 > 0 && L->xperm;
   const bool f4 = c.prefill_gemm == 2 && c.n_fp4 > 0;
   if (f4 && !ws.own) return B200MOE_ERR_STATE;  // the static array holds no plane buffers
-  // the block-scaled path and the tcgen05 prefill write y2 rows only and combine in one launch after W2
-  // (fused into their epilogues the combine's fences, atomics and re-reads stall the pipeline)
-  const bool sep_combine = !rows && (f4 || tc);
+  // W2 writes y2 rows only and one launch after it does the slot-order combine: fused into the W2
+  // epilogue the combine's fences, atomics and re-reads stall the pipeline (measured on B200: the
+  // decode GEMV at M = 64 0.849 against 0.877 ms, the tcgen05 prefill W2 1.10 against 2.12 ms).
+  // The fused form stays for the smallest GEMV batches (at most 32 routes, where it is as fast and
+  // saves a launch) and for the allocation-free decode, whose array holds no route positions.
+  const bool sep_combine = !rows && ws.own && (f4 || tc || S > 32);
   if (sep_combine) ws.counters = nullptr;
   PlanArgs p{};
   p.ids = ids;
@@ -253,7 +256,7 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   p.key_of_expert = L->key_of_expert;
   p.n_keys = c.n_fp4 + c.n_iq2;
   p.perm = ws.perm;
-  p.inv = (f4 || tc) ? L->route_pos : nullptr;
+  p.inv = (f4 || sep_combine) ? L->route_pos : nullptr;
   p.chunk_of = f4 ? L->f4_chunk_of : nullptr;
   p.n_banks = 2;
   p.key_lo[0] = 0;
