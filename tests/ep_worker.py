@@ -23,7 +23,7 @@ __graft_entry__.load_package()
 from b200moe import ep, moe, synth, tiers  # noqa: E402
 
 
-def main(out_path: str, exchange: str) -> None:
+def main(out_path: str, exchange: str, gemm: str) -> None:
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
     dev = torch.device("cuda", torch.cuda.current_device())
@@ -33,19 +33,22 @@ def main(out_path: str, exchange: str) -> None:
     n_hot, n_iq = int((tier == tiers.HOT).sum()), int((tier == tiers.WARM).sum())
     fp4 = synth.make_fp4_bank(n_hot, H, I, "nvfp4", 11, dev)
     iq2 = synth.make_iq2_bank(n_iq, H, I, 12, dev)
-    full = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K, max_tokens=64, tier=tier, device=dev)
+    pg = "fp4" if gemm == "fp4" else "tcgen05"
+    full = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K, max_tokens=64, tier=tier, device=dev,
+                             prefill_gemm=pg)
     synth.load_bank(full, fp4)
     full.set_iq2_tables()
     synth.load_bank(full, iq2)
     sharded = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K, tokens=T, tier=tier, device=dev,
-                                   exchange=exchange)
+                                   exchange=exchange, gemm=gemm)
     exact = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K, tokens=T, tier=tier, device=dev,
-                                 split_k=(2, 2), exchange=exchange)
+                                 split_k=(2, 2), exchange=exchange, gemm=gemm)
     sharded.set_iq2_tables()
     synth.load_local(sharded.layer, tier, fp4, iq2)
     exact.set_iq2_tables()
     synth.load_local(exact.layer, tier, fp4, iq2)
-    full2 = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K, max_tokens=64, tier=tier, device=dev)
+    full2 = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K, max_tokens=64, tier=tier, device=dev,
+                              prefill_gemm=pg)
     synth.load_bank(full2, fp4)
     full2.set_iq2_tables()
     synth.load_bank(full2, iq2)
@@ -87,4 +90,4 @@ def main(out_path: str, exchange: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else "p2p")
+    main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else "p2p", sys.argv[3] if len(sys.argv) > 3 else "skinny")

@@ -221,6 +221,10 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanArgs a) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // a.n_valid (device) bounds the routes of this call below the launch's a.n
   const int n = a.n_valid ? min(a.n, max(0, *a.n_valid)) : a.n;
+  // routes past this call's count have no position (a stale one would send their rows' planes into a live
+  // route's place)
+  if (a.inv)
+    for (int i = n + tid; i < a.n; i += blockDim.x) a.inv[i] = -1;
   if (product && n <= 32) {  // decode-sized plans: one warp, no block-wide phases
     if (warp == 0) plan_small(a, n, sentinel);
     return;
