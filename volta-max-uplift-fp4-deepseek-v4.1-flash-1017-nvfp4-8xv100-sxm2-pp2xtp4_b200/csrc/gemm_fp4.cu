@@ -44,21 +44,25 @@ namespace b200moe {
 namespace {
 
 constexpr int kP = kFp4Planes;             // activation planes
-constexpr int kRC = kFp4TcRoutes;          // routes per chunk
-constexpr int kN = kP * kRC;               // MMA N = 64
 constexpr int kATile = 128 * 128;          // weight tile: 128 rows x 256 FP4 = 16 KB
-constexpr int kBTile = kN * 128;           // activation tile: 64 rows x 256 FP4 = 8 KB
 constexpr int kSFBytes = 4 * 512;          // the scale blocks of one 256-wide K tile
 constexpr int kThreads = 6 * 32;           // producer, MMA, 4 epilogue warps
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSfCol = 256;           // scale columns start after the two accumulator buffers
 
-// Stage layout by weight tiles per unit.  Two tiles (W13: the gate and up
-// tiles; W2: two adjacent 128-row tiles) make 46 KB stages, 4 of them; one
-// tile 28 KB, 7 stages.  Each stage has its own TMEM scale columns: a scale
-// copy never lands under an MMA still in flight.
-template <int TILES>
+// Stage layout by weight tiles per unit and routes per chunk (RC: the MMA's N
+// is 4 planes x RC; small batches use small chunks, so the tensor pipe does not
+// spend its time on empty columns).  Two tiles (W13: the gate and up tiles; W2:
+// two adjacent 128-row tiles) make stages of 36 KB + the plane tile, 4 of them;
+// one tile 18 KB + the plane tile, 7 stages.  Each stage has its own TMEM scale
+// columns: a scale copy never lands under an MMA still in flight.
+template <int TILES, int RC>
 struct Fp4Stage {
+  static constexpr int kRC = RC;         // routes per chunk
+  static constexpr int kN = kP * RC;     // MMA N: 16, 32 or 64
+  static constexpr int kBTile = kN * 128;  // activation tile: kN rows x 256 FP4
+  // kind::mxf4nvf4 block16: A and B E2M1 (1), K-major, N = kN, M = 128, scales UE4M3
+  static constexpr uint32_t kIdesc = (1u << 7) | (1u << 10) | (uint32_t(kN >> 3) << 17) | (uint32_t(128 >> 4) << 24);
   static constexpr int kTiles = TILES;  // weight tiles per unit
   static constexpr int kUnit = kTiles * (kATile + kSFBytes);  // one weight unit, one bulk copy
   static constexpr int kOffAG = 0;
@@ -67,7 +71,7 @@ struct Fp4Stage {
   static constexpr int kOffSFU = kOffSFG + kSFBytes;  // W13 only
   static constexpr int kOffB = kUnit;
   static constexpr int kOffSFB = kOffB + kBTile;
-  static constexpr int kBytes = kOffSFB + kSFBytes;  // 46 KB / 28 KB
+  static constexpr int kBytes = kOffSFB + kSFBytes;
   static constexpr int kStages = TILES == 2 ? 4 : 7;
   static constexpr uint32_t kSfCols = TILES == 2 ? 48 : 32;  // tile 0 (, tile 1), activations: 16 each
   static constexpr uint32_t kSfB = TILES == 2 ? 32 : 16;
@@ -76,9 +80,6 @@ struct Fp4Stage {
   static_assert(kSfCol + kStages * kSfCols <= kTmemCols, "TMEM columns");
   static_assert(kSmem <= 227 * 1024, "shared memory");
 };
-
-// kind::mxf4nvf4 block16: A and B E2M1 (1), K-major, N = 64, M = 128, scales UE4M3
-constexpr uint32_t kIdesc = (1u << 7) | (1u << 10) | (uint32_t(kN >> 3) << 17) | (uint32_t(128 >> 4) << 24);
 
 __device__ __forceinline__ uint64_t desc_sw128(uint32_t addr) {
   return uint64_t((addr >> 4) & 0x3FFF) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) | (uint64_t(1) << 46) |
@@ -94,11 +95,11 @@ __device__ __forceinline__ void sf_copy(uint32_t tcol, uint32_t smem) {
 }
 
 __device__ __forceinline__ void mma_fp4(uint32_t d, uint64_t a, uint64_t b, uint32_t sfa, uint32_t sfb,
-                                        uint32_t accumulate) {
+                                        uint32_t accumulate, uint32_t idesc) {
   asm volatile(
       "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n"
       "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p; }" ::"r"(d),
-      "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate), "r"(sfa), "r"(sfb));
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb));
 }
 
 __device__ __forceinline__ void commit_to(uint64_t* bar) {
@@ -135,11 +136,12 @@ __device__ __forceinline__ __half swiglu1(float g, float u, float limit) {
   return __float2half_rn(__fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), u));
 }
 
-template <int EPI, int TILES>
+template <int EPI, int TILES, int RC>
 __global__ void __launch_bounds__(kThreads, 1)
     fp4_gemm_kernel(const Fp4Args a, const __grid_constant__ CUtensorMap map_x) {
   static_assert(EPI == 1 || TILES == 2, "W13 items pair a gate tile with its up tile");
-  using St = Fp4Stage<TILES>;
+  using St = Fp4Stage<TILES, RC>;
+  constexpr int kRC = St::kRC, kN = St::kN;
   constexpr int kStages = St::kStages, kStage = St::kBytes;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base_u32 = (smem_u32(smem_raw) + 1023u) & ~1023u;
@@ -267,8 +269,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 4; ++j) {
             const uint32_t acc = (kt | j) != 0;
             const uint64_t bdesc = desc_sw128(st + St::kOffB + 32 * j);
-            mma_fp4(dg, desc_sw128(st + St::kOffAG + 32 * j), bdesc, sfg + 4 * j, sfb + 4 * j, acc);
-            if (TILES == 2) mma_fp4(du, desc_sw128(st + St::kOffAU + 32 * j), bdesc, sfu + 4 * j, sfb + 4 * j, acc);
+            mma_fp4(dg, desc_sw128(st + St::kOffAG + 32 * j), bdesc, sfg + 4 * j, sfb + 4 * j, acc, St::kIdesc);
+            if (TILES == 2)
+              mma_fp4(du, desc_sw128(st + St::kOffAU + 32 * j), bdesc, sfu + 4 * j, sfb + 4 * j, acc, St::kIdesc);
           }
           commit_to(&empty[s]);
         }
@@ -318,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < kN; c += 16) tmem_ld16(tmem + lanes + b * 128 + c, d0 + c);
       if (TILES == 2) {
 #pragma unroll
-        for (int c = 0; c < kN; c += 16) tmem_ld16(tmem + lanes + b * 128 + 64 + c, d1 + c);
+        for (int c = 0; c < kN; c += 16) tmem_ld16(tmem + lanes + b * 128 + 64 + c, d1 + c);  // up / second tile
       }
       fence_before();
       __syncwarp();
@@ -585,27 +588,34 @@ __global__ void fp4_tile_kernel(const uint8_t* __restrict__ codes, const uint8_t
   }
 }
 
-template <int EPI, int TILES>
+template <int EPI, int TILES, int RC>
 int launch_fp4_one(cudaStream_t s, const Fp4Args& a, const void* map_x, int grid) {
-  const size_t smem = Fp4Stage<TILES>::kSmem;
+  const size_t smem = Fp4Stage<TILES, RC>::kSmem;
   static std::atomic<uint64_t> attr_set{0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return -1;
   if (!(attr_set.load() >> dev & 1)) {
-    if (cudaFuncSetAttribute(fp4_gemm_kernel<EPI, TILES>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
+    if (cudaFuncSetAttribute(fp4_gemm_kernel<EPI, TILES, RC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(smem)) !=
         cudaSuccess)
       return -1;
     attr_set.fetch_or(uint64_t(1) << dev);
   }
-  fp4_gemm_kernel<EPI, TILES><<<grid, kThreads, smem, s>>>(a, *static_cast<const CUtensorMap*>(map_x));
+  fp4_gemm_kernel<EPI, TILES, RC><<<grid, kThreads, smem, s>>>(a, *static_cast<const CUtensorMap*>(map_x));
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 }  // namespace
 
-int launch_fp4_gemm(cudaStream_t s, int epi, const Fp4Args& a, const void* map_x, int grid) {
+int launch_fp4_gemm(cudaStream_t s, int epi, int rc, const Fp4Args& a, const void* map_x, int grid) {
   // W2 items take two adjacent 128-row tiles, as W13 items take a gate and an up tile
-  return epi == 0 ? launch_fp4_one<0, 2>(s, a, map_x, grid) : launch_fp4_one<1, 2>(s, a, map_x, grid);
+  switch (rc) {
+    case 4: return epi == 0 ? launch_fp4_one<0, 2, 4>(s, a, map_x, grid) : launch_fp4_one<1, 2, 4>(s, a, map_x, grid);
+    case 8: return epi == 0 ? launch_fp4_one<0, 2, 8>(s, a, map_x, grid) : launch_fp4_one<1, 2, 8>(s, a, map_x, grid);
+    case 16:
+      return epi == 0 ? launch_fp4_one<0, 2, 16>(s, a, map_x, grid) : launch_fp4_one<1, 2, 16>(s, a, map_x, grid);
+    default: return -1;
+  }
 }
 
 int launch_fp4_planes(cudaStream_t s, bool by_token, const __half* src, int64_t src_stride, int K,

@@ -62,7 +62,7 @@ struct b200moe_layer {
   int32_t* f4_chunk_of = nullptr;              // [s_max]: (chunk << 8) | index in chunk of an FP4-bank position
   uint32_t* f4_rowmax = nullptr;               // [plane_rows]: amax bits of each SwiGLU row (W2 planes)
   int f4_plane_rows = 0, f4_max_chunks = 0;
-  alignas(128) unsigned char f4_map_x[2][128] = {};
+  alignas(128) unsigned char f4_map_x[2][3][128] = {};  // [W13, W2][4, 8, 16 routes per chunk]
   // prefill on tcgen05: permuted fp16 token rows and the TMA maps of the two B operands
   __half* xperm = nullptr;
   alignas(128) unsigned char map_x[128] = {};
@@ -264,7 +264,7 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   p.key_lo[1] = c.n_fp4;
   p.key_hi[1] = c.n_fp4 + c.n_iq2;
   for (int b = 0; b < 2; ++b) {
-    p.rc[b] = (tc && b == 0) ? kTcTokenTile : (f4 && b == 0) ? kFp4TcRoutes : fixed_rc(L, b);
+    p.rc[b] = (tc && b == 0) ? kTcTokenTile : (f4 && b == 0) ? fp4_routes_per_chunk(S) : fixed_rc(L, b);
     p.ks_model[b] = ks_model(L, b);
     p.max_chunks[b] = (f4 && b == 0) ? std::min(ws.max_chunks, L->f4_max_chunks) : ws.max_chunks;
     p.chunks[b] = ws.chunks[b];
@@ -329,7 +329,9 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
         f.out = out;
         f.H = c.hidden;
         f.err = L->err;
-        if (launch_fp4_gemm(s, epi, f, L->f4_map_x[epi], L->grid)) return B200MOE_ERR_CUDA;
+        const int rc = fp4_routes_per_chunk(S);
+        if (launch_fp4_gemm(s, epi, rc, f, L->f4_map_x[epi][rc == 4 ? 0 : rc == 8 ? 1 : 2], L->grid))
+          return B200MOE_ERR_CUDA;
         marks.mark();
         continue;
       }
@@ -493,7 +495,8 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
   }
   if (f4 && c.n_fp4 > 0) {
     L->f4_plane_rows = L->s_max + kFp4TcRoutes;
-    L->f4_max_chunks = (L->s_max + kFp4TcRoutes - 1) / kFp4TcRoutes + c.n_fp4;
+    // chunks of <= 4, 8 or 16 routes (calls of <= 64, <= 1024 or more routes)
+    L->f4_max_chunks = std::max(std::max(64 / 4, 1024 / 8), (L->s_max + 15) / 16) + c.n_fp4;
     const size_t P = kFp4Planes, R = L->f4_plane_rows, H = c.hidden, I = c.inter;
     take(dalloc(&L->f4_planes[0], P * R * H / 2));
     take(dalloc(&L->f4_planes[1], P * R * I / 2));
@@ -504,8 +507,12 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
     take(dalloc(&L->f4_chunk_of, size_t(L->s_max)));
     take(dalloc(&L->f4_rowmax, R));
     if (st == B200MOE_OK &&
-        (make_u8_tile_map(L->f4_map_x[0], L->f4_planes[0], int64_t(P * R), H / 2, 128, kFp4TcRoutes * kFp4Planes) ||
-         make_u8_tile_map(L->f4_map_x[1], L->f4_planes[1], int64_t(P * R), I / 2, 128, kFp4TcRoutes * kFp4Planes)))
+        (make_u8_tile_map(L->f4_map_x[0][0], L->f4_planes[0], int64_t(P * R), H / 2, 128, 4 * kFp4Planes) ||
+         make_u8_tile_map(L->f4_map_x[0][1], L->f4_planes[0], int64_t(P * R), H / 2, 128, 8 * kFp4Planes) ||
+         make_u8_tile_map(L->f4_map_x[0][2], L->f4_planes[0], int64_t(P * R), H / 2, 128, 16 * kFp4Planes) ||
+         make_u8_tile_map(L->f4_map_x[1][0], L->f4_planes[1], int64_t(P * R), I / 2, 128, 4 * kFp4Planes) ||
+         make_u8_tile_map(L->f4_map_x[1][1], L->f4_planes[1], int64_t(P * R), I / 2, 128, 8 * kFp4Planes) ||
+         make_u8_tile_map(L->f4_map_x[1][2], L->f4_planes[1], int64_t(P * R), I / 2, 128, 16 * kFp4Planes)))
       st = B200MOE_ERR_CUDA;
   }
   if (c.prefill_gemm == 1 && c.max_prefill_tokens > 0 && c.n_fp4 > 0) {
