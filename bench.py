@@ -464,9 +464,9 @@ def run_c1(job) -> None:
                                "launch_ms": {k: float(v) for k, v in zip(names, per)}},
             "e2e": dict({"value": job.world * m / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms},
                         **e2e_bytes),
-            # gating, bf16 copy, route plan, [x planes], W13 (+SwiGLU), [SwiGLU planes], W2, combine
-            # (the GEMV path fuses the combine into W2 up to 32 routes)
-            "gpu_launches": (8 if f4 else 6 if m * K_TOP > 32 else 5) * args.steps,
+            # fp4: gating, route plan, x planes (read bf16 x directly), W13 (+SwiGLU), SwiGLU planes, W2, combine;
+            # gemv: gating, bf16 copy, route plan, W13 (+SwiGLU), W2, combine (fused into W2 up to 32 routes)
+            "gpu_launches": (7 if f4 else 6 if m * K_TOP > 32 else 5) * args.steps,
             "cpu_baseline": cpu,
             "clocks": clk,
         })

@@ -407,9 +407,25 @@ __device__ __forceinline__ uint32_t e4m3_rn(float x) {
 // of one sorted position, its amax taken by the W13 epilogue (rowmax).
 constexpr int kPlaneThreads = 128;
 constexpr int kSlice = kPlaneThreads * 8;
-template <int BY_TOKEN>
+// eight 16-bit values (f16, or bf16 when BF16) as floats
+template <int BF16>
+__device__ __forceinline__ void load8(const uint4& v, float (&r)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    if (BF16) {
+      r[2 * e] = __uint_as_float(w[e] << 16);
+      r[2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+    } else {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+      r[2 * e] = f.x;
+      r[2 * e + 1] = f.y;
+    }
+  }
+}
+template <int BY_TOKEN, int BF16>
 __global__ void __launch_bounds__(kPlaneThreads) fp4_planes_kernel(
-    const __half* __restrict__ src, int64_t src_stride, int K, const int32_t* __restrict__ inv, int top_k,
+    const uint16_t* __restrict__ src, int64_t src_stride, int K, const int32_t* __restrict__ inv, int top_k,
     const int32_t* __restrict__ chunk_of, int bank, const int32_t* __restrict__ bank_range, int n_tokens,
     uint32_t* rowmax, uint8_t* planes, int plane_rows, uint8_t* sfb, float* gx) {
   __shared__ float red[kPlaneThreads / 32];
@@ -443,29 +459,16 @@ __global__ void __launch_bounds__(kPlaneThreads) fp4_planes_kernel(
       }
       if (lane == 0) n_dst = __popc(have);
     }
-    const __half* row = src + (BY_TOKEN ? int64_t(ri) : int64_t(lo + ri)) * src_stride;
+    const uint16_t* row = src + (BY_TOKEN ? int64_t(ri) : int64_t(lo + ri)) * src_stride;
     float r[8];
-    {
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (own) v = *reinterpret_cast<const uint4*>(row + hb * 8);
-      const __half2* hv = reinterpret_cast<const __half2*>(&v);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __half22float2(hv[e]);
-        r[2 * e] = f.x;
-        r[2 * e + 1] = f.y;
-      }
-    }
+    load8<BF16>(own ? *reinterpret_cast<const uint4*>(row + hb * 8) : make_uint4(0, 0, 0, 0), r);
     float amax = 0.f;
     if (BY_TOKEN) {  // the whole row's amax (every slice's CTA reads the row: it is L2-resident)
       for (int j = t; j < nhb; j += kPlaneThreads) {
-        const uint4 v = *reinterpret_cast<const uint4*>(row + j * 8);
-        const __half2* hv = reinterpret_cast<const __half2*>(&v);
+        float f[8];
+        load8<BF16>(*reinterpret_cast<const uint4*>(row + j * 8), f);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __half22float2(hv[e]);
-          amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
-        }
+        for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
       }
 #pragma unroll
       for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -618,19 +621,25 @@ int launch_fp4_gemm(cudaStream_t s, int epi, int rc, const Fp4Args& a, const voi
   }
 }
 
-int launch_fp4_planes(cudaStream_t s, bool by_token, const __half* src, int64_t src_stride, int K,
+int launch_fp4_planes(cudaStream_t s, bool by_token, bool bf16, const void* src, int64_t src_stride, int K,
                       const int32_t* inv, int top_k, const int32_t* chunk_of, int bank,
                       const int32_t* bank_range, int max_rows, uint32_t* rowmax, uint8_t* planes, int plane_rows,
                       uint8_t* sfb, float* gx) {
   // max_rows: the token rows (by_token) or the bound on the bank's positions
   if (K % 256 || top_k > 32) return -1;
   const dim3 grid(std::max(1, std::min(max_rows, 148 * 8)), (K + kSlice - 1) / kSlice);
-  if (by_token)
-    fp4_planes_kernel<1><<<grid, kPlaneThreads, 0, s>>>(src, src_stride, K, inv, top_k, chunk_of, bank, bank_range,
-                                                        max_rows, rowmax, planes, plane_rows, sfb, gx);
+  const uint16_t* x = static_cast<const uint16_t*>(src);
+  if (by_token && bf16)
+    fp4_planes_kernel<1, 1><<<grid, kPlaneThreads, 0, s>>>(x, src_stride, K, inv, top_k, chunk_of, bank, bank_range,
+                                                           max_rows, rowmax, planes, plane_rows, sfb, gx);
+  else if (by_token)
+    fp4_planes_kernel<1, 0><<<grid, kPlaneThreads, 0, s>>>(x, src_stride, K, inv, top_k, chunk_of, bank, bank_range,
+                                                           max_rows, rowmax, planes, plane_rows, sfb, gx);
+  else if (!bf16)
+    fp4_planes_kernel<0, 0><<<grid, kPlaneThreads, 0, s>>>(x, src_stride, K, inv, top_k, chunk_of, bank, bank_range,
+                                                           0, rowmax, planes, plane_rows, sfb, gx);
   else
-    fp4_planes_kernel<0><<<grid, kPlaneThreads, 0, s>>>(src, src_stride, K, inv, top_k, chunk_of, bank, bank_range,
-                                                        0, rowmax, planes, plane_rows, sfb, gx);
+    return -1;  // SwiGLU rows are fp16
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

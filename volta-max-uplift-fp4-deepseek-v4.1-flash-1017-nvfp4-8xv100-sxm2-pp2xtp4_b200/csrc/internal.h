@@ -118,7 +118,7 @@ struct Fp4Args {
 int launch_fp4_gemm(cudaStream_t s, int epi, int rc, const Fp4Args& a, const void* map_x, int grid);
 // routes per chunk of the block-scaled FP4 path for a call of S routes (the MMA's N is 4 x this)
 inline int fp4_routes_per_chunk(int S) { return S <= 64 ? 4 : S <= 1024 ? 8 : 16; }
-int launch_fp4_planes(cudaStream_t s, bool by_token, const __half* src, int64_t src_stride, int K,
+int launch_fp4_planes(cudaStream_t s, bool by_token, bool bf16, const void* src, int64_t src_stride, int K,
                       const int32_t* inv, int top_k, const int32_t* chunk_of, int bank,
                       const int32_t* bank_range, int max_rows, uint32_t* rowmax, uint8_t* planes, int plane_rows,
                       uint8_t* sfb, float* gx);

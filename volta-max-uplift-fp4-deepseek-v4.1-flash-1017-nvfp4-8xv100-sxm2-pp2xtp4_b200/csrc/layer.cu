@@ -226,8 +226,12 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   }
   const int S = m * c.top_k;
   const __half* xsrc = static_cast<const __half*>(x);
+  // bf16 x feeds the block-scaled path's planes directly; only the GEMV banks (and the tcgen05 row gather,
+  // which converts itself) want it in fp16
+  const bool x_bf16_direct =
+      x_dtype == B200MOE_BF16 && c.prefill_gemm == 2 && c.n_fp4 > 0 && c.n_iq2 == 0 && ws.own;
   marks.mark();
-  if (x_dtype == B200MOE_BF16) {
+  if (x_dtype == B200MOE_BF16 && !x_bf16_direct) {
     if (launch_convert_bf16(s, x, int64_t(m) * c.hidden, ws.x16)) return B200MOE_ERR_CUDA;
     xsrc = ws.x16;
   }
@@ -289,7 +293,9 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   }
   for (int epi = 0; epi < 2; ++epi) {
     if (f4) {  // the FP4 bank's activation rows as E2M1 planes for its block-scaled GEMM
-      if (launch_fp4_planes(s, epi == 0, epi == 0 ? xsrc : ws.inter, epi == 0 ? c.hidden : c.inter,
+      if (launch_fp4_planes(s, epi == 0, epi == 0 && x_bf16_direct,
+                            epi == 0 ? (x_bf16_direct ? x : static_cast<const void*>(xsrc)) : ws.inter,
+                            epi == 0 ? c.hidden : c.inter,
                             epi == 0 ? c.hidden : c.inter, L->route_pos, c.top_k, L->f4_chunk_of, 0,
                             ws.bank_range, epi == 0 ? m : S, L->f4_rowmax, L->f4_planes[epi], L->f4_plane_rows,
                             L->f4_sfb[epi], L->f4_gx[epi]))
