@@ -124,3 +124,39 @@ def test_ep_two_gpus(tmp_path, exchange, gemm):
         # every route goes to rank 0's experts: rank 1 receives none
         assert res["one_owner_routes_in"] == 0 if rank == 1 else res["one_owner_routes_in"] > 0
         assert res["zipf_comm_ms"] > 0
+
+
+@pytest.mark.parametrize("gemm", ["skinny", "fp4"])
+def test_rows_forward_device_count(dev, pkg, gemm):
+    """The top-1 rows forward of expert parallelism with fewer valid rows than
+    the launch bound (the count lives on the device): rows past the count are
+    ignored even when an earlier call left their routes in other places."""
+    from b200moe import _lib, moe, synth
+
+    H, I, E, R = 1024, 512, 32, 96
+    layer = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=1, max_tokens=64, max_prefill_tokens=R,
+                              tier=np.zeros(E, np.int8), device=dev, prefill_gemm="fp4" if gemm == "fp4" else "skinny")
+    synth.load_bank(layer, synth.make_fp4_bank(E, H, I, "nvfp4", 21, dev))
+    layer.set_split_k(2, 0)
+    g = torch.Generator(device=dev).manual_seed(22)
+    rows = torch.randn((R, H), generator=g, device=dev).to(torch.float16)
+    eids = torch.randint(0, E, (R,), generator=g, device=dev, dtype=torch.int32)
+    y2 = torch.empty((R, H), dtype=torch.float16, device=dev)
+    st = torch.cuda.current_stream().cuda_stream
+    L = _lib.lib()
+
+    def run(n):
+        cnt = torch.tensor([n], dtype=torch.int32, device=dev)
+        rng = torch.tensor([0, n], dtype=torch.int32, device=dev)
+        y2.fill_(float("nan"))
+        _lib.check("b200moe_forward_rows", L.b200moe_forward_rows(
+            layer._h, st, rows.data_ptr(), eids.data_ptr(), cnt.data_ptr(), rng.data_ptr(), R, y2.data_ptr()))
+        layer.check_errors()
+        return y2.clone()
+
+    full = run(R)
+    eids[R // 2:] = (eids[R // 2:] + 7) % E  # the stale half now belongs to other experts
+    half = run(R // 2)
+    assert torch.equal(half[:R // 2], full[:R // 2])
+    assert torch.isnan(half[R // 2:].float()).all()  # nothing written past the count
+    layer.close()
