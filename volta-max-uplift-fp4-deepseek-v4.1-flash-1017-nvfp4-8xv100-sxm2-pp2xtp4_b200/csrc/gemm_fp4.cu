@@ -56,13 +56,15 @@ constexpr uint32_t kSfCol = 256;           // scale columns start after the two 
 // two adjacent 128-row tiles) make stages of 36 KB + the plane tile, 4 of them;
 // one tile 18 KB + the plane tile, 7 stages.  Each stage has its own TMEM scale
 // columns: a scale copy never lands under an MMA still in flight.
-template <int TILES, int RC>
+template <int TILES, int RC, int MX = 0>
 struct Fp4Stage {
   static constexpr int kRC = RC;         // routes per chunk
   static constexpr int kN = kP * RC;     // MMA N: 16, 32 or 64
   static constexpr int kBTile = kN * 128;  // activation tile: kN rows x 256 FP4
-  // kind::mxf4nvf4 block16: A and B E2M1 (1), K-major, N = kN, M = 128, scales UE4M3
-  static constexpr uint32_t kIdesc = (1u << 7) | (1u << 10) | (uint32_t(kN >> 3) << 17) | (uint32_t(128 >> 4) << 24);
+  // kind::mxf4nvf4: A and B E2M1 (1), K-major, N = kN, M = 128; scales UE4M3 per 16 (NVFP4) or, bit 23,
+  // UE8M0 per 32 (MXFP4)
+  static constexpr uint32_t kIdesc = (1u << 7) | (1u << 10) | (uint32_t(kN >> 3) << 17) | (uint32_t(MX) << 23) |
+                                     (uint32_t(128 >> 4) << 24);
   static constexpr int kTiles = TILES;  // weight tiles per unit
   static constexpr int kUnit = kTiles * (kATile + kSFBytes);  // one weight unit, one bulk copy
   static constexpr int kOffAG = 0;
@@ -94,12 +96,19 @@ __device__ __forceinline__ void sf_copy(uint32_t tcol, uint32_t smem) {
   asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(tcol), "l"(desc_sf(smem)));
 }
 
+template <int MX>
 __device__ __forceinline__ void mma_fp4(uint32_t d, uint64_t a, uint64_t b, uint32_t sfa, uint32_t sfb,
                                         uint32_t accumulate, uint32_t idesc) {
-  asm volatile(
-      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n"
-      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p; }" ::"r"(d),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb));
+  if (MX)
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p; }" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb));
+  else
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p; }" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb));
 }
 
 __device__ __forceinline__ void commit_to(uint64_t* bar) {
@@ -136,11 +145,11 @@ __device__ __forceinline__ __half swiglu1(float g, float u, float limit) {
   return __float2half_rn(__fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), u));
 }
 
-template <int EPI, int TILES, int RC>
+template <int EPI, int TILES, int RC, int MX>
 __global__ void __launch_bounds__(kThreads, 1)
     fp4_gemm_kernel(const Fp4Args a, const __grid_constant__ CUtensorMap map_x) {
   static_assert(EPI == 1 || TILES == 2, "W13 items pair a gate tile with its up tile");
-  using St = Fp4Stage<TILES, RC>;
+  using St = Fp4Stage<TILES, RC, MX>;
   constexpr int kRC = St::kRC, kN = St::kN;
   constexpr int kStages = St::kStages, kStage = St::kBytes;
   extern __shared__ uint8_t smem_raw[];
@@ -269,9 +278,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 4; ++j) {
             const uint32_t acc = (kt | j) != 0;
             const uint64_t bdesc = desc_sw128(st + St::kOffB + 32 * j);
-            mma_fp4(dg, desc_sw128(st + St::kOffAG + 32 * j), bdesc, sfg + 4 * j, sfb + 4 * j, acc, St::kIdesc);
+            mma_fp4<MX>(dg, desc_sw128(st + St::kOffAG + 32 * j), bdesc, sfg + 4 * j, sfb + 4 * j, acc, St::kIdesc);
             if (TILES == 2)
-              mma_fp4(du, desc_sw128(st + St::kOffAU + 32 * j), bdesc, sfu + 4 * j, sfb + 4 * j, acc, St::kIdesc);
+              mma_fp4<MX>(du, desc_sw128(st + St::kOffAU + 32 * j), bdesc, sfu + 4 * j, sfb + 4 * j, acc, St::kIdesc);
           }
           commit_to(&empty[s]);
         }
@@ -423,7 +432,7 @@ __device__ __forceinline__ void load8(const uint4& v, float (&r)[8]) {
     }
   }
 }
-template <int BY_TOKEN, int BF16>
+template <int BY_TOKEN, int BF16, int MX>
 __global__ void __launch_bounds__(kPlaneThreads) fp4_planes_kernel(
     const uint16_t* __restrict__ src, int64_t src_stride, int K, const int32_t* __restrict__ inv, int top_k,
     const int32_t* __restrict__ chunk_of, int bank, const int32_t* __restrict__ bank_range, int n_tokens,
@@ -484,16 +493,26 @@ __global__ void __launch_bounds__(kPlaneThreads) fp4_planes_kernel(
     } else {
       amax = __uint_as_float(rowmax[dst_pos[0]]);
     }
-    const float g = amax / (6.f * 448.f);
+    // MXFP4: power-of-two block scales cover any row, so no row factor (g = 1)
+    const float g = MX ? 1.f : amax / (6.f * 448.f);
     const float inv_g = g > 0.f ? 1.f / g : 0.f;
 #pragma unroll
     for (int p = 0; p < kP; ++p) {
       float bm = 0.f;
 #pragma unroll
       for (int e = 0; e < 8; ++e) bm = fmaxf(bm, fabsf(r[e]));
-      bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 1));  // the other half of the block
-      const uint32_t sc = own ? e4m3_rn(bm / 6.f * inv_g) : 0u;
-      const float scale = e4m3_value(sc) * g;
+      bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 1));  // the other half of the 16-block
+      if (MX) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 2));  // the 32-block: four half-blocks
+      uint32_t sc;
+      float scale;
+      if (MX) {  // UE8M0: the smallest 2^e with 6 * 2^e >= bm
+        const int e = bm > 0.f ? max(-126, min(127, mx_exponent(bm))) : -127;
+        sc = own && bm > 0.f ? uint32_t(e + 127) : 0u;
+        scale = sc ? ldexpf(1.f, e) : 0.f;
+      } else {
+        sc = own ? e4m3_rn(bm / 6.f * inv_g) : 0u;
+        scale = e4m3_value(sc) * g;
+      }
       const float rs = scale > 0.f ? 1.f / scale : 0.f;
       uint32_t w = 0u;
 #pragma unroll
@@ -503,11 +522,16 @@ __global__ void __launch_bounds__(kPlaneThreads) fp4_planes_kernel(
         r[e] -= copysignf(q, v) * scale;
         w |= (e2m1_code_of(q) | (v < 0.f ? 8u : 0u)) << (4 * e);
       }
-      // the four scale bytes of blocks 4j .. 4j + 3 as one word from lane 8j
+      // the scale bytes of one 64-wide K step as one word from lane 8j: NVFP4 blocks 4j .. 4j + 3 (lanes
+      // 8j, +2, +4, +6), MXFP4 blocks 2j, 2j + 1 (lanes 8j, 8j + 4)
       uint32_t word = sc;
-      word |= __shfl_down_sync(0xffffffffu, sc, 2) << 8;
-      word |= __shfl_down_sync(0xffffffffu, sc, 4) << 16;
-      word |= __shfl_down_sync(0xffffffffu, sc, 6) << 24;
+      if (MX) {
+        word |= __shfl_down_sync(0xffffffffu, sc, 4) << 8;
+      } else {
+        word |= __shfl_down_sync(0xffffffffu, sc, 2) << 8;
+        word |= __shfl_down_sync(0xffffffffu, sc, 4) << 16;
+        word |= __shfl_down_sync(0xffffffffu, sc, 6) << 24;
+      }
       if (own) {
         for (int d = 0; d < nd; ++d) {
           const int pos = dst_pos[d];
@@ -557,14 +581,16 @@ __global__ void fp4_combine_kernel(const __half* __restrict__ y2, const int32_t*
 }
 
 // --------------------------------------------------------------- prepack
-// NVFP4 codes [slot][rows][K/2] and E4M3 scales [slot][rows][K/16] -> weight
-// units [slot][rt][kt], one bulk copy each: the unit's tiles (W13: the gate
-// tile, rows rt * 128 .. of W1, then the up tile, the same rows of W3; W2:
-// rows rt * 256 .. and rt * 256 + 128 ..) of
+// FP4 codes [slot][rows][K/2] and block scales [slot][rows][K/VS] (NVFP4: E4M3
+// per 16, MXFP4: E8M0 per 32) -> weight units [slot][rt][kt], one bulk copy
+// each: the unit's tiles (W13: the gate tile, rows rt * 128 .. of W1, then the
+// up tile, the same rows of W3; W2: rows rt * 256 .. and rt * 256 + 128 ..) of
 // 128 rows x 128 bytes of codes in the 128-byte swizzled order the MMA reads
 // (16-byte chunk c of row r at r * 128 + ((c ^ (r & 7)) << 4)), then per tile
-// its four 512-byte scale blocks (byte m0 * 16 + m1 * 4 + s of block q = the
-// scale of row m1 * 32 + m0, 16-wide K block 4 q + s of the tile).
+// its four 512-byte scale blocks, one per 64-wide K step q (byte m0 * 16 +
+// m1 * 4 + s of block q = the scale of row m1 * 32 + m0, K block 4 q + s for
+// NVFP4, 2 q + s for MXFP4, whose bytes 2 and 3 stay zero).
+template <int MX>
 __global__ void fp4_tile_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ scales, int n_slots,
                                 int rows_per_slot, int K, int n_tiles, int n_rt, int rt_rows, int tile_rows,
                                 uint8_t* __restrict__ out) {
@@ -584,44 +610,54 @@ __global__ void fp4_tile_kernel(const uint8_t* __restrict__ codes, const uint8_t
       }
       for (int i = threadIdx.x; i < 128 * 4; i += blockDim.x) {
         const int r = i >> 2, q = i & 3;
-        const uint32_t v = *reinterpret_cast<const uint32_t*>(scales + (row0 + r) * (K / 16) + kt * 16 + q * 4);
+        const uint32_t v =
+            MX ? uint32_t(*reinterpret_cast<const uint16_t*>(scales + (row0 + r) * (K / 32) + kt * 8 + q * 2))
+               : *reinterpret_cast<const uint32_t*>(scales + (row0 + r) * (K / 16) + kt * 16 + q * 4);
         *reinterpret_cast<uint32_t*>(dst + n_tiles * kATile + j * kSFBytes + q * 512 + (r & 31) * 16 + (r >> 5) * 4) = v;
       }
     }
   }
 }
 
-template <int EPI, int TILES, int RC>
+template <int EPI, int TILES, int RC, int MX>
 int launch_fp4_one(cudaStream_t s, const Fp4Args& a, const void* map_x, int grid) {
-  const size_t smem = Fp4Stage<TILES, RC>::kSmem;
+  const size_t smem = Fp4Stage<TILES, RC, MX>::kSmem;
   static std::atomic<uint64_t> attr_set{0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return -1;
   if (!(attr_set.load() >> dev & 1)) {
-    if (cudaFuncSetAttribute(fp4_gemm_kernel<EPI, TILES, RC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(fp4_gemm_kernel<EPI, TILES, RC, MX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              int(smem)) !=
         cudaSuccess)
       return -1;
     attr_set.fetch_or(uint64_t(1) << dev);
   }
-  fp4_gemm_kernel<EPI, TILES, RC><<<grid, kThreads, smem, s>>>(a, *static_cast<const CUtensorMap*>(map_x));
+  fp4_gemm_kernel<EPI, TILES, RC, MX><<<grid, kThreads, smem, s>>>(a, *static_cast<const CUtensorMap*>(map_x));
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
-}  // namespace
-
-int launch_fp4_gemm(cudaStream_t s, int epi, int rc, const Fp4Args& a, const void* map_x, int grid) {
-  // W2 items take two adjacent 128-row tiles, as W13 items take a gate and an up tile
+template <int MX>
+int launch_fp4_rc(cudaStream_t s, int epi, int rc, const Fp4Args& a, const void* map_x, int grid) {
   switch (rc) {
-    case 4: return epi == 0 ? launch_fp4_one<0, 2, 4>(s, a, map_x, grid) : launch_fp4_one<1, 2, 4>(s, a, map_x, grid);
-    case 8: return epi == 0 ? launch_fp4_one<0, 2, 8>(s, a, map_x, grid) : launch_fp4_one<1, 2, 8>(s, a, map_x, grid);
+    case 4:
+      return epi == 0 ? launch_fp4_one<0, 2, 4, MX>(s, a, map_x, grid) : launch_fp4_one<1, 2, 4, MX>(s, a, map_x, grid);
+    case 8:
+      return epi == 0 ? launch_fp4_one<0, 2, 8, MX>(s, a, map_x, grid) : launch_fp4_one<1, 2, 8, MX>(s, a, map_x, grid);
     case 16:
-      return epi == 0 ? launch_fp4_one<0, 2, 16>(s, a, map_x, grid) : launch_fp4_one<1, 2, 16>(s, a, map_x, grid);
+      return epi == 0 ? launch_fp4_one<0, 2, 16, MX>(s, a, map_x, grid)
+                      : launch_fp4_one<1, 2, 16, MX>(s, a, map_x, grid);
     default: return -1;
   }
 }
 
-int launch_fp4_planes(cudaStream_t s, bool by_token, bool bf16, const void* src, int64_t src_stride, int K,
+}  // namespace
+
+int launch_fp4_gemm(cudaStream_t s, int epi, int rc, bool mx, const Fp4Args& a, const void* map_x, int grid) {
+  // W2 items take two adjacent 128-row tiles, as W13 items take a gate and an up tile
+  return mx ? launch_fp4_rc<1>(s, epi, rc, a, map_x, grid) : launch_fp4_rc<0>(s, epi, rc, a, map_x, grid);
+}
+
+int launch_fp4_planes(cudaStream_t s, bool by_token, bool bf16, bool mx, const void* src, int64_t src_stride, int K,
                       const int32_t* inv, int top_k, const int32_t* chunk_of, int bank,
                       const int32_t* bank_range, int max_rows, uint32_t* rowmax, uint8_t* planes, int plane_rows,
                       uint8_t* sfb, float* gx) {
@@ -629,17 +665,12 @@ int launch_fp4_planes(cudaStream_t s, bool by_token, bool bf16, const void* src,
   if (K % 256 || top_k > 32) return -1;
   const dim3 grid(std::max(1, std::min(max_rows, 148 * 8)), (K + kSlice - 1) / kSlice);
   const uint16_t* x = static_cast<const uint16_t*>(src);
-  if (by_token && bf16)
-    fp4_planes_kernel<1, 1><<<grid, kPlaneThreads, 0, s>>>(x, src_stride, K, inv, top_k, chunk_of, bank, bank_range,
-                                                           max_rows, rowmax, planes, plane_rows, sfb, gx);
-  else if (by_token)
-    fp4_planes_kernel<1, 0><<<grid, kPlaneThreads, 0, s>>>(x, src_stride, K, inv, top_k, chunk_of, bank, bank_range,
-                                                           max_rows, rowmax, planes, plane_rows, sfb, gx);
-  else if (!bf16)
-    fp4_planes_kernel<0, 0><<<grid, kPlaneThreads, 0, s>>>(x, src_stride, K, inv, top_k, chunk_of, bank, bank_range,
-                                                           0, rowmax, planes, plane_rows, sfb, gx);
-  else
-    return -1;  // SwiGLU rows are fp16
+  auto kernel = by_token ? (bf16 ? (mx ? fp4_planes_kernel<1, 1, 1> : fp4_planes_kernel<1, 1, 0>)
+                                 : (mx ? fp4_planes_kernel<1, 0, 1> : fp4_planes_kernel<1, 0, 0>))
+                         : (mx ? fp4_planes_kernel<0, 0, 1> : fp4_planes_kernel<0, 0, 0>);
+  if (!by_token && bf16) return -1;  // SwiGLU rows are fp16
+  kernel<<<grid, kPlaneThreads, 0, s>>>(x, src_stride, K, inv, top_k, chunk_of, bank, bank_range, by_token ? max_rows : 0,
+                                        rowmax, planes, plane_rows, sfb, gx);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -652,16 +683,17 @@ int launch_route_combine(cudaStream_t s, const __half* y2, const int32_t* inv, c
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
-int launch_fp4_tile(cudaStream_t s, const uint8_t* codes, const uint8_t* scales, int n_slots, int rows_per_slot,
-                    int K, bool gate_up, uint8_t* out) {
+int launch_fp4_tile(cudaStream_t s, bool mx, const uint8_t* codes, const uint8_t* scales, int n_slots,
+                    int rows_per_slot, int K, bool gate_up, uint8_t* out) {
   // W13 (gate_up): tile 0 = rows rt * 128 .. of W1, tile 1 the same rows of W3;
   // W2: tiles 0 and 1 = rows rt * 256 .. and rt * 256 + 128 ..
   if (K % 256 || rows_per_slot % 256 || n_slots < 1) return -1;
   const int n_rt = rows_per_slot / 256;
   const int64_t units = int64_t(n_slots) * n_rt * (K / 256);
   const int blocks = int(std::min<int64_t>(units, 148 * 8));
-  fp4_tile_kernel<<<blocks, 256, 0, s>>>(codes, scales, n_slots, rows_per_slot, K, 2, n_rt, gate_up ? 128 : 256,
-                                         gate_up ? rows_per_slot / 2 : 128, out);
+  auto kernel = mx ? fp4_tile_kernel<1> : fp4_tile_kernel<0>;
+  kernel<<<blocks, 256, 0, s>>>(codes, scales, n_slots, rows_per_slot, K, 2, n_rt, gate_up ? 128 : 256,
+                                gate_up ? rows_per_slot / 2 : 128, out);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

@@ -115,17 +115,17 @@ struct Fp4Args {
   int H;
   uint32_t* err;
 };
-int launch_fp4_gemm(cudaStream_t s, int epi, int rc, const Fp4Args& a, const void* map_x, int grid);
+int launch_fp4_gemm(cudaStream_t s, int epi, int rc, bool mx, const Fp4Args& a, const void* map_x, int grid);
 // routes per chunk of the block-scaled FP4 path for a call of S routes (the MMA's N is 4 x this)
 inline int fp4_routes_per_chunk(int S) { return S <= 64 ? 4 : S <= 1024 ? 8 : 16; }
-int launch_fp4_planes(cudaStream_t s, bool by_token, bool bf16, const void* src, int64_t src_stride, int K,
+int launch_fp4_planes(cudaStream_t s, bool by_token, bool bf16, bool mx, const void* src, int64_t src_stride, int K,
                       const int32_t* inv, int top_k, const int32_t* chunk_of, int bank,
                       const int32_t* bank_range, int max_rows, uint32_t* rowmax, uint8_t* planes, int plane_rows,
                       uint8_t* sfb, float* gx);
 int launch_route_combine(cudaStream_t s, const __half* y2, const int32_t* inv, const int32_t* bank_range,
                          int n_banks, const float* w, int T, int k, int H, float* out);
-int launch_fp4_tile(cudaStream_t s, const uint8_t* codes, const uint8_t* scales, int n_slots, int rows_per_slot,
-                    int K, bool gate_up, uint8_t* out);
+int launch_fp4_tile(cudaStream_t s, bool mx, const uint8_t* codes, const uint8_t* scales, int n_slots,
+                    int rows_per_slot, int K, bool gate_up, uint8_t* out);
 // 2D uint8 TMA map with 128-byte swizzle: rows x row_bytes, box box_bytes x box_rows, zero fill out of range
 int make_u8_tile_map(void* map_out, const void* base, int64_t rows, int64_t row_bytes, int box_bytes, int box_rows);
 

@@ -293,7 +293,7 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   }
   for (int epi = 0; epi < 2; ++epi) {
     if (f4) {  // the FP4 bank's activation rows as E2M1 planes for its block-scaled GEMM
-      if (launch_fp4_planes(s, epi == 0, epi == 0 && x_bf16_direct,
+      if (launch_fp4_planes(s, epi == 0, epi == 0 && x_bf16_direct, c.fp4_format == B200MOE_MXFP4,
                             epi == 0 ? (x_bf16_direct ? x : static_cast<const void*>(xsrc)) : ws.inter,
                             epi == 0 ? c.hidden : c.inter,
                             epi == 0 ? c.hidden : c.inter, L->route_pos, c.top_k, L->f4_chunk_of, 0,
@@ -312,7 +312,7 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
       if (f4 && b == 0) {
         Fp4Args f{};
         f.wt = L->f4_units[epi];
-        f.globals = L->globals;
+        f.globals = c.fp4_format == B200MOE_NVFP4 ? L->globals : nullptr;  // MXFP4 has no FP32 global scale
         f.K = epi == 0 ? c.hidden : c.inter;
         f.n_rt = epi == 0 ? c.inter / 128 : c.hidden / 256;  // items of two 128-row tiles
         f.sfb = L->f4_sfb[epi];
@@ -336,7 +336,8 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
         f.H = c.hidden;
         f.err = L->err;
         const int rc = fp4_routes_per_chunk(S);
-        if (launch_fp4_gemm(s, epi, rc, f, L->f4_map_x[epi][rc == 4 ? 0 : rc == 8 ? 1 : 2], L->grid))
+        if (launch_fp4_gemm(s, epi, rc, c.fp4_format == B200MOE_MXFP4, f, L->f4_map_x[epi][rc == 4 ? 0 : rc == 8 ? 1 : 2],
+                            L->grid))
           return B200MOE_ERR_CUDA;
         marks.mark();
         continue;
@@ -451,7 +452,7 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
   if (c.n_iq2 > 0 && c.inter % 256) return B200MOE_ERR_INVALID_ARG;
   if (c.prefill_gemm < 0 || c.prefill_gemm > 2) return B200MOE_ERR_INVALID_ARG;
   // the block-scaled FP4 path: NVFP4 (E4M3 scales per 16), K tiles of 256 on both projections
-  if (c.prefill_gemm == 2 && (c.fp4_format != B200MOE_NVFP4 || c.hidden % 256 || c.inter % 256))
+  if (c.prefill_gemm == 2 && (c.hidden % 256 || c.inter % 256))
     return B200MOE_ERR_INVALID_ARG;
   DeviceGuard guard(device);
   cudaDeviceProp prop;
@@ -618,8 +619,9 @@ int b200moe_load_fp4(b200moe_layer* L, void* stream, int slot_begin, int n, cons
     return B200MOE_ERR_CUDA;
   if (c.prefill_gemm == 2) {  // weight units for the block-scaled tensor path
     const size_t H = c.hidden, I = c.inter, b = size_t(slot_begin);
-    if (launch_fp4_tile(s, w13c, w13s, n, int(2 * I), int(H), true, L->f4_units[0] + b * 2 * I * (H / 2 + H / 16)) ||
-        launch_fp4_tile(s, w2c, w2s, n, int(H), int(I), false, L->f4_units[1] + b * H * (I / 2 + I / 16)))
+    const bool mx = c.fp4_format == B200MOE_MXFP4;
+    if (launch_fp4_tile(s, mx, w13c, w13s, n, int(2 * I), int(H), true, L->f4_units[0] + b * 2 * I * (H / 2 + H / 16)) ||
+        launch_fp4_tile(s, mx, w2c, w2s, n, int(H), int(I), false, L->f4_units[1] + b * H * (I / 2 + I / 16)))
       return B200MOE_ERR_CUDA;
     return B200MOE_OK;
   }

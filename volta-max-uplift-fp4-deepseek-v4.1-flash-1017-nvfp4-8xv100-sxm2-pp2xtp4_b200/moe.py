@@ -45,12 +45,13 @@ class B200NativeMoe:
     ``prefill_gemm`` picks the FP4 bank's kernels: "tcgen05" (forward_prefill
     on the tensor-core grouped GEMM over dequantized f16 tiles, 128-route
     tiles; decode on the skinny kernels), "skinny" (the skinny kernels for
-    both) or "fp4" (NVFP4 only, hidden and inter multiples of 256: every
-    FP4-bank launch, decode and prefill, on the block-scaled FP4 tensor cores,
-    tcgen05.mma.kind::mxf4nvf4, with the activations as four E2M1 planes
-    (~1e-4 relative); the fastest decode, while long prefills are faster on
-    "tcgen05"; the bank is stored as swizzled weight units, so forward_static
-    refuses such a layer).  IQ2_XXS experts always use their int8 kernel.
+    both) or "fp4" (hidden and inter multiples of 256: every FP4-bank launch,
+    decode and prefill, on the block-scaled FP4 tensor cores,
+    tcgen05.mma.kind::mxf4nvf4 with the format's own block scales (E4M3 per 16
+    or E8M0 per 32), the activations as four E2M1 planes (~1e-4 relative); the
+    fastest decode, while long prefills are faster on "tcgen05"; the bank is
+    stored as swizzled weight units, so forward_static refuses such a layer).
+    IQ2_XXS experts always use their int8 kernel.
     """
 
     def __init__(self, *, hidden: int, inter: int, num_experts: int, top_k: int, max_tokens: int,
