@@ -50,16 +50,27 @@ constexpr uint32_t kTmemCols = 2 * BNW;  // 512
 constexpr int kUnits = BNW / 32;         // tile pairs per item
 constexpr int kListInts = 1 + 2 * 32 * (BNW / 32);  // per epilogue warp: count + (token, tile) pairs
 
+// FMT 0 / 1: NVFP4 / MXFP4 in the decode bank's units (tile pair x 128 K, eight
+// per raw stage: 256 weight rows x 128 K).  FMT 2: NVFP4 weight units of the
+// block-scaled path's layout (two 128-row tiles x 256 K, codes swizzled, E4M3
+// scales blocked), one per raw stage; fewer token and weight stages keep the
+// larger raw stages inside shared memory.
 template <int FMT>
 struct TcFmt {
-  static constexpr int U = fp4_unit_bytes(FMT);  // one bank unit (tile pair x 128 K)
-  static constexpr int RAW = kUnits * U;         // eight tile pairs = 256 weight rows
+  static constexpr bool kWeightUnits = FMT == 2;
+  static constexpr int U = kWeightUnits ? 2 * (128 * 128 + 4 * 512) : fp4_unit_bytes(FMT);
+  static constexpr int RAW = kWeightUnits ? U : kUnits * U;
+  static constexpr int KB_PER_RAW = kWeightUnits ? 4 : 2;  // 64-wide K blocks per raw stage
+  static constexpr int KT = kWeightUnits ? 256 : kFp4KTile;  // K per unit
+  static constexpr int TOK_STAGES = kWeightUnits ? 4 : kTokStages;
+  static constexpr int W_STAGES = kWeightUnits ? 2 : kWStages;
 };
 
 template <int FMT>
 constexpr size_t tc_smem() {
-  return 1024 /*align*/ + size_t(kTokStages) * kTokBytes + size_t(kWStages) * kWBytes +
-         size_t(kRawStages) * TcFmt<FMT>::RAW + 4 * kListInts * 4 /*completion lists*/ + 256 /*barriers*/;
+  using F = TcFmt<FMT>;
+  return 1024 /*align*/ + size_t(F::TOK_STAGES) * kTokBytes + size_t(F::W_STAGES) * kWBytes +
+         size_t(kRawStages) * F::RAW + 4 * kListInts * 4 /*completion lists*/ + 256 /*barriers*/;
 }
 
 // ---- tcgen05 helpers
@@ -128,6 +139,8 @@ template <int FMT, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmap) {
   using F = TcFmt<FMT>;
+  constexpr int kTokStages = F::TOK_STAGES, kWStages = F::W_STAGES;
+  static_assert(tc_smem<FMT>() <= 227 * 1024, "shared memory");
   extern __shared__ uint8_t smem_raw[];
   // 1024-aligned tiles (swizzle atoms)
   const uint32_t base_u32 = (smem_u32(smem_raw) + 1023u) & ~1023u;
@@ -181,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = tmem_base_sh;
 
   const int n_kb = a.K / BK;
-  const int n_kt = a.K / kFp4KTile;
+  const int n_kt = a.K / F::KT;
   const int n_items = a.n_chunks[a.bank] * a.n_rt;
 
   auto item_ok = [&](const Chunk& ch) {
@@ -204,7 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int rt = item % a.n_rt;
         const uint8_t* wbase = a.region + int64_t(ch.slot) * a.slot_stride;
         for (int kb = 0; kb < n_kb; ++kb) {
-          if ((kb & 1) == 0) {
+          if (kb % F::KB_PER_RAW == 0) {
             const int r = graw % kRawStages;
             const uint32_t ph = (graw / kRawStages) & 1u;
             if (*abort_ptr || !mbar_wait(&raw_empty[r], ph ^ 1u, a.err)) {
@@ -212,11 +225,15 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             mbar_arrive_expect_tx(&raw_full[r], uint32_t(F::RAW));
-            const int kt = kb >> 1;
-            for (int u = 0; u < kUnits; ++u) {
-              const int tp = rt * kUnits + u;
-              bulk_g2s_hint(raw + r * F::RAW + u * F::U, wbase + (int64_t(tp) * n_kt + kt) * F::U, F::U,
-                            &raw_full[r], pol);
+            const int kt = kb / F::KB_PER_RAW;
+            if (F::kWeightUnits) {  // the item's weight unit of this K tile: one copy
+              bulk_g2s_hint(raw + r * F::RAW, wbase + (int64_t(rt) * n_kt + kt) * F::U, F::U, &raw_full[r], pol);
+            } else {
+              for (int u = 0; u < kUnits; ++u) {
+                const int tp = rt * kUnits + u;
+                bulk_g2s_hint(raw + r * F::RAW + u * F::U, wbase + (int64_t(tp) * n_kt + kt) * F::U, F::U,
+                              &raw_full[r], pol);
+              }
             }
             issued_r |= 1u << r;
             par_r = (par_r & ~(1u << r)) | (ph << r);
@@ -300,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kb = 0; kb < n_kb && ok; ++kb, ++gk) {
         const int rs = graw % kRawStages;
         const uint32_t rph = (graw / kRawStages) & 1u;
-        if ((kb & 1) == 0) {
+        if (kb % F::KB_PER_RAW == 0) {
           ok = !*abort_ptr && mbar_wait(&raw_full[rs], rph, a.err);
           ok = __all_sync(0xffffffffu, ok);
           if (!ok) break;
@@ -312,6 +329,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         uint8_t* dst = wt + sw * kWBytes;
         const int half = kb & 1;
+        if (F::kWeightUnits) {
+          // one weight row per thread: B row = its row in the unit (W13: gate tile then up tile; W2: the
+          // 256 rows in order), the 64 K of this block = 16-byte chunks 2 q, 2 q + 1 of the swizzled row
+          const int row = dw * 32 + lane, tile = row >> 7, rr = row & 127, q4 = kb & 3;
+          const uint8_t* unit = raw + rs * F::RAW;
+          const uint8_t* crow = unit + tile * (128 * 128) + rr * 128;
+          const uint32_t sw4 =
+              *reinterpret_cast<const uint32_t*>(unit + 2 * (128 * 128) + tile * 2048 + q4 * 512 + (rr & 31) * 16 +
+                                                 (rr >> 5) * 4);
+          const uint32_t p01 = e4m3x2_to_f16x2(sw4 & 0xffffu), p23 = e4m3x2_to_f16x2(sw4 >> 16);
+          const uint32_t sc[4] = {lo_half2(p01), hi_half2(p01), lo_half2(p23), hi_half2(p23)};
+          uint8_t* drow = dst + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            const int c = 2 * q4 + cc;
+            const uint4 cw = *reinterpret_cast<const uint4*>(crow + ((c ^ (rr & 7)) << 4));
+            const uint32_t wv[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {  // elements 32 cc + 8 w .. +7: 16-wide block 2 cc + w / 2
+              uint32_t o[4];
+              e2m1x8_scaled(wv[w], sc[2 * cc + (w >> 1)], o);
+              *reinterpret_cast<uint4*>(drow + (((4 * cc + w) ^ (row & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+          }
+        } else {
 #pragma unroll
         for (int pc = dw; pc < 2 * kUnits; pc += kDequantWarps) {
           const int u = pc >> 1, mt = pc & 1;
@@ -348,13 +390,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+        }
         fence_proxy_async();
         __syncwarp();
+        const bool raw_done = kb % F::KB_PER_RAW == F::KB_PER_RAW - 1;
         if (lane == 0) {
           mbar_arrive(&w_full[sw]);
-          if (half == 1) mbar_arrive(&raw_empty[rs]);
+          if (raw_done) mbar_arrive(&raw_empty[rs]);
         }
-        if (half == 1) ++graw;
+        if (raw_done) ++graw;
       }
       if (!ok) {
         *abort_ptr = 1;
@@ -543,6 +587,7 @@ int make_u8_tile_map(void* map_out, const void* base, int64_t rows, int64_t row_
 int launch_tc_gemm(cudaStream_t s, int fmt, int epi, const TcArgs& a, const void* map, int grid) {
   if (fmt == 0) return epi == 0 ? launch_tc_one<0, 0>(s, a, map, grid) : launch_tc_one<0, 1>(s, a, map, grid);
   if (fmt == 1) return epi == 0 ? launch_tc_one<1, 0>(s, a, map, grid) : launch_tc_one<1, 1>(s, a, map, grid);
+  if (fmt == 2) return epi == 0 ? launch_tc_one<2, 0>(s, a, map, grid) : launch_tc_one<2, 1>(s, a, map, grid);
   return -1;
 }
 

@@ -180,6 +180,8 @@ size_t tc_map_bytes();
 int launch_gather_rows(cudaStream_t s, const void* x, int bf16, const int32_t* perm, int S, int k, int H,
                        void* xperm);
 constexpr int kTcTokenTile = 128;
+// prefill calls of at least this many routes run an NVFP4 block-scaled-layout bank on the tcgen05 f16 GEMM
+constexpr int kTcUnitsMinRoutes = 4096;
 
 size_t gemv_smem_bytes(int fmt, int ks);
 int gemv_ctas_per_sm(int fmt);

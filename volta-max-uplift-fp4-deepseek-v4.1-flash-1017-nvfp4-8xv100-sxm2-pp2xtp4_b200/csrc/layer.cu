@@ -242,8 +242,10 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
     marks.mark();
   }
   // prefill with the tcgen05 GEMM: the FP4 bank's chunks are 128-route token tiles
-  const bool tc = !rows && prefill && c.prefill_gemm == 1 && c.n_fp4 > 0 && L->xperm;
-  const bool f4 = c.prefill_gemm == 2 && c.n_fp4 > 0;
+  // (NVFP4 weight units of the block-scaled layout feed the tcgen05 GEMM too: long prefills run there)
+  const bool tc_units = c.prefill_gemm == 2 && c.fp4_format == B200MOE_NVFP4 && S >= kTcUnitsMinRoutes;
+  const bool tc = !rows && prefill && (c.prefill_gemm == 1 || tc_units) && c.n_fp4 > 0 && L->xperm;
+  const bool f4 = c.prefill_gemm == 2 && c.n_fp4 > 0 && !tc;
   if (f4 && !ws.own) return B200MOE_ERR_STATE;  // the static array holds no plane buffers
   // W2 writes y2 rows only and one launch after it does the slot-order combine: fused into the W2
   // epilogue the combine's fences, atomics and re-reads stall the pipeline (measured on B200: the
@@ -344,8 +346,14 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
       }
       if (tc && b == 0) {
         TcArgs t{};
-        t.region = L->bank[0] + (epi == 0 ? 0 : L->geom[0].w13_bytes);
-        t.slot_stride = L->geom[0].slot_bytes;
+        if (c.prefill_gemm == 2) {  // weight units: [slot][rt][kt] of 36 KB
+          t.region = L->f4_units[epi];
+          t.slot_stride = epi == 0 ? int64_t(2) * c.inter * (c.hidden / 2 + c.hidden / 16)
+                                   : int64_t(c.hidden) * (c.inter / 2 + c.inter / 16);
+        } else {
+          t.region = L->bank[0] + (epi == 0 ? 0 : L->geom[0].w13_bytes);
+          t.slot_stride = L->geom[0].slot_bytes;
+        }
         t.n_slots = n_slots;
         t.globals = L->globals;
         t.K = epi == 0 ? c.hidden : c.inter;
@@ -365,7 +373,8 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
         t.out = out;
         t.H = c.hidden;
         t.err = L->err;
-        if (launch_tc_gemm(s, c.fp4_format, epi, t, epi == 0 ? L->map_x : L->map_inter, L->grid))
+        if (launch_tc_gemm(s, c.prefill_gemm == 2 ? 2 : c.fp4_format, epi, t, epi == 0 ? L->map_x : L->map_inter,
+                           L->grid))
           return B200MOE_ERR_CUDA;
         marks.mark();
         continue;
@@ -522,7 +531,8 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
          make_u8_tile_map(L->f4_map_x[1][2], L->f4_planes[1], int64_t(P * R), I / 2, 128, 16 * kFp4Planes)))
       st = B200MOE_ERR_CUDA;
   }
-  if (c.prefill_gemm == 1 && c.max_prefill_tokens > 0 && c.n_fp4 > 0) {
+  if ((c.prefill_gemm == 1 || (c.prefill_gemm == 2 && c.fp4_format == B200MOE_NVFP4)) && c.max_prefill_tokens > 0 &&
+      c.n_fp4 > 0) {
     take(dalloc(&L->xperm, size_t(L->s_max) * c.hidden));
     if (st == B200MOE_OK && (make_token_map(L->map_x, L->xperm, L->s_max, c.hidden) ||
                              make_token_map(L->map_inter, L->inter, L->s_max, c.inter)))
