@@ -99,8 +99,9 @@ def parse():
                     help="fix the GEMV split-K (0 = chosen per call; set only to give a small ncu capture "
                          "the split-K of the full-size run)")
     ap.add_argument("--gemm", choices=["fp4", "gemv"], default="fp4",
-                    help="c1, c2, c4: the NVFP4 bank on the block-scaled FP4 tensor path (tcgen05.mma "
-                         "kind::mxf4nvf4, default) or on the skinny GEMV")
+                    help="c1, c2, c4: the FP4 bank on the block-scaled FP4 tensor path (tcgen05.mma "
+                         "kind::mxf4nvf4, default) or on the skinny GEMV; c3: the tcgen05 prefill GEMM reading "
+                         "the block-scaled layout's weight units (default) or the decode bank's units")
     ap.add_argument("--profile", action="store_true",
                     help="warm-up + timed steps only (no per-launch, e2e or CPU passes): the ncu command")
     a = ap.parse_args()
@@ -624,9 +625,10 @@ def run_c3(job) -> None:
     from b200moe import moe, synth
 
     args, dev, T = job.args, job.dev, job.args.tokens
+    units = args.gemm == "fp4"  # the block-scaled layout's weight units also feed the tcgen05 prefill GEMM
     layer = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, max_tokens=8,
                               tier=np.zeros(E, np.int8), fp4_format="mxfp4", device=dev, max_prefill_tokens=T,
-                              prefill_gemm="tcgen05")
+                              prefill_gemm="fp4" if units else "tcgen05")
     bank = synth.make_fp4_bank(E, H, I, "mxfp4", 3000, dev)
     synth.load_bank(layer, bank)
     layer.check_errors()
@@ -638,7 +640,10 @@ def run_c3(job) -> None:
         profile_run(layer, lambda: layer.forward_prefill(x, *layer.route(logits)), args, {"tokens": T})
         return
     config = {"workload": f"configs[3] prefill layer: hidden {H}, {E} experts MXFP4, inter {I}, top-{K_TOP}, T={T}",
-              "tokens_per_step": T, "format": "mxfp4", "gemm": "tcgen05 grouped GEMM (kind::f16, TMEM accumulators)",
+              "tokens_per_step": T, "format": "mxfp4",
+              "gemm": "tcgen05 grouped GEMM (kind::f16, TMEM accumulators) on " +
+                      ("the weight units of the block-scaled layout (one bulk copy per 256-K unit, per-row dequant)"
+                       if units else "the decode bank's units"),
               "l2": "inputs larger than L2 (all 384 experts, 5.1 GB, streamed per step)",
               "parallelism": "single GPU"}
 
@@ -698,7 +703,8 @@ def run_c3(job) -> None:
             "e2e": {"value": job.world * T / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": int(hx.numel() * 2 + hl.numel() * 4),
                     "d2h_bytes_per_step": int(hout.numel() * 4)},
-            "gpu_launches": 7 * steps,  # gating, bf16 copy, plan, row gather, W13, W2, combine
+            # gating, [bf16 copy], plan, row gather (converts bf16 itself), W13, W2, combine
+            "gpu_launches": (6 if units else 7) * steps,
             "cpu_baseline": cpu,
             "clocks": clk,
         })

@@ -346,13 +346,14 @@ def test_all_iq2_layer(dev, pkg, m):
 
 @pytest.mark.parametrize("m,mixed,fmt", [(1, False, "nvfp4"), (8, False, "nvfp4"), (64, False, "nvfp4"),
                                          (300, False, "nvfp4"), (32, True, "nvfp4"), (600, True, "nvfp4"),
-                                         (1, False, "mxfp4"), (64, False, "mxfp4"), (300, True, "mxfp4")])
+                                         (1, False, "mxfp4"), (64, False, "mxfp4"), (300, True, "mxfp4"),
+                                         (600, False, "mxfp4")])
 def test_block_scaled_fp4_path(dev, pkg, m, mixed, fmt):
     """prefill_gemm="fp4": the FP4 bank on tcgen05.mma.kind::mxf4nvf4 (E2M1 x E2M1
     with E4M3 block scales per 16 for NVFP4, E8M0 per 32 for MXFP4; activations
     as four E2M1 planes), decode and prefill, against the fp32
-    dequant-then-matmul reference.  Prefills of >= 4096 NVFP4 routes (m = 600)
-    run the same weight units through the tcgen05 f16 grouped GEMM."""
+    dequant-then-matmul reference.  Prefills of >= 4096 routes (m = 600) run
+    the same weight units through the tcgen05 f16 grouped GEMM."""
     from b200moe import tiers
 
     H, I, E, K = 2048, 1024, 64, 8

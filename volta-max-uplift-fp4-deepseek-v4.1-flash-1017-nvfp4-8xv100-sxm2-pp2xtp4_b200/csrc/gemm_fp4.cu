@@ -590,9 +590,14 @@ __global__ void fp4_combine_kernel(const __half* __restrict__ y2, const int32_t*
 // its four 512-byte scale blocks, one per 64-wide K step q (byte m0 * 16 +
 // m1 * 4 + s of block q = the scale of row m1 * 32 + m0, K block 4 q + s for
 // NVFP4, 2 q + s for MXFP4, whose bytes 2 and 3 stay zero).
+// MXFP4 (globals given): a nonzero block whose exponent falls outside the f16
+// range of its projection's rebase (global 2^(emax - 140)) is flagged
+// B200MOE_ERR_RANGE, as the decode bank's prepack does: the tcgen05 prefill
+// dequantizes to f16 with that rebase.
 template <int MX>
 __global__ void fp4_tile_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ scales, int n_slots,
                                 int rows_per_slot, int K, int n_tiles, int n_rt, int rt_rows, int tile_rows,
+                                const float* __restrict__ globals, int proj0, uint32_t* err,
                                 uint8_t* __restrict__ out) {
   const int n_kt = K / 256;
   const int64_t unit_bytes = int64_t(n_tiles) * (kATile + kSFBytes);
@@ -613,6 +618,18 @@ __global__ void fp4_tile_kernel(const uint8_t* __restrict__ codes, const uint8_t
         const uint32_t v =
             MX ? uint32_t(*reinterpret_cast<const uint16_t*>(scales + (row0 + r) * (K / 32) + kt * 8 + q * 2))
                : *reinterpret_cast<const uint32_t*>(scales + (row0 + r) * (K / 16) + kt * 16 + q * 4);
+        if (MX && globals) {
+          const int proj = proj0 + (proj0 == 0 ? j : 0);  // W13: tile 0 = W1, tile 1 = W3; W2: 2
+          int gexp;
+          frexpf(globals[slot * 3 + proj], &gexp);
+#pragma unroll
+          for (int b = 0; b < 2; ++b) {
+            const uint4 cw = *reinterpret_cast<const uint4*>(codes + (row0 + r) * (K / 2) + kt * 128 + (2 * q + b) * 16);
+            const bool zero = ((cw.x | cw.y | cw.z | cw.w) & 0x77777777u) == 0;
+            const int f = int((v >> (8 * b)) & 255u) - 127 - (gexp - 1) + 15;
+            if (!zero && (f < 1 || f > 30)) set_error(err, kErrRange);
+          }
+        }
         *reinterpret_cast<uint32_t*>(dst + n_tiles * kATile + j * kSFBytes + q * 512 + (r & 31) * 16 + (r >> 5) * 4) = v;
       }
     }
@@ -684,7 +701,7 @@ int launch_route_combine(cudaStream_t s, const __half* y2, const int32_t* inv, c
 }
 
 int launch_fp4_tile(cudaStream_t s, bool mx, const uint8_t* codes, const uint8_t* scales, int n_slots,
-                    int rows_per_slot, int K, bool gate_up, uint8_t* out) {
+                    int rows_per_slot, int K, bool gate_up, const float* globals, uint32_t* err, uint8_t* out) {
   // W13 (gate_up): tile 0 = rows rt * 128 .. of W1, tile 1 the same rows of W3;
   // W2: tiles 0 and 1 = rows rt * 256 .. and rt * 256 + 128 ..
   if (K % 256 || rows_per_slot % 256 || n_slots < 1) return -1;
@@ -693,7 +710,7 @@ int launch_fp4_tile(cudaStream_t s, bool mx, const uint8_t* codes, const uint8_t
   const int blocks = int(std::min<int64_t>(units, 148 * 8));
   auto kernel = mx ? fp4_tile_kernel<1> : fp4_tile_kernel<0>;
   kernel<<<blocks, 256, 0, s>>>(codes, scales, n_slots, rows_per_slot, K, 2, n_rt, gate_up ? 128 : 256,
-                                gate_up ? rows_per_slot / 2 : 128, out);
+                                gate_up ? rows_per_slot / 2 : 128, globals, gate_up ? 0 : 2, err, out);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

@@ -51,13 +51,15 @@ constexpr int kUnits = BNW / 32;         // tile pairs per item
 constexpr int kListInts = 1 + 2 * 32 * (BNW / 32);  // per epilogue warp: count + (token, tile) pairs
 
 // FMT 0 / 1: NVFP4 / MXFP4 in the decode bank's units (tile pair x 128 K, eight
-// per raw stage: 256 weight rows x 128 K).  FMT 2: NVFP4 weight units of the
-// block-scaled path's layout (two 128-row tiles x 256 K, codes swizzled, E4M3
-// scales blocked), one per raw stage; fewer token and weight stages keep the
-// larger raw stages inside shared memory.
+// per raw stage: 256 weight rows x 128 K).  FMT 2 / 3: NVFP4 / MXFP4 weight
+// units of the block-scaled path's layout (two 128-row tiles x 256 K, codes
+// swizzled, scales blocked), one per raw stage; fewer token and weight stages
+// keep the larger raw stages inside shared memory.  MXFP4 scales are rebased
+// on the fly by the projection's global (2^(emax - 140)), as the decode bank's
+// prepack stores them.
 template <int FMT>
 struct TcFmt {
-  static constexpr bool kWeightUnits = FMT == 2;
+  static constexpr bool kWeightUnits = FMT >= 2;
   static constexpr int U = kWeightUnits ? 2 * (128 * 128 + 4 * 512) : fp4_unit_bytes(FMT);
   static constexpr int RAW = kWeightUnits ? U : kUnits * U;
   static constexpr int KB_PER_RAW = kWeightUnits ? 4 : 2;  // 64-wide K blocks per raw stage
@@ -338,8 +340,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sw4 =
               *reinterpret_cast<const uint32_t*>(unit + 2 * (128 * 128) + tile * 2048 + q4 * 512 + (rr & 31) * 16 +
                                                  (rr >> 5) * 4);
-          const uint32_t p01 = e4m3x2_to_f16x2(sw4 & 0xffffu), p23 = e4m3x2_to_f16x2(sw4 >> 16);
-          const uint32_t sc[4] = {lo_half2(p01), hi_half2(p01), lo_half2(p23), hi_half2(p23)};
+          uint32_t sc[4];
+          if (FMT == 2) {  // four E4M3 scales, one per 16
+            const uint32_t p01 = e4m3x2_to_f16x2(sw4 & 0xffffu), p23 = e4m3x2_to_f16x2(sw4 >> 16);
+            sc[0] = lo_half2(p01);
+            sc[1] = hi_half2(p01);
+            sc[2] = lo_half2(p23);
+            sc[3] = hi_half2(p23);
+          } else {  // two E8M0 scales, one per 32, as f16 2^(e - 127 - rebase)
+            int gexp;
+            frexpf(a.globals[ch.slot * 3 + (EPI == 0 ? tile : 2)], &gexp);  // global = 2^(gexp - 1)
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              int f = int((sw4 >> (8 * j)) & 255u) - 127 - (gexp - 1) + 15;
+              f = f < 1 ? 1 : f > 30 ? 30 : f;  // out-of-range blocks are all-zero (checked at load)
+              sc[2 * j] = sc[2 * j + 1] = (uint32_t(f) << 10) * 0x10001u;
+            }
+          }
           uint8_t* drow = dst + (row >> 3) * 1024 + (row & 7) * 128;
 #pragma unroll
           for (int cc = 0; cc < 2; ++cc) {
@@ -588,6 +605,7 @@ int launch_tc_gemm(cudaStream_t s, int fmt, int epi, const TcArgs& a, const void
   if (fmt == 0) return epi == 0 ? launch_tc_one<0, 0>(s, a, map, grid) : launch_tc_one<0, 1>(s, a, map, grid);
   if (fmt == 1) return epi == 0 ? launch_tc_one<1, 0>(s, a, map, grid) : launch_tc_one<1, 1>(s, a, map, grid);
   if (fmt == 2) return epi == 0 ? launch_tc_one<2, 0>(s, a, map, grid) : launch_tc_one<2, 1>(s, a, map, grid);
+  if (fmt == 3) return epi == 0 ? launch_tc_one<3, 0>(s, a, map, grid) : launch_tc_one<3, 1>(s, a, map, grid);
   return -1;
 }
 

@@ -15,6 +15,9 @@ constexpr int kFp4Planes = 4;
 constexpr int kFp4TcRoutes = 16;  // largest routes per chunk of the block-scaled FP4 path
 
 // ---- packing (pack.cu)
+// MXFP4: per (slot, projection) global 2^(emax - 140) so the largest nonzero block maps to f16 exponent 28
+int launch_mx_rebase(cudaStream_t s, int hidden, int inter, int n, const uint8_t* w13c, const uint8_t* w13s,
+                     const uint8_t* w2c, const uint8_t* w2s, float* slot_globals, int* span_scratch, uint32_t* err);
 int launch_fp4_prepack(cudaStream_t s, int fmt, int hidden, int inter, int n, const uint8_t* w13c,
                        const uint8_t* w13s, const uint8_t* w2c, const uint8_t* w2s, float* slot_globals,
                        int* span_scratch, uint8_t* bank_slot0, int64_t slot_stride, int64_t w13_bytes,
@@ -125,7 +128,7 @@ int launch_fp4_planes(cudaStream_t s, bool by_token, bool bf16, bool mx, const v
 int launch_route_combine(cudaStream_t s, const __half* y2, const int32_t* inv, const int32_t* bank_range,
                          int n_banks, const float* w, int T, int k, int H, float* out);
 int launch_fp4_tile(cudaStream_t s, bool mx, const uint8_t* codes, const uint8_t* scales, int n_slots,
-                    int rows_per_slot, int K, bool gate_up, uint8_t* out);
+                    int rows_per_slot, int K, bool gate_up, const float* globals, uint32_t* err, uint8_t* out);
 // 2D uint8 TMA map with 128-byte swizzle: rows x row_bytes, box box_bytes x box_rows, zero fill out of range
 int make_u8_tile_map(void* map_out, const void* base, int64_t rows, int64_t row_bytes, int box_bytes, int box_rows);
 
@@ -180,7 +183,7 @@ size_t tc_map_bytes();
 int launch_gather_rows(cudaStream_t s, const void* x, int bf16, const int32_t* perm, int S, int k, int H,
                        void* xperm);
 constexpr int kTcTokenTile = 128;
-// prefill calls of at least this many routes run an NVFP4 block-scaled-layout bank on the tcgen05 f16 GEMM
+// prefill calls of at least this many routes run a block-scaled-layout bank on the tcgen05 f16 GEMM
 constexpr int kTcUnitsMinRoutes = 4096;
 
 size_t gemv_smem_bytes(int fmt, int ks);

@@ -243,7 +243,7 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   }
   // prefill with the tcgen05 GEMM: the FP4 bank's chunks are 128-route token tiles
   // (NVFP4 weight units of the block-scaled layout feed the tcgen05 GEMM too: long prefills run there)
-  const bool tc_units = c.prefill_gemm == 2 && c.fp4_format == B200MOE_NVFP4 && S >= kTcUnitsMinRoutes;
+  const bool tc_units = c.prefill_gemm == 2 && S >= kTcUnitsMinRoutes;
   const bool tc = !rows && prefill && (c.prefill_gemm == 1 || tc_units) && c.n_fp4 > 0 && L->xperm;
   const bool f4 = c.prefill_gemm == 2 && c.n_fp4 > 0 && !tc;
   if (f4 && !ws.own) return B200MOE_ERR_STATE;  // the static array holds no plane buffers
@@ -373,8 +373,8 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
         t.out = out;
         t.H = c.hidden;
         t.err = L->err;
-        if (launch_tc_gemm(s, c.prefill_gemm == 2 ? 2 : c.fp4_format, epi, t, epi == 0 ? L->map_x : L->map_inter,
-                           L->grid))
+        const int tfmt = c.prefill_gemm == 2 ? (c.fp4_format == B200MOE_NVFP4 ? 2 : 3) : c.fp4_format;
+        if (launch_tc_gemm(s, tfmt, epi, t, epi == 0 ? L->map_x : L->map_inter, L->grid))
           return B200MOE_ERR_CUDA;
         marks.mark();
         continue;
@@ -531,8 +531,7 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
          make_u8_tile_map(L->f4_map_x[1][2], L->f4_planes[1], int64_t(P * R), I / 2, 128, 16 * kFp4Planes)))
       st = B200MOE_ERR_CUDA;
   }
-  if ((c.prefill_gemm == 1 || (c.prefill_gemm == 2 && c.fp4_format == B200MOE_NVFP4)) && c.max_prefill_tokens > 0 &&
-      c.n_fp4 > 0) {
+  if (c.prefill_gemm >= 1 && c.max_prefill_tokens > 0 && c.n_fp4 > 0) {
     take(dalloc(&L->xperm, size_t(L->s_max) * c.hidden));
     if (st == B200MOE_OK && (make_token_map(L->map_x, L->xperm, L->s_max, c.hidden) ||
                              make_token_map(L->map_inter, L->inter, L->s_max, c.inter)))
@@ -627,11 +626,16 @@ int b200moe_load_fp4(b200moe_layer* L, void* stream, int slot_begin, int n, cons
   if (c.fp4_format == B200MOE_NVFP4 &&
       cudaMemcpyAsync(gdst, globals, size_t(n) * 12, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
     return B200MOE_ERR_CUDA;
-  if (c.prefill_gemm == 2) {  // weight units for the block-scaled tensor path
+  if (c.prefill_gemm == 2) {  // weight units for the block-scaled tensor path (and the tcgen05 prefill)
     const size_t H = c.hidden, I = c.inter, b = size_t(slot_begin);
     const bool mx = c.fp4_format == B200MOE_MXFP4;
-    if (launch_fp4_tile(s, mx, w13c, w13s, n, int(2 * I), int(H), true, L->f4_units[0] + b * 2 * I * (H / 2 + H / 16)) ||
-        launch_fp4_tile(s, mx, w2c, w2s, n, int(H), int(I), false, L->f4_units[1] + b * H * (I / 2 + I / 16)))
+    if (mx && launch_mx_rebase(s, c.hidden, c.inter, n, w13c, w13s, w2c, w2s, gdst, L->span, L->err))
+      return B200MOE_ERR_CUDA;
+    const float* g = mx ? gdst : nullptr;
+    if (launch_fp4_tile(s, mx, w13c, w13s, n, int(2 * I), int(H), true, g, L->err,
+                        L->f4_units[0] + b * 2 * I * (H / 2 + H / 16)) ||
+        launch_fp4_tile(s, mx, w2c, w2s, n, int(H), int(I), false, g, L->err,
+                        L->f4_units[1] + b * H * (I / 2 + I / 16)))
       return B200MOE_ERR_CUDA;
     return B200MOE_OK;
   }

@@ -291,6 +291,17 @@ static inline int grid_for(int64_t n, int block) {
   return int(g < 1 ? 1 : (g > 1048576 ? 1048576 : g));
 }
 
+int launch_mx_rebase(cudaStream_t s, int hidden, int inter, int n, const uint8_t* w13c, const uint8_t* w13s,
+                     const uint8_t* w2c, const uint8_t* w2s, float* slot_globals, int* span_scratch, uint32_t* err) {
+  span_init_kernel<<<grid_for(int64_t(n) * 6, 256), 256, 0, s>>>(span_scratch, n * 6);
+  mx_span_kernel<<<grid_for(int64_t(n) * 2 * inter * (hidden / 32), 256), 256, 0, s>>>(
+      w13c, w13s, 2 * inter, hidden, inter, n, 0, span_scratch, err);
+  mx_span_kernel<<<grid_for(int64_t(n) * hidden * (inter / 32), 256), 256, 0, s>>>(
+      w2c, w2s, hidden, inter, hidden, n, 2, span_scratch, err);
+  mx_globals_kernel<<<grid_for(n * 3, 128), 128, 0, s>>>(span_scratch, n, slot_globals);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
 int launch_fp4_prepack(cudaStream_t s, int fmt, int hidden, int inter, int n,
                        const uint8_t* w13c, const uint8_t* w13s, const uint8_t* w2c, const uint8_t* w2s,
                        float* slot_globals, int* span_scratch, uint8_t* bank_slot0, int64_t slot_stride,
