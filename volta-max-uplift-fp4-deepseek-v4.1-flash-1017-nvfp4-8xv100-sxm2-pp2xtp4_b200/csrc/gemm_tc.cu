@@ -17,9 +17,8 @@
 //   warps 10-13 (epilogue): tcgen05.ld (one TMEM lane = one route), then
 //     W13: columns 0-127 are 128 gate rows and 128-255 the matching up rows,
 //     so each thread forms fp16 y13 and the limited SwiGLU of its own route;
-//     W2: fp16 y2 rows; each warp collects the (token, 32-row tile) pairs its
-//     routes complete and reduces them together: sum over slots of
-//     f32(y2) * router weight in slot order (as the decode kernel).
+//     W2: the fp16 y2 rows of its route (the weighted combine is one launch
+//     after W2: fused here its atomics and re-reads stalled the epilogue).
 // Every wait is bounded; after an abort the roles drain in-flight copies and
 // MMAs before TMEM is freed.
 #include <cuda.h>
@@ -48,7 +47,6 @@ constexpr int kTokBytes = BM * BK * 2;   // 16 KB
 constexpr int kWBytes = BNW * BK * 2;    // 32 KB
 constexpr uint32_t kTmemCols = 2 * BNW;  // 512
 constexpr int kUnits = BNW / 32;         // tile pairs per item
-constexpr int kListInts = 1 + 2 * 32 * (BNW / 32);  // per epilogue warp: count + (token, tile) pairs
 
 // FMT 0 / 1: NVFP4 / MXFP4 in the decode bank's units (tile pair x 128 K, eight
 // per raw stage: 256 weight rows x 128 K).  FMT 2 / 3: NVFP4 / MXFP4 weight
@@ -66,13 +64,14 @@ struct TcFmt {
   static constexpr int KT = kWeightUnits ? 256 : kFp4KTile;  // K per unit
   static constexpr int TOK_STAGES = kWeightUnits ? 4 : kTokStages;
   static constexpr int W_STAGES = kWeightUnits ? 2 : kWStages;
+  static constexpr int RAW_STAGES = kRawStages;
 };
 
 template <int FMT>
 constexpr size_t tc_smem() {
   using F = TcFmt<FMT>;
   return 1024 /*align*/ + size_t(F::TOK_STAGES) * kTokBytes + size_t(F::W_STAGES) * kWBytes +
-         size_t(kRawStages) * F::RAW + 4 * kListInts * 4 /*completion lists*/ + 256 /*barriers*/;
+         size_t(F::RAW_STAGES) * F::RAW + 256 /*barriers*/;
 }
 
 // ---- tcgen05 helpers
@@ -141,7 +140,7 @@ template <int FMT, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmap) {
   using F = TcFmt<FMT>;
-  constexpr int kTokStages = F::TOK_STAGES, kWStages = F::W_STAGES;
+  constexpr int kTokStages = F::TOK_STAGES, kWStages = F::W_STAGES, kRawStages = F::RAW_STAGES;
   static_assert(tc_smem<FMT>() <= 227 * 1024, "shared memory");
   extern __shared__ uint8_t smem_raw[];
   // 1024-aligned tiles (swizzle atoms)
@@ -150,8 +149,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* tok = base;                                  // [kTokStages][16 KB]
   uint8_t* wt = tok + kTokStages * kTokBytes;           // [kWStages][32 KB]
   uint8_t* raw = wt + kWStages * kWBytes;               // [kRawStages][RAW]
-  int* lists = reinterpret_cast<int*>(raw + kRawStages * F::RAW);  // [4 warps][kListInts]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(lists + 4 * kListInts);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(raw + kRawStages * F::RAW);
   uint64_t* tok_full = bars;                          // TMA tx
   uint64_t* tok_empty = tok_full + kTokStages;        // MMA commit
   uint64_t* w_full = tok_empty + kTokStages;          // dequant warps
@@ -490,47 +488,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
       ++acc_i;
-      if (EPI == 1 && a.counters) {
-        // completion count per (token, 32-row tile) of this item's 256 rows
-        int* list = lists + quarter * kListInts;
-        if (lane == 0) list[0] = 0;
-        __threadfence();
-        __syncwarp();
-        const int tiles = a.H / 32;
-        if (mine) {
-          const int tok = route / a.top_k;
-          int* cnt0 = a.counters + int64_t(tok) * tiles + rt * (BNW / 32);
-          int olds[BNW / 32];
-#pragma unroll
-          for (int t8 = 0; t8 < BNW / 32; ++t8) olds[t8] = atomicAdd(cnt0 + t8, 1);  // independent round trips
-#pragma unroll
-          for (int t8 = 0; t8 < BNW / 32; ++t8)
-            if (olds[t8] == a.top_k - 1) {
-              const int pos = atomicAdd(&list[0], 1);
-              list[1 + 2 * pos] = tok;
-              list[2 + 2 * pos] = rt * (BNW / 32) + t8;
-            }
-        }
-        __syncwarp();
-        // the warp sums each completed tile together: lane = row, slots in order
-        const int nl = list[0];
-        if (nl > 0) __threadfence();
-        const unsigned short* y2 = static_cast<const unsigned short*>(a.y2);
-        for (int e = 0; e < nl; ++e) {
-          const int tok = list[1 + 2 * e], tile = list[2 + 2 * e];
-          const int hrow = 32 * tile + lane;
-          float sum = 0.f;
-#pragma unroll 8
-          for (int slot = 0; slot < a.top_k; ++slot) {
-            const int rr = tok * a.top_k + slot;
-            const float y = __half2float(__ushort_as_half(__ldcg(y2 + int64_t(rr) * a.H + hrow)));
-            sum = __fmaf_rn(y, __ldcg(a.w_eff + rr), sum);
-          }
-          a.out[int64_t(tok) * a.H + hrow] = sum;
-          if (lane == 0) a.counters[int64_t(tok) * tiles + tile] = 0;
-        }
-        __syncwarp();
-      }
     }
   }
   tc_fence_before();

@@ -206,10 +206,7 @@ struct TcArgs {
   void* inter;             // W13 output f16 [S][I] by sorted position
   int inter_stride;
   float limit;
-  const float* w_eff;
-  void* y2;                // fp16 [S][H] W2 rows by route index
-  int32_t* counters;
-  float* out;
+  void* y2;                // fp16 [S][H] W2 rows by route index (combined by the launch after W2)
   int H;
   uint32_t* err;
 };

@@ -367,10 +367,7 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
         t.inter = ws.inter;
         t.inter_stride = c.inter;
         t.limit = c.swiglu_limit;
-        t.w_eff = ws.w_eff;
         t.y2 = ws.y2;
-        t.counters = ws.counters;
-        t.out = out;
         t.H = c.hidden;
         t.err = L->err;
         const int tfmt = c.prefill_gemm == 2 ? (c.fp4_format == B200MOE_NVFP4 ? 2 : 3) : c.fp4_format;
