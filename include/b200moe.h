@@ -83,13 +83,12 @@ typedef struct {
   int32_t prefill_gemm;       /* FP4 bank kernels: 0 = the skinny decode kernels for every call,
                                  1 = forward_prefill on the tcgen05 grouped GEMM (f16 dequantized
                                  weight tiles, route tiles of 128), decode on the skinny kernels,
-                                 2 = hidden and inter multiples of 256: every call on the
-                                 block-scaled FP4 tensor cores (tcgen05.mma.kind::mxf4nvf4 with
-                                 the format's block scales in TMEM: E4M3 per 16 or E8M0 per 32;
-                                 activations as four E2M1 planes, ~1e-4 relative), the fastest
-                                 decode; the bank is stored as swizzled weight units for it, and
-                                 b200moe_forward_static returns B200MOE_ERR_STATE (no plane
-                                 buffers in its array) */
+                                 2 = hidden and inter multiples of 256: decode and short prefills
+                                 on the block-scaled FP4 tensor cores (tcgen05.mma.kind::mxf4nvf4
+                                 with the format's block scales in TMEM: E4M3 per 16 or E8M0 per
+                                 32; activations as four E2M1 planes, ~1e-4 relative), prefills of
+                                 >= 4096 routes on the tcgen05 f16 GEMM; both read the bank as
+                                 swizzled weight units; the fastest layout for decode and prefill */
 } b200moe_config;
 
 typedef struct b200moe_layer b200moe_layer;

@@ -18,8 +18,10 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-2  # the layer tolerance every other parity test uses (rel-L2)
 
 
-@pytest.fixture(scope="module")
-def layer(pkg):
+@pytest.fixture(scope="module", params=["tcgen05", "fp4"])
+def layer(pkg, request):
+    """Decode on the skinny GEMV ("tcgen05" layers) and on the block-scaled FP4
+    tensor path ("fp4" layers, whose plane buffers are the layer's own)."""
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     from b200moe import moe, synth, tiers
@@ -28,7 +30,8 @@ def layer(pkg):
     torch.cuda.set_device(dev)
     H, I, E, K = 4096, 2048, 64, 8
     tier, _ = tiers.zipf_tier(E, 40, seed=11)  # both banks: 40 NVFP4 + 24 IQ2_XXS experts
-    lay = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K, max_tokens=16, tier=tier, device=dev)
+    lay = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K, max_tokens=16, tier=tier, device=dev,
+                            prefill_gemm=request.param)
     synth.load_bank(lay, synth.make_fp4_bank(int((tier == tiers.HOT).sum()), H, I, "nvfp4", 11, dev))
     lay.set_iq2_tables()
     synth.load_bank(lay, synth.make_iq2_bank(int((tier == tiers.WARM).sum()), H, I, 12, dev))

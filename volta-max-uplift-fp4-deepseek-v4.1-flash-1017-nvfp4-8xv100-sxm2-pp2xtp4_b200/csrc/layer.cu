@@ -246,13 +246,14 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   const bool tc_units = c.prefill_gemm == 2 && S >= kTcUnitsMinRoutes;
   const bool tc = !rows && prefill && (c.prefill_gemm == 1 || tc_units) && c.n_fp4 > 0 && L->xperm;
   const bool f4 = c.prefill_gemm == 2 && c.n_fp4 > 0 && !tc;
-  if (f4 && !ws.own) return B200MOE_ERR_STATE;  // the static array holds no plane buffers
+  // the block-scaled path's plane buffers are the layer's own (sized at create), also under the static array
+  if (f4 && S > L->s_max) return B200MOE_ERR_RANGE;
   // W2 writes y2 rows only and one launch after it does the slot-order combine: fused into the W2
   // epilogue the combine's fences, atomics and re-reads stall the pipeline (measured on B200: the
   // decode GEMV at M = 64 0.849 against 0.877 ms, the tcgen05 prefill W2 1.10 against 2.12 ms).
-  // The fused form stays for the smallest GEMV batches (at most 32 routes, where it is as fast and
-  // saves a launch) and for the allocation-free decode, whose array holds no route positions.
-  const bool sep_combine = !rows && ws.own && (f4 || tc || S > 32);
+  // The GEMV keeps the fused form for the smallest batches (at most 32 routes, where it is as fast
+  // and saves a launch) and in the allocation-free decode.
+  const bool sep_combine = !rows && (f4 || tc || (ws.own && S > 32));
   if (sep_combine) ws.counters = nullptr;
   PlanArgs p{};
   p.ids = ids;

@@ -49,9 +49,9 @@ class B200NativeMoe:
     decode and prefill, on the block-scaled FP4 tensor cores,
     tcgen05.mma.kind::mxf4nvf4 with the format's own block scales (E4M3 per 16
     or E8M0 per 32), the activations as four E2M1 planes (~1e-4 relative); the
-    fastest decode, while long prefills are faster on "tcgen05"; the bank is
-    stored as swizzled weight units, so forward_static refuses such a layer).
-    IQ2_XXS experts always use their int8 kernel.
+    fastest decode and, through the tcgen05 f16 GEMM over the same weight
+    units, the fastest long prefill).  IQ2_XXS experts always use their int8
+    kernel.
     """
 
     def __init__(self, *, hidden: int, inter: int, num_experts: int, top_k: int, max_tokens: int,
