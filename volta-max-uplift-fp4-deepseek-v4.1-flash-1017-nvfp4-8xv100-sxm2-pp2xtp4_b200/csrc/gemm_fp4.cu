@@ -1,35 +1,39 @@
-// Block-scaled FP4 expert GEMM on the 5th-generation tensor cores: the
-// NVFP4 weights go from HBM to shared memory to tcgen05.mma.kind::mxf4nvf4
-// (E2M1 operands, E4M3 scale per 16 along K, read by the tensor core from
-// TMEM) without any conversion on the SM.  Used for every launch of the FP4
-// bank (decode and prefill) of a layer created with prefill_gemm = 2.
+// Block-scaled FP4 expert GEMM on the 5th-generation tensor cores: the FP4
+// weights go from HBM to shared memory to tcgen05.mma.kind::mxf4nvf4 (E2M1
+// operands; E4M3 scale per 16 for NVFP4, E8M0 per 32 for MXFP4, read by the
+// tensor core from TMEM) without any conversion on the SM.  Used for every
+// decode launch of the FP4 bank, and for prefills below 4,096 routes, of a
+// layer created with prefill_gemm = 2 (longer prefills run the tcgen05 f16
+// GEMM over the same weight units).
 //
 // Replaces the reference's QPN launches (engine/.../experts/nvfp4_8r_native.py:929-944,
-// prefill RB2/RB4 at :1039-1075) and, in the epilogues, its SwiGLU and
-// weighted reduce, as the other expert kernels here do.
+// prefill RB2/RB4 at :1039-1075) and, in the W13 epilogue, its SwiGLU.
 //
 // Activations.  The block-scaled FP4 kind takes FP4 on both sides, so each
 // activation row x is written as four E2M1 planes, x ~ g * sum_p s_pb * q_p:
-// plane p quantizes the residual of the planes before it, with an E4M3 scale
-// s_pb per 16 elements and one FP32 factor g per row (its amax over 6 * 448,
-// so plane 0's block scales use E4M3's range and the later ones stay inside
-// it).  Each plane cuts the error about ten times; four planes leave ~1e-4
-// relative on the layer's inputs (the fp16 activations of the reference are
-// ~5e-4).  The planes are stored route-major (row 4 * position + p), so the
-// 16 routes of a chunk are 64 consecutive rows: one TMA box is the MMA's B
-// operand (N = 64, column 4n + p), one MMA per 64-wide K step covers every
-// plane of every route, and the epilogue sums a route's four columns times g.
+// plane p quantizes the residual of the planes before it, with a block scale
+// s_pb (E4M3 per 16, or a power of two per 32 for MXFP4) and one FP32 factor g
+// per row (NVFP4: its amax over 6 * 448, so plane 0's block scales use E4M3's
+// range and the later ones stay inside it; MXFP4: 1).  Each plane cuts the
+// error about ten times; four planes leave ~1e-4 relative on the layer's
+// inputs (the fp16 activations of the reference are ~5e-4).  The planes are
+// stored route-major (row 4 * position + p), so the RC routes of a chunk are
+// 4 RC consecutive rows: one TMA box is the MMA's B operand (N = 4 RC, column
+// 4n + p), one MMA per 64-wide K step covers every plane of every route, and
+// the epilogue sums a route's four columns times g.
 //
-// Tiles.  An item is a chunk of <= 16 routes of one expert x a tile of 128
-// weight rows (W13: 128 gate rows and the 128 matching up rows, two MMAs into
-// two accumulators, so a TMEM lane holds a gate and its up value).  Per 256-wide
-// K tile the producer warp loads by TMA the weight tile(s) [128 rows x 128 B,
-// 128-byte swizzle] and the four activation planes [16 rows x 128 B each],
-// and by bulk copy the pre-blocked scales (4 x 512 B per operand); the MMA
-// thread copies the scales into TMEM (tcgen05.cp 32x128b.warpx4) and issues
+// Tiles.  An item is a chunk of <= RC routes of one expert (RC = 4, 8 or 16
+// by the call's size) x one weight unit row of two 128-row tiles (W13: 128
+// gate rows and the 128 matching up rows, so a TMEM lane holds a gate and its
+// up value; W2: two adjacent row tiles), two MMAs into two accumulators.  Per
+// 256-wide K tile the producer loads the 36 KB weight unit (codes already in
+// the 128-byte swizzled order, scales pre-blocked) with one bulk copy, the
+// chunk's plane rows with one TMA box and their scales with one bulk copy; the
+// MMA thread copies the scales into TMEM (tcgen05.cp 32x128b.warpx4) and issues
 // four MMAs (K = 64) per accumulator; four epilogue warps (one TMEM lane
-// quarter each = 32 weight rows) finish the item: W13 forms fp16 y13 and the
-// limited SwiGLU, W2 the fp16 y2 rows and the slot-order combine.
+// quarter each = 32 weight rows) finish the item: W13 forms fp16 y13, the
+// limited SwiGLU and the SwiGLU row's amax (for its W2 planes), W2 the fp16 y2
+// rows; the weighted combine is one launch after W2.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
