@@ -92,3 +92,88 @@ def iq2_inputs():
     d = (0.02 / 48.0) * rng.uniform(0.5, 1.5, size=(rows, nb))
     out[..., :2] = d.astype(np.float16).view(np.uint8).reshape(rows, nb, 2)
     return out
+
+
+# ---------------------------------------------------------------- host readers and planner
+# Tier planner tallies: 6 layers x 384 experts, heavy-tailed counts with about
+# a third of the experts never routed to.
+TIER_SEED = 20261202
+TIER_LAYERS = 6
+TIER_TYPES = [(16, 16), (29, 29), (17, 17), (17, 29), (16, 29), (29, 16)]  # (gate/up, down) per layer
+
+
+def tier_tally() -> np.ndarray:
+    rng = np.random.default_rng(TIER_SEED)
+    c = np.floor(rng.pareto(1.1, size=(TIER_LAYERS, 384)) * 40).astype(np.int64)
+    c[rng.random(size=c.shape) < 0.33] = 0
+    return c
+
+
+# Pack reader: a small geometry (the record's field order and padding rules at
+# the reference's layout; 40 layers and 4 ranks as its manifests require).
+PACK_SEED = 20261203
+PACK_GEOM = dict(hidden=256, tp_inter=64, w2_k=96, tp_ranks=4, num_experts=12, num_layers=40)
+PACK_LAYERS = (0, 7)
+
+
+def pack_full_experts(layer: int):
+    """Whole MXFP4 experts of one layer: (w13 codes, w13 scales, w2 codes, w2
+    scales) with I = tp_ranks x tp_inter, E8M0 scales in 110..140."""
+    g = PACK_GEOM
+    rng = np.random.default_rng(PACK_SEED + layer)
+    E, H, I = g["num_experts"], g["hidden"], g["tp_ranks"] * g["tp_inter"]
+    w13c = rng.integers(0, 256, size=(E, 2 * I, H // 2), dtype=np.uint8)
+    w13s = rng.integers(110, 141, size=(E, 2 * I, H // 32), dtype=np.uint8)
+    w2c = rng.integers(0, 256, size=(E, H, I // 2), dtype=np.uint8)
+    w2s = rng.integers(110, 141, size=(E, H, I // 32), dtype=np.uint8)
+    return w13c, w13s, w2c, w2s
+
+
+def pack_v1_split(layer: int, rank: int) -> dict:
+    """A seeded hot / cold partition of the experts for the v1 pack."""
+    rng = np.random.default_rng(PACK_SEED + 1000 * layer + rank)
+    E = PACK_GEOM["num_experts"]
+    hot = np.sort(rng.permutation(E)[: E // 2 + rank]).tolist()
+    return {"hot": [int(e) for e in hot], "cold": [e for e in range(E) if e not in hot]}
+
+
+def residency_cases():
+    key, share = "nvfp4_8r_residency", "nvfp4_8r_host_route_share"
+    return [
+        {key: "two_tier"}, {key: "hot_iq"}, {key: "hot_iq_host", share: 0.0}, {key: "hot_iq_host", share: 0},
+        {key: "hot_iq_host", share: 0.05}, {key: "hot_iq_host", share: 0.013}, {}, {key: "hot_iq_host"},
+        {key: "two_tier", share: 0.0}, {key: "hot_iq", share: 0.01}, {key: "hot_iq_host", share: 0.0500001},
+        {key: "hot_iq_host", share: -0.001}, {key: "hot_iq_host", share: "0.0"}, {key: "hot_iq_host", share: True},
+        {key: "hot_iq_host", share: float("nan")}, {key: "three_tier"}, {key: 1}, {key: "hot_iq_host", share: None},
+        {key: "hot_iq_host", share: 1},
+    ]
+
+
+def write_seeded_packs(root, packs):
+    """Seeded v1 and v2 packs of the same records (layers PACK_LAYERS) under
+    ``root``, laid out by the product's ``packs`` module (its ``split_expert``
+    and ``write_id_order_pack``); returns (v1 dir, v2 dir)."""
+    import json
+    from pathlib import Path
+
+    root = Path(root)
+    geom = packs.PackGeometry(**PACK_GEOM)
+    v1, v2 = root / "v1", root / "v2"
+    v1.mkdir(parents=True)
+    records = {}
+    for layer in PACK_LAYERS:
+        for r, rec in enumerate(packs.split_expert(*pack_full_experts(layer), geom=geom)):
+            records[(layer, r)] = rec
+    packs.write_id_order_pack(v2, records, geom, comment="seeded")
+    layers = []
+    for layer in range(geom.num_layers):
+        per_rank = []
+        for r in range(geom.tp_ranks):
+            split = pack_v1_split(layer, r)
+            per_rank.append(split)
+            if layer in PACK_LAYERS:
+                for temp in ("hot", "cold"):
+                    records[(layer, r)][np.asarray(split[temp], np.int64)].tofile(v1 / f"L{layer:02d}-r{r}-{temp}.bin")
+        layers.append(per_rank)
+    (v1 / "manifest.json").write_text(json.dumps({"format": "nvfp4-8r-mxfp4-v1", "layers": layers}))
+    return v1, v2
