@@ -23,7 +23,7 @@ __graft_entry__.load_package()
 from b200moe import ep, moe, synth, tiers  # noqa: E402
 
 
-def main(out_path: str, exchange: str, gemm: str) -> None:
+def main(out_path: str, exchange: str, gemm: str, placement: str) -> None:
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
     dev = torch.device("cuda", torch.cuda.current_device())
@@ -39,10 +39,14 @@ def main(out_path: str, exchange: str, gemm: str) -> None:
     synth.load_bank(full, fp4)
     full.set_iq2_tables()
     synth.load_bank(full, iq2)
+    # "balanced": experts dealt by expected routes (the zipf popularity), not by id range
+    owner = None
+    if placement == "balanced":
+        owner = tiers.balanced_owners(tier, world, (1e6 / (pop_rank + 1.0) ** 1.1).astype(np.int64))
     sharded = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K, tokens=T, tier=tier, device=dev,
-                                   exchange=exchange, gemm=gemm)
+                                   exchange=exchange, gemm=gemm, owner=owner)
     exact = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K, tokens=T, tier=tier, device=dev,
-                                 split_k=(2, 2), exchange=exchange, gemm=gemm)
+                                 split_k=(2, 2), exchange=exchange, gemm=gemm, owner=owner)
     sharded.set_iq2_tables()
     synth.load_local(sharded.layer, tier, fp4, iq2)
     exact.set_iq2_tables()
@@ -58,7 +62,7 @@ def main(out_path: str, exchange: str, gemm: str) -> None:
     cases = {"zipf": (T, synth.zipf_logits(T, pop_rank, 1.0, 1.1, 200 + rank, dev)),
              "ragged": (17 + 9 * rank, torch.randn((17 + 9 * rank, E), generator=g, device=dev)),
              # every route of every rank goes to rank 0's experts
-             "one_owner": (T, torch.where(torch.arange(E, device=dev) < E // world, 5.0, -5.0).expand(T, E)
+             "one_owner": (T, torch.where(torch.from_numpy(sharded.owner_np == 0).to(dev), 5.0, -5.0).expand(T, E)
                            + 0.1 * torch.randn((T, E), generator=g, device=dev))}
     for name, (t, logits) in cases.items():
         x = torch.randn((t, H), generator=g, device=dev).to(torch.bfloat16)
@@ -90,4 +94,5 @@ def main(out_path: str, exchange: str, gemm: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else "p2p", sys.argv[3] if len(sys.argv) > 3 else "skinny")
+    main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else "p2p", sys.argv[3] if len(sys.argv) > 3 else "skinny",
+         sys.argv[4] if len(sys.argv) > 4 else "range")

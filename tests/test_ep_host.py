@@ -20,7 +20,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank: int, world: int, port: int, tier_flip: bool, q) -> None:
+def _worker(rank: int, world: int, port: int, tier_flip: bool, q, owner_mode=None) -> None:
     import sys
 
     from pathlib import Path
@@ -38,8 +38,14 @@ def _worker(rank: int, world: int, port: int, tier_flip: bool, q) -> None:
         if tier_flip and rank == 1:
             tier = tier.copy()
             tier[7] ^= 1
+        owner = None
+        if owner_mode is not None:  # a placement by expected routes; "flip": rank 1 counted other routes
+            counts = np.arange(384, dtype=np.int64)[::-1].copy()
+            if owner_mode == "flip" and rank == 1:
+                counts[[0, 1]] = counts[[1, 0]] + np.array([0, 5])
+            owner = tiers.balanced_owners(tier, world, counts)
         try:
-            ep.check_placement(tier, world)
+            ep.check_placement(tier, world, owner=owner)
             placement = "agree"
         except RuntimeError:
             placement = "refused"
@@ -54,11 +60,11 @@ def _worker(rank: int, world: int, port: int, tier_flip: bool, q) -> None:
         dist.destroy_process_group()
 
 
-def _run(tier_flip: bool):
+def _run(tier_flip: bool, owner_mode=None):
     world, port = 2, _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, tier_flip, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, tier_flip, q, owner_mode)) for r in range(world)]
     for p in procs:
         p.start()
     out = [q.get(timeout=120) for _ in range(world)]
@@ -80,6 +86,11 @@ def test_placement_agrees_and_counts_transpose():
 def test_placement_mismatch_refused_on_every_rank():
     res = _run(True)
     assert all(v[0] == "refused" for v in res.values())
+
+
+def test_owner_map_is_part_of_the_placement():
+    assert all(v[0] == "agree" for v in _run(False, "same").values())
+    assert all(v[0] == "refused" for v in _run(False, "flip").values())
 
 
 def test_owner_ranges_cover_all_experts():

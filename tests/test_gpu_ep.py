@@ -100,8 +100,9 @@ def test_ep_world1_matches_layer(dev, pkg, exchange, gemm):
     full.close()
 
 
-@pytest.mark.parametrize("exchange,gemm", [("p2p", "skinny"), ("nccl", "skinny"), ("p2p", "fp4")])
-def test_ep_two_gpus(tmp_path, exchange, gemm):
+@pytest.mark.parametrize("exchange,gemm,placement", [("p2p", "skinny", "range"), ("nccl", "skinny", "range"),
+                                                     ("p2p", "fp4", "range"), ("p2p", "fp4", "balanced")])
+def test_ep_two_gpus(tmp_path, exchange, gemm, placement):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     with socket.socket() as s:
@@ -111,7 +112,7 @@ def test_ep_two_gpus(tmp_path, exchange, gemm):
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={port}",
-           str(Path(__file__).with_name("ep_worker.py")), str(out), exchange, gemm]
+           str(Path(__file__).with_name("ep_worker.py")), str(out), exchange, gemm, placement]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     for rank in range(2):

@@ -464,3 +464,43 @@ def test_prefill_tcgen05_skewed_mixed_tier(dev, pkg):
     layer.check_errors()
     assert tr.rel_l2(out, tr.layer_forward(x, ids.long(), w, dequant)) < TOL
     layer.close()
+
+
+# ------------------------------------------------------------------ pack loading
+@pytest.mark.parametrize("gemm", ["tcgen05", "fp4"])
+def test_pack_layer_load(dev, pkg, tmp_path, gemm):
+    """Whole MXFP4 experts -> the reference's four TP-rank records -> a v2
+    pack on disk -> load_pack_layer: the layer's output matches the fp32
+    dequant of the original experts; an EP rank loads only its own experts."""
+    from b200moe import moe, packs, tiers
+
+    H, I, E, K, M = 1024, 512, 16, 4, 9
+    geom = packs.PackGeometry(hidden=H, tp_inter=I // 4, w2_k=I // 4 + 32, tp_ranks=4, num_experts=E, num_layers=40)
+    rng = np.random.default_rng(31)
+    q13 = [mo.mxfp4_quantize(rng.normal(0, 0.02, (2 * I, H)).astype(np.float32)) for _ in range(E)]
+    q2 = [mo.mxfp4_quantize(rng.normal(0, 0.02, (H, I)).astype(np.float32)) for _ in range(E)]
+    full = (np.stack([c for c, _ in q13]), np.stack([s for _, s in q13]), np.stack([c for c, _ in q2]),
+            np.stack([s for _, s in q2]))
+    recs = packs.split_expert(*full, geom=geom)
+    packs.write_id_order_pack(tmp_path, {(3, r): rec for r, rec in enumerate(recs)}, geom)
+    tier = np.zeros(E, np.int8)
+    layer = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K, max_tokens=64, tier=tier,
+                              fp4_format="mxfp4", device=dev, prefill_gemm=gemm)
+    assert packs.load_pack_layer(layer, tmp_path, 3, geom, chunk=5) == E
+    d = [torch.from_numpy(a).to(dev) for a in full]
+
+    def dequant(e):
+        return tr.mxfp4_decode(d[0][e], d[1][e]), tr.mxfp4_decode(d[2][e], d[3][e])
+
+    g = torch.Generator(device=dev).manual_seed(31)
+    x = torch.randn((M, H), generator=g, device=dev).to(torch.bfloat16)
+    ids, w = layer.route(torch.randn((M, E), generator=g, device=dev))
+    out = layer.forward(x, ids, w).clone()
+    layer.check_errors()
+    assert tr.rel_l2(out, tr.layer_forward(x, ids.long(), w, dequant)) < TOL
+    layer.close()
+    owner = tiers.balanced_owners(tier, 2)
+    part = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=1, max_tokens=64, tier=tier,
+                             fp4_format="mxfp4", device=dev, prefill_gemm=gemm, rank=1, world=2, owner=owner)
+    assert packs.load_pack_layer(part, tmp_path, 3, geom) == int((owner == 1).sum())
+    part.close()

@@ -54,11 +54,11 @@ def gate(logits: torch.Tensor, top_k: int) -> tuple[torch.Tensor, torch.Tensor]:
     return ids, w
 
 
-def check_placement(tier, world: int, group=None) -> str:
-    """Every rank must hold the same tier array and world size; a rank that
-    differs makes every rank raise (the reference's stage digest check,
-    engine/.../experts/nvfp4_8r_native.py:1657-1659)."""
-    digest = tiersmod.placement_digest(tier, world)
+def check_placement(tier, world: int, group=None, owner=None) -> str:
+    """Every rank must hold the same tier array, world size and owner map; a
+    rank that differs makes every rank raise (the reference's stage digest
+    check, engine/.../experts/nvfp4_8r_native.py:1657-1659)."""
+    digest = tiersmod.placement_digest(tier, world, owner)
     if world == 1 or not dist.is_initialized():
         return digest
     digests = [None] * world
@@ -69,10 +69,8 @@ def check_placement(tier, world: int, group=None) -> str:
 
 
 def owner_of_expert(num_experts: int, world: int) -> np.ndarray:
-    out = np.empty(num_experts, np.int32)
-    for r, rng in enumerate(tiersmod.owner_ranges(num_experts, world)):
-        out[rng.start:rng.stop] = r
-    return out
+    """The default placement: contiguous expert-id ranges."""
+    return tiersmod.owner_by_range(num_experts, world)
 
 
 def exchange_counts(send_counts: torch.Tensor, world: int, group=None) -> tuple[list[int], list[int]]:
@@ -155,7 +153,7 @@ class ExpertParallelMoe:
     def __init__(self, *, hidden: int, inter: int, num_experts: int, top_k: int, tokens: int, tier,
                  fp4_format: str = "nvfp4", group=None, device: torch.device | None = None,
                  split_k: tuple[int, int] | None = None, exchange: str = "p2p", peer: PeerExchange | None = None,
-                 gemm: str = "skinny"):
+                 gemm: str = "skinny", owner=None):
         if exchange not in ("p2p", "nccl"):
             raise ValueError("exchange is 'p2p' or 'nccl'")
         self.exchange = exchange
@@ -165,17 +163,20 @@ class ExpertParallelMoe:
         dev = device or torch.device("cuda", torch.cuda.current_device())
         self.device = dev
         self.tier = tiersmod.check_tier_array(tier, num_experts)
-        self.digest = check_placement(self.tier, self.world, group)
+        owner_np = (owner_of_expert(num_experts, self.world) if owner is None
+                    else tiersmod.check_owner(owner, num_experts, self.world))
+        self.digest = check_placement(self.tier, self.world, group, None if owner is None else owner_np)
         self.hidden, self.inter, self.num_experts, self.top_k, self.tokens = hidden, inter, num_experts, top_k, tokens
         S = tokens * top_k
         r_max = S * self.world  # every route of every rank could land here
         self.layer = B200NativeMoe(hidden=hidden, inter=inter, num_experts=num_experts, top_k=1,
                                    max_tokens=min(64, r_max), max_prefill_tokens=r_max, tier=self.tier,
                                    fp4_format=fp4_format, device=dev, rank=self.rank, world=self.world,
-                                   prefill_gemm=gemm)
+                                   prefill_gemm=gemm, owner=owner_np)
         if split_k is not None:
             self.layer.set_split_k(*split_k)
-        self.owner = torch.from_numpy(owner_of_expert(num_experts, self.world)).to(dev)
+        self.owner_np = owner_np
+        self.owner = torch.from_numpy(owner_np).to(dev)
         f16 = dict(dtype=torch.float16, device=dev)
         i32 = dict(dtype=torch.int32, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)

@@ -38,8 +38,9 @@ class B200NativeMoe:
 
     ``tier`` int8 [E]: HOT experts are FP4 (``fp4_format`` "nvfp4" or
     "mxfp4"), WARM experts IQ2_XXS.  ``rank`` / ``world`` select this GPU's
-    experts under expert parallelism (contiguous id ranges); with world 1 every
-    expert is local.  Buffers are fixed at construction (``max_tokens`` for the
+    experts under expert parallelism (contiguous id ranges, or ``owner``, int32
+    [E] rank of each expert, e.g. ``tiers.balanced_owners``); with world 1
+    every expert is local.  Buffers are fixed at construction (``max_tokens`` for the
     graph-capturable decode ``forward``, ``max_prefill_tokens`` for
     ``forward_prefill``); forward never allocates or syncs with the host.
     ``prefill_gemm`` picks the FP4 bank's kernels: "tcgen05" (forward_prefill
@@ -57,7 +58,7 @@ class B200NativeMoe:
     def __init__(self, *, hidden: int, inter: int, num_experts: int, top_k: int, max_tokens: int,
                  tier, fp4_format: str = "nvfp4", max_prefill_tokens: int = 0,
                  swiglu_limit: float = SWIGLU_LIMIT, device: torch.device | int | None = None,
-                 rank: int = 0, world: int = 1, prefill_gemm: str = "tcgen05"):
+                 rank: int = 0, world: int = 1, prefill_gemm: str = "tcgen05", owner=None):
         if fp4_format not in ("nvfp4", "mxfp4"):
             raise ValueError(f"fp4_format must be nvfp4 or mxfp4, got {fp4_format!r}")
         if prefill_gemm not in ("tcgen05", "skinny", "fp4"):
@@ -69,7 +70,7 @@ class B200NativeMoe:
             raise ValueError("the layer needs an indexed CUDA device")
         self.device = dev
         tier = tiersmod.check_tier_array(tier, num_experts)
-        fp4_map, iq2_map = tiersmod.local_maps(tier, rank, world)
+        fp4_map, iq2_map = tiersmod.local_maps(tier, rank, world, owner)
         self.tier = tier
         self.hidden, self.inter, self.num_experts, self.top_k = hidden, inter, num_experts, top_k
         self.max_tokens, self.max_prefill_tokens = max_tokens, max_prefill_tokens

@@ -111,8 +111,10 @@ def zipf_logits(tokens: int, rank, alpha: float, s: float, seed: int, device) ->
 def load_local(layer, tier, fp4: Fp4Bank | None, iq2: Iq2Bank | None) -> None:
     """Load one rank's experts from banks that hold every expert of the layer:
     the bank of a format is indexed by the expert's rank among that format's
-    experts (ascending id); a rank's experts of a format are a contiguous run."""
+    experts (ascending id); the rank's experts, in local slot order, are
+    gathered from it (any placement)."""
     import numpy as np
+    import torch
 
     from . import tiers as tiersmod
 
@@ -121,12 +123,16 @@ def load_local(layer, tier, fp4: Fp4Bank | None, iq2: Iq2Bank | None) -> None:
         mine = np.flatnonzero(local >= 0)
         if mine.size == 0:
             continue
-        g0, n = int(glob[mine[0]]), mine.size
-        if not np.array_equal(glob[mine], np.arange(g0, g0 + n)) or not np.array_equal(local[mine], np.arange(n)):
-            raise ValueError("local experts of a format must be a contiguous run of the bank")
+        mine = mine[np.argsort(local[mine])]
+        if not np.array_equal(local[mine], np.arange(mine.size)):
+            raise ValueError("local slots of a format must be 0..n-1")
+        rows = glob[mine]
+        run = int(rows[0])
+        pick = (lambda t: t[run:run + rows.size]) if np.array_equal(rows, np.arange(run, run + rows.size)) else (
+            lambda t: t.index_select(0, torch.as_tensor(rows, dtype=torch.int64, device=t.device)))
         if fmt == "fp4":
-            layer.load_fp4(0, bank.w13_codes[g0:g0 + n], bank.w13_scales[g0:g0 + n], bank.w2_codes[g0:g0 + n],
-                           bank.w2_scales[g0:g0 + n], None if bank.globals is None else bank.globals[g0:g0 + n])
+            layer.load_fp4(0, pick(bank.w13_codes).contiguous(), pick(bank.w13_scales).contiguous(),
+                           pick(bank.w2_codes).contiguous(), pick(bank.w2_scales).contiguous(),
+                           None if bank.globals is None else pick(bank.globals).contiguous())
         else:
-            layer.load_iq2(0, bank.w1[g0:g0 + n].contiguous(), bank.w3[g0:g0 + n].contiguous(),
-                           bank.w2[g0:g0 + n].contiguous())
+            layer.load_iq2(0, pick(bank.w1).contiguous(), pick(bank.w3).contiguous(), pick(bank.w2).contiguous())
