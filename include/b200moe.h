@@ -201,6 +201,21 @@ int b200moe_route_plan(void* stream, const int32_t* ids, int n, int num_experts,
  * engine/patches/gguf_moe.patch:57-58).  Expert e lives on rank
  * owner_of_expert[e]; the exchange is NCCL all-to-all issued by the host. */
 
+/* Decode route counters of one layer, updated on the device (one launch, so a
+ * captured graph counts at every replay).  Replaces RouteStats.count,
+ * engine/src/vllm/model_executor/layers/fused_moe/experts/nvfp4_8r_stats.py:81-98.
+ * topk_ids: n route ids of one call; is_host / is_warm: uint8 [num_experts]
+ * tier masks; stat int64 [5] (calls, routes, HOST routes, distinct HOST experts
+ * per call summed, WARM routes), gap_hist int64 [7] (HOST routes by rounds
+ * since their expert's last HOST use: <=1, 2, <=4, <=16, <=64, <=256, more or
+ * never), routes int64 [num_experts], last_round int32 [num_experts + 1]
+ * (-2^30 = never; entry num_experts takes the non-HOST routes' writes).  The
+ * round of a call is stat[0] before it.  An id outside [0, num_experts) is
+ * skipped and sets the bounds bit in *err. */
+int b200moe_route_stats(void* stream, const int32_t* topk_ids, int n, int num_experts, const uint8_t* is_host,
+                        const uint8_t* is_warm, int64_t* stat, int64_t* gap_hist, int64_t* routes,
+                        int32_t* last_round, uint32_t* err);
+
 /* Softmax top-k gating without a layer (same rule as b200moe_route). */
 int b200moe_gate(void* stream, const float* logits, int T, int num_experts, int top_k, int32_t* topk_ids,
                  float* topk_weights, uint32_t* err);

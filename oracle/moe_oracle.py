@@ -521,3 +521,53 @@ def rel_l2(a: np.ndarray, b: np.ndarray) -> float:
     b = np.asarray(b, np.float64)
     den = np.linalg.norm(b)
     return float(np.linalg.norm(a - b) / den) if den > 0 else float(np.linalg.norm(a - b))
+
+
+# ---------------------------------------------------------------------------
+# decode route counters (EXP/nvfp4_8r_stats.py:41-110)
+# ---------------------------------------------------------------------------
+
+#: stat fields, gap-histogram edges and "recent" windows (EXP/nvfp4_8r_stats.py:45-50)
+STAT_FIELDS = ("calls", "routes", "host_routes", "host_groups", "warm_routes")
+GAP_EDGES = (1, 2, 4, 16, 64, 256)
+RECENT = (4, 16, 64, 256)
+NEVER = -(2**30)
+
+
+def route_stats_new(num_experts: int) -> dict:
+    """Zeroed counters of one layer: stat int64 [5], gap_hist int64 [7],
+    routes int64 [E], last_round int32 [E + 1] (entry E takes the writes of
+    non-HOST routes), as RouteStats.__init__ (EXP/nvfp4_8r_stats.py:68-79)."""
+    return {"stat": np.zeros(len(STAT_FIELDS), np.int64), "gap_hist": np.zeros(len(GAP_EDGES) + 1, np.int64),
+            "routes": np.zeros(num_experts, np.int64),
+            "last_round": np.full(num_experts + 1, NEVER, np.int32)}
+
+
+def route_stats_count(c: dict, ids: np.ndarray, is_host: np.ndarray, is_warm: np.ndarray) -> None:
+    """One decode call's routes, in place (RouteStats.count,
+    EXP/nvfp4_8r_stats.py:81-98): the round r = calls so far; each HOST route
+    adds to the gap bucket of r - (its expert's last HOST round), buckets
+    (<=1, 2, <=4, <=16, <=64, <=256, more or never); then the HOST experts'
+    last round becomes r; routes per expert, HOST routes, distinct HOST experts
+    of this call, WARM routes, routes and calls are counted."""
+    flat = np.asarray(ids, np.int64).reshape(-1)
+    E = c["routes"].size
+    host = is_host[flat].astype(bool)
+    slot = np.where(host, flat, E)
+    r = int(c["stat"][0])
+    gap = r - c["last_round"][slot].astype(np.int64)
+    bucket = np.searchsorted(np.asarray(GAP_EDGES, np.int64), gap, side="left")
+    np.add.at(c["gap_hist"], bucket[host], 1)
+    c["last_round"][slot] = np.where(host, r, NEVER).astype(np.int32)
+    np.add.at(c["routes"], flat, 1)
+    c["stat"][2] += int(host.sum())
+    c["stat"][3] += int((c["last_round"][:E] == r).sum())
+    c["stat"][4] += int(is_warm[flat].astype(bool).sum())
+    c["stat"][1] += flat.size
+    c["stat"][0] += 1
+
+
+def route_stats_recent(c: dict) -> np.ndarray:
+    """Experts whose last HOST use is within each RECENT window (RouteStats.read)."""
+    age = int(c["stat"][0]) - c["last_round"][:-1].astype(np.int64)
+    return np.array([int((age <= g).sum()) for g in RECENT], np.int64)

@@ -177,3 +177,22 @@ def write_seeded_packs(root, packs):
         layers.append(per_rank)
     (v1 / "manifest.json").write_text(json.dumps({"format": "nvfp4-8r-mxfp4-v1", "layers": layers}))
     return v1, v2
+
+
+# Route counters: a tier map with all three tiers and a run of decode calls
+# (M <= 6 tokens x 6 routes, the reference's decode batch), popular experts
+# often and rare ones after long gaps, so every gap bucket fills.
+ROUTE_STATS_SEED = 20261204
+ROUTE_STATS_CALLS = 420
+
+
+def route_stats_inputs():
+    rng = np.random.default_rng(ROUTE_STATS_SEED)
+    tier = rng.choice(np.array([0, 1, 2], np.int8), size=384, p=[0.3, 0.3, 0.4]).astype(np.int8)
+    p = 1.0 / (rng.permutation(384) + 1.0) ** 1.3
+    p /= p.sum()
+    calls = []
+    for _ in range(ROUTE_STATS_CALLS):
+        m = int(rng.integers(1, 7))
+        calls.append(np.stack([rng.choice(384, size=6, replace=False, p=p) for _ in range(m)]).astype(np.int32))
+    return tier, calls

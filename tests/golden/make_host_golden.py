@@ -15,7 +15,9 @@ engine/src/vllm/model_executor/layers/fused_moe/experts/):
   document and mutations of it, plan_from_map (:403-431);
 - nvfp4_8r_native.read_rank_experts (:205-231), check_packs (:193-202) and
   _split_records (:234-250) on seeded v1 and v2 packs of a small geometry
-  (the module's size constants are set to that geometry for the run).
+  (the module's size constants are set to that geometry for the run);
+- nvfp4_8r_stats.RouteStats.count / read (:65-110), run on CPU tensors over a
+  seeded sequence of decode calls (counters after selected calls).
 """
 
 from __future__ import annotations
@@ -235,11 +237,38 @@ def make_packs(out: Path) -> None:
     print(f"packs: {len(record['reads'])} reads, refusals {record['refusals']} -> {out.name}")
 
 
+# ------------------------------------------------------------------- route counters
+ROUTE_STATS_MARKS = (0, 1, 2, 50, 200, 419)
+
+
+def make_route_stats(out: Path) -> None:
+    import importlib
+
+    import torch
+
+    import_reference_engine()
+    stats = importlib.import_module("vllm.model_executor.layers.fused_moe.experts.nvfp4_8r_stats")
+    tier, calls = gi.route_stats_inputs()
+    rs = stats.RouteStats(tier, torch.device("cpu"))
+    arrays = {}
+    for i, ids in enumerate(calls):
+        rs.count(torch.from_numpy(ids))
+        if i in ROUTE_STATS_MARKS:
+            got = rs.read()
+            for k in ("stat", "gap_hist", "recent", "routes"):
+                arrays[f"{k}_{i}"] = np.array(got[k], np.int64, copy=True)  # CPU tensors share memory
+            arrays[f"last_round_{i}"] = rs.last_round.numpy().copy()
+    np.savez_compressed(out, marks=np.asarray(ROUTE_STATS_MARKS), **arrays)
+    print(f"route stats: {len(calls)} calls, final stat {arrays[f'stat_{ROUTE_STATS_MARKS[-1]}'].tolist()}, "
+          f"gap_hist {arrays[f'gap_hist_{ROUTE_STATS_MARKS[-1]}'].tolist()} -> {out.name}")
+
+
 def main() -> None:
     if not REF.is_dir():
         raise SystemExit(f"reference tree {REF} not present")
     make_tiers(HERE / "tiers.npz")
     make_packs(HERE / "packs.npz")
+    make_route_stats(HERE / "route_stats.npz")
 
 
 if __name__ == "__main__":

@@ -504,3 +504,64 @@ def test_pack_layer_load(dev, pkg, tmp_path, gemm):
                              fp4_format="mxfp4", device=dev, prefill_gemm=gemm, rank=1, world=2, owner=owner)
     assert packs.load_pack_layer(part, tmp_path, 3, geom) == int((owner == 1).sum())
     part.close()
+
+
+# ------------------------------------------------------------------ route counters
+def test_route_stats_kernel(dev, pkg):
+    """b200moe_route_stats against the reference's RouteStats counters (the
+    golden run of 420 decode calls), bit for bit, eagerly and as graph replays."""
+    from b200moe import stats
+
+    tier, calls = gi.route_stats_inputs()
+    z = np.load(GOLDEN / "route_stats.npz")
+    marks = set(z["marks"].tolist())
+    rs = stats.RouteStats(tier, dev)
+    for i, ids in enumerate(calls):
+        rs.count(torch.from_numpy(ids).to(dev))
+        if i in marks:
+            got = rs.read()
+            for k in ("stat", "gap_hist", "recent", "routes"):
+                np.testing.assert_array_equal(got[k], z[f"{k}_{i}"], err_msg=f"{k} after call {i}")
+            np.testing.assert_array_equal(rs.last_round.cpu().numpy(), z[f"last_round_{i}"])
+    rs.check_errors()
+    # captured once, replayed: the counters keep counting (round = replays so far)
+    rs2 = stats.RouteStats(tier, dev)
+    c = mo.route_stats_new(384)
+    ids = torch.from_numpy(calls[7]).to(dev)
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph):
+            rs2.count(ids)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    for _ in range(300):
+        graph.replay()
+        mo.route_stats_count(c, calls[7], (tier == 2).astype(np.uint8), (tier == 1).astype(np.uint8))
+    torch.cuda.synchronize(dev)
+    got = rs2.read()
+    for k in ("stat", "gap_hist", "routes"):
+        np.testing.assert_array_equal(got[k], c[k])
+    del graph
+    with pytest.raises(RuntimeError):
+        rs2.count(torch.tensor([[3, 400]], dtype=torch.int32, device=dev))
+        rs2.check_errors()
+
+
+def test_layer_route_stats(dev, pkg):
+    """A layer with its counters on: every decode forward adds its routes."""
+    H, I, E, K, M = 1024, 512, 32, 4, 12
+    layer, _, _, _ = _make_layer(dev, H, I, E, K, M, seed=4)
+    st = layer.enable_route_stats()
+    g = torch.Generator(device=dev).manual_seed(4)
+    want = np.zeros(E, np.int64)
+    for m in (M, 3):
+        x = torch.randn((m, H), generator=g, device=dev).to(torch.bfloat16)
+        ids, w = layer.route(torch.randn((m, E), generator=g, device=dev))
+        layer.forward(x, ids, w)
+        want += np.bincount(ids.cpu().numpy().reshape(-1), minlength=E)
+    got = st.read()
+    np.testing.assert_array_equal(got["routes"], want)
+    assert got["stat"].tolist()[:2] == [2, int(want.sum())] and got["stat"][2] == 0
+    layer.check_errors()
+    layer.close()

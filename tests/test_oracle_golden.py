@@ -181,3 +181,20 @@ def test_gating_ties_and_weights():
     ref = np.take_along_axis(p, ids, 1)
     assert np.allclose(w, ref / ref.sum(1, keepdims=True), rtol=1e-6)
     assert np.all(np.diff(np.take_along_axis(lg, ids, 1), axis=1) <= 0)
+
+
+def test_route_stats_vs_reference_counters():
+    """The counter restatement against the reference's RouteStats run on CPU
+    tensors over the same 420 decode calls (EXP/nvfp4_8r_stats.py:81-110)."""
+    z = np.load(GOLDEN / "route_stats.npz")
+    tier, calls = gi.route_stats_inputs()
+    c = mo.route_stats_new(384)
+    is_host, is_warm = (tier == 2).astype(np.uint8), (tier == 1).astype(np.uint8)
+    marks = set(z["marks"].tolist())
+    for i, ids in enumerate(calls):
+        mo.route_stats_count(c, ids, is_host, is_warm)
+        if i in marks:
+            for k in ("stat", "gap_hist", "routes", "last_round"):
+                np.testing.assert_array_equal(c[k], z[f"{k}_{i}"], err_msg=f"{k} after call {i}")
+            np.testing.assert_array_equal(mo.route_stats_recent(c), z[f"recent_{i}"])
+    assert np.all(z[f"gap_hist_{max(marks)}"] > 0)  # every bucket was reached

@@ -66,6 +66,7 @@ SIGNATURES = {
     "b200moe_quantize_mxfp4": ([P, P, I32, I32, P, P, P], I32),
     "b200moe_fold_nvfp4_to_mxfp4": ([P, P, P, P, I32, I32, P, P, P], I32),
     "b200moe_gate": ([P, P, I32, I32, I32, P, P, P], I32),
+    "b200moe_route_stats": ([P, P, I32, I32, P, P, P, P, P, P, P], I32),
     "b200moe_ep_workspace_bytes": ([I32, I32], ctypes.c_size_t),
     "b200moe_ep_dispatch": ([P, P, I32, P, I32, I32, I32, I32, P, I32, P, P, P, P, P, ctypes.c_size_t, P], I32),
     "b200moe_ep_combine": ([P, P, P, P, I32, I32, I32, P, P], I32),

@@ -88,6 +88,7 @@ class B200NativeMoe:
             self._h, fp4_map.ctypes.data_as(ctypes.c_void_p), iq2_map.ctypes.data_as(ctypes.c_void_p)))
         self.out = torch.empty((max_tokens, hidden), dtype=torch.float32, device=dev)
         self._tables_set = False
+        self.stats = None  # decode route counters (enable_route_stats)
 
     # -------------------------------------------------------------- weights
     def load_fp4(self, slot_begin: int, w13_codes, w13_scales, w2_codes, w2_scales, globals=None) -> None:
@@ -163,9 +164,21 @@ class B200NativeMoe:
         if not 0 < m <= self.max_tokens:
             raise ValueError(f"bad routing shape {tuple(topk_ids.shape)} for M={m}")
         out = self.out[:m]
+        if self.stats is not None:
+            self.stats.count(topk_ids)
         _lib.check("b200moe_forward", _lib.lib().b200moe_forward(
             self._h, _stream(), x.data_ptr(), dt, topk_ids.data_ptr(), topk_weights.data_ptr(), out.data_ptr(), m))
         return out
+
+    def enable_route_stats(self):
+        """Count this layer's decode routes on the device from now on (one
+        extra launch per ``forward``, captured with it in a graph); returns the
+        ``stats.RouteStats`` (the reference's counters, off unless asked for)."""
+        from .stats import RouteStats
+
+        if self.stats is None:
+            self.stats = RouteStats(self.tier, self.device)
+        return self.stats
 
     def forward_prefill(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor) -> torch.Tensor:
         """Any M up to max_prefill_tokens -> a new fp32 [M, H] tensor."""
