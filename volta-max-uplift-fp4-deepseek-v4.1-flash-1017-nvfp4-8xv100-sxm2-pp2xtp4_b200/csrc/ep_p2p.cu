@@ -106,32 +106,44 @@ __global__ void __launch_bounds__(256) ep_push_kernel(const EpP2P a) {
   }
   __syncthreads();
   if (s_ok) {
-    const int chunks = a.H / 8;  // 16-byte pieces of a row
-    const int64_t total = int64_t(s_sb[W]) * chunks;
-    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
-      const int p = int(i / chunks), c = int(i % chunks);
+    // one warp per route: its owner, row and source looked up once, then the
+    // row's 16-byte pieces (H / 8 of them) four at a time per lane
+    const int lane = threadIdx.x & 31;
+    const int warps = int(gridDim.x * blockDim.x) >> 5;
+    const int chunks = a.H / 8;
+    for (int p = int(blockIdx.x * blockDim.x + threadIdx.x) >> 5; p < s_sb[W]; p += warps) {
       int dst = 0;
       while (dst + 1 < W && s_sb[dst + 1] <= p) ++dst;
       const int row = s_off[dst] + (p - s_sb[dst]);
       const int route = a.perm[p];
-      const int64_t src_off = int64_t(route / a.k) * a.H + 8 * c;
-      uint4 v;
-      if (a.x_bf16) {
-        const uint4 b = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.x) + src_off);
-        const uint32_t w[4] = {b.x, b.y, b.z, b.w};
-        uint32_t o[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const __half2 h = __floats2half2_rn(__uint_as_float(w[j] << 16), __uint_as_float(w[j] & 0xFFFF0000u));
-          o[j] = *reinterpret_cast<const uint32_t*>(&h);
-        }
-        v = make_uint4(o[0], o[1], o[2], o[3]);
-      } else {
-        v = *reinterpret_cast<const uint4*>(static_cast<const __half*>(a.x) + src_off);
-      }
+      const uint16_t* src = static_cast<const uint16_t*>(a.x) + int64_t(route / a.k) * a.H;
       uint8_t* base = a.peer[dst];
-      *reinterpret_cast<uint4*>(base + a.off_rows + (int64_t(row) * a.H + 8 * c) * 2) = v;
-      if (c == 0) {
+      uint4* drow = reinterpret_cast<uint4*>(base + a.off_rows + int64_t(row) * a.H * 2);
+      for (int c0 = lane; c0 < chunks; c0 += 32 * 4) {
+        uint4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = c0 + 32 * u;
+          if (c < chunks) v[u] = *reinterpret_cast<const uint4*>(src + 8 * c);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = c0 + 32 * u;
+          if (c >= chunks) continue;
+          if (a.x_bf16) {
+            const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+            uint32_t o[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const __half2 h = __floats2half2_rn(__uint_as_float(w[j] << 16), __uint_as_float(w[j] & 0xFFFF0000u));
+              o[j] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+            v[u] = make_uint4(o[0], o[1], o[2], o[3]);
+          }
+          drow[c] = v[u];
+        }
+      }
+      if (lane == 0) {
         reinterpret_cast<int*>(base + a.off_eid)[row] = a.ids[route];
         reinterpret_cast<int*>(base + a.off_home)[row] = (a.rank << 24) | route;
       }
@@ -157,17 +169,27 @@ __global__ void __launch_bounds__(256) ep_return_kernel(const EpP2P a, const __h
   const int n = a.recv[0];
   const int chunks = a.H / 8;
   const int* home = reinterpret_cast<const int*>(a.peer[a.rank] + a.off_home);
-  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < int64_t(n) * chunks;
-       i += int64_t(gridDim.x) * blockDim.x) {
-    const int row = int(i / chunks), c = int(i % chunks);
+  // one warp per received row: its home looked up once, the row four 16-byte pieces at a time per lane
+  const int lane = threadIdx.x & 31;
+  const int warps = int(gridDim.x * blockDim.x) >> 5;
+  for (int row = int(blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < n; row += warps) {
     const int h = home[row];
     const int hr = h >> 24, hp = h & 0xFFFFFF;
     if (hr < 0 || hr >= a.world) {
-      set_error(a.err, kErrBounds);
+      if (lane == 0) set_error(a.err, kErrBounds);
       continue;
     }
-    const uint4 v = *reinterpret_cast<const uint4*>(y2 + int64_t(row) * a.H + 8 * c);
-    *reinterpret_cast<uint4*>(a.peer[hr] + a.off_y2home + (int64_t(hp) * a.H + 8 * c) * 2) = v;
+    const uint4* srow = reinterpret_cast<const uint4*>(y2 + int64_t(row) * a.H);
+    uint4* drow = reinterpret_cast<uint4*>(a.peer[hr] + a.off_y2home + int64_t(hp) * a.H * 2);
+    for (int c0 = lane; c0 < chunks; c0 += 32 * 4) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (c0 + 32 * u < chunks) v[u] = srow[c0 + 32 * u];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (c0 + 32 * u < chunks) drow[c0 + 32 * u] = v[u];
+    }
   }
   last_cta_signal(a, 2, e, false);
 }
@@ -426,8 +448,7 @@ int b200moe_ep_push(b200moe_ep* E, void* stream, const void* x, int x_dtype, con
   a.perm = E->perm;
   a.owner = owner_of_expert;
   a.send_counts = E->send_counts;
-  const int64_t work = int64_t(S) * (E->H / 8);
-  const int blocks = int(std::min<int64_t>(std::max<int64_t>((work + 255) / 256, 1), int64_t(E->grid) * 2));
+  const int blocks = std::min(std::max((S + 7) / 8, 1), E->grid * 2);  // a warp per route
   ep_push_kernel<<<blocks, 256, 0, s>>>(a);
   ep_recv_kernel<<<1, 32, 0, s>>>(a);
   return cudaGetLastError() == cudaSuccess ? B200MOE_OK : B200MOE_ERR_CUDA;
@@ -439,8 +460,7 @@ int b200moe_ep_return(b200moe_ep* E, void* stream) {
   if (!connected(E)) return B200MOE_ERR_STATE;
   EpDeviceGuard guard(E->device);
   EpP2P a = ep_args(E);
-  const int64_t work = int64_t(E->r_cap) * (E->H / 8);  // bounded by the rows received
-  const int blocks = int(std::min<int64_t>(std::max<int64_t>((work + 255) / 256, 1), int64_t(E->grid) * 2));
+  const int blocks = std::min(std::max((E->r_cap + 7) / 8, 1), E->grid * 2);  // a warp per row received
   ep_return_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(a, E->y2);
   return cudaGetLastError() == cudaSuccess ? B200MOE_OK : B200MOE_ERR_CUDA;
 }
