@@ -67,8 +67,9 @@ typedef enum { B200MOE_F16 = 0, B200MOE_BF16 = 1, B200MOE_F32 = 2 } b200moe_dtyp
 typedef enum { B200MOE_NVFP4 = 0, B200MOE_MXFP4 = 1, B200MOE_IQ2XXS = 2 } b200moe_format;
 
 /* Shape and residency of one layer on one GPU.  Bank 0 holds FP4 experts
- * (NVFP4 or MXFP4), bank 1 IQ2_XXS experts; the slot maps say which expert id
- * sits in which slot of which bank. */
+ * (NVFP4 or MXFP4), bank 1 IQ codebook experts (IQ2_XXS, IQ2_XS or IQ1_M per
+ * projection); the slot maps say which expert id sits in which slot of which
+ * bank. */
 typedef struct {
   int32_t hidden;             /* H: multiple of 256 */
   int32_t inter;              /* I: multiple of 128 (256 when bank 1 is used) */
@@ -78,7 +79,7 @@ typedef struct {
   int32_t max_prefill_tokens; /* T limit of forward_prefill (0: no prefill workspace) */
   int32_t fp4_format;         /* B200MOE_NVFP4 or B200MOE_MXFP4 */
   int32_t n_fp4;              /* slots in bank 0 */
-  int32_t n_iq2;              /* slots in bank 1 */
+  int32_t n_iq2;              /* slots in bank 1 (IQ codebook experts) */
   float swiglu_limit;         /* limited SwiGLU bound (reference: 10.0) */
   int32_t prefill_gemm;       /* FP4 bank kernels: 0 = the skinny decode kernels for every call,
                                  1 = forward_prefill on the tcgen05 grouped GEMM (f16 dequantized
@@ -89,6 +90,10 @@ typedef struct {
                                  32; activations as four E2M1 planes, ~1e-4 relative), prefills of
                                  >= 4096 routes on the tcgen05 f16 GEMM; both read the bank as
                                  swizzled weight units; the fastest layout for decode and prefill */
+  int32_t iq_type13;          /* GGML type of bank 1's gate/up (W1, W3): 16 IQ2_XXS (0 = 16),
+                                 17 IQ2_XS, 29 IQ1_M -- the routed-expert types GGUF layers mix,
+                                 engine/.../experts/nvfp4_8r_tiers.py:35 */
+  int32_t iq_type2;           /* GGML type of bank 1's down projection (W2), same codes */
 } b200moe_config;
 
 typedef struct b200moe_layer b200moe_layer;
@@ -108,6 +113,14 @@ int b200moe_set_slot_maps(b200moe_layer* layer, const int32_t* fp4_slot, const i
 /* IQ2_XXS codebook: grid int8 [256][8] and ksigns uint8 [128] (host). */
 int b200moe_set_iq2_tables(b200moe_layer* layer, const int8_t* grid, const uint8_t* ksigns);
 
+/* Codebook of one IQ format by GGML type (host arrays, ggml's data): 16
+ * IQ2_XXS grid int8 [256][8] of 8/25/43 + ksigns [128]; 17 IQ2_XS grid
+ * [512][8] of 8/25/43 + ksigns [128]; 29 IQ1_M grid [2048][8] of -1/0/1, no
+ * ksigns (NULL).  n_entries = the grid's rows.  Every format the layer's IQ
+ * bank uses (config iq_type13 / iq_type2) needs its codebook before a forward. */
+int b200moe_set_iq_grid(b200moe_layer* layer, int ggml_type, const int8_t* grid, int n_entries,
+                        const uint8_t* ksigns);
+
 /* Load n consecutive bank-0 slots from natural-layout device arrays:
  *   w13_codes [n][2I][H/2] (W1 rows then W3 rows, low nibble = even element),
  *   w13_scales [n][2I][H/bs], w2_codes [n][H][I/2], w2_scales [n][H][I/bs],
@@ -118,8 +131,9 @@ int b200moe_load_fp4(b200moe_layer* layer, void* stream, int slot_begin, int n,
                      const uint8_t* w13_codes, const uint8_t* w13_scales, const uint8_t* w2_codes,
                      const uint8_t* w2_scales, const float* globals);
 
-/* Load n consecutive bank-1 slots from ggml IQ2_XXS blocks (66 bytes per 256):
- * w1, w3 [n][I][H/256][66], w2 [n][H][I/256][66] (device). */
+/* Load n consecutive bank-1 slots from ggml blocks of the configured IQ types
+ * (B bytes per 256 weights: IQ2_XXS 66, IQ2_XS 74, IQ1_M 56): w1, w3
+ * [n][I][H/256][B of iq_type13], w2 [n][H][I/256][B of iq_type2] (device). */
 int b200moe_load_iq2(b200moe_layer* layer, void* stream, int slot_begin, int n, const uint8_t* w1,
                      const uint8_t* w3, const uint8_t* w2);
 

@@ -271,6 +271,111 @@ def iq2xxs_random_blocks(rng: np.random.Generator, rows: int, k: int, wscale: fl
     return out
 
 
+IQ2XS_BLOCK_BYTES = 74
+IQ1M_BLOCK_BYTES = 56
+IQ1M_DELTA = np.float32(0.125)
+
+
+def iq_tables(ggml_type: int):
+    """(grid int8 [n, 8], ksigns uint8 [128] or None) of GGML type 16 (IQ2_XXS),
+    17 (IQ2_XS) or 29 (IQ1_M), from gguf-py 0.19.0 at run time (ggml data)."""
+    from gguf.quants import IQ1_M, IQ2_XS, IQ2_XXS
+
+    cls = {16: IQ2_XXS, 17: IQ2_XS, 29: IQ1_M}[ggml_type]
+    cls.init_grid()
+    grid = np.asarray(cls.grid, np.float32).reshape(-1, 8).astype(np.int8)
+    ksigns = None if ggml_type == 29 else np.frombuffer(IQ2_XXS.ksigns, np.uint8).copy()
+    return grid, ksigns
+
+
+def iq2xs_decode(blocks: np.ndarray, grid: np.ndarray, ksigns: np.ndarray) -> np.ndarray:
+    """IQ2_XS blocks uint8 [R, K/256, 74] -> float32 [R, K].
+
+    ggml's published decode (gguf-py 0.19.0 ``IQ2_XS.dequantize_blocks``):
+    d = fp16 bytes 0..1, 32 u16 qs at 2..65, 8 scale bytes at 66..73; group
+    g = 4ib + l of 8 values (sub-block ib, entry l) takes grid[qs[g] & 511],
+    negated per bit j of ksigns[qs[g] >> 9]; its scale is
+    db = d * (0.5 + s) * 0.25, s = low nibble of scale byte ib for l < 2, high
+    nibble for l >= 2."""
+    blocks = np.asarray(blocks, np.uint8)
+    rows, nb, nbytes = blocks.shape
+    if nbytes != IQ2XS_BLOCK_BYTES:
+        raise ValueError("IQ2_XS blocks are 74 bytes")
+    d = blocks[..., :2].copy().view(np.float16).astype(np.float32).reshape(rows, nb)
+    qs = blocks[..., 2:66].copy().view(np.uint16).reshape(rows, nb, 32)
+    sc = blocks[..., 66:74]
+    s = np.stack([sc & 15, sc >> 4], axis=-1).reshape(rows, nb, 16).astype(np.float32)  # per 16 values
+    db = (d[..., None] * (np.float32(0.5) + s)) * np.float32(0.25)
+    vals = grid[(qs & 511).astype(np.int64)].astype(np.float32)  # [R, nb, 32, 8]
+    neg = (ksigns[(qs >> 9).astype(np.int64)][..., None] >> np.arange(8, dtype=np.uint8)) & 1
+    sgn = np.where(neg == 1, np.float32(-1), np.float32(1))
+    out = (np.repeat(db, 2, axis=-1)[..., None] * vals) * sgn
+    return out.astype(np.float32).reshape(rows, nb * IQ2_BLOCK)
+
+
+def iq1m_decode(blocks: np.ndarray, grid: np.ndarray) -> np.ndarray:
+    """IQ1_M blocks uint8 [R, K/256, 56] -> float32 [R, K].
+
+    ggml's published decode (gguf-py 0.19.0 ``IQ1_M.dequantize_blocks``):
+    qs bytes 0..31, qh bytes 32..47, four u16 scale words at 48..55.  d is the
+    fp16 whose four nibbles are the words' top nibbles (word 0 lowest); the
+    3-bit scale s of the 16-value half i is bits 3(i % 4).. of word i // 4,
+    dl = d * (2s + 1).  Group g of 8 values takes nibble g % 2 of qh byte g // 2:
+    bits 0..2 extend qs[g] to an 11-bit grid index, bit 3 makes delta -1/8
+    (else +1/8); value = dl * (grid + delta)."""
+    blocks = np.asarray(blocks, np.uint8)
+    rows, nb, nbytes = blocks.shape
+    if nbytes != IQ1M_BLOCK_BYTES:
+        raise ValueError("IQ1_M blocks are 56 bytes")
+    qs = blocks[..., :32].astype(np.int64)
+    qh = blocks[..., 32:48]
+    w = blocks[..., 48:56].copy().view(np.uint16).reshape(rows, nb, 4).astype(np.uint32)
+    dbits = ((w[..., 0] >> 12) | ((w[..., 1] >> 8) & 0xF0) | ((w[..., 2] >> 4) & 0xF00) | (w[..., 3] & 0xF000))
+    d = dbits.astype(np.uint16).view(np.float16).astype(np.float32)
+    s = ((w[..., :, None] >> np.array([0, 3, 6, 9], np.uint32)) & 7).reshape(rows, nb, 16).astype(np.float32)
+    dl = d[..., None] * (np.float32(2) * s + np.float32(1))  # [R, nb, 16]
+    nib = np.stack([qh & 15, qh >> 4], axis=-1).reshape(rows, nb, 32)
+    idx = qs | ((nib & 7).astype(np.int64) << 8)
+    delta = np.where((nib & 8) == 0, IQ1M_DELTA, -IQ1M_DELTA).astype(np.float32)
+    vals = grid[idx].astype(np.float32) + delta[..., None]  # [R, nb, 32, 8]
+    out = np.repeat(dl, 2, axis=-1)[..., None] * vals
+    return out.astype(np.float32).reshape(rows, nb * IQ2_BLOCK)
+
+
+def iq_random_blocks(rng: np.random.Generator, ggml_type: int, rows: int, k: int, wscale: float) -> np.ndarray:
+    """Seeded random valid blocks of IQ2_XXS (16), IQ2_XS (17) or IQ1_M (29):
+    every pattern of the index, sign and scale bits is legal; the fp16 d is set
+    so the decoded weights have roughly ``wscale`` spread."""
+    if ggml_type == 16:
+        return iq2xxs_random_blocks(rng, rows, k, wscale)
+    if k % IQ2_BLOCK:
+        raise ValueError("K must be a multiple of 256")
+    nb = k // IQ2_BLOCK
+    if ggml_type == 17:
+        out = rng.integers(0, 256, size=(rows, nb, IQ2XS_BLOCK_BYTES), dtype=np.uint8)
+        d = (wscale / 48.0) * rng.uniform(0.75, 1.25, size=(rows, nb))
+        out[..., :2] = d.astype(np.float16).view(np.uint8).reshape(rows, nb, 2)
+        return out
+    if ggml_type == 29:
+        out = rng.integers(0, 256, size=(rows, nb, IQ1M_BLOCK_BYTES), dtype=np.uint8)
+        d = ((wscale / 6.0) * rng.uniform(0.75, 1.25, size=(rows, nb))).astype(np.float16).view(np.uint16)
+        w = out[..., 48:56].copy().view(np.uint16).reshape(rows, nb, 4) & np.uint16(0x0FFF)
+        for i in range(4):  # d's nibble i in word i's top nibble
+            w[..., i] |= ((d >> np.uint16(4 * i)) & np.uint16(15)) << np.uint16(12)
+        out[..., 48:56] = w.view(np.uint8).reshape(rows, nb, 8)
+        return out
+    raise ValueError(f"GGML type {ggml_type} is not IQ2_XXS / IQ2_XS / IQ1_M")
+
+
+def iq_decode(ggml_type: int, blocks: np.ndarray) -> np.ndarray:
+    grid, ksigns = iq_tables(ggml_type)
+    if ggml_type == 16:
+        return iq2xxs_decode(blocks, grid, ksigns)
+    if ggml_type == 17:
+        return iq2xs_decode(blocks, grid, ksigns)
+    return iq1m_decode(blocks, grid)
+
+
 # ---------------------------------------------------------------------------
 # Router gating (this build's definition; the engine's router is not in the mount)
 # ---------------------------------------------------------------------------

@@ -52,7 +52,7 @@ def test_status_names_and_version(lib):
 def test_config_struct_layout(pkg):
     from b200moe import _lib
 
-    assert ctypes.sizeof(_lib.Config) == 44
+    assert ctypes.sizeof(_lib.Config) == 52
     text = HEADER.read_text()
     block = text[text.index("typedef struct {"):text.index("} b200moe_config;")]
     fields = re.findall(r"(?:int32_t|float)\s+(\w+);", block)
@@ -66,6 +66,8 @@ def test_create_refuses_bad_config_without_gpu(lib, pkg):
     bad = _lib.Config(300, 2048, 384, 8, 64, 0, 0, 384, 0, 10.0, 0)  # hidden not a multiple of 256
     assert lib.b200moe_layer_create(ctypes.byref(bad), 0, ctypes.byref(h)) == 1
     bad = _lib.Config(4096, 2048, 384, 8, 65, 0, 0, 384, 0, 10.0, 0)  # max_tokens > 64
+    assert lib.b200moe_layer_create(ctypes.byref(bad), 0, ctypes.byref(h)) == 1
+    bad = _lib.Config(4096, 2048, 384, 8, 64, 0, 0, 200, 184, 10.0, 0, 17, 18)  # GGML type 18 is no IQ type
     assert lib.b200moe_layer_create(ctypes.byref(bad), 0, ctypes.byref(h)) == 1
 
 

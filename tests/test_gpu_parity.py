@@ -164,30 +164,37 @@ def _fp4_dequant(bank, fmt, inter):
     return dq
 
 
-def _make_layer(dev, H, I, E, K, max_tokens, fmt="nvfp4", tier=None, seed=0, max_prefill=0, gemm="tcgen05"):
+def _make_layer(dev, H, I, E, K, max_tokens, fmt="nvfp4", tier=None, seed=0, max_prefill=0, gemm="tcgen05",
+                iq_types=(16, 16)):
     from b200moe import moe, synth, tiers
 
     tier = np.zeros(E, np.int8) if tier is None else tier
     layer = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K, max_tokens=max_tokens, tier=tier,
-                              fp4_format=fmt, device=dev, max_prefill_tokens=max_prefill, prefill_gemm=gemm)
+                              fp4_format=fmt, device=dev, max_prefill_tokens=max_prefill, prefill_gemm=gemm,
+                              iq_types=iq_types)
     n_hot, n_iq = int((tier == tiers.HOT).sum()), int((tier == tiers.WARM).sum())
     fp4 = synth.make_fp4_bank(n_hot, H, I, fmt, seed, dev) if n_hot else None
-    iq2 = synth.make_iq2_bank(n_iq, H, I, seed + 1, dev) if n_iq else None
+    iq2 = synth.make_iq2_bank(n_iq, H, I, seed + 1, dev, iq_types=iq_types) if n_iq else None
     if fp4 is not None:
         synth.load_bank(layer, fp4)
     if iq2 is not None:
-        layer.set_iq2_tables()
+        layer.set_iq_tables()
         synth.load_bank(layer, iq2)
     layer.check_errors()
     grid, ksigns = mo.iq2xxs_tables()
     fp4_dq = _fp4_dequant(fp4, fmt, I) if fp4 is not None else None
 
+    def iq_dq(t, blocks):
+        if t == 16:
+            return tr.iq2xxs_decode(blocks, grid, ksigns)
+        return torch.from_numpy(mo.iq_decode(t, blocks.cpu().numpy())).to(dev)
+
     def dequant(e):
         if tier[e] == tiers.HOT:
             return fp4_dq(int(layer.fp4_slot[e]))
         s = int(layer.iq2_slot[e])
-        return (torch.cat([tr.iq2xxs_decode(iq2.w1[s], grid, ksigns), tr.iq2xxs_decode(iq2.w3[s], grid, ksigns)]),
-                tr.iq2xxs_decode(iq2.w2[s], grid, ksigns))
+        return (torch.cat([iq_dq(iq_types[0], iq2.w1[s]), iq_dq(iq_types[0], iq2.w3[s])]),
+                iq_dq(iq_types[1], iq2.w2[s]))
 
     return layer, dequant, fp4, iq2
 
@@ -341,6 +348,44 @@ def test_all_iq2_layer(dev, pkg, m):
     layer.check_errors()
     err = tr.rel_l2(out, tr.layer_forward(x, ids.long(), w, dequant))
     assert err < 2e-3, err
+    layer.close()
+
+
+@pytest.mark.parametrize("iq_types,m", [((17, 17), 1), ((17, 17), 48), ((29, 29), 8), ((29, 29), 64),
+                                        ((17, 29), 16), ((29, 16), 300), ((16, 17), 33)])
+def test_iq_types_layer(dev, pkg, iq_types, m):
+    """IQ2_XS (17) and IQ1_M (29) experts, alone and mixed per projection with
+    IQ2_XXS (16): the int8 tensor path against the fp32 dequant (gguf-py's
+    published decode, restated in the oracle) of the same blocks."""
+    from b200moe import tiers
+
+    E = 48
+    tier = np.full(E, tiers.WARM, np.int8)
+    layer, dequant, _, _ = _make_layer(dev, 2048, 1024, E, 8, 64, tier=tier, seed=19, max_prefill=300,
+                                       iq_types=iq_types)
+    g = torch.Generator(device=dev).manual_seed(190 + m)
+    x = torch.randn((m, 2048), generator=g, device=dev).to(torch.bfloat16)
+    ids, w = layer.route(torch.randn((m, E), generator=g, device=dev))
+    out = (layer.forward(x, ids, w) if m <= 64 else layer.forward_prefill(x, ids, w)).clone()
+    layer.check_errors()
+    err = tr.rel_l2(out, tr.layer_forward(x, ids.long(), w, dequant))
+    assert err < 2e-3, err
+    layer.close()
+
+
+def test_iq_types_mixed_with_fp4(dev, pkg):
+    """NVFP4 HOT experts beside IQ1_M gate/up + IQ2_XS down WARM experts."""
+    from b200moe import synth, tiers
+
+    tier, rank = tiers.zipf_tier(96, 40, seed=5)
+    layer, dequant, _, _ = _make_layer(dev, 2048, 1024, 96, 8, 32, tier=tier, seed=5, iq_types=(29, 17))
+    g = torch.Generator(device=dev).manual_seed(55)
+    x = torch.randn((32, 2048), generator=g, device=dev).to(torch.bfloat16)
+    ids, w = layer.route(synth.zipf_logits(32, rank, 1.0, 1.1, 55, dev))
+    out = layer.forward(x, ids, w).clone()
+    layer.check_errors()
+    assert (tier[ids.cpu().numpy()] == tiers.WARM).any() and (tier[ids.cpu().numpy()] == tiers.HOT).any()
+    assert tr.rel_l2(out, tr.layer_forward(x, ids.long(), w, dequant)) < TOL
     layer.close()
 
 

@@ -198,3 +198,18 @@ def test_route_stats_vs_reference_counters():
                 np.testing.assert_array_equal(c[k], z[f"{k}_{i}"], err_msg=f"{k} after call {i}")
             np.testing.assert_array_equal(mo.route_stats_recent(c), z[f"recent_{i}"])
     assert np.all(z[f"gap_hist_{max(marks)}"] > 0)  # every bucket was reached
+
+
+@pytest.mark.parametrize("ggml_type", [17, 29])
+def test_iq_formats_vs_gguf(ggml_type):
+    """IQ2_XS / IQ1_M decode restatements against gguf-py 0.19.0's dequantize
+    (the third-party implementation of ggml's published formats), bit for bit."""
+    from gguf import GGMLQuantizationType as Q
+    from gguf.quants import dequantize
+
+    rng = np.random.default_rng(700 + ggml_type)
+    blocks = mo.iq_random_blocks(rng, ggml_type, 96, 2048, 0.02)
+    mine = mo.iq_decode(ggml_type, blocks)
+    ref = dequantize(blocks.reshape(96, -1), Q.IQ2_XS if ggml_type == 17 else Q.IQ1_M).astype(np.float32)
+    assert np.array_equal(mine.view(np.uint32), ref.reshape(mine.shape).view(np.uint32))
+    assert np.abs(mine).mean() > 1e-3

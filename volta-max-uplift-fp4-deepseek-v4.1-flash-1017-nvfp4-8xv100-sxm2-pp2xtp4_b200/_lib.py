@@ -38,7 +38,7 @@ class Config(ctypes.Structure):
                 ("top_k", ctypes.c_int32), ("max_tokens", ctypes.c_int32),
                 ("max_prefill_tokens", ctypes.c_int32), ("fp4_format", ctypes.c_int32),
                 ("n_fp4", ctypes.c_int32), ("n_iq2", ctypes.c_int32), ("swiglu_limit", ctypes.c_float),
-                ("prefill_gemm", ctypes.c_int32)]
+                ("prefill_gemm", ctypes.c_int32), ("iq_type13", ctypes.c_int32), ("iq_type2", ctypes.c_int32)]
 
 
 # name -> (argtypes, restype); every symbol include/b200moe.h declares
@@ -49,6 +49,7 @@ SIGNATURES = {
     "b200moe_layer_destroy": ([P], I32),
     "b200moe_set_slot_maps": ([P, P, P], I32),
     "b200moe_set_iq2_tables": ([P, P, P], I32),
+    "b200moe_set_iq_grid": ([P, I32, P, I32, P], I32),
     "b200moe_load_fp4": ([P, P, I32, I32, P, P, P, P, P], I32),
     "b200moe_load_iq2": ([P, P, I32, I32, P, P, P], I32),
     "b200moe_route": ([P, P, P, P, P, I32], I32),

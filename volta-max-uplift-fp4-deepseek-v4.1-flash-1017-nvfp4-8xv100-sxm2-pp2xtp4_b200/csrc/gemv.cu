@@ -35,17 +35,20 @@ constexpr int kConsumerWarps = 8;
 constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;
 constexpr int kRouteSlots = kRouteSlotsPerChunk;  // activation row slots per stage (KS * route chunk)
 
-// FP4: two CTAs per SM (18 warps) with a 4-stage ring each; IQ2: one CTA with 6.
+// FMT 0 / 1: NVFP4 / MXFP4; 2 / 3 / 4: the IQ bank's IQ2_XXS / IQ2_XS / IQ1_M.
+// FP4: two CTAs per SM (18 warps) with a 4-stage ring each; IQ: one CTA with 6.
 template <int FMT>
 struct Fmt {
-  static constexpr int KT = FMT == 2 ? kIq2KTile : kFp4KTile;            // K per unit
-  static constexpr int U = FMT == 2 ? kIq2UnitBytes : fp4_unit_bytes(FMT); // unit bytes
-  // activation bytes of one row per K tile (f16 for FP4; int8 + scale for IQ2)
-  static constexpr int XB = FMT == 2 ? kIq2XBlockBytes : 2 * KT;
-  static constexpr int XRS = FMT == 2 ? 544 : 2 * KT + 64;               // x row slot bytes
+  static constexpr bool IQ = FMT >= 2;
+  static constexpr int KT = IQ ? kIq2KTile : kFp4KTile;                  // K per unit
+  static constexpr int U = IQ ? iq_unit_bytes(FMT) : fp4_unit_bytes(FMT); // unit bytes
+  // activation bytes of one row per K tile (f16 for FP4; int8 + scale for IQ)
+  static constexpr int XB = IQ ? kIq2XBlockBytes : 2 * KT;
+  static constexpr int XRS = IQ ? 544 : 2 * KT + 64;                     // x row slot bytes
   static constexpr int STAGE = kConsumerWarps * U + kRouteSlots * XRS;
-  static constexpr int CTAS = FMT == 2 ? 1 : 2;                          // CTAs per SM
+  static constexpr int CTAS = IQ ? 1 : 2;                                // CTAs per SM
   static constexpr int STAGES = CTAS == 2 ? 4 : 6;
+  static constexpr int TW = IQ ? iq_table_words(FMT) : 0;                // decode table words
 };
 constexpr int kMaxStages = 6;
 
@@ -54,15 +57,18 @@ constexpr int kListInts = 1 + 2 * 128;
 
 template <int FMT>
 constexpr size_t smem_total() {
-  return 128 + size_t(Fmt<FMT>::STAGES) * Fmt<FMT>::STAGE + kRedBytes + (FMT == 2 ? kIq2TableWords * 4 : 0) +
-         kListInts * 4;
+  return 128 + size_t(Fmt<FMT>::STAGES) * Fmt<FMT>::STAGE + kRedBytes + size_t(Fmt<FMT>::TW) * 4 + kListInts * 4;
 }
 
 size_t gemv_smem_bytes(int fmt, int) {
-  return fmt == 0 ? smem_total<0>() : fmt == 1 ? smem_total<1>() : smem_total<2>();
+  return fmt == 0   ? smem_total<0>()
+         : fmt == 1 ? smem_total<1>()
+         : fmt == 2 ? smem_total<2>()
+         : fmt == 3 ? smem_total<3>()
+                    : smem_total<4>();
 }
 
-int gemv_ctas_per_sm(int fmt) { return fmt == 2 ? Fmt<2>::CTAS : Fmt<0>::CTAS; }
+int gemv_ctas_per_sm(int fmt) { return fmt >= 2 ? Fmt<2>::CTAS : Fmt<0>::CTAS; }
 
 // ---------------------------------------------------------------- FP4 step
 // acc[mt][nt][j]: one accumulator per k16 step parity, so each tile has two
@@ -218,6 +224,195 @@ __device__ __forceinline__ void iq2_step(uint32_t wb, uint32_t xb, uint32_t tbl,
   }
 }
 
+// ---------------------------------------------------------------- IQ2_XS / IQ1_M steps
+// Both formats scale every 16 weights on their own, so each 32-wide sub-block
+// takes two m16n8k16 MMAs, one per 16-weight group, each s32 partial scaled
+// by its group's integer 2s + 1.  Thread q owns elements 4q..4q+3 of each
+// group (half q & 1 of grid entry q >> 1, and of entry 2 + (q >> 1) in the
+// second group): the k16 fragments' K positions, activations in natural order.
+// The fp16 d / 8 and the activation scale apply once per super-block in FP32,
+// as in iq2_step.
+__device__ __forceinline__ void iq_finish(const int (&t)[2][2][2][4], const float (&dl)[2][2], uint32_t xb,
+                                          int ntiles, int lane, float (&acc)[2][2][2][4]) {
+  constexpr int XRS = Fmt<2>::XRS;
+  constexpr float kPlane2 = 1.f / 254.f;
+  const int q = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    if (nt >= ntiles) continue;
+    const float sx0 = __uint_as_float(lds32(xb + (nt * 8 + 2 * q) * XRS + 512));
+    const float sx1 = __uint_as_float(lds32(xb + (nt * 8 + 2 * q + 1) * XRS + 512));
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      const float sc[4] = {dl[mt][0] * sx0, dl[mt][0] * sx1, dl[mt][1] * sx0, dl[mt][1] * sx1};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        acc[mt][nt][0][i] = fmaf(fmaf(float(t[1][mt][nt][i]), kPlane2, float(t[0][mt][nt][i])), sc[i], acc[mt][nt][0][i]);
+    }
+  }
+}
+
+// the activation fragments of one sub-block: [nt][plane][group]
+__device__ __forceinline__ void iq_load_x(uint32_t xb, int ib, int ntiles, int lane, uint32_t (&xv)[2][2][2]) {
+  constexpr int XRS = Fmt<2>::XRS;
+  const int r = lane >> 2, q = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int pl = 0; pl < 2; ++pl)
+#pragma unroll
+      for (int grp = 0; grp < 2; ++grp)
+        xv[nt][pl][grp] = nt < ntiles ? lds32(xb + (nt * 8 + r) * XRS + pl * 256 + ib * 32 + grp * 16 + 4 * q) : 0u;
+}
+
+// the two MMAs of one sub-block and tile, one per 16-weight group, for both planes
+__device__ __forceinline__ void iq_group_mmas(const uint32_t (&a)[2][2], const int (&c)[2][2],
+                                              const uint32_t (&xv)[2][2][2], int ntiles, int (&t)[2][2][2][4],
+                                              int mt) {
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    if (nt >= ntiles) continue;
+#pragma unroll
+    for (int pl = 0; pl < 2; ++pl)
+#pragma unroll
+      for (int grp = 0; grp < 2; ++grp) {
+        int d[4] = {0, 0, 0, 0};
+        mma_16816_s8(d, a[grp][0], a[grp][1], xv[nt][pl][grp]);
+        t[pl][mt][nt][0] += d[0] * c[grp][0];
+        t[pl][mt][nt][1] += d[1] * c[grp][0];
+        t[pl][mt][nt][2] += d[2] * c[grp][1];
+        t[pl][mt][nt][3] += d[3] * c[grp][1];
+      }
+  }
+}
+
+// IQ2_XS (ggml's dequantize: d * (0.5 + s) * 0.25 * grid * sign, s the 4-bit
+// scale of each 16 weights): a weight is g * sign (g in {8, 25, 43}) from the
+// 9-bit grid index's magnitude codes and the 7-bit sign index's nibbles.
+__device__ __forceinline__ void iq2xs_step(uint32_t wb, uint32_t xb, uint32_t tbl, int ntiles, int lane,
+                                           float (&acc)[2][2][2][4]) {
+  constexpr uint32_t kPos = 0x002B1908u, kNeg = 0x00D5E7F8u;  // bytes 8, 25, 43, 0 and -8, -25, -43, 0
+  const int r = lane >> 2, q = lane & 3;
+  const int e_sh = 16 * (q >> 1), h_sh = 16 * (q & 1);
+  int t[2][2][2][4];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) (&t[0][0][0][0])[i] = 0;
+  const uint32_t tsign = tbl + 512 * 4;
+  uint2 sc[2][2];  // [mt][h]: the row's 8 scale bytes
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) sc[mt][h] = lds64(wb + 2048 + mt * 128 + (h * 8 + r) * 8);
+#pragma unroll 1
+  for (int ibp = 0; ibp < 4; ++ibp) {
+    uint4 qw[2][2];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) qw[mt][h] = lds128(wb + mt * 1024 + (h * 8 + r) * 64 + ibp * 16);
+#pragma unroll
+    for (int i2 = 0; i2 < 2; ++i2) {
+      const int ib = 2 * ibp + i2;
+      uint32_t xv[2][2][2];
+      iq_load_x(xb, ib, ntiles, lane, xv);
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        uint32_t a[2][2];
+        int c[2][2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t w01 = i2 == 0 ? qw[mt][h].x : qw[mt][h].z;  // u16 entries 0, 1 of the sub-block
+          const uint32_t w23 = i2 == 0 ? qw[mt][h].y : qw[mt][h].w;  // entries 2, 3
+#pragma unroll
+          for (int grp = 0; grp < 2; ++grp) {
+            const uint32_t u = ((grp ? w23 : w01) >> e_sh) & 0xFFFFu;
+            const uint32_t sel = lds32(tbl + (u & 511u) * 4) | lds32(tsign + (u >> 9) * 4);
+            a[grp][h] = __byte_perm(kPos, kNeg, sel >> h_sh);
+          }
+          const uint32_t sb = ((ib < 4 ? sc[mt][h].x : sc[mt][h].y) >> (8 * (ib & 3))) & 255u;
+          c[0][h] = int(2 * (sb & 15u) + 1);
+          c[1][h] = int(2 * (sb >> 4) + 1);
+        }
+        iq_group_mmas(a, c, xv, ntiles, t, mt);
+      }
+    }
+  }
+  float dl[2][2];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+    const uint32_t dp = lds32(wb + 2304 + mt * 32 + r * 4);
+    const __half2 d2 = *reinterpret_cast<const __half2*>(&dp);
+    dl[mt][0] = __low2float(d2) * 0.125f;
+    dl[mt][1] = __high2float(d2) * 0.125f;
+  }
+  iq_finish(t, dl, xb, ntiles, lane, acc);
+}
+
+// IQ1_M (ggml's dequantize: d * (2s + 1) * (grid + delta), grid in {-1, 0, 1},
+// delta = +-1/8 per 8 weights, s the 3-bit scale of each 16 weights, d the
+// fp16 in the scales' top nibbles): a weight is 8 * grid +- 1 in int8, times
+// (2s + 1) on the s32 partial, times d / 8 in FP32.
+__device__ __forceinline__ void iq1m_step(uint32_t wb, uint32_t xb, uint32_t tbl, int ntiles, int lane,
+                                          float (&acc)[2][2][2][4]) {
+  constexpr uint32_t kPos = 0x000901F9u, kNeg = 0x0007FFF7u;  // bytes -7, 1, 9 (delta +) and -9, -1, 7 (delta -)
+  const int r = lane >> 2, q = lane & 3;
+  const int e0 = q >> 1, h_sh = 16 * (q & 1);
+  int t[2][2][2][4];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) (&t[0][0][0][0])[i] = 0;
+  uint2 sc[2][2];  // [mt][h]: the row's four u16 scale words
+  float dl[2][2];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      sc[mt][h] = lds64(wb + 1536 + mt * 128 + (h * 8 + r) * 8);
+      const uint32_t lo = sc[mt][h].x, hi = sc[mt][h].y;
+      const uint32_t dbits = ((lo >> 12) & 0x000Fu) | ((lo >> 24) & 0x00F0u) | ((hi >> 4) & 0x0F00u) | ((hi >> 16) & 0xF000u);
+      dl[mt][h] = __half2float(__ushort_as_half(static_cast<unsigned short>(dbits))) * 0.125f;
+    }
+#pragma unroll 1
+  for (int ibp = 0; ibp < 4; ++ibp) {
+    uint2 qs[2][2];
+    uint32_t qh[2][2];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        qs[mt][h] = lds64(wb + mt * 512 + (h * 8 + r) * 32 + ibp * 8);
+        qh[mt][h] = lds32(wb + 1024 + mt * 256 + (h * 8 + r) * 16 + ibp * 4);
+      }
+#pragma unroll
+    for (int i2 = 0; i2 < 2; ++i2) {
+      const int ib = 2 * ibp + i2;
+      uint32_t xv[2][2][2];
+      iq_load_x(xb, ib, ntiles, lane, xv);
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        uint32_t a[2][2];
+        int c[2][2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t qsw = i2 == 0 ? qs[mt][h].x : qs[mt][h].y;  // qs bytes of entries 0..3
+          const uint32_t sword = ibp < 2 ? (ibp == 0 ? sc[mt][h].x & 0xFFFFu : sc[mt][h].x >> 16)
+                                         : (ibp == 2 ? sc[mt][h].y & 0xFFFFu : sc[mt][h].y >> 16);
+#pragma unroll
+          for (int grp = 0; grp < 2; ++grp) {
+            const int l = 2 * grp + e0;  // entry of the sub-block
+            const uint32_t nib = (qh[mt][h] >> (8 * (2 * i2 + grp) + 4 * e0)) & 15u;
+            const uint32_t idx = ((qsw >> (8 * l)) & 255u) | ((nib & 7u) << 8);
+            const uint32_t sel = lds32(tbl + idx * 4) | ((nib & 8u) ? 0x44444444u : 0u);
+            a[grp][h] = __byte_perm(kPos, kNeg, sel >> h_sh);
+            c[grp][h] = int(2 * ((sword >> (3 * (2 * i2 + grp))) & 7u) + 1);
+          }
+        }
+        iq_group_mmas(a, c, xv, ntiles, t, mt);
+      }
+    }
+  }
+  iq_finish(t, dl, xb, ntiles, lane, acc);
+}
+
 __device__ __forceinline__ bool chunk_ok(const Chunk& ch, int rc, const GemvArgs& a) {
   return ch.slot >= 0 && ch.slot < a.n_slots && ch.count >= 1 && ch.count <= rc && ch.begin >= 0 &&
          ch.begin + ch.count <= a.S;
@@ -244,7 +439,7 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, uint8_t* smem) {
   uint8_t* stages = smem + 128;
   float* red = reinterpret_cast<float*>(stages + size_t(kStages) * F::STAGE);  // [warp][16][lane]
   uint32_t* tables = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(red) + kRedBytes);
-  int* list = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(tables) + (FMT == 2 ? kIq2TableWords * 4 : 0));
+  int* list = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(tables) + F::TW * 4);
   __shared__ int abort_flag;
   volatile int* abort_ptr = &abort_flag;
 
@@ -258,8 +453,8 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, uint8_t* smem) {
     abort_flag = 0;
     list[0] = 0;
   }
-  if (FMT == 2)
-    for (int i = threadIdx.x; i < kIq2TableWords; i += kGemvThreads) tables[i] = a.iq2_tables[i];
+  if (F::IQ)
+    for (int i = threadIdx.x; i < F::TW; i += kGemvThreads) tables[i] = a.iq2_tables[i];
   __syncthreads();
 
   const int n_kt = a.K / F::KT;
@@ -316,7 +511,7 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, uint8_t* smem) {
           const int kt = xks * steps + st;
           // f16 rows (FP4) or int8 blocks of kIq2XBlockBytes per K tile (IQ2)
           const uint8_t* src = static_cast<const uint8_t*>(a.xsrc) +
-                               (FMT == 2 ? (xrow * n_kt + kt) * F::XB : (xrow * a.x_row_stride + int64_t(kt) * F::KT) * 2);
+                               (F::IQ ? (xrow * n_kt + kt) * F::XB : (xrow * a.x_row_stride + int64_t(kt) * F::KT) * 2);
           bulk_g2s(sb + kConsumerWarps * F::U + xi * F::XRS, src, F::XB, &full[s]);
         }
       }
@@ -360,7 +555,9 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, uint8_t* smem) {
         const uint32_t sb = smem_u32(stages + size_t(s) * F::STAGE);
         const uint32_t wb = sb + warp * F::U;
         const uint32_t xb = sb + kConsumerWarps * F::U + ks * RC * F::XRS;
-        if (FMT == 2) iq2_step(wb, xb, tbl, ntiles, lane, acc2);
+        if constexpr (FMT == 2) iq2_step(wb, xb, tbl, ntiles, lane, acc2);
+        else if constexpr (FMT == 3) iq2xs_step(wb, xb, tbl, ntiles, lane, acc2);
+        else if constexpr (FMT == 4) iq1m_step(wb, xb, tbl, ntiles, lane, acc2);
         else fp4_step<FMT>(wb, xb, ntiles, lane, acc2);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
@@ -568,6 +765,8 @@ int launch_gemv(cudaStream_t s, const GemvArgs& a) {
   if (a.fmt == 0) return a.epi == 0 ? launch_one<0, 0>(s, a) : launch_one<0, 1>(s, a);
   if (a.fmt == 1) return a.epi == 0 ? launch_one<1, 0>(s, a) : launch_one<1, 1>(s, a);
   if (a.fmt == 2) return a.epi == 0 ? launch_one<2, 0>(s, a) : launch_one<2, 1>(s, a);
+  if (a.fmt == 3) return a.epi == 0 ? launch_one<3, 0>(s, a) : launch_one<3, 1>(s, a);
+  if (a.fmt == 4) return a.epi == 0 ? launch_one<4, 0>(s, a) : launch_one<4, 1>(s, a);
   return -1;
 }
 

@@ -22,8 +22,10 @@ int launch_fp4_prepack(cudaStream_t s, int fmt, int hidden, int inter, int n, co
                        const uint8_t* w13s, const uint8_t* w2c, const uint8_t* w2s, float* slot_globals,
                        int* span_scratch, uint8_t* bank_slot0, int64_t slot_stride, int64_t w13_bytes,
                        uint32_t* err);
-int launch_iq2_prepack(cudaStream_t s, int hidden, int inter, int n, const uint8_t* w1, const uint8_t* w3,
-                       const uint8_t* w2, uint8_t* bank_slot0, int64_t slot_stride, int64_t w13_bytes);
+// IQ bank: W13 units in format fmt13, W2 units in fmt2 (2 IQ2_XXS, 3 IQ2_XS, 4 IQ1_M) from ggml blocks
+int launch_iq2_prepack(cudaStream_t s, int fmt13, int fmt2, int hidden, int inter, int n, const uint8_t* w1,
+                       const uint8_t* w3, const uint8_t* w2, uint8_t* bank_slot0, int64_t slot_stride,
+                       int64_t w13_bytes);
 
 // ---- routing (route.cu)
 struct Chunk {  // one route chunk of one expert group: routes perm[begin .. begin+count)
@@ -171,7 +173,7 @@ struct GemvArgs {
   int32_t* counters;          // [tokens][H/32]
   float* out;                 // [tokens][H]
   int H;
-  const uint32_t* iq2_tables; // kIq2TableWords: grid magnitude codes [256], sign nibbles [128]
+  const uint32_t* iq2_tables; // the IQ format's decode tables (iq_table_words(fmt) words)
   uint32_t* err;
   int grid;                   // persistent CTAs
 };

@@ -25,14 +25,16 @@ struct b200moe_layer {
   b200moe_config cfg;
   int device = 0;
   int grid = 148;
-  // banks: 0 = FP4 (NVFP4 / MXFP4), 1 = IQ2_XXS
+  // banks: 0 = FP4 (NVFP4 / MXFP4), 1 = IQ codebook experts (IQ2_XXS / IQ2_XS / IQ1_M per projection)
   uint8_t* bank[2] = {nullptr, nullptr};
   BankGeom geom[2] = {};
   float* globals = nullptr;        // [n_fp4][3]
   int* span = nullptr;             // [n_fp4][3][2] MXFP4 load scratch
-  uint32_t* iq2_tables = nullptr;  // grid f16, sign masks, scale f16x2
+  int iq_fmt[2] = {2, 2};          // kernel format of the IQ bank's W13 and W2 (2 / 3 / 4)
+  uint32_t* iq_tables[2] = {nullptr, nullptr};  // decode tables of those formats
+  bool iq_tables_set[2] = {false, false};
   int32_t* key_of_expert = nullptr;
-  bool maps_set = false, tables_set = false;
+  bool maps_set = false, tables_set = false;  // tables_set: both projections' tables
   int ks_fixed[2] = {0, 0};  // split-K per bank set by the caller (0: chosen per launch)
 
   // workspace
@@ -102,7 +104,7 @@ int dalloc(T** p, size_t count) {
 }
 
 void free_layer(b200moe_layer* L) {
-  void* ptrs[] = {L->bank[0], L->bank[1], L->globals, L->span, L->iq2_tables, L->key_of_expert, L->perm,
+  void* ptrs[] = {L->bank[0], L->bank[1], L->globals, L->span, L->iq_tables[0], L->iq_tables[1], L->key_of_expert, L->perm,
                   L->w_eff, L->chunks[0], L->chunks[1], L->n_chunks, L->x16, L->inter, L->y2,
                   L->counters, L->err, L->xperm, L->ks_sel, L->bank_range, L->xq, L->interq,
                   L->f4_units[0], L->f4_units[1], L->f4_planes[0], L->f4_planes[1],
@@ -136,7 +138,7 @@ KsModel ks_model(const b200moe_layer* L, int bank) {
     if ((c.hidden / kt) % ks == 0 && (c.inter / kt) % ks == 0) m.allowed |= 1 << j;
   }
   m.slots = float(L->grid * gemv_ctas_per_sm(iq2 ? 2 : c.fp4_format));
-  m.bpe = iq2 ? 32.f * 66.f / 256.f : (c.fp4_format == B200MOE_NVFP4 ? 18.f : 17.f);
+  m.bpe = iq2 ? 32.f * float(iq_block_bytes(L->iq_fmt[0])) / 256.f : (c.fp4_format == B200MOE_NVFP4 ? 18.f : 17.f);
   m.bw_cta = iq2 ? 6e9f : 18.4e9f;
   m.bw_hbm = iq2 ? 2.0e12f : 4.8e12f;
   m.per_wave = 2e-6f;
@@ -378,7 +380,7 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
         continue;
       }
       GemvArgs g{};
-      g.fmt = b == 0 ? c.fp4_format : 2;
+      g.fmt = b == 0 ? c.fp4_format : L->iq_fmt[epi];
       g.epi = epi;
       g.ks_sel = ws.ks_sel;
       g.region = L->bank[b] + (epi == 0 ? 0 : L->geom[b].w13_bytes);
@@ -407,7 +409,7 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
       g.counters = ws.counters;
       g.out = out;
       g.H = c.hidden;
-      g.iq2_tables = L->iq2_tables;
+      g.iq2_tables = b == 1 ? L->iq_tables[epi] : nullptr;
       g.err = L->err;
       g.grid = L->grid * gemv_ctas_per_sm(g.fmt);
       if (launch_gemv(s, g)) return B200MOE_ERR_CUDA;
@@ -457,6 +459,8 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
     return B200MOE_ERR_INVALID_ARG;
   if (c.fp4_format != B200MOE_NVFP4 && c.fp4_format != B200MOE_MXFP4) return B200MOE_ERR_INVALID_ARG;
   if (c.n_iq2 > 0 && c.inter % 256) return B200MOE_ERR_INVALID_ARG;
+  for (int t : {c.iq_type13, c.iq_type2})
+    if (t != 0 && iq_fmt_of_type(t) < 0) return B200MOE_ERR_INVALID_ARG;
   if (c.prefill_gemm < 0 || c.prefill_gemm > 2) return B200MOE_ERR_INVALID_ARG;
   // the block-scaled FP4 path: NVFP4 (E4M3 scales per 16), K tiles of 256 on both projections
   if (c.prefill_gemm == 2 && (c.hidden % 256 || c.inter % 256))
@@ -470,7 +474,9 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
   L->device = device;
   L->grid = prop.multiProcessorCount;
   L->geom[0] = fp4_geom(c.fp4_format, c.hidden, c.inter);
-  L->geom[1] = iq2_geom(c.hidden, c.inter);
+  L->iq_fmt[0] = iq_fmt_of_type(c.iq_type13 ? c.iq_type13 : kGgmlIq2xxs);
+  L->iq_fmt[1] = iq_fmt_of_type(c.iq_type2 ? c.iq_type2 : kGgmlIq2xxs);
+  L->geom[1] = iq_geom(L->iq_fmt[0], L->iq_fmt[1], c.hidden, c.inter);
   L->t_max = std::max(c.max_tokens, c.max_prefill_tokens);
   L->s_max = L->t_max * c.top_k;
   L->max_chunks = L->s_max + c.num_experts;
@@ -488,7 +494,8 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
   take(dalloc(&L->bank[1], size_t(c.n_iq2) * L->geom[1].slot_bytes));
   take(dalloc(&L->globals, size_t(std::max(c.n_fp4, 1)) * 3));
   take(dalloc(&L->span, size_t(std::max(c.n_fp4, 1)) * 6));
-  take(dalloc(&L->iq2_tables, size_t(kIq2TableWords)));
+  take(dalloc(&L->iq_tables[0], size_t(iq_table_words(L->iq_fmt[0]))));
+  take(dalloc(&L->iq_tables[1], size_t(iq_table_words(L->iq_fmt[1]))));
   take(dalloc(&L->key_of_expert, size_t(c.num_experts)));
   take(dalloc(&L->perm, size_t(L->s_max)));
   take(dalloc(&L->route_pos, size_t(L->s_max)));
@@ -591,24 +598,45 @@ int b200moe_set_slot_maps(b200moe_layer* L, const int32_t* fp4_slot, const int32
   return B200MOE_OK;
 }
 
-int b200moe_set_iq2_tables(b200moe_layer* L, const int8_t* grid, const uint8_t* ksigns) {
-  if (!L || !grid || !ksigns) return B200MOE_ERR_INVALID_ARG;
-  // magnitude code per grid value (ggml's IQ2_XXS grid holds 8, 25 and 43 only)
-  std::vector<uint32_t> t(kIq2TableWords, 0u);
-  for (int e = 0; e < 256; ++e)
+// Decode tables of one IQ format (layout.cuh): per grid entry its 8 values as
+// nibble codes (IQ2: magnitudes 8, 25, 43 -> 0, 1, 2; IQ1_M: -1, 0, 1 -> 0, 1, 2),
+// then for the IQ2 formats per 7-bit sign index its 8 signs in bit 2 of each
+// nibble.  Written to the projections whose format it is.
+static int set_iq_tables(b200moe_layer* L, int fmt, const int8_t* grid, int n_entries, const uint8_t* ksigns) {
+  const int want = fmt == 2 ? 256 : fmt == 3 ? 512 : 2048;
+  if (!L || !grid || n_entries != want || (fmt != 4 && !ksigns)) return B200MOE_ERR_INVALID_ARG;
+  if (L->iq_fmt[0] != fmt && L->iq_fmt[1] != fmt) return B200MOE_ERR_INVALID_ARG;
+  std::vector<uint32_t> t(iq_table_words(fmt), 0u);
+  for (int e = 0; e < n_entries; ++e)
     for (int j = 0; j < 8; ++j) {
       const int8_t g = grid[e * 8 + j];
-      const int code = g == 8 ? 0 : g == 25 ? 1 : g == 43 ? 2 : -1;
+      const int code = fmt == 4 ? (g == -1 ? 0 : g == 0 ? 1 : g == 1 ? 2 : -1)
+                                : (g == 8 ? 0 : g == 25 ? 1 : g == 43 ? 2 : -1);
       if (code < 0) return B200MOE_ERR_INVALID_ARG;
       t[e] |= uint32_t(code) << (4 * j);
     }
-  for (int si = 0; si < 128; ++si)
-    for (int j = 0; j < 8; ++j) t[256 + si] |= ((uint32_t(ksigns[si]) >> j) & 1u) << (4 * j + 2);
+  if (fmt != 4)
+    for (int si = 0; si < 128; ++si)
+      for (int j = 0; j < 8; ++j) t[n_entries + si] |= ((uint32_t(ksigns[si]) >> j) & 1u) << (4 * j + 2);
   DeviceGuard guard(L->device);
-  if (cudaMemcpy(L->iq2_tables, t.data(), t.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
-    return B200MOE_ERR_CUDA;
-  L->tables_set = true;
+  for (int p = 0; p < 2; ++p)
+    if (L->iq_fmt[p] == fmt) {
+      if (cudaMemcpy(L->iq_tables[p], t.data(), t.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+        return B200MOE_ERR_CUDA;
+      L->iq_tables_set[p] = true;
+    }
+  L->tables_set = L->iq_tables_set[0] && L->iq_tables_set[1];
   return B200MOE_OK;
+}
+
+int b200moe_set_iq2_tables(b200moe_layer* L, const int8_t* grid, const uint8_t* ksigns) {
+  return set_iq_tables(L, 2, grid, 256, ksigns);
+}
+
+int b200moe_set_iq_grid(b200moe_layer* L, int ggml_type, const int8_t* grid, int n_entries, const uint8_t* ksigns) {
+  const int fmt = iq_fmt_of_type(ggml_type);
+  if (fmt < 0) return B200MOE_ERR_INVALID_ARG;
+  return set_iq_tables(L, fmt, grid, n_entries, ksigns);
 }
 
 int b200moe_load_fp4(b200moe_layer* L, void* stream, int slot_begin, int n, const uint8_t* w13c,
@@ -651,8 +679,8 @@ int b200moe_load_iq2(b200moe_layer* L, void* stream, int slot_begin, int n, cons
   const auto& c = L->cfg;
   DeviceGuard guard(L->device);
   uint8_t* dst = L->bank[1] + size_t(slot_begin) * L->geom[1].slot_bytes;
-  if (launch_iq2_prepack(static_cast<cudaStream_t>(stream), c.hidden, c.inter, n, w1, w3, w2, dst,
-                         L->geom[1].slot_bytes, L->geom[1].w13_bytes))
+  if (launch_iq2_prepack(static_cast<cudaStream_t>(stream), L->iq_fmt[0], L->iq_fmt[1], c.hidden, c.inter, n, w1,
+                         w3, w2, dst, L->geom[1].slot_bytes, L->geom[1].w13_bytes))
     return B200MOE_ERR_CUDA;
   return B200MOE_OK;
 }

@@ -19,6 +19,16 @@
 //   [tp < H/32][kb < I/256]; a unit is [mt0 qs 1024][mt1 qs 1024][mt0 d 32][mt1 d 32]:
 //   qs of one m16 tile = [h 2][r 8][64 B] (the block's 64 qs bytes, ggml order);
 //   d = [r 8][h 2] fp16 super-block scales.
+// IQ2_XS (74 B per 256 weights: d, 32 x u16 qs = 9-bit grid index | 7-bit
+//   sign index, 8 scale bytes of two 4-bit scales per 32): units as IQ2_XXS,
+//   [mt0 qs 1024][mt1 qs 1024][mt0 scales 128][mt1 scales 128][mt0 d 32][mt1 d 32];
+//   qs = [h 2][r 8][64 B], scales = [h 2][r 8][8 B], d = [r 8][h 2].
+// IQ1_M (56 B per 256 weights: 32 qs bytes, 16 qh bytes = per 8-weight group a
+//   nibble of 3 high index bits and the delta sign, 4 x u16 scales = 3-bit
+//   scale per 16 weights, the fp16 d in their top nibbles): units
+//   [qs 2 x 512][qh 2 x 256][scales 2 x 128], each [mt][h 2][r 8][its bytes].
+// IQ bank slots hold W13 units of the gate/up format then W2 units of the down
+//   format (the two may differ, as GGUF layers mix them).
 #pragma once
 
 #include <stdint.h>
@@ -60,10 +70,29 @@ inline BankGeom fp4_geom(int fmt, int hidden, int inter) {
   return g;
 }
 
-inline BankGeom iq2_geom(int hidden, int inter) {
+// Codebook formats of the IQ bank, by kernel format id (2, 3, 4) and GGML type.
+constexpr int kIq2xsUnitBytes = 2 * 1024 + 2 * 128 + 2 * 32;
+constexpr int kIq1mUnitBytes = 2 * 512 + 2 * 256 + 2 * 128;
+constexpr int kIq2xsTableWords = 512 + 128;  // grid magnitude codes [512], sign nibbles [128]
+constexpr int kIq1mTableWords = 2048;        // grid value codes [2048]
+constexpr int kGgmlIq2xxs = 16, kGgmlIq2xs = 17, kGgmlIq1m = 29;
+
+__host__ __device__ constexpr int iq_unit_bytes(int fmt) {
+  return fmt == 2 ? kIq2UnitBytes : fmt == 3 ? kIq2xsUnitBytes : kIq1mUnitBytes;
+}
+__host__ __device__ constexpr int iq_table_words(int fmt) {
+  return fmt == 2 ? kIq2TableWords : fmt == 3 ? kIq2xsTableWords : kIq1mTableWords;
+}
+__host__ __device__ constexpr int iq_block_bytes(int fmt) { return fmt == 2 ? 66 : fmt == 3 ? 74 : 56; }
+// GGML type id -> kernel format id, -1 for a type the IQ bank does not hold
+inline int iq_fmt_of_type(int ggml_type) {
+  return ggml_type == kGgmlIq2xxs ? 2 : ggml_type == kGgmlIq2xs ? 3 : ggml_type == kGgmlIq1m ? 4 : -1;
+}
+
+inline BankGeom iq_geom(int fmt13, int fmt2, int hidden, int inter) {
   BankGeom g;
-  g.w13_bytes = int64_t(inter / 16) * (hidden / kIq2KTile) * kIq2UnitBytes;
-  g.w2_bytes = int64_t(hidden / 32) * (inter / kIq2KTile) * kIq2UnitBytes;
+  g.w13_bytes = int64_t(inter / 16) * (hidden / kIq2KTile) * iq_unit_bytes(fmt13);
+  g.w2_bytes = int64_t(hidden / 32) * (inter / kIq2KTile) * iq_unit_bytes(fmt2);
   g.slot_bytes = g.w13_bytes + g.w2_bytes;
   return g;
 }

@@ -285,6 +285,44 @@ __global__ void iq2_prepack_kernel(const uint8_t* __restrict__ src_a, const uint
   }
 }
 
+// ----------------------------------------------------- IQ2_XS / IQ1_M prepack
+// One CTA of 32 threads per unit: thread (mt, h, r) copies the fields of its
+// row's block into the unit (layout.cuh: IQ2_XS qs / scales / d, IQ1_M
+// qs / qh / scales, each [mt][h][r] but IQ2_XS's d as [mt][r][h]).
+template <int FMT>
+__global__ void iq_prepack_kernel(const uint8_t* __restrict__ src_a, const uint8_t* __restrict__ src_b,
+                                  int rows_per_slot_a, int rows_per_slot_b, int k, int pair_second,
+                                  uint8_t* __restrict__ dst, int64_t dst_slot_stride) {
+  constexpr int BB = iq_block_bytes(FMT);
+  const int n_kb = k / kIq2KTile;
+  const int slot = blockIdx.y, unit = blockIdx.x;
+  const int tp = unit / n_kb, kb = unit % n_kb;
+  uint8_t* out = dst + int64_t(slot) * dst_slot_stride + int64_t(unit) * iq_unit_bytes(FMT);
+  const int t = threadIdx.x;
+  const int mt = t >> 4, h = (t >> 3) & 1, r = t & 7, rr = h * 8 + r;
+  const uint8_t* src;
+  int row;
+  if (pair_second) {  // W13: mt 0 = W1 rows 16tp.., mt 1 = W3 rows 16tp..
+    src = mt == 0 ? src_a + int64_t(slot) * rows_per_slot_a * n_kb * BB
+                  : src_b + int64_t(slot) * rows_per_slot_b * n_kb * BB;
+    row = 16 * tp + rr;
+  } else {  // W2: rows 32tp + 16mt ..
+    src = src_a + int64_t(slot) * rows_per_slot_a * n_kb * BB;
+    row = 32 * tp + 16 * mt + rr;
+  }
+  const uint8_t* blk = src + (int64_t(row) * n_kb + kb) * BB;
+  if (FMT == 3) {  // d [0, 2), qs [2, 66), scales [66, 74)
+    for (int i = 0; i < 64; ++i) out[mt * 1024 + rr * 64 + i] = blk[2 + i];
+    for (int i = 0; i < 8; ++i) out[2048 + mt * 128 + rr * 8 + i] = blk[66 + i];
+    out[2304 + mt * 32 + r * 4 + h * 2] = blk[0];
+    out[2304 + mt * 32 + r * 4 + h * 2 + 1] = blk[1];
+  } else {  // IQ1_M: qs [0, 32), qh [32, 48), scales [48, 56)
+    for (int i = 0; i < 32; ++i) out[mt * 512 + rr * 32 + i] = blk[i];
+    for (int i = 0; i < 16; ++i) out[1024 + mt * 256 + rr * 16 + i] = blk[32 + i];
+    for (int i = 0; i < 8; ++i) out[1536 + mt * 128 + rr * 8 + i] = blk[48 + i];
+  }
+}
+
 // ----------------------------------------------------------- host launchers
 static inline int grid_for(int64_t n, int block) {
   int64_t g = (n + block - 1) / block;
@@ -332,12 +370,24 @@ int launch_fp4_prepack(cudaStream_t s, int fmt, int hidden, int inter, int n,
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
-int launch_iq2_prepack(cudaStream_t s, int hidden, int inter, int n, const uint8_t* w1, const uint8_t* w3,
-                       const uint8_t* w2, uint8_t* bank_slot0, int64_t slot_stride, int64_t w13_bytes) {
+int launch_iq2_prepack(cudaStream_t s, int fmt13, int fmt2, int hidden, int inter, int n, const uint8_t* w1,
+                       const uint8_t* w3, const uint8_t* w2, uint8_t* bank_slot0, int64_t slot_stride,
+                       int64_t w13_bytes) {
   dim3 g13((inter / 16) * (hidden / kIq2KTile), n);
   dim3 g2((hidden / 32) * (inter / kIq2KTile), n);
-  iq2_prepack_kernel<<<g13, 64, 0, s>>>(w1, w3, inter, inter, hidden, 1, bank_slot0, slot_stride);
-  iq2_prepack_kernel<<<g2, 64, 0, s>>>(w2, nullptr, hidden, hidden, inter, 0, bank_slot0 + w13_bytes, slot_stride);
+  uint8_t* w2dst = bank_slot0 + w13_bytes;
+  switch (fmt13) {
+    case 2: iq2_prepack_kernel<<<g13, 64, 0, s>>>(w1, w3, inter, inter, hidden, 1, bank_slot0, slot_stride); break;
+    case 3: iq_prepack_kernel<3><<<g13, 32, 0, s>>>(w1, w3, inter, inter, hidden, 1, bank_slot0, slot_stride); break;
+    case 4: iq_prepack_kernel<4><<<g13, 32, 0, s>>>(w1, w3, inter, inter, hidden, 1, bank_slot0, slot_stride); break;
+    default: return -1;
+  }
+  switch (fmt2) {
+    case 2: iq2_prepack_kernel<<<g2, 64, 0, s>>>(w2, nullptr, hidden, hidden, inter, 0, w2dst, slot_stride); break;
+    case 3: iq_prepack_kernel<3><<<g2, 32, 0, s>>>(w2, nullptr, hidden, hidden, inter, 0, w2dst, slot_stride); break;
+    case 4: iq_prepack_kernel<4><<<g2, 32, 0, s>>>(w2, nullptr, hidden, hidden, inter, 0, w2dst, slot_stride); break;
+    default: return -1;
+  }
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

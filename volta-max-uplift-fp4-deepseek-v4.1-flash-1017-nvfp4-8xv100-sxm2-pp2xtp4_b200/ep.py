@@ -153,7 +153,7 @@ class ExpertParallelMoe:
     def __init__(self, *, hidden: int, inter: int, num_experts: int, top_k: int, tokens: int, tier,
                  fp4_format: str = "nvfp4", group=None, device: torch.device | None = None,
                  split_k: tuple[int, int] | None = None, exchange: str = "p2p", peer: PeerExchange | None = None,
-                 gemm: str = "skinny", owner=None):
+                 gemm: str = "skinny", owner=None, iq_types: tuple[int, int] = (16, 16)):
         if exchange not in ("p2p", "nccl"):
             raise ValueError("exchange is 'p2p' or 'nccl'")
         self.exchange = exchange
@@ -172,7 +172,7 @@ class ExpertParallelMoe:
         self.layer = B200NativeMoe(hidden=hidden, inter=inter, num_experts=num_experts, top_k=1,
                                    max_tokens=min(64, r_max), max_prefill_tokens=r_max, tier=self.tier,
                                    fp4_format=fp4_format, device=dev, rank=self.rank, world=self.world,
-                                   prefill_gemm=gemm, owner=owner_np)
+                                   prefill_gemm=gemm, owner=owner_np, iq_types=iq_types)
         if split_k is not None:
             self.layer.set_split_k(*split_k)
         self.owner_np = owner_np
@@ -212,6 +212,9 @@ class ExpertParallelMoe:
 
     def set_iq2_tables(self, *args, **kw):
         self.layer.set_iq2_tables(*args, **kw)
+
+    def set_iq_tables(self):
+        self.layer.set_iq_tables()
 
     def route(self, logits: torch.Tensor):
         return gate(logits, self.top_k)

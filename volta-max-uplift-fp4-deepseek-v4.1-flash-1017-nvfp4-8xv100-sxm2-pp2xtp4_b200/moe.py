@@ -17,6 +17,7 @@ from . import _lib
 from . import tiers as tiersmod
 
 SWIGLU_LIMIT = 10.0
+IQ_BLOCK_BYTES = {16: 66, 17: 74, 29: 56}  # GGML type -> bytes per 256 weights (IQ2_XXS, IQ2_XS, IQ1_M)
 
 
 def _stream() -> int:
@@ -58,12 +59,17 @@ class B200NativeMoe:
     def __init__(self, *, hidden: int, inter: int, num_experts: int, top_k: int, max_tokens: int,
                  tier, fp4_format: str = "nvfp4", max_prefill_tokens: int = 0,
                  swiglu_limit: float = SWIGLU_LIMIT, device: torch.device | int | None = None,
-                 rank: int = 0, world: int = 1, prefill_gemm: str = "tcgen05", owner=None):
+                 rank: int = 0, world: int = 1, prefill_gemm: str = "tcgen05", owner=None,
+                 iq_types: tuple[int, int] = (16, 16)):
         if fp4_format not in ("nvfp4", "mxfp4"):
             raise ValueError(f"fp4_format must be nvfp4 or mxfp4, got {fp4_format!r}")
         if prefill_gemm not in ("tcgen05", "skinny", "fp4"):
             raise ValueError(f"prefill_gemm must be tcgen05, skinny or fp4, got {prefill_gemm!r}")
         self.prefill_gemm = prefill_gemm
+        if len(iq_types) != 2 or any(t not in IQ_BLOCK_BYTES for t in iq_types):
+            raise ValueError(f"iq_types are GGML types (gate/up, down) of 16 IQ2_XXS, 17 IQ2_XS, 29 IQ1_M, "
+                             f"got {iq_types!r}")
+        self.iq_types = (int(iq_types[0]), int(iq_types[1]))
         dev = torch.device("cuda", torch.cuda.current_device() if device is None else
                            (device if isinstance(device, int) else device.index))
         if dev.index is None:
@@ -79,7 +85,8 @@ class B200NativeMoe:
         self.fp4_slot, self.iq2_slot = fp4_map, iq2_map
         cfg = _lib.Config(hidden, inter, num_experts, top_k, max_tokens, max_prefill_tokens,
                           _lib.NVFP4 if fp4_format == "nvfp4" else _lib.MXFP4, self.n_fp4, self.n_iq2,
-                          float(swiglu_limit), {"skinny": 0, "tcgen05": 1, "fp4": 2}[prefill_gemm])
+                          float(swiglu_limit), {"skinny": 0, "tcgen05": 1, "fp4": 2}[prefill_gemm],
+                          self.iq_types[0], self.iq_types[1])
         handle = ctypes.c_void_p()
         L = _lib.lib()
         _lib.check("b200moe_layer_create", L.b200moe_layer_create(ctypes.byref(cfg), dev.index, ctypes.byref(handle)))
@@ -108,16 +115,36 @@ class B200NativeMoe:
             w2_scales.data_ptr(), _lib.ptr(globals)))
 
     def load_iq2(self, slot_begin: int, w1, w3, w2) -> None:
-        """Load consecutive IQ2_XXS slots from ggml blocks (uint8 [n][rows][K/256][66])."""
+        """Load consecutive IQ slots from ggml blocks (uint8 [n][rows][K/256][B]):
+        W1 / W3 blocks of the gate/up type, W2 blocks of the down type
+        (``iq_types``; B = 66 IQ2_XXS, 74 IQ2_XS, 56 IQ1_M)."""
         n = w1.shape[0]
         H, I = self.hidden, self.inter
-        _want("w1", w1, torch.uint8, (n, I, H // 256, 66), self.device)
-        _want("w3", w3, torch.uint8, (n, I, H // 256, 66), self.device)
-        _want("w2", w2, torch.uint8, (n, H, I // 256, 66), self.device)
+        b13, b2 = IQ_BLOCK_BYTES[self.iq_types[0]], IQ_BLOCK_BYTES[self.iq_types[1]]
+        _want("w1", w1, torch.uint8, (n, I, H // 256, b13), self.device)
+        _want("w3", w3, torch.uint8, (n, I, H // 256, b13), self.device)
+        _want("w2", w2, torch.uint8, (n, H, I // 256, b2), self.device)
         if not self._tables_set:
-            self.set_iq2_tables()
+            self.set_iq_tables()
         _lib.check("b200moe_load_iq2", _lib.lib().b200moe_load_iq2(
             self._h, _stream(), slot_begin, n, w1.data_ptr(), w3.data_ptr(), w2.data_ptr()))
+
+    def set_iq_tables(self) -> None:
+        """The codebooks of the layer's IQ types (ggml data, loaded from gguf-py)."""
+        for t in sorted(set(self.iq_types)):
+            if t == 16:
+                self.set_iq2_tables()
+                continue
+            from gguf.quants import IQ1_M, IQ2_XS, IQ2_XXS
+
+            cls = IQ2_XS if t == 17 else IQ1_M
+            cls.init_grid()
+            grid = np.ascontiguousarray(np.asarray(cls.grid, np.float32).reshape(-1, 8).astype(np.int8))
+            ksigns = None if t == 29 else np.frombuffer(IQ2_XXS.ksigns, np.uint8).copy()
+            _lib.check("b200moe_set_iq_grid", _lib.lib().b200moe_set_iq_grid(
+                self._h, t, grid.ctypes.data_as(ctypes.c_void_p), grid.shape[0],
+                None if ksigns is None else ksigns.ctypes.data_as(ctypes.c_void_p)))
+        self._tables_set = True
 
     def set_iq2_tables(self, grid: np.ndarray | None = None, ksigns: np.ndarray | None = None) -> None:
         """The IQ2_XXS codebook (ggml data): loaded from gguf-py when not given."""
@@ -133,7 +160,7 @@ class B200NativeMoe:
             raise ValueError("IQ2_XXS tables are grid int8 [256, 8] and ksigns uint8 [128]")
         _lib.check("b200moe_set_iq2_tables", _lib.lib().b200moe_set_iq2_tables(
             self._h, grid.ctypes.data_as(ctypes.c_void_p), ksigns.ctypes.data_as(ctypes.c_void_p)))
-        self._tables_set = True
+        self._tables_set = set(self.iq_types) == {16}
 
     # -------------------------------------------------------------- forward
     def route(self, router_logits: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:

@@ -33,9 +33,9 @@ class Fp4Bank:
 
 @dataclass
 class Iq2Bank:
-    w1: torch.Tensor  # [n, I, H/256, 66]
+    w1: torch.Tensor  # [n, I, H/256, block bytes of the gate/up type]
     w3: torch.Tensor
-    w2: torch.Tensor  # [n, H, I/256, 66]
+    w2: torch.Tensor  # [n, H, I/256, block bytes of the down type]
 
     @property
     def n(self) -> int:
@@ -69,19 +69,33 @@ def make_fp4_bank(n: int, hidden: int, inter: int, fmt: str, seed: int, device, 
     return bank
 
 
-def _iq2_blocks(g, rows: int, k: int, n: int, std: float, device) -> torch.Tensor:
-    nb = k // 256
-    b = torch.randint(0, 256, (n, rows, nb, 66), generator=g, device=device, dtype=torch.int32).to(torch.uint8)
-    d = (std / 48.0) * (0.75 + 0.5 * torch.rand((n, rows, nb), generator=g, device=device))
-    b[..., :2] = d.to(torch.float16).view(torch.uint8).reshape(n, rows, nb, 2)
+IQ_BLOCK_BYTES = {16: 66, 17: 74, 29: 56}  # IQ2_XXS, IQ2_XS, IQ1_M
+
+
+def _iq2_blocks(g, rows: int, k: int, n: int, std: float, device, ggml_type: int = 16) -> torch.Tensor:
+    """Random valid ggml blocks: any index, sign and scale bits; d sized for ``std``."""
+    nb, bb = k // 256, IQ_BLOCK_BYTES[ggml_type]
+    b = torch.randint(0, 256, (n, rows, nb, bb), generator=g, device=device, dtype=torch.int32).to(torch.uint8)
+    if ggml_type == 29:  # IQ1_M: d is the fp16 made of the four scale words' top nibbles
+        d = ((std / 6.0) * (0.75 + 0.5 * torch.rand((n, rows, nb), generator=g, device=device)))
+        dbits = d.to(torch.float16).view(torch.int16).to(torch.int32) & 0xFFFF
+        w = b[..., 48:56].contiguous().view(torch.int16).to(torch.int32) & 0x0FFF
+        w = w | (((dbits[..., None] >> torch.tensor([0, 4, 8, 12], device=device)) & 15) << 12)
+        b[..., 48:56] = w.to(torch.int16).view(torch.uint8)
+    else:
+        d = (std / 48.0) * (0.75 + 0.5 * torch.rand((n, rows, nb), generator=g, device=device))
+        b[..., :2] = d.to(torch.float16).view(torch.uint8).reshape(n, rows, nb, 2)
     return b
 
 
-def make_iq2_bank(n: int, hidden: int, inter: int, seed: int, device, std: float = 0.02) -> Iq2Bank:
+def make_iq2_bank(n: int, hidden: int, inter: int, seed: int, device, std: float = 0.02,
+                  iq_types: tuple[int, int] = (16, 16)) -> Iq2Bank:
+    """Seeded random IQ experts: gate/up of GGML type iq_types[0], down of iq_types[1]."""
     g = torch.Generator(device=device)
     g.manual_seed(seed)
-    return Iq2Bank(_iq2_blocks(g, inter, hidden, n, std, device), _iq2_blocks(g, inter, hidden, n, std, device),
-                   _iq2_blocks(g, hidden, inter, n, std, device))
+    t13, t2 = iq_types
+    return Iq2Bank(_iq2_blocks(g, inter, hidden, n, std, device, t13), _iq2_blocks(g, inter, hidden, n, std, device, t13),
+                   _iq2_blocks(g, hidden, inter, n, std, device, t2))
 
 
 def load_bank(layer, bank, slot_begin: int = 0, step: int = 16) -> None:
