@@ -98,6 +98,8 @@ def parse():
     ap.add_argument("--split-k", type=int, default=0,
                     help="fix the GEMV split-K (0 = chosen per call; set only to give a small ncu capture "
                          "the split-K of the full-size run)")
+    ap.add_argument("--iq-types", default="16,16",
+                    help="c2: GGML types of the IQ experts' gate/up and down (16 IQ2_XXS, 17 IQ2_XS, 29 IQ1_M)")
     ap.add_argument("--gemm", choices=["fp4", "gemv"], default="fp4",
                     help="c1, c2, c4: the FP4 bank on the block-scaled FP4 tensor path (tcgen05.mma "
                          "kind::mxf4nvf4, default) or on the skinny GEMV; c3: the tcgen05 prefill GEMM reading "
@@ -502,13 +504,19 @@ def run_c2(job) -> None:
     args, dev, m = job.args, job.dev, job.args.m
     tier, tier_rank = tiers.zipf_tier(E, C2_HOT, seed=2)
     f4 = args.gemm == "fp4"
+    iq_types = tuple(int(t) for t in args.iq_types.split(","))
     layer = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, max_tokens=64, tier=tier, device=dev,
-                              prefill_gemm="fp4" if f4 else "tcgen05")
+                              prefill_gemm="fp4" if f4 else "tcgen05", iq_types=iq_types)
     fp4 = synth.make_fp4_bank(C2_HOT, H, I, "nvfp4", 2000, dev)
     synth.load_bank(layer, fp4)
-    iq2 = synth.make_iq2_bank(E - C2_HOT, H, I, 2001, dev)
-    layer.set_iq2_tables()
+    iq2 = synth.make_iq2_bank(E - C2_HOT, H, I, 2001, dev, iq_types=iq_types)
+    layer.set_iq_tables()
     synth.load_bank(layer, iq2)
+    iq_w13_bytes = 2 * I * H // 256 * moe.IQ_BLOCK_BYTES[iq_types[0]]
+    iq_w2_bytes = H * I // 256 * moe.IQ_BLOCK_BYTES[iq_types[1]]
+    iq_name = {16: "IQ2_XXS", 17: "IQ2_XS", 29: "IQ1_M"}
+    iq_desc = iq_name[iq_types[0]] if iq_types[0] == iq_types[1] else \
+        f"{iq_name[iq_types[0]]} gate/up + {iq_name[iq_types[1]]} down"
     layer.check_errors()
     alpha, share, logits = c2_inputs(layer, tier_rank, m, dev)
     g = torch.Generator(device=dev).manual_seed(2032)
@@ -518,7 +526,7 @@ def run_c2(job) -> None:
         profile_run(layer, lambda: layer.forward(x, *layer.route(logits)), args, {"alpha": alpha, "share": share})
         return
     use_graph = not args.eager
-    config = {"workload": f"configs[2] mixed-tier decode layer: hidden {H}, {C2_HOT} NVFP4 + {E - C2_HOT} IQ2_XXS "
+    config = {"workload": f"configs[2] mixed-tier decode layer: hidden {H}, {C2_HOT} NVFP4 + {E - C2_HOT} {iq_desc} "
                           f"experts (Zipf 1.1 tier map, seed 2), inter {I}, top-{K_TOP}, M={m}",
               "tokens_per_step": m, "alpha": alpha, "hot_route_share": share,
               "l2": "inputs larger than L2 (expert weights streamed per step)",
@@ -547,17 +555,17 @@ def run_c2(job) -> None:
         i13, i2, extra = (3, 4), (6, 7), dict({"inter_int8": 5}, **({"combine": 8} if sep else {}))
     pk = peaks()
     launches = {"w13_fp4": (per[i13[0]], hot_used.size * W13_BYTES),
-                "w13_iq2": (per[i13[1]], iq_used.size * IQ_W13_BYTES),
-                "w2_fp4": (per[i2[0]], hot_used.size * W2_BYTES), "w2_iq2": (per[i2[1]], iq_used.size * IQ_W2_BYTES)}
+                "w13_iq2": (per[i13[1]], iq_used.size * iq_w13_bytes),
+                "w2_fp4": (per[i2[0]], hot_used.size * W2_BYTES), "w2_iq2": (per[i2[1]], iq_used.size * iq_w2_bytes)}
     dom = max(launches, key=lambda k: launches[k][0])
     t_dom, b_dom = launches[dom]
     achieved = b_dom / (t_dom / 1e3) / 1e9
-    layer_bytes = hot_used.size * EXPERT_BYTES + iq_used.size * (IQ_W13_BYTES + IQ_W2_BYTES)
+    layer_bytes = hot_used.size * EXPERT_BYTES + iq_used.size * (iq_w13_bytes + iq_w2_bytes)
     e2e_ms, e2e_bytes = e2e_decode(job, layer, x, logits, layer.out[:m], args.steps, use_graph)
 
     cpu = None
     if job.rank == 0 and job.world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_c2(fp4, iq2, layer, ids_np, w.cpu().numpy(), x.float().cpu().numpy(), m)
+        cpu = cpu_c2(fp4, iq2, layer, ids_np, w.cpu().numpy(), x.float().cpu().numpy(), m, iq_types=iq_types)
     if job.rank == 0:
         line = line_base(job, args, "MoE-layer tokens/s (mixed-tier decode M=%d) & %% HBM roofline" % m,
                          job.world * m / (ms / 1e3), ms, config)
@@ -585,7 +593,7 @@ def run_c2(job) -> None:
     layer.close()
 
 
-def cpu_c2(fp4, iq2, layer, ids_np, w_np, x_np, m, sample_iq=6) -> dict:
+def cpu_c2(fp4, iq2, layer, ids_np, w_np, x_np, m, sample_iq=6, iq_types=(16, 16)) -> dict:
     """CPU layer of the mixed tier: NVFP4 experts through the C oracle, IQ2
     experts as the reference's CPU path does them (gguf dequantize, then fp32
     matmuls; numpy restatement), on a bounded sample of IQ2 experts scaled by
@@ -599,14 +607,13 @@ def cpu_c2(fp4, iq2, layer, ids_np, w_np, x_np, m, sample_iq=6) -> dict:
     hot = cpu_fp4_layer(lambda e: fp4_expert(fp4, int(layer.fp4_slot[e]), 0),
                         np.where(np.isin(ids_np, hot_ids), ids_np, -1), w_np, x_np, m, reps=1)
     hot_s = hot["ms_per_layer"] / 1e3
-    grid, ksigns = mo.iq2xxs_tables()
     pick = iq_ids[:sample_iq]
     t0 = time.perf_counter()
     for e in pick.tolist():
         s = int(layer.iq2_slot[e])
-        w13 = np.concatenate([mo.iq2xxs_decode(iq2.w1[s].cpu().numpy(), grid, ksigns),
-                              mo.iq2xxs_decode(iq2.w3[s].cpu().numpy(), grid, ksigns)])
-        w2 = mo.iq2xxs_decode(iq2.w2[s].cpu().numpy(), grid, ksigns)
+        w13 = np.concatenate([mo.iq_decode(iq_types[0], iq2.w1[s].cpu().numpy()),
+                              mo.iq_decode(iq_types[0], iq2.w3[s].cpu().numpy())])
+        w2 = mo.iq_decode(iq_types[1], iq2.w2[s].cpu().numpy())
         rows = np.nonzero(ids_np == e)[0]
         mo.expert_fp32(x_np[rows], w13, w2)
     dt = time.perf_counter() - t0
