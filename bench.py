@@ -98,6 +98,8 @@ def parse():
     ap.add_argument("--split-k", type=int, default=0,
                     help="fix the GEMV split-K (0 = chosen per call; set only to give a small ncu capture "
                          "the split-K of the full-size run)")
+    ap.add_argument("--placement", choices=["range", "balanced"], default="range",
+                    help="c4 over N > 1 GPUs: experts by id range, or tiers.balanced_owners on the expected routes")
     ap.add_argument("--iq-types", default="16,16",
                     help="c2: GGML types of the IQ experts' gate/up and down (16 IQ2_XXS, 17 IQ2_XS, 29 IQ1_M)")
     ap.add_argument("--gemm", choices=["fp4", "gemv"], default="fp4",
@@ -732,9 +734,18 @@ def run_c4(job) -> None:
     T = batch // world
     peer = ep.PeerExchange(H, T * K_TOP, None, dev) if world > 1 else None
     layers = []
-    alpha = None
+    # the routing bias of configs[2], chosen once on a whole-layer tier map
+    tier0, trank0 = tiers.zipf_tier(E, C2_HOT, seed=4000)
+    probe = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, max_tokens=min(T, 64),
+                              max_prefill_tokens=T, tier=tier0, device=dev)
+    alpha = c2_inputs(probe, trank0, T, dev)[0]
+    probe.close()
     for li in range(n_layers):
         tier, trank = tiers.zipf_tier(E, C2_HOT, seed=4000 + li)
+        owner = None
+        if world > 1 and args.placement == "balanced":  # expected routes ~ p(rank)^alpha of the Zipf(1.1) popularity
+            expect = np.floor(1e9 * (trank + 1.0) ** (-1.1 * alpha)).astype(np.int64)
+            owner = tiers.balanced_owners(tier, world, expect)
         if world == 1:
             lay = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, max_tokens=min(T, 64),
                                     max_prefill_tokens=T, tier=tier, device=dev,
@@ -742,7 +753,8 @@ def run_c4(job) -> None:
             local = lay
         else:
             lay = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, tokens=T, tier=tier,
-                                       device=dev, peer=peer, gemm="fp4" if args.gemm == "fp4" else "skinny")
+                                       device=dev, peer=peer, gemm="fp4" if args.gemm == "fp4" else "skinny",
+                                       owner=owner)
             local = lay.layer
         n_hot, n_iq = int((local.fp4_slot >= 0).sum()), int((local.iq2_slot >= 0).sum())
         if n_hot:
@@ -750,11 +762,6 @@ def run_c4(job) -> None:
         local.set_iq2_tables()
         if n_iq:
             synth.load_bank(local, synth.make_iq2_bank(n_iq, H, I, 9000 + 131 * li + rank, dev))
-        if alpha is None:  # the routing bias of configs[2], chosen once on a whole-layer tier map
-            probe = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, max_tokens=min(T, 64),
-                                      max_prefill_tokens=T, tier=tier, device=dev)
-            alpha = c2_inputs(probe, trank, T, dev)[0]
-            probe.close()
         logits = synth.zipf_logits(T, trank, alpha, 1.1, 4000 + li + 7919 * rank, dev)
         layers.append((lay, logits))
         torch.cuda.empty_cache()
@@ -857,6 +864,8 @@ def run_c4(job) -> None:
                               f"{T} per GPU, residual add between layers",
                   "layers": n_layers, "batch": batch, "tokens_per_gpu": T, "alpha": alpha,
                   "experts_per_gpu_per_layer": E // world,
+                  "placement": ("experts by id range" if args.placement == "range" else
+                                "tiers.balanced_owners on the expected routes") if world > 1 else "all experts",
                   "l2": "inputs larger than L2 (GBs of expert weights per step)",
                   "launch": "one CUDA graph replay per step" if not args.eager else "eager",
                   "parallelism": f"expert parallel x{world} (NVLink peer-memory exchange kernels)" if world > 1
