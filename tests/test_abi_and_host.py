@@ -119,3 +119,21 @@ def test_library_missing_fails_loudly(pkg, monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "LIB_PATH", tmp_path / "libb200moe.so")
     with pytest.raises(RuntimeError, match="only implementation"):
         _lib.lib()
+
+
+def test_library_sha256_pin(pkg, lib, monkeypatch):
+    """The loader refuses a library whose bytes differ from the pinned digest
+    (the reference's own rule for its kernel library)."""
+    import hashlib
+
+    from b200moe import _lib
+
+    assert _lib.PIN_PATH.read_text().strip() == hashlib.sha256(_lib.LIB_PATH.read_bytes()).hexdigest()
+    saved = _lib._LIB
+    try:
+        _lib._LIB = None
+        monkeypatch.setenv("B200MOE_LIB_SHA256", "0" * 64)
+        with pytest.raises(RuntimeError):
+            _lib.lib()
+    finally:
+        _lib._LIB = saved

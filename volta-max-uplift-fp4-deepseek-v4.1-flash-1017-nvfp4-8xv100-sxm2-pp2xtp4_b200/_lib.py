@@ -1,16 +1,23 @@
 """ctypes binding of ``libb200moe.so`` (the C ABI of ``include/b200moe.h``).
 
 The library is the only compute path: if it is missing or fails to load, every
-entry point raises; there is no CPU or PyTorch fallback.
+entry point raises; there is no CPU or PyTorch fallback.  As the reference pins
+its compiled kernel library by sha256 (engine/.../experts/nvfp4_8r_qpn_rb.py:37-41,
+70-81), the loader refuses a library whose bytes differ from the digest the build
+wrote beside it (``libb200moe.so.sha256``) or from ``B200MOE_LIB_SHA256`` when
+that is set.
 """
 
 from __future__ import annotations
 
 import ctypes
+import hashlib
+import os
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "libb200moe.so"
+PIN_PATH = HERE / "libb200moe.so.sha256"
 
 P = ctypes.c_void_p
 I32 = ctypes.c_int
@@ -103,6 +110,12 @@ def lib() -> ctypes.CDLL:
         if not LIB_PATH.exists():
             raise RuntimeError(f"{LIB_PATH} is missing: build it with __graft_entry__.build() "
                                "(the CUDA library is the only implementation)")
+        want = os.environ.get("B200MOE_LIB_SHA256") or (PIN_PATH.read_text().strip() if PIN_PATH.exists() else "")
+        if want:
+            got = hashlib.sha256(LIB_PATH.read_bytes()).hexdigest()
+            if got != want:
+                raise RuntimeError(f"{LIB_PATH} is sha256 {got}, the pin is {want}: rebuild with "
+                                   "__graft_entry__.build()")
         dll = ctypes.CDLL(str(LIB_PATH))
         for name, (args, res) in SIGNATURES.items():
             fn = getattr(dll, name)

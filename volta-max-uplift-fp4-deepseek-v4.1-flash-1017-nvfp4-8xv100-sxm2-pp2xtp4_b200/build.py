@@ -7,6 +7,7 @@ loads.  Objects are rebuilt only when a source or header is newer.
 
 from __future__ import annotations
 
+import hashlib
 import os
 import subprocess
 import sys
@@ -17,6 +18,7 @@ HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 OBJ = HERE / "_build"
 LIB = HERE / "libb200moe.so"
+PIN = HERE / "libb200moe.so.sha256"
 INCLUDE = HERE.parent / "include"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -53,6 +55,8 @@ def build(verbose: bool = False) -> Path:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    # the digest the loader checks the library against (a different file is refused)
+    PIN.write_text(hashlib.sha256(LIB.read_bytes()).hexdigest() + "\n")
     return LIB
 
 
