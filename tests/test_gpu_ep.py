@@ -161,3 +161,42 @@ def test_rows_forward_device_count(dev, pkg, gemm):
     assert torch.equal(half[:R // 2], full[:R // 2])
     assert torch.isnan(half[R // 2:].float()).all()  # nothing written past the count
     layer.close()
+
+
+def test_ep_bounded_wait_times_out_and_recovers(dev, pkg):
+    """A flag that nothing sets: a push without its return leaves the
+    combine's return flag behind the step's epoch.  The combine's wait ends
+    at its bound (2 s) with B200MOE_ERR_TIMEOUT, writes nothing, and the
+    exchange keeps working: the next full step gives the same bits as before."""
+    import time
+
+    from b200moe import _lib, ep, synth
+
+    H, I, E, K, T = 1024, 512, 32, 4, 16
+    tier = np.zeros(E, np.int8)
+    lay = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K, tokens=T, tier=tier, device=dev)
+    synth.load_bank(lay.layer, synth.make_fp4_bank(E, H, I, "nvfp4", 3, dev))
+    g = torch.Generator(device=dev).manual_seed(3)
+    x = torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
+    ids, w = lay.route(torch.randn((T, E), generator=g, device=dev))
+    y0 = lay.forward(x, ids, w).clone()
+    lay.check_errors()
+    L, pe = _lib.lib(), lay._peer
+    st = torch.cuda.current_stream(dev).cuda_stream
+    _lib.check("push", L.b200moe_ep_push(pe.handle, st, x.data_ptr(), _lib.BF16, ids.data_ptr(), T, K, E,
+                                         lay.owner.data_ptr()))
+    out = torch.full((T, H), 7.0, dtype=torch.float32, device=dev)
+    torch.cuda.synchronize(dev)
+    t0 = time.monotonic()
+    _lib.check("combine", L.b200moe_ep_combine_p2p(pe.handle, st, ids.data_ptr(), w.data_ptr(), T, K, E,
+                                                   lay.owner.data_ptr(), None, out.data_ptr()))
+    status = pe.check()
+    waited = time.monotonic() - t0
+    assert _lib.STATUS[status] == "B200MOE_ERR_TIMEOUT", status
+    assert 1.5 < waited < 60, waited
+    assert torch.all(out == 7.0)  # nothing written after the wait gave up
+    assert pe.check() == 0  # the error word was cleared
+    y1 = lay.forward(x, ids, w).clone()
+    lay.check_errors()
+    assert torch.equal(y0, y1)
+    lay.close()
