@@ -162,7 +162,7 @@ int b200moe_forward_prefill(b200moe_layer* layer, void* stream, const void* x, i
  * free HBM to its KV cache after start-up and allows no cudaMalloc later.
  * Limits: M <= 16, top_k <= 8, hidden <= 4096, inter <= 2048, and at most 512
  * experts held by the layer; larger sizes return B200MOE_ERR_RANGE.  The array
- * (about 1.7 MB) is held on every GPU that loads the library until exit.  The
+ * (about 2.4 MB) is held on every GPU that loads the library until exit.  The
  * first call on a device looks up the array's device address; make that first
  * call before any stream capture.  Every call shares the array and zeroes its
  * combine counters on `stream` first; calls that overlap on the GPU race. */

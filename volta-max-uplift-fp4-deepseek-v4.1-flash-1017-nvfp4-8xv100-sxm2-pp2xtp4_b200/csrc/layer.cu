@@ -859,7 +859,7 @@ constexpr size_t kOffInterq =
 constexpr size_t kStaticScratchBytes =
     kOffInterq + align256(size_t(kStaticRoutes) * (kStaticMaxInter / kIq2KTile) * kIq2XBlockBytes);
 
-// About 2 MB per GPU (see the limits above).
+// 2,409,728 bytes per GPU at the limits above.
 static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
 
 // Device address of g_static_scratch per device, looked up on the first call
