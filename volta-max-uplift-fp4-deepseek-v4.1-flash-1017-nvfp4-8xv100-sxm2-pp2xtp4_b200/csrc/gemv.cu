@@ -141,6 +141,26 @@ __device__ __forceinline__ void fp4_step(uint32_t wb, uint32_t xb, int ntiles, i
 // (t1 + t2 / 254) * d / 8 * sx is applied once in FP32.
 // Thread q owns elements 8q..8q+7 of each sub-block (grid entry q), which are
 // the MMA's K positions 4q..4q+3 and 16+4q..16+4q+3, for weights and activations alike.
+// Chunks of at most 4 routes (most decode chunks of the IQ bank) fill only
+// half of an n8 MMA tile, so both activation planes share one MMA there
+// ("packed"): column n holds route n & 3 of plane n >> 2.  Lanes q = 0, 1 then
+// hold plane 1 of routes 2q, 2q + 1 and lanes q + 2 plane 2 of the same
+// routes; iq_unpack_planes moves the plane-2 sums to the usual [plane] slots.
+// The s32 sums are the same numbers, so both forms give the same bits.
+__device__ __forceinline__ void iq_unpack_planes(int (&t)[2][2][2][4], int lane) {
+  const bool low = (lane & 3) < 2;
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int v = t[0][mt][0][i];
+      const int o = __shfl_xor_sync(0xffffffffu, v, 2);
+      t[0][mt][0][i] = low ? v : 0;
+      t[1][mt][0][i] = low ? o : 0;
+    }
+}
+
+template <bool PACK>
 __device__ __forceinline__ void iq2_step(uint32_t wb, uint32_t xb, uint32_t tbl, int ntiles, int lane,
                                          float (&acc)[2][2][2][4]) {
   constexpr int XRS = Fmt<2>::XRS;
@@ -167,12 +187,16 @@ __device__ __forceinline__ void iq2_step(uint32_t wb, uint32_t xb, uint32_t tbl,
     for (int i2 = 0; i2 < 2; ++i2) {
       const int ib = 2 * ibp + i2;
       uint2 xv[2][2];  // [plane][nt]
+      if (PACK) {
+        xv[0][0] = lds64(xb + (r & 3) * XRS + (r >> 2) * 256 + ib * 32 + q * 8);
+      } else {
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-        if (nt < ntiles) {
-          xv[0][nt] = lds64(xb + (nt * 8 + r) * XRS + ib * 32 + q * 8);
-          xv[1][nt] = lds64(xb + (nt * 8 + r) * XRS + 256 + ib * 32 + q * 8);
-        }
+        for (int nt = 0; nt < 2; ++nt)
+          if (nt < ntiles) {
+            xv[0][nt] = lds64(xb + (nt * 8 + r) * XRS + ib * 32 + q * 8);
+            xv[1][nt] = lds64(xb + (nt * 8 + r) * XRS + 256 + ib * 32 + q * 8);
+          }
+      }
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt) {
         uint32_t sel[2];
@@ -188,6 +212,15 @@ __device__ __forceinline__ void iq2_step(uint32_t wb, uint32_t xb, uint32_t tbl,
         }
         const uint32_t a[4] = {__byte_perm(kPos, kNeg, sel[0]), __byte_perm(kPos, kNeg, sel[1]),
                                __byte_perm(kPos, kNeg, sel[0] >> 16), __byte_perm(kPos, kNeg, sel[1] >> 16)};
+        if (PACK) {
+          int d[4] = {0, 0, 0, 0};
+          mma_16832_s8(d, a, xv[0][0].x, xv[0][0].y);
+          t[0][mt][0][0] += d[0] * c[0];
+          t[0][mt][0][1] += d[1] * c[0];
+          t[0][mt][0][2] += d[2] * c[1];
+          t[0][mt][0][3] += d[3] * c[1];
+          continue;
+        }
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) {
           if (nt < ntiles) {
@@ -205,6 +238,7 @@ __device__ __forceinline__ void iq2_step(uint32_t wb, uint32_t xb, uint32_t tbl,
       }
     }
   }
+  if (PACK) iq_unpack_planes(t, lane);
   constexpr float kPlane2 = 1.f / 254.f;
 #pragma unroll
   for (int mt = 0; mt < 2; ++mt) {
@@ -252,10 +286,17 @@ __device__ __forceinline__ void iq_finish(const int (&t)[2][2][2][4], const floa
   }
 }
 
-// the activation fragments of one sub-block: [nt][plane][group]
+// the activation fragments of one sub-block: [nt][plane][group] (packed: [0][0][group])
+template <bool PACK>
 __device__ __forceinline__ void iq_load_x(uint32_t xb, int ib, int ntiles, int lane, uint32_t (&xv)[2][2][2]) {
   constexpr int XRS = Fmt<2>::XRS;
   const int r = lane >> 2, q = lane & 3;
+  if (PACK) {
+#pragma unroll
+    for (int grp = 0; grp < 2; ++grp)
+      xv[0][0][grp] = lds32(xb + (r & 3) * XRS + (r >> 2) * 256 + ib * 32 + grp * 16 + 4 * q);
+    return;
+  }
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
@@ -266,9 +307,22 @@ __device__ __forceinline__ void iq_load_x(uint32_t xb, int ib, int ntiles, int l
 }
 
 // the two MMAs of one sub-block and tile, one per 16-weight group, for both planes
+template <bool PACK>
 __device__ __forceinline__ void iq_group_mmas(const uint32_t (&a)[2][2], const int (&c)[2][2],
                                               const uint32_t (&xv)[2][2][2], int ntiles, int (&t)[2][2][2][4],
                                               int mt) {
+  if (PACK) {
+#pragma unroll
+    for (int grp = 0; grp < 2; ++grp) {
+      int d[4] = {0, 0, 0, 0};
+      mma_16816_s8(d, a[grp][0], a[grp][1], xv[0][0][grp]);
+      t[0][mt][0][0] += d[0] * c[grp][0];
+      t[0][mt][0][1] += d[1] * c[grp][0];
+      t[0][mt][0][2] += d[2] * c[grp][1];
+      t[0][mt][0][3] += d[3] * c[grp][1];
+    }
+    return;
+  }
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt) {
     if (nt >= ntiles) continue;
@@ -289,6 +343,7 @@ __device__ __forceinline__ void iq_group_mmas(const uint32_t (&a)[2][2], const i
 // IQ2_XS (ggml's dequantize: d * (0.5 + s) * 0.25 * grid * sign, s the 4-bit
 // scale of each 16 weights): a weight is g * sign (g in {8, 25, 43}) from the
 // 9-bit grid index's magnitude codes and the 7-bit sign index's nibbles.
+template <bool PACK>
 __device__ __forceinline__ void iq2xs_step(uint32_t wb, uint32_t xb, uint32_t tbl, int ntiles, int lane,
                                            float (&acc)[2][2][2][4]) {
   constexpr uint32_t kPos = 0x002B1908u, kNeg = 0x00D5E7F8u;  // bytes 8, 25, 43, 0 and -8, -25, -43, 0
@@ -314,7 +369,7 @@ __device__ __forceinline__ void iq2xs_step(uint32_t wb, uint32_t xb, uint32_t tb
     for (int i2 = 0; i2 < 2; ++i2) {
       const int ib = 2 * ibp + i2;
       uint32_t xv[2][2][2];
-      iq_load_x(xb, ib, ntiles, lane, xv);
+      iq_load_x<PACK>(xb, ib, ntiles, lane, xv);
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt) {
         uint32_t a[2][2];
@@ -333,7 +388,7 @@ __device__ __forceinline__ void iq2xs_step(uint32_t wb, uint32_t xb, uint32_t tb
           c[0][h] = int(2 * (sb & 15u) + 1);
           c[1][h] = int(2 * (sb >> 4) + 1);
         }
-        iq_group_mmas(a, c, xv, ntiles, t, mt);
+        iq_group_mmas<PACK>(a, c, xv, ntiles, t, mt);
       }
     }
   }
@@ -345,6 +400,7 @@ __device__ __forceinline__ void iq2xs_step(uint32_t wb, uint32_t xb, uint32_t tb
     dl[mt][0] = __low2float(d2) * 0.125f;
     dl[mt][1] = __high2float(d2) * 0.125f;
   }
+  if (PACK) iq_unpack_planes(t, lane);
   iq_finish(t, dl, xb, ntiles, lane, acc);
 }
 
@@ -352,6 +408,7 @@ __device__ __forceinline__ void iq2xs_step(uint32_t wb, uint32_t xb, uint32_t tb
 // delta = +-1/8 per 8 weights, s the 3-bit scale of each 16 weights, d the
 // fp16 in the scales' top nibbles): a weight is 8 * grid +- 1 in int8, times
 // (2s + 1) on the s32 partial, times d / 8 in FP32.
+template <bool PACK>
 __device__ __forceinline__ void iq1m_step(uint32_t wb, uint32_t xb, uint32_t tbl, int ntiles, int lane,
                                           float (&acc)[2][2][2][4]) {
   constexpr uint32_t kPos = 0x000901F9u, kNeg = 0x0007FFF7u;  // bytes -7, 1, 9 (delta +) and -9, -1, 7 (delta -)
@@ -386,7 +443,7 @@ __device__ __forceinline__ void iq1m_step(uint32_t wb, uint32_t xb, uint32_t tbl
     for (int i2 = 0; i2 < 2; ++i2) {
       const int ib = 2 * ibp + i2;
       uint32_t xv[2][2][2];
-      iq_load_x(xb, ib, ntiles, lane, xv);
+      iq_load_x<PACK>(xb, ib, ntiles, lane, xv);
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt) {
         uint32_t a[2][2];
@@ -406,10 +463,11 @@ __device__ __forceinline__ void iq1m_step(uint32_t wb, uint32_t xb, uint32_t tbl
             c[grp][h] = int(2 * ((sword >> (3 * (2 * i2 + grp))) & 7u) + 1);
           }
         }
-        iq_group_mmas(a, c, xv, ntiles, t, mt);
+        iq_group_mmas<PACK>(a, c, xv, ntiles, t, mt);
       }
     }
   }
+  if (PACK) iq_unpack_planes(t, lane);
   iq_finish(t, dl, xb, ntiles, lane, acc);
 }
 
@@ -555,10 +613,18 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, uint8_t* smem) {
         const uint32_t sb = smem_u32(stages + size_t(s) * F::STAGE);
         const uint32_t wb = sb + warp * F::U;
         const uint32_t xb = sb + kConsumerWarps * F::U + ks * RC * F::XRS;
-        if constexpr (FMT == 2) iq2_step(wb, xb, tbl, ntiles, lane, acc2);
-        else if constexpr (FMT == 3) iq2xs_step(wb, xb, tbl, ntiles, lane, acc2);
-        else if constexpr (FMT == 4) iq1m_step(wb, xb, tbl, ntiles, lane, acc2);
-        else fp4_step<FMT>(wb, xb, ntiles, lane, acc2);
+        if constexpr (FMT == 2) {
+          if (ch.count <= 4) iq2_step<true>(wb, xb, tbl, ntiles, lane, acc2);
+          else iq2_step<false>(wb, xb, tbl, ntiles, lane, acc2);
+        } else if constexpr (FMT == 3) {
+          if (ch.count <= 4) iq2xs_step<true>(wb, xb, tbl, ntiles, lane, acc2);
+          else iq2xs_step<false>(wb, xb, tbl, ntiles, lane, acc2);
+        } else if constexpr (FMT == 4) {
+          if (ch.count <= 4) iq1m_step<true>(wb, xb, tbl, ntiles, lane, acc2);
+          else iq1m_step<false>(wb, xb, tbl, ntiles, lane, acc2);
+        } else {
+          fp4_step<FMT>(wb, xb, ntiles, lane, acc2);
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
       }
