@@ -205,7 +205,7 @@ __device__ __forceinline__ void iq2_step(uint32_t wb, uint32_t xb, uint32_t tbl,
         for (int h = 0; h < 2; ++h) {
           const uint32_t a0 = i2 == 0 ? qw[mt][h].x : qw[mt][h].z;
           const uint32_t a1 = i2 == 0 ? qw[mt][h].y : qw[mt][h].w;
-          const uint32_t gi = (a0 >> (8 * q)) & 255u;
+          const uint32_t gi = __byte_perm(a0, 0u, 0x4440u | uint32_t(q));  // byte q of a0
           const uint32_t si = (a1 >> (7 * q)) & 127u;
           sel[h] = lds32(tbl + gi * 4) | lds32(tsign + si * 4);
           c[h] = int(((a1 >> 27) & 0x1Eu) | 1u);
@@ -348,11 +348,12 @@ __device__ __forceinline__ void iq2xs_step(uint32_t wb, uint32_t xb, uint32_t tb
                                            float (&acc)[2][2][2][4]) {
   constexpr uint32_t kPos = 0x002B1908u, kNeg = 0x00D5E7F8u;  // bytes 8, 25, 43, 0 and -8, -25, -43, 0
   const int r = lane >> 2, q = lane & 3;
-  const int e_sh = 16 * (q >> 1), h_sh = 16 * (q & 1);
+  const uint32_t usel = (q >> 1) ? 0x4432u : 0x4410u;  // the u16 entry q >> 1 of a word, zero-extended
   int t[2][2][2][4];
 #pragma unroll
   for (int i = 0; i < 32; ++i) (&t[0][0][0][0])[i] = 0;
-  const uint32_t tsign = tbl + 512 * 4;
+  const uint32_t tgrid = tbl + (q & 1) * (kIq2xsUpper * 4);  // this lane's half of every entry
+  const uint32_t tsign = tgrid + 512 * 4;
   uint2 sc[2][2];  // [mt][h]: the row's 8 scale bytes
 #pragma unroll
   for (int mt = 0; mt < 2; ++mt)
@@ -380,9 +381,9 @@ __device__ __forceinline__ void iq2xs_step(uint32_t wb, uint32_t xb, uint32_t tb
           const uint32_t w23 = i2 == 0 ? qw[mt][h].y : qw[mt][h].w;  // entries 2, 3
 #pragma unroll
           for (int grp = 0; grp < 2; ++grp) {
-            const uint32_t u = ((grp ? w23 : w01) >> e_sh) & 0xFFFFu;
-            const uint32_t sel = lds32(tbl + (u & 511u) * 4) | lds32(tsign + (u >> 9) * 4);
-            a[grp][h] = __byte_perm(kPos, kNeg, sel >> h_sh);
+            const uint32_t u = __byte_perm(grp ? w23 : w01, 0u, usel);
+            const uint32_t sel = lds32(tgrid + (u & 511u) * 4) | lds32(tsign + (u >> 9) * 4);
+            a[grp][h] = __byte_perm(kPos, kNeg, sel);
           }
           const uint32_t sb = ((ib < 4 ? sc[mt][h].x : sc[mt][h].y) >> (8 * (ib & 3))) & 255u;
           c[0][h] = int(2 * (sb & 15u) + 1);
@@ -413,7 +414,9 @@ __device__ __forceinline__ void iq1m_step(uint32_t wb, uint32_t xb, uint32_t tbl
                                           float (&acc)[2][2][2][4]) {
   constexpr uint32_t kPos = 0x000901F9u, kNeg = 0x0007FFF7u;  // bytes -7, 1, 9 (delta +) and -9, -1, 7 (delta -)
   const int r = lane >> 2, q = lane & 3;
-  const int e0 = q >> 1, h_sh = 16 * (q & 1);
+  const int e0 = q >> 1;
+  const uint32_t lsel[2] = {0x4440u | uint32_t(e0), 0x4440u | uint32_t(2 + e0)};  // qs byte of entry 2 grp + e0
+  const uint32_t tgrid = tbl + (q & 1) * (kIq1mUpper * 4);  // this lane's half of every entry
   int t[2][2][2][4];
 #pragma unroll
   for (int i = 0; i < 32; ++i) (&t[0][0][0][0])[i] = 0;
@@ -455,11 +458,10 @@ __device__ __forceinline__ void iq1m_step(uint32_t wb, uint32_t xb, uint32_t tbl
                                          : (ibp == 2 ? sc[mt][h].y & 0xFFFFu : sc[mt][h].y >> 16);
 #pragma unroll
           for (int grp = 0; grp < 2; ++grp) {
-            const int l = 2 * grp + e0;  // entry of the sub-block
             const uint32_t nib = (qh[mt][h] >> (8 * (2 * i2 + grp) + 4 * e0)) & 15u;
-            const uint32_t idx = ((qsw >> (8 * l)) & 255u) | ((nib & 7u) << 8);
-            const uint32_t sel = lds32(tbl + idx * 4) | ((nib & 8u) ? 0x44444444u : 0u);
-            a[grp][h] = __byte_perm(kPos, kNeg, sel >> h_sh);
+            const uint32_t idx = __byte_perm(qsw, 0u, lsel[grp]) | ((nib & 7u) << 8);
+            const uint32_t sel = lds32(tgrid + idx * 4) | ((nib & 8u) ? 0x44444444u : 0u);
+            a[grp][h] = __byte_perm(kPos, kNeg, sel);
             c[grp][h] = int(2 * ((sword >> (3 * (2 * i2 + grp))) & 7u) + 1);
           }
         }

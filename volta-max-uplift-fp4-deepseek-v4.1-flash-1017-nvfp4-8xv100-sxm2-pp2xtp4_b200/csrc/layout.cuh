@@ -73,8 +73,18 @@ inline BankGeom fp4_geom(int fmt, int hidden, int inter) {
 // Codebook formats of the IQ bank, by kernel format id (2, 3, 4) and GGML type.
 constexpr int kIq2xsUnitBytes = 2 * 1024 + 2 * 128 + 2 * 32;
 constexpr int kIq1mUnitBytes = 2 * 512 + 2 * 256 + 2 * 128;
-constexpr int kIq2xsTableWords = 512 + 128;  // grid magnitude codes [512], sign nibbles [128]
-constexpr int kIq1mTableWords = 2048;        // grid value codes [2048]
+// IQ2_XS / IQ1_M tables come twice: as built, then each word shifted right by
+// 16 (the selector nibbles of an entry's elements 4..7), so a lane that owns
+// the upper half of its entries reads its byte-permute selectors directly.
+// The copy starts 16 words (half the banks) past the first: the two lanes that
+// read the same entry then hit different banks instead of one bank twice.
+constexpr int kIq2xsHalfWords = 512 + 128;   // grid magnitude codes [512], sign nibbles [128]
+constexpr int kIq1mHalfWords = 2048;         // grid value codes [2048]
+constexpr int kIqUpperPad = 16;
+constexpr int kIq2xsUpper = kIq2xsHalfWords + kIqUpperPad;  // word offset of the shifted copy
+constexpr int kIq1mUpper = kIq1mHalfWords + kIqUpperPad;
+constexpr int kIq2xsTableWords = kIq2xsUpper + kIq2xsHalfWords;
+constexpr int kIq1mTableWords = kIq1mUpper + kIq1mHalfWords;
 constexpr int kGgmlIq2xxs = 16, kGgmlIq2xs = 17, kGgmlIq1m = 29;
 
 __host__ __device__ constexpr int iq_unit_bytes(int fmt) {
