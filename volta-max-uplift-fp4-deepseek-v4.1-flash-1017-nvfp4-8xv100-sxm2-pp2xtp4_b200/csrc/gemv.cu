@@ -352,8 +352,9 @@ __device__ __forceinline__ void iq2xs_step(uint32_t wb, uint32_t xb, uint32_t tb
   int t[2][2][2][4];
 #pragma unroll
   for (int i = 0; i < 32; ++i) (&t[0][0][0][0])[i] = 0;
-  const uint32_t tgrid = tbl + (q & 1) * (kIq2xsUpper * 4);  // this lane's half of every entry
-  const uint32_t tsign = tgrid + 512 * 4;
+  const uint32_t tgrid = tbl + (q & 1) * (kIq2xsUpper * 4);  // this lane's half of every grid entry
+  const uint32_t tsign = tbl + 512 * 4;  // sign nibbles from the unshifted copy: both lanes of an entry share a word
+  const int h_sh = 16 * (q & 1);
   uint2 sc[2][2];  // [mt][h]: the row's 8 scale bytes
 #pragma unroll
   for (int mt = 0; mt < 2; ++mt)
@@ -382,7 +383,7 @@ __device__ __forceinline__ void iq2xs_step(uint32_t wb, uint32_t xb, uint32_t tb
 #pragma unroll
           for (int grp = 0; grp < 2; ++grp) {
             const uint32_t u = __byte_perm(grp ? w23 : w01, 0u, usel);
-            const uint32_t sel = lds32(tgrid + (u & 511u) * 4) | lds32(tsign + (u >> 9) * 4);
+            const uint32_t sel = lds32(tgrid + (u & 511u) * 4) | (lds32(tsign + (u >> 9) * 4) >> h_sh);
             a[grp][h] = __byte_perm(kPos, kNeg, sel);
           }
           const uint32_t sb = ((ib < 4 ? sc[mt][h].x : sc[mt][h].y) >> (8 * (ib & 3))) & 255u;
