@@ -160,12 +160,14 @@ int b200moe_forward_prefill(b200moe_layer* layer, void* stream, const void* x, i
  * instead of the layer's workspace.  It is for callers that cannot allocate
  * device memory when they run a decode step, e.g. an engine that gives all
  * free HBM to its KV cache after start-up and allows no cudaMalloc later.
- * Limits: M <= 16, top_k <= 8, hidden <= 4096, inter <= 2048, and at most 512
- * experts held by the layer; larger sizes return B200MOE_ERR_RANGE.  The array
- * (about 2.4 MB) is held on every GPU that loads the library until exit.  The
- * first call on a device looks up the array's device address; make that first
- * call before any stream capture.  Every call shares the array and zeroes its
- * combine counters on `stream` first; calls that overlap on the GPU race. */
+ * Limits: M <= 16 (and, as for b200moe_forward, M <= the layer's max_tokens,
+ * else B200MOE_ERR_INVALID_ARG), top_k <= 8, hidden <= 4096, inter <= 2048,
+ * and at most 512 experts held by the layer; larger sizes return
+ * B200MOE_ERR_RANGE.  The array (about 2.4 MB) is held on every GPU that loads
+ * the library until exit.  b200moe_layer_create looks up the array's device
+ * address on the layer's device, so this call itself does no set-up.  Every
+ * call shares the array and zeroes its combine counters on `stream` first;
+ * calls that overlap on the GPU race. */
 int b200moe_forward_static(b200moe_layer* layer, void* stream, const void* x, int x_dtype,
                            const int32_t* topk_ids, const float* topk_weights, float* out, int M);
 

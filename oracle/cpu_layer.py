@@ -19,9 +19,29 @@ REF_LIB = HERE / "_ref" / "libcpumoe_ref.so"
 P = ctypes.c_void_p
 
 
+def reference_root() -> Path | None:
+    """The reference project's root: REFERENCE_ROOT, else the ``reference_path``
+    that BASELINE.json at the repository root names; None when neither is a
+    directory here (the GPU boxes use the prebuilt ``_ref`` library)."""
+    root = os.environ.get("REFERENCE_ROOT")
+    if not root:
+        base = HERE.parent / "BASELINE.json"
+        if base.exists():
+            import json
+
+            root = json.loads(base.read_text()).get("reference_path")
+    return Path(root) if root and Path(root).is_dir() else None
+
+
 def build(ref: bool = False) -> None:
     """Compile the C oracle (and, with ``ref``, the reference's CPU kernel)."""
-    subprocess.run(["make", "-s", "-C", str(HERE)] + (["ref"] if ref else []), check=True)
+    env = dict(os.environ)
+    if ref:
+        root = reference_root()
+        if root is None:
+            raise FileNotFoundError("the reference tree is not present: set REFERENCE_ROOT")
+        env["REFERENCE_ROOT"] = str(root)
+    subprocess.run(["make", "-s", "-C", str(HERE)] + (["ref"] if ref else []), check=True, env=env)
 
 
 def _ptr(a: np.ndarray):

@@ -1,7 +1,7 @@
 """Generate the golden fixtures in this directory from the reference's own code.
 
-Run here, where the reference project is mounted read-only (default
-``/root/reference``; override with REFERENCE_ROOT).  It imports the reference's
+Run where the reference project is mounted read-only, with REFERENCE_ROOT
+set to its root directory.  It imports the reference's
 Python modules directly (no copy of their source is made) and writes small
 ``.npz`` fixtures that the CPU and GPU tests read.  Nothing at test time reads
 the reference tree.
@@ -44,7 +44,14 @@ HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE))
 import golden_inputs as gi  # noqa: E402
 
-REF = Path(os.environ.get("REFERENCE_ROOT", "/root/reference"))
+def _reference_root() -> Path:
+    root = os.environ.get("REFERENCE_ROOT")
+    if not root:
+        raise SystemExit("set REFERENCE_ROOT to the reference project's root directory")
+    return Path(root)
+
+
+REF = _reference_root()
 EXP = REF / "engine/src/vllm/model_executor/layers/fused_moe/experts"
 HB = REF / "harness/benchmarks"
 

@@ -1,8 +1,8 @@
 """Golden fixtures for the host-side tier planner, tier-map reader and pack
 reader, generated from the reference's own code.
 
-Run here, where the reference project is mounted read-only (default
-``/root/reference``; override with REFERENCE_ROOT).  It imports the reference's
+Run where the reference project is mounted read-only, with REFERENCE_ROOT
+set to its root directory.  It imports the reference's
 modules (as ``make_golden.py`` does; nothing is copied) and writes
 ``tiers.npz`` and ``packs.npz`` beside this file.  Nothing at test time reads
 the reference tree.

@@ -137,3 +137,42 @@ def test_library_sha256_pin(pkg, lib, monkeypatch):
             _lib.lib()
     finally:
         _lib._LIB = saved
+
+
+def test_plugin_refusals_follow_the_reference_hook(pkg):
+    """``B200NativeMoEMethod`` refuses what the reference hook refuses
+    (engine/patches/gguf_moe.patch, ``apply``: anything but output-weighted
+    SiLU; ``_apply_nvfp4_8r``: non-fp32 router weights), and accepts an
+    ``expert_map`` only when its local experts are exactly the layer's."""
+    import types
+
+    import torch
+    from b200moe import moe
+
+    fake = types.SimpleNamespace(fp4_slot=np.array([0, 1, -1, -1], np.int32),
+                                 iq2_slot=np.array([-1, -1, 0, -1], np.int32))
+    method = moe.B200NativeMoEMethod(fake)
+    x = torch.zeros((2, 8), dtype=torch.float16)
+    w = torch.zeros((2, 2), dtype=torch.float32)
+    layer = types.SimpleNamespace(activation="silu", apply_router_weight_on_input=False, expert_map=None)
+    method._checks(layer, x, w)
+    for act in ("swigluoai", "gelu", "silu_no_mul"):
+        with pytest.raises(ValueError, match="SiLU"):
+            method._checks(types.SimpleNamespace(activation=act, expert_map=None), x, w)
+    try:
+        from vllm.model_executor.layers.fused_moe.activation import MoEActivation
+    except Exception:
+        MoEActivation = None
+    if MoEActivation is not None:
+        method._checks(types.SimpleNamespace(activation=MoEActivation.SILU, expert_map=None), x, w)
+        with pytest.raises(ValueError):
+            method._checks(types.SimpleNamespace(activation=MoEActivation.SWIGLUOAI, expert_map=None), x, w)
+    with pytest.raises(ValueError):
+        method._checks(types.SimpleNamespace(activation="silu", apply_router_weight_on_input=True), x, w)
+    with pytest.raises(RuntimeError, match="fp32"):
+        method._checks(layer, x, w.half())
+    ok = types.SimpleNamespace(activation="silu", expert_map=torch.tensor([0, 1, 2, -1], dtype=torch.int32))
+    method._checks(ok, x, w)
+    bad = types.SimpleNamespace(activation="silu", expert_map=torch.tensor([0, 1, -1, 2], dtype=torch.int32))
+    with pytest.raises(RuntimeError, match="expert_map"):
+        method._checks(bad, x, w)

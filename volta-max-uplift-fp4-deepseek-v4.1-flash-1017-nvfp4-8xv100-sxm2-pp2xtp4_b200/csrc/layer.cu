@@ -448,6 +448,14 @@ const char* b200moe_status_name(int status) {
 
 const char* b200moe_version(void) { return "b200moe 0.1 sm_100a"; }
 
+}  // extern "C"
+
+// Device address of the allocation-free decode's scratch array (defined with
+// b200moe_forward_static below); layer creation looks it up on its device.
+int static_scratch(int device, uint8_t** out);
+
+extern "C" {
+
 int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** out) {
   if (!cfg || !out) return B200MOE_ERR_INVALID_ARG;
   *out = nullptr;
@@ -551,6 +559,13 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
         (L->f4_sfb[1] && cudaMemset(L->f4_sfb[1], 0, size_t(L->f4_max_chunks) * (c.inter / 64) * 512) != cudaSuccess) ||
         cudaDeviceSynchronize() != cudaSuccess)
       st = B200MOE_ERR_CUDA;
+  }
+  if (st == B200MOE_OK) {
+    // Look up the allocation-free decode's scratch address on this device now,
+    // outside any stream capture (the lookup may load the module), so that the
+    // first b200moe_forward_static call does no set-up of its own.
+    uint8_t* scratch = nullptr;
+    st = static_scratch(device, &scratch);
   }
   if (st != B200MOE_OK) {
     free_layer(L);
@@ -867,11 +882,14 @@ constexpr size_t kStaticScratchBytes =
 // 2,409,728 bytes per GPU at the limits above.
 static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
 
-// Device address of g_static_scratch per device, looked up on the first call
-// on that device (the host-side name of the array is not a device address).
+// Device address of g_static_scratch per device (the host-side name of the
+// array is not a device address), looked up by b200moe_layer_create on the
+// layer's device with that device current.
 constexpr int kMaxDevices = 64;
 uint8_t* g_scratch_addr[kMaxDevices] = {};
 std::mutex g_scratch_mutex;
+
+}  // namespace
 
 int static_scratch(int device, uint8_t** out) {
   if (device < 0 || device >= kMaxDevices) return B200MOE_ERR_INVALID_ARG;
@@ -888,11 +906,9 @@ int static_scratch(int device, uint8_t** out) {
   return B200MOE_OK;
 }
 
-}  // namespace
-
 extern "C" int b200moe_forward_static(b200moe_layer* L, void* stream, const void* x, int x_dtype,
                                       const int32_t* ids, const float* w, float* out, int M) {
-  if (!L || M < 1) return B200MOE_ERR_INVALID_ARG;
+  if (!L || M < 1 || M > L->cfg.max_tokens) return B200MOE_ERR_INVALID_ARG;
   const auto& c = L->cfg;
   if (M > kStaticMaxTokens || c.top_k > kStaticMaxTopK || c.hidden > kStaticMaxHidden ||
       c.inter > kStaticMaxInter || c.n_fp4 + c.n_iq2 > kStaticMaxSlots)

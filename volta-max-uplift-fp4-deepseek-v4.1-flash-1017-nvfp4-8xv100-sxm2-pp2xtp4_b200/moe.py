@@ -285,15 +285,30 @@ class B200NativeMoEMethod:
 
     def __init__(self, moe: B200NativeMoe):
         self.native_moe = moe
+        self._checked_map = None  # the expert_map tensor already checked against the layer's experts
 
     def _checks(self, layer, x, topk_weights) -> None:
-        if getattr(layer, "apply_router_weight_on_input", False):
-            raise ValueError("b200moe experts weight outputs, not inputs")
+        """The refusals of the reference hook (gguf_moe.patch, ``apply`` and
+        ``_apply_nvfp4_8r``): output-weighted SiLU only, fp32 router weights.
+        The reference refuses any ``expert_map`` (it holds every expert); this
+        layer may hold a share of them (expert parallelism), so a map is
+        accepted only when its local experts (entries >= 0) are exactly this
+        layer's, checked once per map tensor."""
         act = getattr(layer, "activation", "silu")
-        if str(getattr(act, "value", act)).lower() not in ("silu", "swigluoai", "moeactivation.silu"):
+        if getattr(layer, "apply_router_weight_on_input", False) or \
+                str(getattr(act, "value", act)).lower() != "silu":
             raise ValueError("b200moe experts require output-weighted SiLU routing")
         if topk_weights.dtype != torch.float32 or x.dtype not in (torch.float16, torch.bfloat16):
             raise RuntimeError(f"b200moe needs fp16/bf16 x and fp32 weights, got {x.dtype}/{topk_weights.dtype}")
+        emap = getattr(layer, "expert_map", None)
+        if emap is not None and emap is not self._checked_map:
+            moe = self.native_moe
+            local = np.asarray(torch.as_tensor(emap).cpu()) >= 0
+            mine = (moe.fp4_slot >= 0) | (moe.iq2_slot >= 0)
+            if local.shape != mine.shape or not np.array_equal(local, mine):
+                raise RuntimeError("layer.expert_map does not match the experts this layer holds "
+                                   "(b200moe takes global ids; its local experts come from its owner map)")
+            self._checked_map = emap
 
     def apply(self, layer, x: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor,
               shared_experts=None, shared_experts_input=None) -> torch.Tensor:
