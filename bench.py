@@ -7,48 +7,54 @@ random-init and packed by the library's own quantizers):
 ``c1`` (default) configs[1], the decode layer the metric is quoted on: hidden
     4096, 384 routed experts, intermediate 2048, top-8 from router logits
     ~N(0,1), all experts NVFP4 (weights ~N(0,0.02)), bf16 activations ~N(0,1),
-    M = 64 tokens per step (``--m`` picks 1, 8, 32 or 64).  At M = 64 a step
-    streams ~4 GB of expert weights, far above the 126 MB L2, so no flush is
-    needed (``config.l2``).
+    M = 64 tokens per step (``--m`` picks 1, 8, 32 or 64).  At M >= 8 a step
+    streams >= 0.8 GB of expert weights, far above the 126 MB L2; at M = 1 the
+    8 routed experts (113 MB) would fit, so M = 1 rotates over 8 seeded
+    routings, one per step (``config.l2``).
 ``c2`` configs[2], the mixed-tier decode layer at M = 32: a seeded Zipf(1.1)
     tier map puts the 150 most popular experts in NVFP4 and 234 in IQ2_XXS;
-    router logits alpha * log p(rank) + Gumbel noise, alpha chosen on the
-    device from a grid so that about 80 % of routes reach the NVFP4 experts.
+    router logits alpha * log p(rank) + Gumbel noise, alpha chosen from a grid
+    so that about 80 % of routes reach the NVFP4 experts.
 ``c3`` configs[3], prefill: T = 4096 tokens (``--tokens 16384``), MXFP4
-    experts, logits ~U(0,1); the W13/W2 launches are the tcgen05 grouped GEMM.
-``c4`` configs[4], a 40-layer stack of c2 layers (own seeded tier map and
-    experts per layer), one decode batch of 256 tokens for the whole box
-    (256 / N per GPU: strong scaling), Zipf routing, residual add between
-    layers; experts sharded by id over the N GPUs (peer-memory exchange); the
-    whole 40-layer step is one CUDA graph.  Reports box tokens/s and the
-    exposed exchange time summed over the layers.
+    experts, logits ~U(0,1).
+``c4`` configs[4], a 40-layer stack of c2 layers, one decode batch of 256
+    tokens for the whole box (strong scaling), residual adds between layers,
+    experts sharded over the N GPUs (peer-memory exchange); one CUDA graph.
+
+The default run (``python bench.py``) prints the configs[1] M = 64 line and,
+under ``also``, the same measurements for configs[1] M = 1 / 8 / 32,
+configs[2] and configs[3] T = 4096, so that one driver run measures every
+single-GPU config (``--no-also`` skips them).
 
 A step = gating (router logits -> top-8) + the layer forward, all on the GPU.
-Decode steps (c1, c2) replay one CUDA graph per step (the reference captures
-its decode path the same way); ``--eager`` launches them one by one.
+Decode steps replay one CUDA graph per step (the reference captures its
+decode path the same way); ``--eager`` launches them one by one.
 
-``value``   tokens/s of the whole job, inputs resident in HBM, CUDA events on
-            the launching stream around exactly K steps, max over ranks.
-``e2e``     the same through the public API with host buffers: each step
-            copies x and the logits from pinned host memory and reads the
-            output back, inside the timed region.
+``value``    tokens/s of the whole job, inputs resident in HBM, CUDA events on
+             the launching stream around exactly K steps, max over ranks.
+``e2e``      the same through the public API with host buffers: each step
+             copies x and the logits from pinned host memory and reads the
+             output back, inside the timed region.
+``parity``   the run's own output against a plain fp32 dequant-then-matmul
+             reference (torch on the GPU, tests/torch_ref.py) on the same
+             inputs, before the timed region: rel-L2 and the tolerance.  Under
+             expert parallelism: bit-equality with the single-GPU layer.
 ``roofline`` the dominant launch: algorithmic bytes (routed distinct experts x
-            the projection's packed bytes) or FLOPs (c3: 2 x routes x weights)
-            over its event-timed duration, against MEASURED_PEAKS.json.
-``cpu_baseline`` the C restatement of the reference's CPU expert kernel
-            (oracle/cpu_moe.c, OpenMP on the host cores) on the same routing,
-            whole layer or a bounded sample of experts scaled to the layer.
+             the projection's packed bytes) or FLOPs (c3: 2 x routes x
+             weights) over its event-timed duration, against
+             MEASURED_PEAKS.json.
+``cpu_baseline`` this build's AVX2 restatement of the reference's CPU expert
+             kernel (oracle/cpu_moe.c, OpenMP on every core of the process's
+             affinity) on the same routing.
 
-``--impl reference`` times that CPU implementation alone on the workload (the
-reference's own GPU kernels are V100-only and are not in its source tree).
+``--impl reference`` times the reference's CPU expert path on the workload
+(rank 0 only, without the product library; see ``run_reference``).
 
-Multi-GPU (torchrun, N ranks): expert parallel on c1.  Rank r owns experts
-[r*384/N, (r+1)*384/N); each rank is home to its own M = 64 tokens (weak
-scaling: tokens per GPU fixed), gates them, dispatches every route to its
-owner over NCCL all-to-all, runs its local experts on the routes it receives
-and combines the returned rows in slot order.  ``value`` = N*M / (max over
-ranks of the step time); ``exposed_comm_ms`` = the all-to-all time on the
-critical path (counts + rows out, y2 back), from CUDA events.
+Multi-GPU (torchrun, N ranks, expert parallel over the library's NVLink
+peer-memory exchange): the configs[1] decode batch of 64 tokens is split over
+the N GPUs (64 / N tokens per GPU: strong scaling, the same work as the
+N = 1 line), experts sharded by id; ``weak_scaling`` adds the 64-tokens-per-
+GPU run.  ``c4`` runs the 40-layer stack instead.
 """
 
 from __future__ import annotations
@@ -75,6 +81,17 @@ MX_W2_BYTES = H * I // 2 + H * I // 32
 IQ_W13_BYTES = 2 * I * H // 256 * 66           # 4,325,376
 IQ_W2_BYTES = H * I // 256 * 66                # 2,162,688
 C2_HOT, C2_HOT_SHARE = 150, 0.80
+TOL_FP4 = 2e-3   # block-scaled FP4 path (four E2M1 activation planes) vs the fp32 dequant reference
+TOL_LAYER = 1e-2  # the reference's layer rule (harness/benchmarks/nvfp4_8r/accept_p2.py:36)
+
+# DRAM bytes per routed expert of the W13 launch, copied from the ncu captures
+# of `python bench.py --profile` (dram__bytes_read.sum + dram__bytes_write.sum
+# of that launch over its 289 distinct experts), kept with the capture's
+# command in profiles/fp4_w13_c1_decode.md and profiles/gemv_w13_c1_decode.md.
+NCU_W13_TRAFFIC_PER_EXPERT = {"fp4": 2.744e9 / 289, "gemv": None}
+
+DTYPE_FP4 = "e2m1x4 activations (E4M3 block scales) x nvfp4 weights, f32 accumulate"
+DTYPE_GEMV = "f16 activations x nvfp4 weights dequantized to f16, f32 accumulate"
 
 
 def parse():
@@ -87,12 +104,13 @@ def parse():
     ap.add_argument("--layers", type=int, default=40, help="c4: layers in the stack")
     ap.add_argument("--batch", type=int, default=256, help="c4: decode tokens of the whole box per step")
     ap.add_argument("--m", type=int, default=None, choices=[1, 8, 32, 64],
-                    help="decode tokens per step (c1 default 64, c2 default 32)")
+                    help="decode tokens per step (c1 default 64, c2 default 32; multi-GPU: of the whole box)")
     ap.add_argument("--tokens", type=int, default=4096, choices=[4096, 16384], help="c3 prefill tokens")
     ap.add_argument("--eager", action="store_true", help="decode: launch each kernel instead of a graph replay")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="multi-GPU: the library's NVLink peer-memory exchange (default) or NCCL all-to-all")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-also", action="store_true", help="default run: skip the other configs' sub-results")
     ap.add_argument("--experts", type=int, default=E,
                     help="routed experts (384 = configs[1]; fewer only for a small ncu capture)")
     ap.add_argument("--split-k", type=int, default=0,
@@ -120,6 +138,17 @@ def peaks() -> dict:
         d = json.loads(p.read_text())
         return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def loaded_libraries() -> list[str]:
+    """Shared objects of this repository mapped into this process."""
+    try:
+        maps = Path("/proc/self/maps").read_text().splitlines()
+    except OSError:
+        return []
+    root = str(ROOT)
+    return sorted({ln.split()[-1][len(root) + 1:] for ln in maps
+                   if ln.split() and ln.split()[-1].startswith(root) and ".so" in ln.split()[-1]})
 
 
 class Clocks:
@@ -179,25 +208,62 @@ class Clocks:
                 "samples": len(self.samples), "source": "nvml, polled every 2 ms during the timed region"}
 
 
-def measured_traffic(distinct: int, summary: str = "gemv_w13_c1_decode.md") -> dict | None:
-    """DRAM bytes of one W13 launch from the committed ncu summary
-    (dram__bytes_read.sum + dram__bytes_write.sum of this bench's W13 launch),
-    scaled from the captured routing's distinct experts to this one's."""
-    import re
+# ------------------------------------------------------------------ parity
+def torch_ref():
+    sys.path.insert(0, str(ROOT / "tests"))
+    import torch_ref as tr
 
-    p = ROOT / "profiles" / summary
-    if not p.exists():
-        return None
-    txt = p.read_text()
-    m1 = re.search(r"^traffic_bytes_per_launch:\s*([0-9.e+]+)", txt, re.M)
-    m2 = re.search(r"^captured_distinct_experts:\s*([0-9]+)", txt, re.M)
-    if not (m1 and m2):
-        return None
-    b, d = float(m1.group(1)), int(m2.group(1))
-    return {"bytes": b * distinct / d, "captured_bytes": b, "captured_distinct_experts": d,
-            "source": f"profiles/{summary} (ncu dram__bytes_read.sum + dram__bytes_write.sum)"}
+    return tr
 
 
+def fp4_dequant(bank, inter: int):
+    """Slot -> (W13 fp32 [2I, H], W2 fp32 [H, I]) of a natural-layout FP4 bank,
+    by the reference's decode formula (torch, on the bank's device)."""
+    import torch
+
+    tr = torch_ref()
+
+    def deq(j: int):
+        if bank.fmt == "nvfp4":
+            g = bank.globals[j]
+            w13 = torch.cat([tr.nvfp4_decode(bank.w13_codes[j, :inter], bank.w13_scales[j, :inter], g[0]),
+                                tr.nvfp4_decode(bank.w13_codes[j, inter:], bank.w13_scales[j, inter:], g[1])])
+            return w13, tr.nvfp4_decode(bank.w2_codes[j], bank.w2_scales[j], g[2])
+        return tr.mxfp4_decode(bank.w13_codes[j], bank.w13_scales[j]), tr.mxfp4_decode(bank.w2_codes[j],
+                                                                                         bank.w2_scales[j])
+    return deq
+
+
+def iq2xxs_dequant(bank):
+    import torch
+    from gguf.quants import IQ2_XXS
+
+    tr = torch_ref()
+    IQ2_XXS.init_grid()
+    grid = np.asarray(IQ2_XXS.grid, np.float32).reshape(256, 8).astype(np.int8)
+    ksigns = np.frombuffer(IQ2_XXS.ksigns, np.uint8).copy()
+
+    def deq(j: int):
+        w13 = torch.cat([tr.iq2xxs_decode(bank.w1[j], grid, ksigns), tr.iq2xxs_decode(bank.w3[j], grid, ksigns)])
+        return w13, tr.iq2xxs_decode(bank.w2[j], grid, ksigns)
+    return deq
+
+
+def parity(out, x, ids, w, dequant, tol: float, rows=None, what: str = "") -> dict:
+    """rel-L2 of the layer output against the fp32 dequant-then-matmul
+    reference on the same inputs (``rows``: a sample of the tokens)."""
+    import torch
+
+    tr = torch_ref()
+    sel = slice(None) if rows is None else torch.as_tensor(rows, device=x.device, dtype=torch.long)
+    ref = tr.layer_forward(x[sel].float(), ids[sel], w[sel], dequant)
+    err = tr.rel_l2(out[sel].float(), ref)
+    n = x.shape[0] if rows is None else len(rows)
+    return {"rel_l2": err, "tol": tol, "ok": bool(err < tol), "tokens_checked": int(n),
+            "reference": "fp32 dequant-then-matmul (torch on the GPU, tests/torch_ref.py)" + (f"; {what}" if what else "")}
+
+
+# ------------------------------------------------------------------ CPU legs
 def fp4_expert(bank, j: int, fmt: int) -> dict:
     """One expert of a natural-layout FP4 bank as the C oracle takes it."""
     g = bank.globals[j].cpu().numpy() if bank.globals is not None else np.ones(3, np.float32)
@@ -207,14 +273,15 @@ def fp4_expert(bank, j: int, fmt: int) -> dict:
 
 
 def cpu_fp4_layer(experts_of, ids_np, w_np, x_np, tokens, sample_experts=None, reps=2) -> dict:
-    """The C oracle (OpenMP, all host cores) on the layer of this routing: every
-    routed expert, or a bounded sample of them scaled to the layer by routes."""
+    """The AVX2 C port (OpenMP, every core of this process's affinity) on the
+    layer of this routing: every routed expert, or a bounded sample of them
+    scaled to the layer by routes."""
     from oracle import cpu_layer
 
     used = np.unique(ids_np[ids_np >= 0])
     pick = used if sample_experts is None else used[:sample_experts]
     experts = {int(e): experts_of(int(e)) for e in pick.tolist()}
-    cpu = cpu_layer.CpuMoe(H, I)
+    cpu = cpu_layer.CpuMoe(H, I, avx2=True)
     cpu.forward(x_np, ids_np, w_np, experts, only=pick)  # warm
     t0 = time.perf_counter()
     for _ in range(reps):
@@ -226,9 +293,31 @@ def cpu_fp4_layer(experts_of, ids_np, w_np, x_np, tokens, sample_experts=None, r
     what = "full layer" if sample_experts is None else f"{pick.size} of {used.size} routed experts " \
                                                        f"({routes_pick} of {routes_all} routes), scaled by routes"
     return {"value": tokens / layer_s, "unit": "tokens/s", "cores": cpu_layer.threads(), "kind": "port",
-            "sample": f"{what}; {reps} timed runs, {dt * 1e3:.1f} ms each", "ms_per_layer": layer_s * 1e3}
+            "sample": f"{what}; {reps} timed runs, {dt * 1e3:.1f} ms each (oracle/cpu_moe.c oracle_expert_avx2)",
+            "ms_per_layer": layer_s * 1e3}
 
 
+def cpu_iq_part(iq_blocks_of, iq_ids, ids_np, x_np, iq_types, sample: int) -> tuple[float, str]:
+    """Seconds per layer of the IQ experts on the host: ggml dequant (numpy
+    restatement of gguf-py's) then fp32 matmuls, the reference's CPU route for
+    them (harness/benchmarks/nvfp4_8r/make_t3_refs.py:58-72), on a bounded
+    sample scaled by routes."""
+    from oracle import moe_oracle as mo
+
+    pick = iq_ids[:sample]
+    t0 = time.perf_counter()
+    for e in pick.tolist():
+        b1, b3, b2 = iq_blocks_of(int(e))
+        w13 = np.concatenate([mo.iq_decode(iq_types[0], b1), mo.iq_decode(iq_types[0], b3)])
+        w2 = mo.iq_decode(iq_types[1], b2)
+        rows = np.nonzero(ids_np == e)[0]
+        mo.expert_fp32(x_np[rows], w13, w2)
+    dt = time.perf_counter() - t0
+    routes_pick = int(np.isin(ids_np, pick).sum())
+    return dt * np.isin(ids_np, iq_ids).sum() / max(routes_pick, 1), f"{pick.size} of {iq_ids.size} IQ experts"
+
+
+# ------------------------------------------------------------------ job
 class Job:
     """Rank, device and the timing helpers shared by the workloads."""
 
@@ -257,6 +346,9 @@ class Job:
         t = torch.tensor([v], dtype=torch.float64, device=self.dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    def allok(self, ok: bool) -> bool:
+        return self.maxall(0.0 if ok else 1.0) == 0.0
 
     def barrier(self):
         if self.world > 1:
@@ -313,200 +405,231 @@ def graphed(step, use_graph: bool, warm: int):
     return g.replay, g
 
 
-def per_launch(layer, step, steps: int, n_events: int) -> np.ndarray:
-    """Mean duration (ms) between the layer's timing events (eager steps)."""
+def rotating(steps, use_graph: bool, warm: int):
+    """One graph per step function; the returned step replays them in turn
+    (a different routing per step keeps a small working set out of L2)."""
+    runs, graphs = [], []
+    for s in steps:
+        r, g = graphed(s, use_graph, warm)
+        runs.append(r)
+        graphs.append(g)
+    if len(runs) == 1:
+        return runs[0], graphs
+    state = {"i": 0}
+
+    def run():
+        runs[state["i"] % len(runs)]()
+        state["i"] += 1
+    return run, graphs
+
+
+def per_launch(layer, steps_fns, steps: int, n_events: int) -> np.ndarray:
+    """Mean duration (ms) between the layer's timing events (eager steps,
+    rotating over ``steps_fns``)."""
     import torch
 
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(n_events)]
     layer.set_timing_events(evs)
     per = np.zeros(n_events - 1)
-    for _ in range(steps):
-        step()
+    for i in range(steps):
+        steps_fns[i % len(steps_fns)]()
         torch.cuda.synchronize()
-        per += [evs[i].elapsed_time(evs[i + 1]) for i in range(n_events - 1)]
+        per += [evs[j].elapsed_time(evs[j + 1]) for j in range(n_events - 1)]
     layer.set_timing_events(None)
     return per / steps
 
 
-def e2e_decode(job, layer, x, logits, out_like, steps: int, use_graph: bool) -> tuple[float, dict]:
+def e2e_decode(job, layer, xs, logits_list, m: int, steps: int, use_graph: bool) -> dict:
     """The public API with pinned host buffers: H2D of x and logits, gating,
-    forward, D2H of the output, every step inside the timed region."""
+    forward, D2H of the output, every step inside the timed region (rotating
+    over the routings like the device-timed run)."""
     import torch
 
-    hx = x.cpu().pin_memory()
-    hl = logits.cpu().pin_memory()
-    hout = torch.empty(out_like.shape, dtype=out_like.dtype).pin_memory()
-    dx, dl = torch.empty_like(x), torch.empty_like(logits)
+    fns = []
+    keep = []
+    for x, logits in zip(xs, logits_list):
+        hx = x.cpu().pin_memory()
+        hl = logits.cpu().pin_memory()
+        hout = torch.empty((m, layer.hidden), dtype=torch.float32).pin_memory()
+        dx, dl = torch.empty_like(x), torch.empty_like(logits)
+        keep.append((hx, hl, hout, dx, dl))
 
-    def step():
-        dx.copy_(hx, non_blocking=True)
-        dl.copy_(hl, non_blocking=True)
-        hout.copy_(layer.forward(dx, *layer.route(dl)), non_blocking=True)
-
-    run, g = graphed(step, use_graph, 2)
+        def step(hx=hx, hl=hl, hout=hout, dx=dx, dl=dl):
+            dx.copy_(hx, non_blocking=True)
+            dl.copy_(hl, non_blocking=True)
+            hout.copy_(layer.forward(dx, *layer.route(dl)), non_blocking=True)
+        fns.append(step)
+    run, graphs = rotating(fns, use_graph, 2)
     ms, _ = job.timed(run, steps, clocks=False)
     layer.check_errors()
-    del g
-    return ms, {"h2d_bytes_per_step": int(hx.numel() * hx.element_size() + hl.numel() * hl.element_size()),
-                "d2h_bytes_per_step": int(hout.numel() * hout.element_size())}
+    del graphs
+    hx, hl, hout = keep[0][:3]
+    return {"value": job.world * m / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+            "h2d_bytes_per_step": int(hx.numel() * hx.element_size() + hl.numel() * hl.element_size()),
+            "d2h_bytes_per_step": int(hout.numel() * hout.element_size())}
 
 
-def line_base(job, args, metric, value, ms, config, dtype="f16") -> dict:
-    return {"metric": metric, "value": value, "unit": "tokens/s", "n_gpus": job.world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": dtype, "data": "synthetic (seeded; random-init experts)", "config": config}
-
-
-def profile_run(layer, step, args, info: dict) -> None:
-    """The ncu command: eager warm-up and timed steps only, then one line."""
-    import torch
-
-    torch.cuda.synchronize()
-    for _ in range(args.warmup + args.steps):
-        step()
-    torch.cuda.synchronize()
-    layer.check_errors()
-    layer.close()
-    print(json.dumps(dict({"profile_run": True, "workload": args.workload}, **info)), flush=True)
+def line_base(job, args, metric, value, ms, config, dtype, steps=None) -> dict:
+    return {"metric": metric, "value": value, "unit": "tokens/s", "n_gpus": job.world,
+            "steps": args.steps if steps is None else steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype,
+            "data": "synthetic (seeded; random-init experts)", "config": config}
 
 
 # --------------------------------------------------------------------------- c1
-def run_c1(job) -> None:
+def c1_inputs(m: int, n_exp: int, dev, rotations: int):
+    """x bf16 [m, H] and logits [m, E] of configs[1] (seed 1000 + m), plus
+    further seeded routings when the step rotates."""
     import torch
 
+    xs, ls = [], []
+    for r in range(rotations):
+        g = torch.Generator(device=dev).manual_seed(1000 + m + 100003 * r)
+        xs.append(torch.randn((m, H), generator=g, device=dev).to(torch.bfloat16))
+        ls.append(torch.randn((m, E), generator=g, device=dev)[:, :n_exp].contiguous())
+    return xs, ls
+
+
+def c1_layer(job, n_exp: int, f4: bool):
     from b200moe import moe, synth
 
-    args, dev, m = job.args, job.dev, job.args.m
-    g = torch.Generator(device=dev).manual_seed(1000 + m)
-    x = torch.randn((m, H), generator=g, device=dev).to(torch.bfloat16)
-    logits = torch.randn((m, E), generator=g, device=dev)
-    use_graph = not args.eager
-    f4 = args.gemm == "fp4"
-    config = {"workload": f"configs[1] decode layer: hidden {H}, {E} experts NVFP4, inter {I}, top-{K_TOP}, M={m}",
-              "gemm": "block-scaled FP4 tensor path (tcgen05.mma kind::mxf4nvf4, E4M3 block scales in TMEM, "
-                      "activations as four E2M1 planes)" if f4 else "skinny GEMV (mma.sync, weights dequantized "
-                                                                     "in registers)",
-              "tokens_per_step": m, "hidden": H, "inter": I, "experts": E, "top_k": K_TOP, "format": "nvfp4",
-              "l2": "inputs larger than L2 (expert weights streamed per step)" if m >= 32 else
-                    "inputs smaller than L2 at this M: weights may stay cached across steps",
-              "launch": "one CUDA graph replay per step" if use_graph else "eager launches",
-              "parallelism": "single GPU"}
-    n_exp = args.experts
-    if n_exp != E:
-        config["workload"] += f" (ncu capture case: {n_exp} experts)"
-        config["experts"] = n_exp
-        logits = logits[:, :n_exp].contiguous()
-
-    bank = synth.make_fp4_bank(n_exp, H, I, "nvfp4", 1000, dev)
+    bank = synth.make_fp4_bank(n_exp, H, I, "nvfp4", 1000, job.dev)
     layer = moe.B200NativeMoe(hidden=H, inter=I, num_experts=n_exp, top_k=K_TOP, max_tokens=64,
-                              tier=np.zeros(n_exp, np.int8), device=dev, prefill_gemm="fp4" if f4 else "tcgen05")
+                              tier=np.zeros(n_exp, np.int8), device=job.dev, prefill_gemm="fp4" if f4 else "tcgen05")
     synth.load_bank(layer, bank)
     layer.check_errors()
+    return layer, bank
+
+
+def run_c1(job, m: int, layer=None, bank=None, main: bool = True) -> dict:
+    """configs[1] decode at M = m on one GPU (the layer and bank may be shared
+    with other M)."""
+    import torch
+
+    args, dev = job.args, job.dev
+    use_graph = not args.eager
+    f4 = args.gemm == "fp4"
+    n_exp = args.experts
+    rotations = 8 if m == 1 else 1
+    own = layer is None
+    if own:
+        layer, bank = c1_layer(job, n_exp, f4)
     if args.split_k:
         layer.set_split_k(args.split_k, 0)
-        config["split_k"] = args.split_k
+    xs, ls = c1_inputs(m, n_exp, dev, rotations)
     if args.profile:
         del bank
         torch.cuda.synchronize()
-        for _ in range(args.warmup):
-            layer.forward(x, *layer.route(logits))
-        for _ in range(args.steps):
-            layer.forward(x, *layer.route(logits))
+        for i in range(args.warmup + args.steps):
+            layer.forward(xs[i % rotations], *layer.route(ls[i % rotations]))
         torch.cuda.synchronize()
         layer.check_errors()
-        distinct = int(torch.unique(layer.route(logits)[0]).numel())
+        distinct = int(torch.unique(layer.route(ls[0])[0]).numel())
         layer.close()
-        print(json.dumps({"profile_run": True, "experts": n_exp, "m": m, "distinct_experts": distinct,
-                          "w13_algorithmic_bytes": distinct * W13_BYTES,
-                          "w2_algorithmic_bytes": distinct * W2_BYTES}), flush=True)
-        return
+        return {"profile_run": True, "experts": n_exp, "m": m, "distinct_experts": distinct,
+                "w13_algorithmic_bytes": distinct * W13_BYTES, "w2_algorithmic_bytes": distinct * W2_BYTES}
+    config = {"workload": f"configs[1] decode layer: hidden {H}, {n_exp} experts NVFP4, inter {I}, top-{K_TOP}, M={m}",
+              "gemm": "block-scaled FP4 tensor path (tcgen05.mma kind::mxf4nvf4, E4M3 block scales in TMEM, "
+                      "activations as four E2M1 planes)" if f4 else "skinny GEMV (mma.sync, weights dequantized "
+                                                                     "in registers)",
+              "tokens_per_step": m, "hidden": H, "inter": I, "experts": n_exp, "top_k": K_TOP, "format": "nvfp4",
+              "l2": "inputs larger than L2 (>= 0.8 GB of expert weights streamed per step)" if m > 1 else
+                    f"inputs larger than L2: {rotations} seeded routings replayed in turn, one per step "
+                    "(8 x ~113 MB of experts, different experts from one step to the next)",
+              "launch": "one CUDA graph replay per step" if use_graph else "eager launches",
+              "parallelism": "single GPU"}
+    if n_exp != E:
+        config["workload"] += f" (ncu capture case: {n_exp} experts)"
 
-    def step():
-        return layer.forward(x, *layer.route(logits))
-
-    run, graph = graphed(step, use_graph, args.warmup)
+    # parity on the first routing, before the timed region
+    ids0, w0 = layer.route(ls[0])
+    out0 = layer.forward(xs[0], ids0, w0).clone()
     layer.check_errors()
-    ids, w = layer.route(logits)
-    distinct = int(torch.unique(ids).numel())
+    par = parity(out0, xs[0], ids0, w0, fp4_dequant(bank, I), TOL_FP4 if f4 else TOL_LAYER)
+
+    fns = [(lambda x=x, lg=lg: layer.forward(x, *layer.route(lg))) for x, lg in zip(xs, ls)]
+    run, graphs = rotating(fns, use_graph, args.warmup)
+    layer.check_errors()
+    distinct = float(np.mean([torch.unique(layer.route(lg)[0]).numel() for lg in ls]))
     ms, clk = job.timed(run, args.steps)
     layer.check_errors()
-    value = job.world * m / (ms / 1e3)
-    del graph
+    value = m / (ms / 1e3)
+    del graphs
 
-    if f4:  # convert, plan, x planes, W13, SwiGLU planes, W2, combine
-        per = per_launch(layer, step, args.steps, 8)
-        t_w13_ms, t_w2_ms = float(per[3]), float(per[5])
+    if f4:  # start, plan, x planes, W13, SwiGLU planes, W2, combine
+        per = per_launch(layer, fns, args.steps, 8)
+        t_w13_ms = float(per[3])
         names = ["convert", "plan", "x_planes", "w13", "swiglu_planes", "w2", "combine"]
     else:  # convert, plan, W13, W2 (+SwiGLU or combine: fused up to 32 routes)
         sep = m * K_TOP > 32
-        per = per_launch(layer, step, args.steps, 6 if sep else 5)
-        t_w13_ms, t_w2_ms = float(per[2]), float(per[3])
+        per = per_launch(layer, fns, args.steps, 6 if sep else 5)
+        t_w13_ms = float(per[2])
         names = ["convert", "plan", "w13", "w2"] + (["combine"] if sep else [])
     pk = peaks()
     achieved = distinct * W13_BYTES / (t_w13_ms / 1e3) / 1e9
     layer_bytes = distinct * EXPERT_BYTES
-    traffic = measured_traffic(distinct, "fp4_w13_c1_decode.md" if f4 else "gemv_w13_c1_decode.md") \
-        if n_exp == E else None
-    e2e_ms, e2e_bytes = e2e_decode(job, layer, x, logits, layer.out[:m], args.steps, use_graph)
+    tpe = NCU_W13_TRAFFIC_PER_EXPERT["fp4" if f4 else "gemv"]
+    traffic = tpe * distinct if (tpe and n_exp == E) else None
+    e2e = e2e_decode(job, layer, xs, ls, m, args.steps, use_graph)
 
     cpu = None
-    if job.rank == 0 and job.world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_fp4_layer(lambda e: fp4_expert(bank, e, 0), ids.cpu().numpy(), w.cpu().numpy(),
-                            x.float().cpu().numpy(), m)
-    if job.rank == 0:
-        line = line_base(job, args, "MoE-layer tokens/s (decode M=%d) & %% HBM roofline" % m, value, ms, config)
-        line.update({
-            "roofline": {"bound": "hbm", "kernel": ("fp4_gemm_kernel" if f4 else "gemv_kernel") + " W13 (+SwiGLU)",
-                         "achieved": achieved,
-                         "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
-                         "peak_source": pk["source"], "traffic": traffic["bytes"] if traffic else None,
-                         "traffic_detail": traffic,
-                         "algorithmic_bytes_per_launch": distinct * W13_BYTES, "distinct_experts": distinct,
-                         "launch_ms": t_w13_ms},
-            "layer_roofline": {"bytes": layer_bytes, "ms": float(per.sum()),
-                               "achieved_gbs": layer_bytes / (per.sum() / 1e3) / 1e9,
-                               "frac": layer_bytes / (per.sum() / 1e3) / 1e9 / pk["hbm_gbs"],
-                               "launch_ms": {k: float(v) for k, v in zip(names, per)}},
-            "e2e": dict({"value": job.world * m / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms},
-                        **e2e_bytes),
-            # fp4: gating, route plan, x planes (read bf16 x directly), W13 (+SwiGLU), SwiGLU planes, W2, combine;
-            # gemv: gating, bf16 copy, route plan, W13 (+SwiGLU), W2, combine (fused into W2 up to 32 routes)
-            "gpu_launches": (7 if f4 else 6 if m * K_TOP > 32 else 5) * args.steps,
-            "cpu_baseline": cpu,
-            "clocks": clk,
-        })
-        print(json.dumps(line), flush=True)
-    layer.close()
+    if main and job.rank == 0 and not args.no_cpu_baseline:
+        ids_np, w_np = ids0.cpu().numpy(), w0.cpu().numpy()
+        cpu = cpu_fp4_layer(lambda e: fp4_expert(bank, e, 0), ids_np, w_np, xs[0].float().cpu().numpy(), m)
+    line = line_base(job, args, "MoE-layer tokens/s (decode M=%d) & %% HBM roofline" % m, value, ms, config,
+                     DTYPE_FP4 if f4 else DTYPE_GEMV)
+    line.update({
+        "parity": par,
+        "roofline": {"bound": "hbm", "kernel": ("fp4_gemm_kernel" if f4 else "gemv_kernel") + " W13 (+SwiGLU)",
+                     "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                     "peak_source": pk["source"] + " (MEASURED_PEAKS.json hbm_gbs, copy bandwidth)",
+                     "traffic": traffic,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per routed expert of the "
+                                       "W13 launch, copied from the capture in profiles/fp4_w13_c1_decode.md, "
+                                       "times this run's distinct experts" if traffic else None,
+                     "algorithmic_bytes_per_launch": distinct * W13_BYTES, "distinct_experts": distinct,
+                     "launch_ms": t_w13_ms},
+        "layer_roofline": {"bytes": layer_bytes, "ms": float(per.sum()),
+                           "achieved_gbs": layer_bytes / (per.sum() / 1e3) / 1e9,
+                           "frac": layer_bytes / (per.sum() / 1e3) / 1e9 / pk["hbm_gbs"],
+                           "launch_ms": {k: float(v) for k, v in zip(names, per)}},
+        "e2e": e2e,
+        # fp4: gating, route plan, x planes (read bf16 x directly), W13 (+SwiGLU), SwiGLU planes, W2, combine;
+        # gemv: gating, bf16 copy, route plan, W13 (+SwiGLU), W2, combine (fused into W2 up to 32 routes)
+        "gpu_launches": (7 if f4 else 6 if m * K_TOP > 32 else 5) * args.steps,
+        "cpu_baseline": cpu,
+        "clocks": clk,
+    })
+    if own:
+        layer.close()
+    return line
 
 
 # --------------------------------------------------------------------------- c2
-def c2_inputs(layer, tier_rank, m, dev):
+def c2_alpha(route_fn, hot_mask: np.ndarray, tier_rank, m, dev):
     """Logits alpha * log p(rank) + Gumbel: alpha from a grid, the one whose
     routing sends closest to 80 % of routes to the NVFP4 experts."""
-    import torch
-
     from b200moe import synth
 
-    hot = torch.from_numpy(layer.fp4_slot >= 0).to(dev)
     best = None
     for alpha in np.round(np.arange(0.40, 1.21, 0.05), 2):
         logits = synth.zipf_logits(m, tier_rank, float(alpha), 1.1, 2000 + m, dev)
-        ids, _ = layer.route(logits)
-        share = float(hot[ids.long()].float().mean())
+        ids = route_fn(logits)
+        share = float(hot_mask[ids].mean())
         if best is None or abs(share - C2_HOT_SHARE) < abs(best[1] - C2_HOT_SHARE):
             best = (float(alpha), share, logits)
     return best
 
 
-def run_c2(job) -> None:
+def run_c2(job, main: bool = True) -> dict:
     import torch
 
     from b200moe import moe, synth, tiers
 
-    args, dev, m = job.args, job.dev, job.args.m
+    args, dev, m = job.args, job.dev, (job.args.m if main else 32)
     tier, tier_rank = tiers.zipf_tier(E, C2_HOT, seed=2)
     f4 = args.gemm == "fp4"
-    iq_types = tuple(int(t) for t in args.iq_types.split(","))
+    iq_types = tuple(int(t) for t in args.iq_types.split(",")) if main else (16, 16)
     layer = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, max_tokens=64, tier=tier, device=dev,
                               prefill_gemm="fp4" if f4 else "tcgen05", iq_types=iq_types)
     fp4 = synth.make_fp4_bank(C2_HOT, H, I, "nvfp4", 2000, dev)
@@ -520,13 +643,19 @@ def run_c2(job) -> None:
     iq_desc = iq_name[iq_types[0]] if iq_types[0] == iq_types[1] else \
         f"{iq_name[iq_types[0]]} gate/up + {iq_name[iq_types[1]]} down"
     layer.check_errors()
-    alpha, share, logits = c2_inputs(layer, tier_rank, m, dev)
+    hot_mask = layer.fp4_slot >= 0
+    alpha, share, logits = c2_alpha(lambda lg: layer.route(lg)[0].cpu().numpy(), hot_mask, tier_rank, m, dev)
     g = torch.Generator(device=dev).manual_seed(2032)
     x = torch.randn((m, H), generator=g, device=dev).to(torch.bfloat16)
     if args.profile:
         del fp4, iq2
-        profile_run(layer, lambda: layer.forward(x, *layer.route(logits)), args, {"alpha": alpha, "share": share})
-        return
+        torch.cuda.synchronize()
+        for _ in range(args.warmup + args.steps):
+            layer.forward(x, *layer.route(logits))
+        torch.cuda.synchronize()
+        layer.check_errors()
+        layer.close()
+        return {"profile_run": True, "workload": "c2", "alpha": alpha, "share": share}
     use_graph = not args.eager
     config = {"workload": f"configs[2] mixed-tier decode layer: hidden {H}, {C2_HOT} NVFP4 + {E - C2_HOT} {iq_desc} "
                           f"experts (Zipf 1.1 tier map, seed 2), inter {I}, top-{K_TOP}, M={m}",
@@ -535,11 +664,21 @@ def run_c2(job) -> None:
               "launch": "one CUDA graph replay per step" if use_graph else "eager launches",
               "parallelism": "single GPU"}
 
+    ids, w = layer.route(logits)
+    out0 = layer.forward(x, ids, w).clone()
+    layer.check_errors()
+    par = None
+    if iq_types == (16, 16):
+        fdeq, ideq = fp4_dequant(fp4, I), iq2xxs_dequant(iq2)
+
+        def deq(e):
+            return fdeq(int(layer.fp4_slot[e])) if layer.fp4_slot[e] >= 0 else ideq(int(layer.iq2_slot[e]))
+        par = parity(out0, x, ids, w, deq, TOL_LAYER, what="IQ2_XXS experts decoded as gguf-py does")
+
     def step():
         return layer.forward(x, *layer.route(logits))
 
     run, graph = graphed(step, use_graph, args.warmup)
-    ids, w = layer.route(logits)
     ids_np = ids.cpu().numpy()
     used = np.unique(ids_np)
     hot_used = used[layer.fp4_slot[used] >= 0]
@@ -549,11 +688,11 @@ def run_c2(job) -> None:
     del graph
     if f4:  # start, convert, x int8 blocks, plan, x planes, W13 fp4, W13 iq2, SwiGLU planes, SwiGLU int8 blocks,
         #     W2 fp4, W2 iq2, combine
-        per = per_launch(layer, step, args.steps, 12)
+        per = per_launch(layer, [step], args.steps, 12)
         i13, i2, extra = (4, 5), (8, 9), {"x_planes": 3, "inter_planes": 6, "inter_int8": 7, "combine": 10}
     else:  # start, convert, x int8 blocks, plan, W13 fp4, W13 iq2, SwiGLU int8 blocks, W2 fp4, W2 iq2, combine
         sep = m * K_TOP > 32
-        per = per_launch(layer, step, args.steps, 10 if sep else 9)
+        per = per_launch(layer, [step], args.steps, 10 if sep else 9)
         i13, i2, extra = (3, 4), (6, 7), dict({"inter_int8": 5}, **({"combine": 8} if sep else {}))
     pk = peaks()
     launches = {"w13_fp4": (per[i13[0]], hot_used.size * W13_BYTES),
@@ -563,77 +702,57 @@ def run_c2(job) -> None:
     t_dom, b_dom = launches[dom]
     achieved = b_dom / (t_dom / 1e3) / 1e9
     layer_bytes = hot_used.size * EXPERT_BYTES + iq_used.size * (iq_w13_bytes + iq_w2_bytes)
-    e2e_ms, e2e_bytes = e2e_decode(job, layer, x, logits, layer.out[:m], args.steps, use_graph)
+    e2e = e2e_decode(job, layer, [x], [logits], m, args.steps, use_graph)
 
     cpu = None
-    if job.rank == 0 and job.world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_c2(fp4, iq2, layer, ids_np, w.cpu().numpy(), x.float().cpu().numpy(), m, iq_types=iq_types)
-    if job.rank == 0:
-        line = line_base(job, args, "MoE-layer tokens/s (mixed-tier decode M=%d) & %% HBM roofline" % m,
-                         job.world * m / (ms / 1e3), ms, config)
-        line.update({
-            "roofline": {"bound": "hbm", "kernel": ("fp4_gemm_kernel " if f4 and dom.endswith("fp4") else
-                                                   "gemv_kernel ") + dom, "achieved": achieved,
-                         "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
-                         "peak_source": pk["source"], "traffic": None, "algorithmic_bytes_per_launch": b_dom,
-                         "launch_ms": t_dom, "distinct_hot": int(hot_used.size), "distinct_iq2": int(iq_used.size)},
-            "layer_roofline": {"bytes": layer_bytes, "ms": float(per.sum()),
-                               "achieved_gbs": layer_bytes / (per.sum() / 1e3) / 1e9,
-                               "frac": layer_bytes / (per.sum() / 1e3) / 1e9 / pk["hbm_gbs"],
-                               "launch_ms": {"convert": float(per[0]), "x_int8": float(per[1]), "plan": float(per[2]),
-                                             **{k: float(per[v]) for k, v in extra.items()},
-                                             **{k: float(v[0]) for k, v in launches.items()}}},
-            "e2e": dict({"value": job.world * m / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms},
-                        **e2e_bytes),
-            # gating, bf16 copy, x int8 blocks, plan, W13 x 2 banks, SwiGLU int8 blocks, W2 x 2 banks, combine
-            # (fp4: + x planes, SwiGLU planes; the GEMV path fuses the combine up to 32 routes)
-            "gpu_launches": (12 if f4 else 10 if m * K_TOP > 32 else 9) * args.steps,
-            "cpu_baseline": cpu,
-            "clocks": clk,
-        })
-        print(json.dumps(line), flush=True)
+    if main and job.rank == 0 and not args.no_cpu_baseline:
+        hot = cpu_fp4_layer(lambda e: fp4_expert(fp4, int(layer.fp4_slot[e]), 0),
+                            np.where(np.isin(ids_np, hot_used), ids_np, -1), w.cpu().numpy(),
+                            x.float().cpu().numpy(), m, reps=1)
+        s = int
+        iq_s, what = cpu_iq_part(lambda e: (iq2.w1[s(layer.iq2_slot[e])].cpu().numpy(),
+                                            iq2.w3[s(layer.iq2_slot[e])].cpu().numpy(),
+                                            iq2.w2[s(layer.iq2_slot[e])].cpu().numpy()),
+                                 iq_used, ids_np, x.float().cpu().numpy(), iq_types, 6)
+        total = hot["ms_per_layer"] / 1e3 + iq_s
+        cpu = {"value": m / total, "unit": "tokens/s", "cores": hot["cores"], "kind": "port",
+               "sample": f"NVFP4 experts: all {hot_used.size} through oracle/cpu_moe.c (AVX2); {what} "
+                         "(numpy dequant + fp32 matmul), scaled by routes", "ms_per_layer": total * 1e3}
+    line = line_base(job, args, "MoE-layer tokens/s (mixed-tier decode M=%d) & %% HBM roofline" % m,
+                     m / (ms / 1e3), ms, config,
+                     ("nvfp4 bank: " + DTYPE_FP4 if f4 else "nvfp4 bank: " + DTYPE_GEMV) +
+                     "; IQ bank: two int8 activation planes x int8 codebook weights, s32 accumulate")
+    line.update({
+        "parity": par,
+        "roofline": {"bound": "hbm", "kernel": ("fp4_gemm_kernel " if f4 and dom.endswith("fp4") else
+                                               "gemv_kernel ") + dom, "achieved": achieved,
+                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                     "peak_source": pk["source"], "traffic": None, "algorithmic_bytes_per_launch": b_dom,
+                     "launch_ms": t_dom, "distinct_hot": int(hot_used.size), "distinct_iq2": int(iq_used.size)},
+        "layer_roofline": {"bytes": layer_bytes, "ms": float(per.sum()),
+                           "achieved_gbs": layer_bytes / (per.sum() / 1e3) / 1e9,
+                           "frac": layer_bytes / (per.sum() / 1e3) / 1e9 / pk["hbm_gbs"],
+                           "launch_ms": {"convert": float(per[0]), "x_int8": float(per[1]), "plan": float(per[2]),
+                                         **{k: float(per[v]) for k, v in extra.items()},
+                                         **{k: float(v[0]) for k, v in launches.items()}}},
+        "e2e": e2e,
+        # gating, bf16 copy, x int8 blocks, plan, W13 x 2 banks, SwiGLU int8 blocks, W2 x 2 banks, combine
+        # (fp4: + x planes, SwiGLU planes; the GEMV path fuses the combine up to 32 routes)
+        "gpu_launches": (12 if f4 else 10 if m * K_TOP > 32 else 9) * args.steps,
+        "cpu_baseline": cpu,
+        "clocks": clk,
+    })
     layer.close()
-
-
-def cpu_c2(fp4, iq2, layer, ids_np, w_np, x_np, m, sample_iq=6, iq_types=(16, 16)) -> dict:
-    """CPU layer of the mixed tier: NVFP4 experts through the C oracle, IQ2
-    experts as the reference's CPU path does them (gguf dequantize, then fp32
-    matmuls; numpy restatement), on a bounded sample of IQ2 experts scaled by
-    routes."""
-    from oracle import cpu_layer
-    from oracle import moe_oracle as mo
-
-    used = np.unique(ids_np)
-    hot_ids = used[layer.fp4_slot[used] >= 0]
-    iq_ids = used[layer.iq2_slot[used] >= 0]
-    hot = cpu_fp4_layer(lambda e: fp4_expert(fp4, int(layer.fp4_slot[e]), 0),
-                        np.where(np.isin(ids_np, hot_ids), ids_np, -1), w_np, x_np, m, reps=1)
-    hot_s = hot["ms_per_layer"] / 1e3
-    pick = iq_ids[:sample_iq]
-    t0 = time.perf_counter()
-    for e in pick.tolist():
-        s = int(layer.iq2_slot[e])
-        w13 = np.concatenate([mo.iq_decode(iq_types[0], iq2.w1[s].cpu().numpy()),
-                              mo.iq_decode(iq_types[0], iq2.w3[s].cpu().numpy())])
-        w2 = mo.iq_decode(iq_types[1], iq2.w2[s].cpu().numpy())
-        rows = np.nonzero(ids_np == e)[0]
-        mo.expert_fp32(x_np[rows], w13, w2)
-    dt = time.perf_counter() - t0
-    routes_pick = int(np.isin(ids_np, pick).sum())
-    iq_s = dt * np.isin(ids_np, iq_ids).sum() / max(routes_pick, 1)
-    total = hot_s + iq_s
-    return {"value": m / total, "unit": "tokens/s", "cores": cpu_layer.threads(), "kind": "port",
-            "sample": f"NVFP4 experts: all {hot_ids.size} through oracle/cpu_moe.c; IQ2_XXS: {pick.size} of "
-                      f"{iq_ids.size} experts (numpy dequant + matmul), scaled by routes", "ms_per_layer": total * 1e3}
+    return line
 
 
 # --------------------------------------------------------------------------- c3
-def run_c3(job) -> None:
+def run_c3(job, main: bool = True) -> dict:
     import torch
 
     from b200moe import moe, synth
 
-    args, dev, T = job.args, job.dev, job.args.tokens
+    args, dev, T = job.args, job.dev, (job.args.tokens if main else 4096)
     units = args.gemm == "fp4"  # the block-scaled layout's weight units also feed the tcgen05 prefill GEMM
     layer = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, max_tokens=8,
                               tier=np.zeros(E, np.int8), fp4_format="mxfp4", device=dev, max_prefill_tokens=T,
@@ -646,8 +765,13 @@ def run_c3(job) -> None:
     logits = torch.rand((T, E), generator=g, device=dev)
     if args.profile:
         del bank
-        profile_run(layer, lambda: layer.forward_prefill(x, *layer.route(logits)), args, {"tokens": T})
-        return
+        torch.cuda.synchronize()
+        for _ in range(args.warmup + args.steps):
+            layer.forward_prefill(x, *layer.route(logits))
+        torch.cuda.synchronize()
+        layer.check_errors()
+        layer.close()
+        return {"profile_run": True, "workload": "c3", "tokens": T}
     config = {"workload": f"configs[3] prefill layer: hidden {H}, {E} experts MXFP4, inter {I}, top-{K_TOP}, T={T}",
               "tokens_per_step": T, "format": "mxfp4",
               "gemm": "tcgen05 grouped GEMM (kind::f16, TMEM accumulators) on " +
@@ -659,15 +783,20 @@ def run_c3(job) -> None:
     def step():
         return layer.forward_prefill(x, *layer.route(logits))
 
+    ids, w = layer.route(logits)
+    out0 = step()
+    layer.check_errors()
+    rows = np.sort(np.random.default_rng(3).choice(T, 256, replace=False))
+    par = parity(out0, x, ids, w, fp4_dequant(bank, I), TOL_LAYER, rows=rows,
+                 what="256 seeded tokens of the T-token call")
     for _ in range(max(3, args.warmup)):
         step()
     layer.check_errors()
-    ids, w = layer.route(logits)
     distinct = int(torch.unique(ids).numel())
     steps = max(3, args.steps // 10)
     ms, clk = job.timed(step, steps)
     layer.check_errors()
-    per = per_launch(layer, step, steps, 7)  # convert, plan, gather, W13, W2, combine
+    per = per_launch(layer, [step], steps, 7)  # convert, plan, gather, W13, W2, combine
     pk = peaks()
     routes = T * K_TOP
     f13, f2 = 2.0 * routes * H * 2 * I, 2.0 * routes * I * H
@@ -675,6 +804,8 @@ def run_c3(job) -> None:
     ach = f13 / (t13 / 1e3) / 1e12
     layer_flops = f13 + f2
     layer_bytes = distinct * (MX_W13_BYTES + MX_W2_BYTES)
+    layer_ms = float(per.sum())
+    bound_ms = max(layer_bytes / pk["hbm_gbs"] / 1e6, layer_flops / pk["bf16_tflops"] / 1e9)
 
     hx = x.cpu().pin_memory()
     hl = logits.cpu().pin_memory()
@@ -690,39 +821,72 @@ def run_c3(job) -> None:
     e2e_ms, _ = job.timed(e2e_step, steps, clocks=False)
 
     cpu = None
-    if job.rank == 0 and job.world == 1 and not args.no_cpu_baseline:
+    if main and job.rank == 0 and not args.no_cpu_baseline:
         cpu = cpu_fp4_layer(lambda e: fp4_expert(bank, e, 1), ids.cpu().numpy(), w.cpu().numpy(),
                             x.float().cpu().numpy(), T, sample_experts=3, reps=1)
-    if job.rank == 0:
-        line = line_base(job, args, "MoE-layer tokens/s (prefill T=%d) & %% tensor roofline" % T,
-                         job.world * T / (ms / 1e3), ms, config)
-        line["steps"] = steps
-        line.update({
-            "roofline": {"bound": "tensor", "kernel": "tcgen05 grouped GEMM W13 (+SwiGLU)", "achieved": ach,
-                         "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": ach / pk["bf16_tflops"],
-                         "peak_source": pk["source"] + " bf16 dense (the MMAs are kind::f16 on dequantized weights)",
-                         "traffic": None, "algorithmic_flops_per_launch": f13, "launch_ms": t13},
-            "layer_roofline": {"flops": layer_flops, "bytes": layer_bytes, "ms": float(per.sum()),
-                               "tflops": layer_flops / (per.sum() / 1e3) / 1e12,
-                               "tensor_frac": layer_flops / (per.sum() / 1e3) / 1e12 / pk["bf16_tflops"],
-                               "hbm_frac": layer_bytes / (per.sum() / 1e3) / 1e9 / pk["hbm_gbs"],
-                               "launch_ms": {"convert": float(per[0]), "plan": float(per[1]),
-                                             "gather": float(per[2]), "w13": t13, "w2": t2,
-                                             "combine": float(per[5])}},
-            "e2e": {"value": job.world * T / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
-                    "h2d_bytes_per_step": int(hx.numel() * 2 + hl.numel() * 4),
-                    "d2h_bytes_per_step": int(hout.numel() * 4)},
-            # gating, [bf16 copy], plan, row gather (converts bf16 itself), W13, W2, combine
-            "gpu_launches": (6 if units else 7) * steps,
-            "cpu_baseline": cpu,
-            "clocks": clk,
-        })
-        print(json.dumps(line), flush=True)
+    line = line_base(job, args, "MoE-layer tokens/s (prefill T=%d) & %% tensor roofline" % T, T / (ms / 1e3), ms,
+                     config, "f16 activations x mxfp4 weights dequantized to f16 on the SM, f32 accumulate",
+                     steps=steps)
+    line.update({
+        "parity": par,
+        "roofline": {"bound": "tensor", "kernel": "tcgen05 grouped GEMM W13 (+SwiGLU)", "achieved": ach,
+                     "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": ach / pk["bf16_tflops"],
+                     "peak_source": pk["source"] + " bf16 dense (the MMAs are kind::f16 on dequantized weights)",
+                     "traffic": None, "algorithmic_flops_per_launch": f13, "launch_ms": t13},
+        "layer_roofline": {"flops": layer_flops, "bytes": layer_bytes, "ms": layer_ms,
+                           "tflops": layer_flops / (layer_ms / 1e3) / 1e12,
+                           "tensor_frac": layer_flops / (layer_ms / 1e3) / 1e12 / pk["bf16_tflops"],
+                           "hbm_frac": layer_bytes / (layer_ms / 1e3) / 1e9 / pk["hbm_gbs"],
+                           "binding_bound_ms": bound_ms, "frac_of_binding_bound": bound_ms / layer_ms,
+                           "launch_ms": {"convert": float(per[0]), "plan": float(per[1]),
+                                         "gather": float(per[2]), "w13": t13, "w2": t2,
+                                         "combine": float(per[5])}},
+        "e2e": {"value": T / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": int(hx.numel() * 2 + hl.numel() * 4),
+                "d2h_bytes_per_step": int(hout.numel() * 4)},
+        # gating, [bf16 copy], plan, row gather (converts bf16 itself), W13, W2, combine
+        "gpu_launches": (6 if units else 7) * steps,
+        "cpu_baseline": cpu,
+        "clocks": clk,
+    })
     layer.close()
+    return line
+
+
+def compact(line: dict) -> dict:
+    """The figures of a sub-result worth keeping in the default run's line."""
+    keep = ("metric", "value", "unit", "ms_per_step", "steps", "dtype", "config", "parity", "roofline",
+            "layer_roofline", "e2e", "gpu_launches", "clocks")
+    return {k: line[k] for k in keep if k in line}
+
+
+def run_default(job) -> dict:
+    """configs[1] M = 64, then (``also``) configs[1] M = 1 / 8 / 32,
+    configs[2] and configs[3] T = 4096 on the same GPU."""
+    import torch
+
+    args = job.args
+    f4 = args.gemm == "fp4"
+    layer, bank = c1_layer(job, args.experts, f4)
+    line = run_c1(job, 64, layer, bank, main=True)
+    if args.no_also or args.experts != E:
+        layer.close()
+        return line
+    also = []
+    for m in (1, 8, 32):
+        also.append(compact(run_c1(job, m, layer, bank, main=False)))
+    layer.close()
+    del bank
+    torch.cuda.empty_cache()
+    also.append(compact(run_c2(job, main=False)))
+    torch.cuda.empty_cache()
+    also.append(compact(run_c3(job, main=False)))
+    line["also"] = also
+    return line
 
 
 # --------------------------------------------------------------------------- c4
-def run_c4(job) -> None:
+def run_c4(job) -> dict:
     import torch
 
     from b200moe import ep, moe, synth, tiers
@@ -738,7 +902,7 @@ def run_c4(job) -> None:
     tier0, trank0 = tiers.zipf_tier(E, C2_HOT, seed=4000)
     probe = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, max_tokens=min(T, 64),
                               max_prefill_tokens=T, tier=tier0, device=dev)
-    alpha = c2_inputs(probe, trank0, T, dev)[0]
+    alpha = c2_alpha(lambda lg: probe.route(lg)[0].cpu().numpy(), probe.fp4_slot >= 0, trank0, T, dev)[0]
     probe.close()
     for li in range(n_layers):
         tier, trank = tiers.zipf_tier(E, C2_HOT, seed=4000 + li)
@@ -771,7 +935,7 @@ def run_c4(job) -> None:
     xb = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
     routes = [lay.route(lg) for lay, lg in layers]
 
-    def single(lay, ids, w):  # world 1: the whole layer on this GPU, fused combine
+    def single(lay, ids, w):  # world 1: the whole layer on this GPU
         return lay.forward(xb, ids, w) if T <= 64 else lay.forward_prefill(xb, ids, w)
 
     def step():
@@ -852,12 +1016,24 @@ def run_c4(job) -> None:
         # one layer on the host cores, scaled by the layer count
         lay0, _ = layers[0]
         ids0, w0 = routes[0]
+        ids_np = ids0.cpu().numpy()
+        used = np.unique(ids_np)
+        hot_used, iq_used = used[lay0.fp4_slot[used] >= 0], used[lay0.iq2_slot[used] >= 0]
         hot0 = synth.make_fp4_bank(C2_HOT, H, I, "nvfp4", 4000, dev)
         iq0 = synth.make_iq2_bank(E - C2_HOT, H, I, 9000, dev)
-        one = cpu_c2(hot0, iq0, lay0, ids0.cpu().numpy(), w0.cpu().numpy(), x0.float().cpu().numpy(), T)
-        one["value"] /= n_layers
-        one["sample"] = f"one layer of the stack ({one['sample']}), time x {n_layers} layers"
-        cpu = one
+        hot = cpu_fp4_layer(lambda e: fp4_expert(hot0, int(lay0.fp4_slot[e]), 0),
+                            np.where(np.isin(ids_np, hot_used), ids_np, -1), w0.cpu().numpy(),
+                            x0.float().cpu().numpy(), T, reps=1)
+        s = int
+        iq_s, what = cpu_iq_part(lambda e: (iq0.w1[s(lay0.iq2_slot[e])].cpu().numpy(),
+                                            iq0.w3[s(lay0.iq2_slot[e])].cpu().numpy(),
+                                            iq0.w2[s(lay0.iq2_slot[e])].cpu().numpy()),
+                                 iq_used, ids_np, x0.float().cpu().numpy(), (16, 16), 6)
+        total = (hot["ms_per_layer"] / 1e3 + iq_s) * n_layers
+        cpu = {"value": batch / total, "unit": "tokens/s", "cores": hot["cores"], "kind": "port",
+               "sample": f"one layer of the stack (NVFP4 experts through oracle/cpu_moe.c AVX2, {what} by numpy), "
+                         f"time x {n_layers} layers", "ms_per_step": total * 1e3}
+    line = None
     if rank == 0:
         config = {"workload": f"configs[4] {n_layers}-layer stack of configs[2] layers ({C2_HOT} NVFP4 + "
                               f"{E - C2_HOT} IQ2_XXS experts each), decode batch {batch} tokens per box, "
@@ -871,8 +1047,8 @@ def run_c4(job) -> None:
                   "parallelism": f"expert parallel x{world} (NVLink peer-memory exchange kernels)" if world > 1
                                  else "single GPU"}
         line = line_base(job, args, f"MoE-stack tokens/s ({n_layers} layers, decode batch {batch}) & % HBM roofline",
-                         value, ms, config)
-        line["steps"] = steps
+                         value, ms, config, "nvfp4 bank: " + (DTYPE_FP4 if args.gemm == "fp4" else DTYPE_GEMV) +
+                         "; IQ bank: two int8 activation planes x int8 codebook weights", steps=steps)
         line["scaling"] = "strong"
         line.update({
             "roofline": {"bound": "hbm", "kernel": "all expert launches of the stack on rank 0 (whole step: " +
@@ -888,201 +1064,369 @@ def run_c4(job) -> None:
             "cpu_baseline": cpu,
             "clocks": clk,
         })
-        print(json.dumps(line), flush=True)
     for lay, _ in layers:
         lay.close()
     if peer is not None:
         peer.close()
+    return line
 
 
 # ------------------------------------------------------------- expert parallel
-def run_expert_parallel(job) -> None:
-    """N ranks, expert parallel over NCCL (see the module docstring)."""
+def run_expert_parallel(job) -> dict | None:
+    """N ranks, expert parallel (see the module docstring): the box batch of
+    configs[1] split over the ranks, then 64 tokens per rank."""
     import torch
 
-    from b200moe import ep, synth
+    from b200moe import ep, moe, synth
 
-    args, dev, rank, world, m = job.args, job.dev, job.rank, job.world, job.args.m
+    args, dev, rank, world = job.args, job.dev, job.rank, job.world
+    m_box = args.m
+    if m_box % world:
+        raise SystemExit(f"--m {m_box} must divide over {world} GPUs")
+    m_rank = m_box // world
     tier = np.zeros(E, np.int8)
     f4 = args.gemm == "fp4"
-    layer = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, tokens=m, tier=tier, device=dev,
+    layer = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, tokens=64, tier=tier, device=dev,
                                  exchange=args.exchange, gemm="fp4" if f4 else "skinny")
     n_local = int((layer.layer.fp4_slot >= 0).sum())
-    bank = synth.make_fp4_bank(n_local, H, I, "nvfp4", 1000 + rank, dev)
-    synth.load_bank(layer.layer, bank)
-    del bank
-    # each rank is home to its own tokens
-    g = torch.Generator(device=dev).manual_seed(1000 + m + 7919 * rank)
-    x = torch.randn((m, H), generator=g, device=dev).to(torch.bfloat16)
-    logits = torch.randn((m, E), generator=g, device=dev)
-    out = torch.empty((m, H), dtype=torch.float32, device=dev)
-    config = {"workload": f"configs[1] decode layer: hidden {H}, {E} experts NVFP4, inter {I}, top-{K_TOP}, M={m}, "
-                          f"expert parallel over {world} GPUs, {m} tokens per GPU",
-              "tokens_per_step": m * world, "experts_per_gpu": n_local, "format": "nvfp4",
-              "l2": "inputs larger than L2 (expert weights streamed per step)",
-              "launch": "one CUDA graph replay per step" if args.exchange == "p2p" and not args.eager else
-                        "eager" + (" (the exchange sizes come from a host read of the route counts)"
-                                   if args.exchange == "nccl" else ""),
-              "parallelism": f"expert parallel x{world} ("
-                             + ("NVLink peer-memory exchange kernels" if args.exchange == "p2p" else "NCCL all-to-all")
-                             + ")"}
+    synth.load_bank(layer.layer, synth.make_fp4_bank(n_local, H, I, "nvfp4", 1000 + rank, dev))
+    # the single-GPU layer with every expert (each rank's bank from its own seed): the parity reference
+    full = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, max_tokens=64, tier=tier, device=dev,
+                             prefill_gemm="fp4" if f4 else "skinny")
+    for r in range(world):
+        synth.load_bank(full, synth.make_fp4_bank(n_local, H, I, "nvfp4", 1000 + r, dev), slot_begin=r * n_local)
+        torch.cuda.empty_cache()
+    if not f4:
+        full.set_split_k(1, 1)
+        layer.layer.set_split_k(1, 1)
+    # strong: this rank's share of the configs[1] box batch; weak: 64 tokens of its own
+    g = torch.Generator(device=dev).manual_seed(1000 + m_box)
+    xb = torch.randn((m_box, H), generator=g, device=dev).to(torch.bfloat16)
+    lb = torch.randn((m_box, E), generator=g, device=dev)
+    x_s = xb[rank * m_rank:(rank + 1) * m_rank].contiguous()
+    l_s = lb[rank * m_rank:(rank + 1) * m_rank].contiguous()
+    g = torch.Generator(device=dev).manual_seed(1000 + 64 + 7919 * rank)
+    x_w = torch.randn((64, H), generator=g, device=dev).to(torch.bfloat16)
+    l_w = torch.randn((64, E), generator=g, device=dev)
+    out = torch.empty((64, H), dtype=torch.float32, device=dev)
 
-    def step():
+    def measure(x, logits, m, main):
+        def step():
+            ids, w = layer.route(logits)
+            return layer.forward(x, ids, w, out=out[:m])
+
+        # parity: bit-equal to the single-GPU layer on this rank's tokens
         ids, w = layer.route(logits)
-        return layer.forward(x, ids, w, out=out)
+        got = layer.forward(x, ids, w, out=out[:m]).clone()
+        want = full.forward(x, ids, w).clone()
+        layer.check_errors()
+        full.check_errors()
+        equal = bool(torch.equal(got, want))
+        err = float((got.double() - want.double()).norm() / want.double().norm())
+        all_equal = job.allok(equal)
+        err_max = job.maxall(err)
+        run, graph = graphed(step, args.exchange == "p2p" and not args.eager, args.warmup)
+        layer.check_errors()
+        ms, clk = job.timed(run, args.steps, clocks=main)
+        layer.check_errors()
+        del graph
+        # exposed exchange and the local W13 launch (separate pass: these read events every step)
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(7 if f4 else 5)]
+        i13 = 3 if f4 else 2
+        layer.layer.set_timing_events(evs)
+        comm, w13_ms, used = 0.0, 0.0, 0
+        n = max(5, args.steps // 4)
+        for _ in range(n):
+            step()
+            torch.cuda.synchronize()
+            comm += layer.comm_ms()
+            w13_ms += evs[i13].elapsed_time(evs[i13 + 1])
+            used += layer.local_experts_used()
+        layer.layer.set_timing_events(None)
+        comm, w13_ms, used = comm / n, w13_ms / n, used / n
+        pk = peaks()
+        w13_gbs = used * W13_BYTES / (w13_ms / 1e3) / 1e9
+        layer_gbs = used * EXPERT_BYTES / (ms / 1e3) / 1e9
+        res = {"value": world * m / (ms / 1e3), "ms_per_step": ms, "tokens_per_gpu": m,
+               "parity": {"bit_equal_to_single_gpu_layer": all_equal, "rel_l2_max_over_ranks": err_max,
+                          "reference": "the single-GPU layer holding every expert (same seeds, same "
+                                       + ("block-scaled FP4 path" if f4 else "GEMV path, split-K 1") +
+                                       "), on each rank's own tokens"},
+               "exposed_comm_ms": job.maxall(comm),
+               "per_gpu": {"local_distinct_experts": used, "w13_launch_ms": w13_ms, "w13_gbs": w13_gbs,
+                           "w13_frac": w13_gbs / pk["hbm_gbs"], "min_w13_frac_over_ranks":
+                               -job.maxall(-w13_gbs / pk["hbm_gbs"]),
+                           "layer_gbs_over_step": layer_gbs, "layer_frac_over_step": layer_gbs / pk["hbm_gbs"],
+                           "min_layer_frac_over_ranks": -job.maxall(-layer_gbs / pk["hbm_gbs"])},
+               "clocks": clk}
+        return res, step
 
-    run, graph = graphed(step, args.exchange == "p2p" and not args.eager, args.warmup)
-    layer.check_errors()
-    ms, clk = job.timed(run, args.steps)
-    layer.check_errors()
-    value = world * m / (ms / 1e3)
-    del graph
+    strong, _ = measure(x_s, l_s, m_rank, True)
+    weak, _ = measure(x_w, l_w, 64, False)
 
-    # exposed communication and the local W13 launch (separate pass: these read events every step)
-    # local expert run: start, convert, plan, [x planes], W13, [SwiGLU planes], W2
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(7 if f4 else 5)]
-    i13 = 3 if f4 else 2
-    layer.layer.set_timing_events(evs)
-    comm, w13_ms, used = 0.0, 0.0, 0
-    for _ in range(args.steps):
-        step()
-        torch.cuda.synchronize()
-        comm += layer.comm_ms()
-        w13_ms += evs[i13].elapsed_time(evs[i13 + 1])
-        used += layer.local_experts_used()
-    layer.layer.set_timing_events(None)
-    comm, w13_ms, used = comm / args.steps, w13_ms / args.steps, used / args.steps
-    comm_max = job.maxall(comm)
-    pk = peaks()
-    achieved = used * W13_BYTES / (w13_ms / 1e3) / 1e9
-    frac_min = -job.maxall(-achieved / pk["hbm_gbs"])
-
-    hx = x.cpu().pin_memory()
-    hl = logits.cpu().pin_memory()
-    hout = torch.empty((m, H), dtype=torch.float32).pin_memory()
-    dx, dl = torch.empty_like(x), torch.empty_like(logits)
+    # e2e of the strong run: pinned host x and logits in, output back, every step
+    hx = x_s.cpu().pin_memory()
+    hl = l_s.cpu().pin_memory()
+    hout = torch.empty((m_rank, H), dtype=torch.float32).pin_memory()
+    dx, dl = torch.empty_like(x_s), torch.empty_like(l_s)
 
     def e2e_step():
         dx.copy_(hx, non_blocking=True)
         dl.copy_(hl, non_blocking=True)
         ids2, w2 = layer.route(dl)
-        hout.copy_(layer.forward(dx, ids2, w2, out=out), non_blocking=True)
+        hout.copy_(layer.forward(dx, ids2, w2, out=out[:m_rank]), non_blocking=True)
 
     e2e_step()
     e2e_ms, _ = job.timed(e2e_step, args.steps, clocks=False)
     layer.check_errors()
+    full.close()
+    line = None
     if rank == 0:
-        line = line_base(job, args, "MoE-layer tokens/s (decode M=%d) & %% HBM roofline" % m, value, ms, config)
+        pk = peaks()
+        config = {"workload": f"configs[1] decode layer: hidden {H}, {E} experts NVFP4, inter {I}, top-{K_TOP}, "
+                              f"M={m_box} tokens per box, expert parallel over {world} GPUs ({m_rank} tokens per GPU)",
+                  "tokens_per_step": m_box, "experts_per_gpu": n_local, "format": "nvfp4",
+                  "l2": "inputs larger than L2 (expert weights streamed per step)",
+                  "launch": "one CUDA graph replay per step" if args.exchange == "p2p" and not args.eager else
+                            "eager" + (" (the exchange sizes come from a host read of the route counts)"
+                                       if args.exchange == "nccl" else ""),
+                  "parallelism": f"expert parallel x{world} ("
+                                 + ("NVLink peer-memory exchange kernels" if args.exchange == "p2p" else
+                                    "NCCL all-to-all") + ")"}
+        line = line_base(job, args, "MoE-layer tokens/s (decode M=%d) & %% HBM roofline" % m_box, strong["value"],
+                         strong["ms_per_step"], config, DTYPE_FP4 if f4 else DTYPE_GEMV)
+        line["scaling"] = "strong"
+        pg = strong["per_gpu"]
         line.update({
+            "parity": strong["parity"],
             "roofline": {"bound": "hbm", "kernel": ("fp4_gemm_kernel" if f4 else "gemv_kernel") +
                                                    " W13 (+SwiGLU) of rank 0's local experts",
-                         "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                         "frac": achieved / pk["hbm_gbs"], "min_frac_over_ranks": frac_min,
-                         "peak_source": pk["source"], "traffic": None,
-                         "algorithmic_bytes_per_launch": used * W13_BYTES, "distinct_local_experts": used,
-                         "launch_ms": w13_ms},
-            "exposed_comm_ms": comm_max,
-            "e2e": {"value": world * m / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                         "achieved": pg["w13_gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": pg["w13_frac"],
+                         "min_frac_over_ranks": pg["min_w13_frac_over_ranks"], "peak_source": pk["source"],
+                         "traffic": None, "algorithmic_bytes_per_launch": pg["local_distinct_experts"] * W13_BYTES,
+                         "launch_ms": pg["w13_launch_ms"]},
+            "per_gpu": pg,
+            "exposed_comm_ms": strong["exposed_comm_ms"],
+            "weak_scaling": dict(weak, note="64 tokens per GPU (the box batch grows with N); each GPU streams "
+                                            "fewer distinct experts as N grows, so this curve is not a "
+                                            "fixed-work scaling curve"),
+            "e2e": {"value": world * m_rank / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": int(hx.numel() * hx.element_size() + hl.numel() * hl.element_size()),
                     "d2h_bytes_per_step": int(hout.numel() * hout.element_size())},
-            # p2p: gating; owner plan, push, receive; local plan, W13, W2; return; combine
-            # nccl: gating; owner plan, row gather, metadata; local plan, W13, W2, f32->f16; combine
-            # (fp4: + the two plane launches of the local run)
+            # p2p: gating; push; local plan, W13, W2; return; combine (fp4: + the two plane launches of the
+            # local run, and the combine of the local rows); nccl: gating; dispatch, local run, f32->f16, combine
             "gpu_launches": (9 + (2 if f4 else 0)) * args.steps,
             "cpu_baseline": None,
-            "clocks": clk,
+            "clocks": strong["clocks"],
         })
-        print(json.dumps(line), flush=True)
     layer.close()
+    return line
 
 
 # ------------------------------------------------------------ reference arm
-def run_reference(job) -> None:
-    """The reference's CPU expert path (restated in C, oracle/cpu_moe.c) on the
-    workload's routing, all host threads; rank 0 only."""
+def run_reference(args) -> None:
+    """The reference's CPU expert path on the workload, rank 0 only (under
+    torchrun the other ranks exit at once; no process group is made).
+
+    The reference's own CPU kernel (harness/benchmarks/nvfp4_8r/cpu_mxfp4_moe.c,
+    AVX2 + OpenMP) is compiled from its source into oracle/_ref/ but has its
+    shapes fixed at hidden 5120 / TP slice 576 and reads MXFP4 only, so it
+    cannot run these configs; the timed value is this build's AVX2 restatement
+    of that kernel with parametric shapes and NVFP4 (oracle/cpu_moe.c,
+    ``oracle_expert_avx2``) on the workload's exact experts and routing, and
+    the reference's kernel is timed beside it at its own shape, per expert
+    slice and per weight byte (``reference_kernel``).  Nothing here loads the
+    product library: experts are packed by oracle/torch_quant.py (bit-equal to
+    the library's quantizers) from the same seeded weights, routing is the
+    oracle's gating, and the GPU (when present) only draws the seeded
+    weights with stock torch ops."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
     import torch
 
-    from b200moe import moe, synth
-
-    args, dev = job.args, job.dev
-    if job.rank != 0:
-        return
     from oracle import cpu_layer
+    from oracle import moe_oracle as mo
+    from oracle import torch_quant as tq
 
-    wl = args.workload
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))) if torch.cuda.is_available() \
+        else torch.device("cpu")
+    wl, n_exp = args.workload, args.experts
+    budget_s = 60.0  # the timed region of the whole run stays about a minute
+    iq_s, iq_what, iq_types = 0.0, "", (16, 16)
     if wl == "c3":
         T = args.tokens
-        tokens, fmt, bank = T, 1, synth.make_fp4_bank(E, H, I, "mxfp4", 3000, dev)
         g = torch.Generator(device=dev).manual_seed(3000 + T // 1024)
         x = torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
-        logits = torch.rand((T, E), generator=g, device=dev)
-        sample = 3
+        logits = torch.rand((T, E), generator=g, device=dev)[:, :n_exp]
+        tokens, fmt, seed, sample = T, "mxfp4", 3000, 3
         metric = "MoE-layer tokens/s (prefill T=%d) & %% tensor roofline" % T
-        workload = f"configs[3] prefill layer: hidden {H}, {E} experts MXFP4, inter {I}, top-{K_TOP}, T={T}"
+        workload = f"configs[3] prefill layer: hidden {H}, {n_exp} experts MXFP4, inter {I}, top-{K_TOP}, T={T}"
+        ids, w = mo.route(logits.cpu().numpy(), K_TOP)
+        hot_ids = None
+    elif wl in ("c2", "c4"):
+        from b200moe import synth, tiers
+
+        if wl == "c2":  # as run_c2: tier map seed 2, banks 2000 / 2001, logits seed 2000 + m, x seed 2032
+            m, seed_t, seed, seed_iq = args.m, 2, 2000, 2001
+        else:  # as run_c4's layer 0 at one GPU: tier map 4000, banks 4000 / 9000, logits 4000, x 4000
+            m, seed_t, seed, seed_iq = args.batch, 4000, 4000, 9000
+        tier, trank = tiers.zipf_tier(E, C2_HOT, seed=seed_t)
+        hot_mask = tier == tiers.HOT
+        alpha, share, logits = c2_alpha(lambda lg: mo.route(lg.cpu().numpy(), K_TOP)[0], hot_mask, trank, m, dev)
+        if wl == "c4":
+            logits = synth.zipf_logits(m, trank, alpha, 1.1, 4000, dev)
+        g = torch.Generator(device=dev).manual_seed(2032 if wl == "c2" else 4000)
+        x = torch.randn((m, H), generator=g, device=dev).to(torch.bfloat16)
+        ids, w = mo.route(logits.cpu().numpy(), K_TOP)
+        tokens, fmt, sample = m, "nvfp4", None
+        metric = ("MoE-layer tokens/s (mixed-tier decode M=%d) & %% HBM roofline" % m if wl == "c2" else
+                  f"MoE-stack tokens/s ({args.layers} layers, decode batch {m}) & % HBM roofline")
+        workload = (f"configs[2] mixed-tier decode layer: hidden {H}, {C2_HOT} NVFP4 + {E - C2_HOT} IQ2_XXS experts, "
+                    f"inter {I}, top-{K_TOP}, M={m}" if wl == "c2" else
+                    f"configs[4] {args.layers}-layer stack of configs[2] layers, decode batch {m} on one GPU (layer 0 "
+                    f"timed, x {args.layers})")
+        hot_ids = np.flatnonzero(hot_mask)
+        slot = np.cumsum(hot_mask) - 1
+        islot = np.cumsum(~hot_mask) - 1
+        used = np.unique(ids)
+        iq_used = used[~hot_mask[used]]
+        iq2 = synth.make_iq2_bank(E - C2_HOT, H, I, seed_iq, dev)
+        iq_s, iq_what = cpu_iq_part(lambda e: (iq2.w1[islot[e]].cpu().numpy(), iq2.w3[islot[e]].cpu().numpy(),
+                                               iq2.w2[islot[e]].cpu().numpy()),
+                                    iq_used, ids, x.float().cpu().numpy(), iq_types, 6)
+        del iq2
+        ids = np.where(hot_mask[ids], slot[ids], -1).astype(np.int32)  # NVFP4 routes, by bank slot
     else:
         m = args.m
-        tokens, fmt, bank = m, 0, synth.make_fp4_bank(E, H, I, "nvfp4", 1000, dev)
         g = torch.Generator(device=dev).manual_seed(1000 + m)
         x = torch.randn((m, H), generator=g, device=dev).to(torch.bfloat16)
-        logits = torch.randn((m, E), generator=g, device=dev)
-        sample = None
+        logits = torch.randn((m, E), generator=g, device=dev)[:, :n_exp]
+        tokens, fmt, seed, sample = m, "nvfp4", 1000, None
         metric = "MoE-layer tokens/s (decode M=%d) & %% HBM roofline" % m
-        workload = f"configs[1] decode layer: hidden {H}, {E} experts NVFP4, inter {I}, top-{K_TOP}, M={m}"
-        if wl == "c2":
-            workload += " (the reference arm times the all-NVFP4 layer: the IQ2 path has no C restatement)"
-    layer = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, max_tokens=64,
-                              tier=np.zeros(E, np.int8), device=dev)
-    ids, w = layer.route(logits)
-    ids_np, w_np = ids.cpu().numpy(), w.cpu().numpy()
+        workload = f"configs[1] decode layer: hidden {H}, {n_exp} experts NVFP4, inter {I}, top-{K_TOP}, M={m}"
+        ids, w = mo.route(logits.cpu().numpy(), K_TOP)
+        hot_ids = None
     x_np = x.float().cpu().numpy()
-    layer.close()
-    used = np.unique(ids_np)
+    used = np.unique(ids[ids >= 0])
+    n_bank = n_exp if hot_ids is None else hot_ids.size
     pick = used if sample is None else used[:sample]
-    experts = {int(e): fp4_expert(bank, int(e), fmt) for e in pick.tolist()}
-    del bank
-    cpu = cpu_layer.CpuMoe(H, I)
-    steps = args.steps if sample is None else max(1, args.steps // 50)
-    warm = args.warmup if sample is None else 1
-    for _ in range(warm):
-        cpu.forward(x_np, ids_np, w_np, experts, only=pick)
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        cpu.forward(x_np, ids_np, w_np, experts, only=pick)
-    dt = (time.perf_counter() - t0) / steps
-    layer_s = dt * ids_np.size / max(int(np.isin(ids_np, pick).sum()), 1)
+    experts = tq.fp4_expert_bank(n_bank, H, I, fmt, seed, dev, pick=pick)
+    cpu = cpu_layer.CpuMoe(H, I, avx2=True)
+    routes_all = int((ids >= 0).sum())
+
+    def layer_seconds(sel):
+        t0 = time.perf_counter()
+        cpu.forward(x_np, ids, w, experts, only=sel)
+        dt = time.perf_counter() - t0
+        return dt, dt * routes_all / max(int(np.isin(ids, sel).sum()), 1)
+
+    # one untimed pass sizes the sample so that --steps K fit the budget
+    warm_dt, _ = layer_seconds(pick)
+    steps = max(1, args.steps)
+    if warm_dt * steps > budget_s and pick.size > 1:
+        keep = max(1, int(pick.size * budget_s / (warm_dt * steps)))
+        pick = pick[:keep]
+    for _ in range(max(0, args.warmup - 1)):
+        layer_seconds(pick)
+    times = [layer_seconds(pick)[1] for _ in range(steps)]
+    fp4_s = float(np.mean(times))
+    layer_s = fp4_s + iq_s
+    if wl == "c4":
+        layer_s *= args.layers
     v = tokens / layer_s
-    what = "full layer" if sample is None else f"{pick.size} of {used.size} routed experts, scaled by routes"
-    line = {"impl": "reference", "metric": metric, "value": v, "unit": "tokens/s", "n_gpus": job.world,
-            "steps": steps, "warmup": warm, "ms_per_step": layer_s * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": workload},
+    what = (f"{pick.size} of {used.size} routed FP4 experts per step, scaled by routes" if pick.size < used.size
+            else f"all {used.size} routed FP4 experts")
+    if iq_what:
+        what += f"; IQ2_XXS: {iq_what} (numpy dequant + fp32 matmul), scaled by routes"
+    if wl == "c4":
+        what += f"; one layer x {args.layers}"
+
+    # the reference's own kernel at its fixed shape, beside the port at the same shape and rows
+    refk = None
+    rows_per_expert = max(1, int(round(routes_all / max(used.size, 1))))
+    if cpu_layer.REF_LIB.exists():
+        ref = cpu_layer.RefCpuExpert()
+        rng = np.random.default_rng(5)
+        rh, ri = ref.HIDDEN, ref.INTER
+        w13 = rng.normal(0, 0.02, (2 * ri, rh)).astype(np.float32)
+        w2 = rng.normal(0, 0.02, (rh, ri)).astype(np.float32)
+        c13, s13 = mo.mxfp4_quantize(w13)
+        c2, s2 = mo.mxfp4_quantize(w2)
+        rec = ref.record(c13, s13, c2, s2)
+        ex = dict(fmt=1, w13c=c13, w13s=s13, g13=np.ones(2, np.float32), w2c=c2, w2s=s2, g2=1.0)
+        mm = min(rows_per_expert, 16)
+        xr = rng.normal(0, 1, (mm, rh)).astype(np.float32)
+        rws = np.arange(mm, dtype=np.int32)
+        ww = np.ones(mm, np.float32)
+        port = cpu_layer.CpuMoe(rh, ri, avx2=True)
+        o = np.zeros((mm, rh), np.float32)
+
+        def clock(fn, n=30):
+            fn()
+            t0 = time.perf_counter()
+            for _ in range(n):
+                fn()
+            return (time.perf_counter() - t0) / n
+
+        t_ref = clock(lambda: ref.expert(rec, xr, rws, ww, o))
+        t_port = clock(lambda: port.expert(ex, xr, rws, ww, o))
+        weights = 3 * rh * ri
+        ours_weights = 3 * H * I
+        refk = {"kernel": "harness/benchmarks/nvfp4_8r/cpu_mxfp4_moe.c expert_slice, compiled from the reference's "
+                          "source into oracle/_ref/ with its own flags",
+                "shape": f"hidden {rh}, TP slice {ri}, MXFP4 record {rec.nbytes} B, {mm} rows (this workload's "
+                         "routes per routed expert, at most the kernel's 16)",
+                "us_per_expert_slice": t_ref * 1e6, "port_us_same_shape": t_port * 1e6,
+                "port_over_reference_time": t_port / t_ref,
+                "reference_gb_per_s_of_record": rec.nbytes / t_ref / 1e9,
+                "layer_estimate_tokens_per_s": tokens / (layer_s * (t_ref / t_port)),
+                "layer_estimate_note": f"the port's layer time scaled by the reference kernel's time over the port's "
+                                       f"on the same slice ({weights:,} weights; this config's experts have "
+                                       f"{ours_weights:,})",
+                "published_us_per_expert": 2953.7,
+                "published_source": "docs/measurements.md:1677 (the reference's host, V100 box)"}
+    line = {"impl": "reference", "metric": metric, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": layer_s * 1e3, "higher_is_better": True,
+            "scaling": "strong" if wl == "c4" else "weak", "vs_baseline": None,
+            "dtype": "f32 (activations f32, weights decoded from nvfp4/mxfp4 codes, f32 accumulate)",
+            "data": "synthetic (seeded; the same weights, inputs and routing as the product's run)",
+            "config": {"workload": workload, "tokens_per_step": tokens},
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cpu_layer.threads(), "kind": "port",
-                             "sample": f"{what}, {used.size} routed experts per step"},
+                             "sample": what},
+            "reference_kernel": refk,
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "note": "the reference's CPU expert path (harness/benchmarks/nvfp4_8r/cpu_mxfp4_moe.c) restated in C "
-                    "with parametric shapes (oracle/cpu_moe.c); its GPU kernels are V100-only and not in its "
-                    "source tree"}
+            "libraries_loaded": loaded_libraries(),
+            "note": "the reference's CPU expert path, restated with parametric shapes and NVFP4 (its own kernel "
+                    "is fixed at 5120/576 MXFP4 and is timed beside it under reference_kernel); the reference's "
+                    "GPU kernels are V100-only and not in its source tree"}
     print(json.dumps(line), flush=True)
 
 
 def main() -> None:
     args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
     job = Job(args)
     import __graft_entry__
 
     __graft_entry__.load_package()
-    if args.impl == "reference":
-        run_reference(job)
-    elif args.workload == "c4":
-        run_c4(job)
+    if args.workload == "c4":
+        line = run_c4(job)
     elif job.world > 1:
-        run_expert_parallel(job)
+        line = run_expert_parallel(job)
     elif args.workload == "c2":
-        run_c2(job)
+        line = run_c2(job)
     elif args.workload == "c3":
-        run_c3(job)
+        line = run_c3(job)
+    elif args.m == 64 and not args.profile:
+        line = run_default(job)
     else:
-        run_c1(job)
+        line = run_c1(job, args.m)
+    if job.rank == 0 and line is not None:
+        if "profile_run" not in line:
+            line["libraries_loaded"] = loaded_libraries()
+        print(json.dumps(line), flush=True)
     job.finish()
 
 

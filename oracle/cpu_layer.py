@@ -55,19 +55,26 @@ class CpuMoe:
     ``experts[e]`` = dict(fmt=0 (NVFP4) | 1 (MXFP4), w13c, w13s, g13 (2 floats),
     w2c, w2s, g2).  ``forward`` follows the reference's CPU layer loop
     (harness/benchmarks/nvfp4_8r/cpu_moe.py:43-51): one expert call per
-    distinct routed expert, rows and weights gathered from the routing."""
+    distinct routed expert, rows and weights gathered from the routing.
+    ``avx2`` picks the vectorised form (the timed baseline) over the scalar
+    checker; both run on ``threads()`` OpenMP threads."""
 
-    def __init__(self, hidden: int, inter: int, max_rows: int = 64):
+    def __init__(self, hidden: int, inter: int, max_rows: int = 64, avx2: bool = False):
         if not LIB.exists():
             build()
         self.dll = ctypes.CDLL(str(LIB))
-        self.dll.oracle_expert.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, P, P, P,
-                                           ctypes.c_float, P, P, P, ctypes.c_int, ctypes.c_float, P, P]
-        self.dll.oracle_expert.restype = None
+        args = [ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, P, P, P,
+                ctypes.c_float, P, P, P, ctypes.c_int, ctypes.c_float, P, P]
+        for name in ("oracle_expert", "oracle_expert_avx2"):
+            getattr(self.dll, name).argtypes = args
+            getattr(self.dll, name).restype = None
+        self.dll.oracle_set_threads.argtypes = [ctypes.c_int]
+        self.dll.oracle_set_threads(threads())
+        self._expert_fn = self.dll.oracle_expert_avx2 if avx2 else self.dll.oracle_expert
         self.dll.oracle_dequant.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P,
                                             ctypes.c_float, P]
         self.hidden, self.inter, self.max_rows = hidden, inter, max_rows
-        self.scratch = np.zeros(max_rows * (3 * inter + 2 * hidden), np.float32)
+        self.scratch = np.zeros(max_rows * (4 * inter + 3 * hidden), np.float32)
 
     def expert(self, ex: dict, x: np.ndarray, rows: np.ndarray, w: np.ndarray, out: np.ndarray,
                limit: float = 10.0) -> None:
@@ -76,7 +83,7 @@ class CpuMoe:
         g13 = np.ascontiguousarray(ex["g13"], np.float32)
         for s in range(0, rows.size, self.max_rows):
             r, ww = rows[s:s + self.max_rows], w[s:s + self.max_rows]
-            self.dll.oracle_expert(int(ex["fmt"]), self.hidden, self.inter, _ptr(ex["w13c"]),
+            self._expert_fn(int(ex["fmt"]), self.hidden, self.inter, _ptr(ex["w13c"]),
                                    _ptr(ex["w13s"]), _ptr(g13), _ptr(ex["w2c"]), _ptr(ex["w2s"]),
                                    float(ex["g2"]), _ptr(x), _ptr(r), _ptr(ww), int(r.size),
                                    float(limit), _ptr(out), _ptr(self.scratch))
@@ -133,4 +140,9 @@ class RefCpuExpert:
 
 
 def threads() -> int:
-    return int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    """Every host core this process may run on (its CPU affinity), whatever
+    OMP_NUM_THREADS says: torchrun sets that variable to 1."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1

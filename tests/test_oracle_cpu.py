@@ -30,14 +30,18 @@ def _expert(rng, fmt, hidden, inter, scale=0.02):
     return ex, deq
 
 
+@pytest.mark.parametrize("avx2", [False, True])
 @pytest.mark.parametrize("fmt", [0, 1])
-def test_c_oracle_matches_numpy_layer(fmt):
+def test_c_oracle_matches_numpy_layer(fmt, avx2):
+    """Both C forms (the scalar checker and the AVX2 timed baseline) against
+    the numpy oracle in fp64; m = 21 routes per expert crosses the AVX2 form's
+    8-row groups."""
     rng = np.random.default_rng(11 + fmt)
-    hidden, inter, e, k, m = 256, 128, 6, 3, 5
+    hidden, inter, e, k, m = 256, 128, 6, 3, 43
     experts = [_expert(rng, fmt, hidden, inter) for _ in range(e)]
     x = rng.normal(0, 1, (m, hidden)).astype(np.float32)
     ids, w = mo.route(rng.normal(0, 1, (m, e)).astype(np.float32), k)
-    cpu = cpu_layer.CpuMoe(hidden, inter)
+    cpu = cpu_layer.CpuMoe(hidden, inter, avx2=avx2)
     got = cpu.forward(x, ids, w, [ex for ex, _ in experts])
     want = mo.layer_forward(x, ids, w, lambda i: experts[i][1], dtype=np.float64)
     assert mo.rel_l2(got, want) < 1e-5
@@ -64,6 +68,16 @@ def test_c_oracle_matches_reference_cpu_kernel():
     w = np.array([0.5, 0.25, 0.125], np.float32)
     want = np.zeros((4, H), np.float32)
     ref.expert(rec, x, rows, w, want)
-    got = np.zeros((4, H), np.float32)
-    cpu_layer.CpuMoe(H, I).expert(ex, x, rows, w, got)
-    assert mo.rel_l2(got, want) < 1e-5
+    for avx2 in (False, True):
+        got = np.zeros((4, H), np.float32)
+        cpu_layer.CpuMoe(H, I, avx2=avx2).expert(ex, x, rows, w, got)
+        assert mo.rel_l2(got, want) < 1e-5
+
+
+def test_threads_follow_the_affinity_not_omp_num_threads(monkeypatch):
+    """torchrun sets OMP_NUM_THREADS=1; the CPU baseline still uses every core
+    the process may run on."""
+    import os
+
+    monkeypatch.setenv("OMP_NUM_THREADS", "1")
+    assert cpu_layer.threads() == len(os.sched_getaffinity(0))

@@ -213,3 +213,31 @@ def test_iq_formats_vs_gguf(ggml_type):
     ref = dequantize(blocks.reshape(96, -1), Q.IQ2_XS if ggml_type == 17 else Q.IQ1_M).astype(np.float32)
     assert np.array_equal(mine.view(np.uint32), ref.reshape(mine.shape).view(np.uint32))
     assert np.abs(mine).mean() > 1e-3
+
+
+def test_torch_quantizers_match_the_oracle_bit_for_bit():
+    """oracle/torch_quant.py (the reference arm's packer, stock torch ops) =
+    moe_oracle's quantizers, on seeded data with zero blocks, a zero row,
+    binade edges, subnormal-range scales and E4M3 saturation."""
+    import torch
+
+    from oracle import torch_quant as tq
+
+    rng = np.random.default_rng(77)
+    cases = [rng.normal(0, 0.02, (64, 512)).astype(np.float32),
+             (rng.normal(0, 1, (16, 256)) * np.exp2(rng.integers(-30, 10, (16, 1)))).astype(np.float32),
+             rng.standard_cauchy((8, 256)).astype(np.float32)]
+    edge = rng.normal(0, 1e-3, (8, 256)).astype(np.float32)
+    edge[0] = 0.0
+    edge[1, :32] = 0.0
+    edge[2, :16] = np.float32(6.0) * np.exp2(np.arange(16) - 8).astype(np.float32)
+    edge[3, 5] = 1e4  # one huge element: the other blocks' E4M3 scales fall into the subnormal range
+    cases.append(edge)
+    for w in cases:
+        c, s, g = mo.nvfp4_quantize(w)
+        tc, ts, tg = tq.nvfp4_quantize(torch.from_numpy(w))
+        assert np.array_equal(tc.numpy(), c) and np.array_equal(ts.numpy(), s)
+        assert np.float32(tg.item()).view(np.uint32) == np.float32(g).view(np.uint32)
+        c, s = mo.mxfp4_quantize(w)
+        tc, ts = tq.mxfp4_quantize(torch.from_numpy(w))
+        assert np.array_equal(tc.numpy(), c) and np.array_equal(ts.numpy(), s)
