@@ -208,6 +208,34 @@ class Clocks:
                 "samples": len(self.samples), "source": "nvml, polled every 2 ms during the timed region"}
 
 
+# ------------------------------------------------------------------ tensor peaks
+PEAK_KINDS = {0: ("kind::f16 (f16 x f16, N 256)", 100000), 1: ("kind::f8f6f4 (E4M3 x E4M3, N 256)", 100000),
+              2: ("kind::mxf4nvf4 block16 (E2M1, UE4M3 per 16, N 128)", 200000),
+              3: ("kind::mxf4nvf4 block32 (E2M1, UE8M0 per 32, N 128)", 200000),
+              4: ("kind::f16 (f16 x f16, N 128)", 200000)}
+
+
+def tensor_peaks(dev) -> dict:
+    """Dense tcgen05 throughput of this GPU per MMA kind (b200moe_mma_peak: one
+    CTA per SM, back-to-back MMAs on shared-memory operands, ~40 ms each), with
+    the SM clocks seen while they ran."""
+    import ctypes
+
+    from b200moe import _lib
+
+    out = {}
+    clk = Clocks(dev)
+    for kind, (name, iters) in PEAK_KINDS.items():
+        tf, ms = ctypes.c_float(), ctypes.c_float()
+        _lib.check("b200moe_mma_peak", _lib.lib().b200moe_mma_peak(dev.index, kind, iters, ctypes.byref(tf),
+                                                                   ctypes.byref(ms)))
+        out[name] = {"tflops": float(tf.value), "ms": float(ms.value)}
+    out["clocks"] = clk.stop()
+    out["how"] = ("tcgen05.mma, M 128, one CTA per SM (148), operands in shared memory, "
+                  "csrc/peak.cu; dense FLOPs = 2 M N K per MMA")
+    return out
+
+
 # ------------------------------------------------------------------ parity
 def torch_ref():
     sys.path.insert(0, str(ROOT / "tests"))
@@ -872,6 +900,7 @@ def run_default(job) -> dict:
     if args.no_also or args.experts != E:
         layer.close()
         return line
+    line["tensor_peaks"] = tensor_peaks(job.dev)
     also = []
     for m in (1, 8, 32):
         also.append(compact(run_c1(job, m, layer, bank, main=False)))

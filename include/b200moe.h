@@ -292,6 +292,15 @@ int b200moe_ep_received(b200moe_ep* ep, void* stream, int32_t* n, int32_t* exper
 int b200moe_forward_rows(b200moe_layer* layer, void* stream, const void* rows, const int32_t* expert_ids,
                          const int32_t* n_valid, const int32_t* row_range, int max_rows, void* y2);
 
+/* Dense tensor-core throughput of `device`, measured.  No counterpart in the
+ * reference (its tensor path is V100 mma.sync): the roofline denominators of
+ * this build's kernels.  kind 0 tcgen05.mma kind::f16 (N 256), 1 kind::f8f6f4
+ * E4M3 (N 256), 2 kind::mxf4nvf4 block16 UE4M3 (N 128), 3 kind::mxf4nvf4
+ * block32 UE8M0 (N 128), 4 kind::f16 (N 128); M 128, one CTA per SM issuing
+ * `iters` x 4 MMAs on shared-memory operands.  *tflops = dense FLOP/s / 1e12,
+ * *ms = the timed launch. */
+int b200moe_mma_peak(int device, int kind, int iters, float* tflops, float* ms);
+
 /* fp32 -> fp16 copy of n values (n % 4 == 0), round to nearest. */
 int b200moe_f32_to_f16(void* stream, const float* x, int64_t n, void* y);
 

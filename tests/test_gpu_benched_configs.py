@@ -164,3 +164,22 @@ def test_c3_prefill_at_bench_shape(dev, pkg):
     finally:
         layer.close()
         torch.cuda.empty_cache()
+
+
+def test_tensor_peak_microbenchmark(dev, pkg):
+    """b200moe_mma_peak runs every MMA kind the kernels use and reports a
+    throughput in the range of a B200 (the pool's cuBLAS bf16 burst is ~1.6
+    PFLOP/s dense; FP8 about twice, FP4 about four times that)."""
+    import ctypes
+
+    from b200moe import _lib
+
+    got = {}
+    for kind in range(5):
+        tf, ms = ctypes.c_float(), ctypes.c_float()
+        _lib.check("b200moe_mma_peak", _lib.lib().b200moe_mma_peak(0, kind, 20000, ctypes.byref(tf),
+                                                                   ctypes.byref(ms)))
+        assert ms.value > 0
+        got[kind] = tf.value
+    assert 500 < got[0] < 3000, got
+    assert got[1] > 1.3 * got[0] and got[2] > 1.3 * got[1], got

@@ -90,6 +90,7 @@ SIGNATURES = {
     "b200moe_ep_received": ([P, P, P, P, I32], I32),
     "b200moe_forward_rows": ([P, P, P, P, P, P, I32, P], I32),
     "b200moe_f32_to_f16": ([P, P, ctypes.c_int64, P], I32),
+    "b200moe_mma_peak": ([I32, I32, I32, ctypes.POINTER(F32), ctypes.POINTER(F32)], I32),
 }
 
 _LIB: ctypes.CDLL | None = None
