@@ -1168,7 +1168,7 @@ def run_expert_parallel(job) -> dict | None:
         for _ in range(n):
             step()
             torch.cuda.synchronize()
-            comm += layer.comm_ms()
+            comm += layer.comm_ms()  # push, the receive wait in the owner's plan launch, return, combine
             w13_ms += evs[i13].elapsed_time(evs[i13 + 1])
             used += layer.local_experts_used()
         layer.layer.set_timing_events(None)

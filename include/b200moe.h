@@ -259,10 +259,11 @@ int b200moe_ep_combine(void* stream, const void* y2, const int32_t* route_pos, c
  * exchange object whose shared buffers all ranks map through CUDA IPC:
  * create -> ipc_handle (64 bytes) -> exchange the handles among the ranks on
  * the host -> connect (world x 64 bytes, rank order).  A step, on every rank
- * in the same order: ep_push (owner plan of this rank's T*k routes, rows and
- * expert ids stored into the owners' buffers), b200moe_forward_rows of the
- * local top-1 layer on the buffers of ep_recv_buffers, ep_return (y2 rows
- * back to their home ranks), ep_combine_p2p (slot-order combine + residual).
+ * in the same order: ep_push (each of this rank's T*k routes reserves a row in
+ * its owner's buffer and stores its fp16 row and expert id there; no rank
+ * waits for another), ep_forward (the local top-1 layer on the rows received:
+ * its first launch waits for every rank's push), ep_return (y2 rows back to
+ * their home ranks), ep_combine_p2p (slot-order combine + residual).
  * Waits are bounded (B200MOE_ERR_TIMEOUT through ep_check_errors).  All ranks
  * must be alive at destroy (call it after a host barrier).  No reference
  * counterpart: the reference refuses expert parallelism
@@ -276,6 +277,11 @@ int b200moe_ep_recv_buffers(b200moe_ep* ep, void** rows, int32_t** expert_ids, i
                             int32_t** row_range, void** y2, int* max_rows);
 int b200moe_ep_push(b200moe_ep* ep, void* stream, const void* x, int x_dtype, const int32_t* topk_ids, int T,
                     int k, int num_experts, const int32_t* owner_of_expert);
+/* The local experts of a top-1 layer (its owner map = this rank's experts) on
+ * the rows this step brought in: waits (bounded) for every rank's push, then
+ * b200moe_forward_rows on the receive buffers; y2 rows stay local for
+ * ep_return. */
+int b200moe_ep_forward(b200moe_ep* ep, b200moe_layer* layer, void* stream);
 int b200moe_ep_return(b200moe_ep* ep, void* stream);
 int b200moe_ep_combine_p2p(b200moe_ep* ep, void* stream, const int32_t* topk_ids, const float* topk_weights,
                            int T, int k, int num_experts, const int32_t* owner_of_expert, const float* residual,

@@ -6,8 +6,8 @@
 // one device allocation that all ranks map through CUDA IPC (cudaMalloc +
 // cudaIpcOpenMemHandle; no multicast object):
 //
-//   mbox     int32: counts[src][dst] (every rank writes its row into every
-//            rank's mbox), then per source rank count_flag, data_flag, ret_flag
+//   mbox     int32: per source rank data_flag and ret_flag ([2][world]), then
+//            two row-reservation counters (one per epoch parity)
 //   eid      int32 [R_cap]: expert id of each received route
 //   home     int32 [R_cap]: (home rank << 24) | route index at home
 //   rows     fp16 [R_cap][H]: received activation rows, R_cap = world * S_max
@@ -15,18 +15,25 @@
 //
 // One step (all ranks, same order; flags carry a per-step epoch kept on the
 // device, so no host value changes between steps):
-//   push:    publish this rank's per-owner counts into every mbox, wait for
-//            all ranks' counts, then store each route's f16 row, expert id and
-//            home into its owner's buffers at an offset fixed by the counts
-//            of the lower ranks; the last CTA raises data_flag on every rank;
-//   recv:    wait for every rank's data_flag; rows received = column sum;
-//   (the owner runs its experts on the received rows: b200moe_forward_rows)
+//   push:    a warp per route reserves a row in its owner's buffer with one
+//            system-scope atomic on the owner's counter of this epoch (no rank
+//            waits for another's counts), stores the route's f16 row, expert
+//            id and home there; the last CTA raises data_flag on every rank;
+//   (the owner runs its experts on the received rows: b200moe_ep_forward,
+//   whose route-plan launch first waits for every rank's data_flag and takes
+//   the rows received from the counter, resetting both counters)
 //   return:  store each received route's y2 row into its home rank's y2home;
 //            the last CTA raises ret_flag on every rank;
 //   combine: wait for every rank's ret_flag, then out[t] = residual[t] + the
 //            slot-order sum of fma(f32(y2), w) -- the single-GPU combine.
-// Flags are written with st.release.sys after a system fence and read with
-// ld.acquire.sys; every wait is bounded by kWaitLimitNs and sets kErrTimeout.
+// A rank pushes step s + 1 only after its combine of step s saw every owner's
+// return, which each owner raises after its plan of step s read and reset the
+// counters: no reservation of step s + 1 can land before that reset.  Rows
+// land in reservation order, which varies from run to run; every route's row
+// is computed on its own (top-1 rows, per-column MMA sums), so the results do
+// not depend on it.  Flags are written with st.release.sys after a system
+// fence and read with ld.acquire.sys; every wait is bounded by kWaitLimitNs and
+// sets kErrTimeout.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -49,7 +56,7 @@ struct EpP2P {
   const int32_t* ids;
   const int32_t* perm;
   const int32_t* owner;
-  const int32_t* send_counts;
+  int r_cap;  // rows of every rank's receive buffer
   uint8_t* peer[kEpMaxWorld];
   size_t off_mbox, off_eid, off_home, off_rows, off_y2home;
   int* epoch;    // local: epoch of the step in flight (advanced by push)
@@ -62,8 +69,11 @@ __device__ __forceinline__ int* mbox_of(const EpP2P& a, int r) {
   return reinterpret_cast<int*>(a.peer[r] + a.off_mbox);
 }
 
-// The last CTA to finish raises flag slot `which` (0 count, 1 data, 2 ret) for
-// this rank on every rank.
+// mbox words: data flags [0, W), return flags [W, 2W), reservation counters [2W, 2W + 2)
+__device__ __forceinline__ int* resv_of(const EpP2P& a, int r, int e) { return mbox_of(a, r) + 2 * a.world + (e & 1); }
+
+// The last CTA to finish raises flag slot `which` (0 data, 1 ret) for this
+// rank on every rank.
 __device__ __forceinline__ void last_cta_signal(const EpP2P& a, int which, int e, bool advance_epoch) {
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -71,7 +81,7 @@ __device__ __forceinline__ void last_cta_signal(const EpP2P& a, int which, int e
     if (atomicAdd(a.done, 1) == int(gridDim.x) - 1) {
       __threadfence_system();
       const int W = a.world;
-      for (int r = 0; r < W; ++r) st_release_sys(mbox_of(a, r) + W * W + which * W + a.rank, e);
+      for (int r = 0; r < W; ++r) st_release_sys(mbox_of(a, r) + which * W + a.rank, e);
       *a.done = 0;
       if (advance_epoch) *a.epoch = e;
     }
@@ -79,89 +89,60 @@ __device__ __forceinline__ void last_cta_signal(const EpP2P& a, int which, int e
 }
 
 __global__ void __launch_bounds__(256) ep_push_kernel(const EpP2P a) {
-  __shared__ int s_sb[kEpMaxWorld + 1], s_off[kEpMaxWorld], s_ok;
   const int W = a.world;
   const int e = *a.epoch + 1;
-  int* mine = mbox_of(a, a.rank);
-  // every CTA publishes the same counts (no CTA waits on another CTA of this grid)
-  if (threadIdx.x < W) {
-    int* mb = mbox_of(a, threadIdx.x);
-    for (int j = 0; j < W; ++j) mb[a.rank * W + j] = a.send_counts[j];
-    __threadfence_system();
-    st_release_sys(mb + W * W + a.rank, e);
-  }
-  if (threadIdx.x == 0) {
-    s_ok = wait_flags(mine + W * W, W, e, a.err);
-    int run = 0;
-    for (int j = 0; j < W; ++j) {
-      s_sb[j] = run;
-      run += a.send_counts[j];
+  // one warp per route: its owner and row reserved once, then the row's 16-byte
+  // pieces (H / 8 of them) four at a time per lane
+  const int lane = threadIdx.x & 31;
+  const int warps = int(gridDim.x * blockDim.x) >> 5;
+  const int chunks = a.H / 8;
+  for (int route = int(blockIdx.x * blockDim.x + threadIdx.x) >> 5; route < a.S; route += warps) {
+    const int id = a.ids[route];
+    const int dst = (id >= 0 && id < a.num_experts) ? a.owner[id] : -1;
+    if (dst < 0 || dst >= W) {  // no owner: never sent, contributes 0 in the combine
+      if (lane == 0) set_error(a.err, kErrBounds);
+      continue;
     }
-    s_sb[W] = run;
-    for (int dst = 0; dst < W; ++dst) {
-      int off = 0;
-      for (int src = 0; src < a.rank; ++src) off += ld_acquire_sys(mine + src * W + dst);
-      s_off[dst] = off;
+    int row = 0;
+    if (lane == 0) row = atomicAdd_system(resv_of(a, dst, e), 1);
+    row = __shfl_sync(0xffffffffu, row, 0);
+    if (row >= a.r_cap) {
+      if (lane == 0) set_error(a.err, kErrRange);
+      continue;
     }
-  }
-  __syncthreads();
-  if (s_ok) {
-    // one warp per route: its owner, row and source looked up once, then the
-    // row's 16-byte pieces (H / 8 of them) four at a time per lane
-    const int lane = threadIdx.x & 31;
-    const int warps = int(gridDim.x * blockDim.x) >> 5;
-    const int chunks = a.H / 8;
-    for (int p = int(blockIdx.x * blockDim.x + threadIdx.x) >> 5; p < s_sb[W]; p += warps) {
-      int dst = 0;
-      while (dst + 1 < W && s_sb[dst + 1] <= p) ++dst;
-      const int row = s_off[dst] + (p - s_sb[dst]);
-      const int route = a.perm[p];
-      const uint16_t* src = static_cast<const uint16_t*>(a.x) + int64_t(route / a.k) * a.H;
-      uint8_t* base = a.peer[dst];
-      uint4* drow = reinterpret_cast<uint4*>(base + a.off_rows + int64_t(row) * a.H * 2);
-      for (int c0 = lane; c0 < chunks; c0 += 32 * 4) {
-        uint4 v[4];
+    const uint16_t* src = static_cast<const uint16_t*>(a.x) + int64_t(route / a.k) * a.H;
+    uint8_t* base = a.peer[dst];
+    uint4* drow = reinterpret_cast<uint4*>(base + a.off_rows + int64_t(row) * a.H * 2);
+    for (int c0 = lane; c0 < chunks; c0 += 32 * 4) {
+      uint4 v[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int c = c0 + 32 * u;
-          if (c < chunks) v[u] = *reinterpret_cast<const uint4*>(src + 8 * c);
-        }
+      for (int u = 0; u < 4; ++u) {
+        const int c = c0 + 32 * u;
+        if (c < chunks) v[u] = *reinterpret_cast<const uint4*>(src + 8 * c);
+      }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int c = c0 + 32 * u;
-          if (c >= chunks) continue;
-          if (a.x_bf16) {
-            const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-            uint32_t o[4];
+      for (int u = 0; u < 4; ++u) {
+        const int c = c0 + 32 * u;
+        if (c >= chunks) continue;
+        if (a.x_bf16) {
+          const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+          uint32_t o[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const __half2 h = __floats2half2_rn(__uint_as_float(w[j] << 16), __uint_as_float(w[j] & 0xFFFF0000u));
-              o[j] = *reinterpret_cast<const uint32_t*>(&h);
-            }
-            v[u] = make_uint4(o[0], o[1], o[2], o[3]);
+          for (int j = 0; j < 4; ++j) {
+            const __half2 h = __floats2half2_rn(__uint_as_float(w[j] << 16), __uint_as_float(w[j] & 0xFFFF0000u));
+            o[j] = *reinterpret_cast<const uint32_t*>(&h);
           }
-          drow[c] = v[u];
+          v[u] = make_uint4(o[0], o[1], o[2], o[3]);
         }
-      }
-      if (lane == 0) {
-        reinterpret_cast<int*>(base + a.off_eid)[row] = a.ids[route];
-        reinterpret_cast<int*>(base + a.off_home)[row] = (a.rank << 24) | route;
+        drow[c] = v[u];
       }
     }
+    if (lane == 0) {
+      reinterpret_cast<int*>(base + a.off_eid)[row] = id;
+      reinterpret_cast<int*>(base + a.off_home)[row] = (a.rank << 24) | route;
+    }
   }
-  last_cta_signal(a, 1, e, true);
-}
-
-__global__ void ep_recv_kernel(const EpP2P a) {
-  if (threadIdx.x != 0) return;
-  const int W = a.world, e = *a.epoch;
-  int* mine = mbox_of(a, a.rank);
-  int n = 0;
-  if (wait_flags(mine + W * W + W, W, e, a.err))
-    for (int src = 0; src < W; ++src) n += ld_acquire_sys(mine + src * W + a.rank);
-  a.recv[0] = n;
-  a.recv[1] = 0;
-  a.recv[2] = n;
+  last_cta_signal(a, 0, e, true);
 }
 
 __global__ void __launch_bounds__(256) ep_return_kernel(const EpP2P a, const __half* __restrict__ y2) {
@@ -191,14 +172,14 @@ __global__ void __launch_bounds__(256) ep_return_kernel(const EpP2P a, const __h
         if (c0 + 32 * u < chunks) drow[c0 + 32 * u] = v[u];
     }
   }
-  last_cta_signal(a, 2, e, false);
+  last_cta_signal(a, 1, e, false);
 }
 
 __global__ void __launch_bounds__(256) ep_combine_p2p_kernel(const EpP2P a, const float* __restrict__ w, int T,
                                                            const float* __restrict__ residual, float* __restrict__ out) {
   __shared__ int s_ok;
   const int W = a.world, e = *a.epoch;
-  if (threadIdx.x == 0) s_ok = wait_flags(mbox_of(a, a.rank) + W * W + 2 * W, W, e, a.err);
+  if (threadIdx.x == 0) s_ok = wait_flags(mbox_of(a, a.rank) + W, W, e, a.err);
   __syncthreads();
   if (!s_ok) return;
   const __half* y2 = reinterpret_cast<const __half*>(a.peer[a.rank] + a.off_y2home);
@@ -245,10 +226,6 @@ struct b200moe_ep {
   uint8_t* peer[kEpMaxWorld] = {};
   bool opened[kEpMaxWorld] = {};
   // local (not shared)
-  int32_t* perm = nullptr;
-  Chunk* chunks = nullptr;
-  int32_t* n_chunks = nullptr;
-  int32_t* send_counts = nullptr;
   int* epoch = nullptr;
   int* done = nullptr;
   int32_t* recv = nullptr;
@@ -277,8 +254,7 @@ struct EpDeviceGuard {
 void ep_free(b200moe_ep* E) {
   for (int r = 0; r < kEpMaxWorld; ++r)
     if (E->opened[r]) cudaIpcCloseMemHandle(E->peer[r]);
-  void* ptrs[] = {E->shared, E->perm, E->chunks, E->n_chunks, E->send_counts, E->epoch, E->done, E->recv, E->err,
-                  E->y2};
+  void* ptrs[] = {E->shared, E->epoch, E->done, E->recv, E->err, E->y2};
   for (void* p : ptrs)
     if (p) cudaFree(p);
 }
@@ -288,6 +264,7 @@ EpP2P ep_args(const b200moe_ep* E) {
   a.world = E->world;
   a.rank = E->rank;
   a.H = E->H;
+  a.r_cap = E->r_cap;
   for (int r = 0; r < E->world; ++r) a.peer[r] = E->peer[r];
   a.off_mbox = E->off_mbox;
   a.off_eid = E->off_eid;
@@ -331,7 +308,7 @@ int b200moe_ep_create(int device, int world, int rank, int hidden, int max_route
   E->grid = prop.multiProcessorCount;
   size_t o = 0;
   E->off_mbox = o;
-  o += up256(size_t(world * world + 3 * world) * 4);
+  o += up256(size_t(2 * world + 2) * 4);
   E->off_eid = o;
   o += up256(size_t(E->r_cap) * 4);
   E->off_home = o;
@@ -342,9 +319,6 @@ int b200moe_ep_create(int device, int world, int rank, int hidden, int max_route
   o += up256(size_t(max_routes) * hidden * 2);
   E->shared_bytes = o;
   bool ok = cudaMalloc(&E->shared, o) == cudaSuccess &&
-            cudaMalloc(&E->perm, size_t(max_routes) * 4) == cudaSuccess &&
-            cudaMalloc(&E->chunks, size_t(max_routes + world + 1) * sizeof(Chunk)) == cudaSuccess &&
-            cudaMalloc(&E->n_chunks, 8) == cudaSuccess && cudaMalloc(&E->send_counts, 4 * kEpMaxWorld) == cudaSuccess &&
             cudaMalloc(&E->epoch, 4) == cudaSuccess && cudaMalloc(&E->done, 4) == cudaSuccess &&
             cudaMalloc(&E->recv, 16) == cudaSuccess && cudaMalloc(&E->err, 4) == cudaSuccess &&
             cudaMalloc(&E->y2, size_t(E->r_cap) * hidden * 2) == cudaSuccess;
@@ -410,7 +384,8 @@ int b200moe_ep_recv_buffers(b200moe_ep* E, void** rows, int32_t** expert_ids, in
   return B200MOE_OK;
 }
 
-// Owner-rank plan of this rank's T*k routes, then push and receive (two launches after the plan).
+// Store this rank's T*k routes into their owners' buffers (one launch; the
+// owners' b200moe_ep_forward waits for every rank's push).
 int b200moe_ep_push(b200moe_ep* E, void* stream, const void* x, int x_dtype, const int32_t* ids, int T, int k,
                     int num_experts, const int32_t* owner_of_expert) {
   if (!E || !x || !ids || !owner_of_expert || T < 1 || k < 1 || num_experts < E->world) return B200MOE_ERR_INVALID_ARG;
@@ -421,23 +396,6 @@ int b200moe_ep_push(b200moe_ep* E, void* stream, const void* x, int x_dtype, con
   EpDeviceGuard guard(E->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int S = T * k;
-  PlanArgs p{};
-  p.ids = ids;
-  p.n = S;
-  p.num_experts = num_experts;
-  p.key_of_expert = owner_of_expert;  // key = owner rank
-  p.n_keys = E->world;
-  p.perm = E->perm;
-  p.n_banks = 1;
-  p.key_lo[0] = 0;
-  p.key_hi[0] = E->world;
-  p.rc[0] = S;
-  p.max_chunks[0] = S + E->world;
-  p.chunks[0] = E->chunks;
-  p.n_chunks = E->n_chunks;
-  p.key_counts = E->send_counts;
-  p.err = E->err;
-  if (launch_plan(s, p)) return B200MOE_ERR_CUDA;
   EpP2P a = ep_args(E);
   a.k = k;
   a.S = S;
@@ -445,14 +403,34 @@ int b200moe_ep_push(b200moe_ep* E, void* stream, const void* x, int x_dtype, con
   a.x = x;
   a.x_bf16 = x_dtype == B200MOE_BF16;
   a.ids = ids;
-  a.perm = E->perm;
   a.owner = owner_of_expert;
-  a.send_counts = E->send_counts;
   const int blocks = std::min(std::max((S + 7) / 8, 1), E->grid * 2);  // a warp per route
   ep_push_kernel<<<blocks, 256, 0, s>>>(a);
-  ep_recv_kernel<<<1, 32, 0, s>>>(a);
   return cudaGetLastError() == cudaSuccess ? B200MOE_OK : B200MOE_ERR_CUDA;
 }
+
+}  // extern "C"
+
+// What b200moe_ep_forward's route plan needs to receive a step: the data flags
+// of every rank (this rank's mbox), the epoch, the reservation counters and the
+// receive count it writes.
+int b200moe::ep_recv_wait(const b200moe_ep* E, EpRecvWait* w) {
+  if (!E || !w || !connected(E)) return B200MOE_ERR_STATE;
+  int* mbox = reinterpret_cast<int*>(E->shared + E->off_mbox);
+  w->flags = mbox;
+  w->n_flags = E->world;
+  w->epoch = E->epoch;
+  w->resv = mbox + 2 * E->world;
+  w->out = E->recv;
+  w->rows = E->shared + E->off_rows;
+  w->expert_ids = reinterpret_cast<const int32_t*>(E->shared + E->off_eid);
+  w->y2 = E->y2;
+  w->max_rows = E->r_cap;
+  w->device = E->device;
+  return B200MOE_OK;
+}
+
+extern "C" {
 
 // Return the local experts' y2 rows (the buffer of b200moe_ep_recv_buffers) to their home ranks.
 int b200moe_ep_return(b200moe_ep* E, void* stream) {

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+struct b200moe_ep;  // the expert-parallel exchange object of the C ABI (ep_p2p.cu)
+
 namespace b200moe {
 
 // Activation rows staged per GEMV stage: a chunk holds 16 / ks routes.
@@ -46,10 +48,27 @@ struct KsModel {
   float tiles[2], kdim[2];         // tile pairs and K of W13 and W2
 };
 
+// Expert-parallel receive of one step (ep_p2p.cu): the route plan of the
+// owner's forward waits until every rank's data flag reaches *epoch, takes the
+// rows received from the reservation counter of that epoch and resets both.
+struct EpRecvWait {
+  const int* flags;  // [n_flags] data flags of the source ranks
+  int n_flags;
+  const int* epoch;  // the step in flight
+  int* resv;         // [2] reservation counters (by epoch parity)
+  int32_t* out;      // [3]: rows received, then {0, rows}
+  const void* rows;  // fp16 [max_rows][H] received rows
+  const int32_t* expert_ids;
+  void* y2;          // fp16 [max_rows][H] local y2 rows
+  int max_rows;
+  int device;
+};
+
 struct PlanArgs {
   const int32_t* ids;  // [n] expert id per route (flat t*k + slot)
   int n;
   const int32_t* n_valid;  // optional (device): routes of this call, <= n
+  EpRecvWait recv;         // optional (recv.flags set): wait for an expert-parallel receive first
   int num_experts;
   // product keys: key_of_expert[e] in [0, n_keys) or -1 (not on this GPU / invalid)
   const int32_t* key_of_expert;
@@ -135,6 +154,8 @@ int launch_fp4_tile(cudaStream_t s, bool mx, const uint8_t* codes, const uint8_t
 int make_u8_tile_map(void* map_out, const void* base, int64_t rows, int64_t row_bytes, int box_bytes, int box_rows);
 
 size_t plan_smem_bytes(int n_keys);
+// the receive of this rank's expert-parallel exchange object (the C ABI's b200moe_ep)
+int ep_recv_wait(const ::b200moe_ep* E, EpRecvWait* w);
 // fp16 rows -> int8 blocks of kIq2XBlockBytes per 256-wide K tile (IQ2 activations)
 int launch_quant_s8(cudaStream_t s, const __half* src, int64_t src_stride, int K, int rows, const int32_t* range,
                     uint8_t* dst);

@@ -211,7 +211,7 @@ struct Marks {
 
 int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const void* x, int x_dtype,
                 const int32_t* ids, const float* w, float* out, int m, bool prefill = false,
-                const RowsMode* rows = nullptr) {
+                const RowsMode* rows = nullptr, const EpRecvWait* recv = nullptr) {
   const auto& c = L->cfg;
   Marks marks{L, s};
   if (!L->maps_set) return B200MOE_ERR_STATE;
@@ -238,11 +238,14 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
     xsrc = ws.x16;
   }
   marks.mark();  // after the bf16 conversion (or none): the event layout does not depend on x's dtype
-  if (c.n_iq2 > 0) {  // int8 blocks of the token rows for the IQ2 bank's W13
-    if (launch_quant_s8(s, xsrc, c.hidden, c.hidden, m, rows ? rows->row_range : nullptr, ws.xq))
-      return B200MOE_ERR_CUDA;
+  // int8 blocks of the token rows for the IQ2 bank's W13 (in rows mode after the plan, which may be the
+  // launch that learns how many rows this call has)
+  auto quant_rows = [&]() {
+    if (launch_quant_s8(s, xsrc, c.hidden, c.hidden, m, rows ? rows->row_range : nullptr, ws.xq)) return false;
     marks.mark();
-  }
+    return true;
+  };
+  if (c.n_iq2 > 0 && !rows && !quant_rows()) return B200MOE_ERR_CUDA;
   // prefill with the tcgen05 GEMM: the FP4 bank's chunks are 128-route token tiles
   // (NVFP4 weight units of the block-scaled layout feed the tcgen05 GEMM too: long prefills run there)
   const bool tc_units = c.prefill_gemm == 2 && S >= kTcUnitsMinRoutes;
@@ -261,6 +264,7 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   p.ids = ids;
   p.n = S;
   p.n_valid = rows ? rows->n_valid : nullptr;
+  if (recv) p.recv = *recv;
   p.num_experts = c.num_experts;
   p.key_of_expert = L->key_of_expert;
   p.n_keys = c.n_fp4 + c.n_iq2;
@@ -291,6 +295,7 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   p.err = L->err;
   if (launch_plan(s, p)) return B200MOE_ERR_CUDA;
   marks.mark();
+  if (c.n_iq2 > 0 && rows && !quant_rows()) return B200MOE_ERR_CUDA;
   if (tc) {
     if (launch_gather_rows(s, x, x_dtype == B200MOE_BF16, ws.perm, S, c.top_k, c.hidden, L->xperm))
       return B200MOE_ERR_CUDA;
@@ -737,6 +742,17 @@ int b200moe_forward_rows(b200moe_layer* L, void* stream, const void* rows, const
   RowsMode rm{n_valid, row_range, static_cast<__half*>(y2)};
   return run_forward(L, layer_workspace(L), static_cast<cudaStream_t>(stream), rows, B200MOE_F16, expert_ids,
                      nullptr, nullptr, max_rows, true, &rm);
+}
+
+int b200moe_ep_forward(b200moe_ep* ep, b200moe_layer* L, void* stream) {
+  if (!ep || !L) return B200MOE_ERR_INVALID_ARG;
+  EpRecvWait w{};
+  if (int st = ep_recv_wait(ep, &w)) return st;
+  if (w.device != L->device || L->cfg.top_k != 1 || w.max_rows > L->t_max) return B200MOE_ERR_INVALID_ARG;
+  DeviceGuard guard(L->device);
+  RowsMode rm{w.out, w.out + 1, static_cast<__half*>(w.y2)};
+  return run_forward(L, layer_workspace(L), static_cast<cudaStream_t>(stream), w.rows, B200MOE_F16, w.expert_ids,
+                     nullptr, nullptr, w.max_rows, true, &rm, &w);
 }
 
 int b200moe_check_errors(b200moe_layer* L, void* stream, uint32_t* bits) {

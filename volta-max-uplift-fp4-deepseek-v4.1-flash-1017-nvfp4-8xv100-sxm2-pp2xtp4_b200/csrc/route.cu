@@ -219,8 +219,32 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanArgs a) {
   int* start = hist + 32 * nk;  // [nk]
   int* aux = start + nk;        // [nk]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ int s_recv;
+  if (a.recv.flags) {
+    // expert-parallel receive: every source rank's rows are in once its data
+    // flag reaches this step's epoch; the rows received are the reservation
+    // counter of that epoch, then both counters start again from zero (no rank
+    // reserves rows of the next step before this step's return reached it)
+    if (tid == 0) {
+      const int e = *a.recv.epoch;
+      int n_in = 0;
+      if (wait_flags(a.recv.flags, a.recv.n_flags, e, a.err)) {
+        n_in = atomicExch(a.recv.resv + (e & 1), 0);
+        atomicExch(a.recv.resv + ((e + 1) & 1), 0);
+        if (n_in > a.n) {
+          set_error(a.err, kErrRange);
+          n_in = a.n;
+        }
+      }
+      a.recv.out[0] = n_in;
+      a.recv.out[1] = 0;
+      a.recv.out[2] = n_in;
+      s_recv = n_in;
+    }
+    __syncthreads();
+  }
   // a.n_valid (device) bounds the routes of this call below the launch's a.n
-  const int n = a.n_valid ? min(a.n, max(0, *a.n_valid)) : a.n;
+  const int n = a.recv.flags ? s_recv : a.n_valid ? min(a.n, max(0, *a.n_valid)) : a.n;
   // routes past this call's count have no position (a stale one would send their rows' planes into a live
   // route's place)
   if (a.inv)

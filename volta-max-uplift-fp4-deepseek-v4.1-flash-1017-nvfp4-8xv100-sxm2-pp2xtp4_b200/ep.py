@@ -9,14 +9,15 @@ Two exchanges, the same arithmetic (per rank: its own T tokens, all ranks
 call in the same order):
 
 ``exchange="p2p"`` (default): the library's own kernels over NVLink peer
-memory (CUDA IPC, no multicast): ``b200moe_ep_push`` sorts this rank's routes
-by owner and stores each route's fp16 row and expert id straight into its
-owner's receive buffer; the owner runs its experts on what it received
-(``b200moe_forward_rows``, top-1, y2 rows out); ``b200moe_ep_return`` stores
-the y2 rows back into their home ranks; ``b200moe_ep_combine_p2p`` sums them
-per token in slot order and adds the residual.  Counts, offsets and the
-hand-offs live on the device (bounded flag waits), so a step needs no host
-sync and can be captured in a CUDA graph.
+memory (CUDA IPC, no multicast): ``b200moe_ep_push`` stores each route's fp16
+row and expert id straight into its owner's receive buffer, at a row the
+route reserves with one atomic on the owner's counter (no rank waits for
+another's counts); the owner runs its experts on what it received
+(``b200moe_ep_forward``: top-1 rows, y2 rows out; its first launch waits for
+every rank's push); ``b200moe_ep_return`` stores the y2 rows back into their
+home ranks; ``b200moe_ep_combine_p2p`` sums them per token in slot order and
+adds the residual.  Counts and hand-offs live on the device (bounded flag
+waits), so a step needs no host sync and can be captured in a CUDA graph.
 
 ``exchange="nccl"``: ``b200moe_ep_dispatch`` + one host read of the counts +
 NCCL all-to-all out and back + ``b200moe_ep_combine``.
@@ -181,6 +182,8 @@ class ExpertParallelMoe:
         i32 = dict(dtype=torch.int32, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         self._ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        self._plan_ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]  # start, convert, plan
+        self._last_plan_events = []
         self._timed = False
         self.last_routes_in = 0
         self._peer, self._own_peer = None, False
@@ -282,8 +285,15 @@ class ExpertParallelMoe:
                                                         self.num_experts, self.owner.data_ptr()))
         if timed:
             ev[1].record()
-        _lib.check("b200moe_forward_rows", L.b200moe_forward_rows(
-            self.layer._h, st, pe.rows, pe.eids, pe.n_valid, pe.row_range, pe.max_rows, pe.y2))
+        # the receive wait sits in the forward's first launch (the route plan): time that launch too
+        user_events = list(getattr(self.layer, "_timing_events", []) or [])
+        plan_events = user_events if len(user_events) >= 3 else (self._plan_ev if timed else [])
+        if timed and plan_events is self._plan_ev:
+            self.layer.set_timing_events(self._plan_ev)
+        _lib.check("b200moe_ep_forward", L.b200moe_ep_forward(pe.handle, self.layer._h, st))
+        if timed and plan_events is self._plan_ev:
+            self.layer.set_timing_events(user_events or None)
+        self._last_plan_events = plan_events if timed else []
         if timed:
             ev[2].record()
         _lib.check("b200moe_ep_return", L.b200moe_ep_return(pe.handle, st))
@@ -309,13 +319,18 @@ class ExpertParallelMoe:
 
     def comm_ms(self) -> float:
         """Exchange time of the last forward (NCCL: counts + rows + ids out, y2
-        back; p2p: push + receive, return + combine, waits for the slower
-        ranks included); waits for those events."""
+        back; p2p: push, the owner's route-plan launch that waits for every
+        rank's push, return + combine; waits for the slower ranks included);
+        waits for those events."""
         if not self._timed:
             return 0.0
         ev = self._ev
         ev[3].synchronize()
-        return ev[0].elapsed_time(ev[1]) + ev[2].elapsed_time(ev[3])
+        t = ev[0].elapsed_time(ev[1]) + ev[2].elapsed_time(ev[3])
+        pe = self._last_plan_events
+        if self.exchange == "p2p" and len(pe) >= 3:
+            t += pe[1].elapsed_time(pe[2])
+        return t
 
     def check_errors(self) -> None:
         """Synchronize; raise if the dispatch (a route id without an owner), the
