@@ -120,10 +120,11 @@ def parse():
                     help="c4 over N > 1 GPUs: experts by id range, or tiers.balanced_owners on the expected routes")
     ap.add_argument("--iq-types", default="16,16",
                     help="c2: GGML types of the IQ experts' gate/up and down (16 IQ2_XXS, 17 IQ2_XS, 29 IQ1_M)")
-    ap.add_argument("--gemm", choices=["fp4", "gemv"], default="fp4",
-                    help="c1, c2, c4: the FP4 bank on the block-scaled FP4 tensor path (tcgen05.mma "
-                         "kind::mxf4nvf4, default) or on the skinny GEMV; c3: the tcgen05 prefill GEMM reading "
-                         "the block-scaled layout's weight units (default) or the decode bank's units")
+    ap.add_argument("--gemm", choices=["fp4", "fp4-bs", "gemv"], default="fp4",
+                    help="the FP4 bank on the block-scaled FP4 tensor path (tcgen05.mma kind::mxf4nvf4, default; "
+                         "c3: the tcgen05 f16 GEMM over the same weight units), fp4-bs (c3: the block-scaled kernel "
+                         "with 32-route chunks) or gemv (decode: the skinny GEMV; c3: the tcgen05 f16 GEMM over the "
+                         "decode bank's units)")
     ap.add_argument("--profile", action="store_true",
                     help="warm-up + timed steps only (no per-launch, e2e or CPU passes): the ncu command")
     a = ap.parse_args()
@@ -215,15 +216,20 @@ PEAK_KINDS = {0: ("kind::f16 (f16 x f16, N 256)", 100000), 1: ("kind::f8f6f4 (E4
               4: ("kind::f16 (f16 x f16, N 128)", 200000)}
 
 
+_PEAKS: dict = {}
+
+
 def tensor_peaks(dev) -> dict:
     """Dense tcgen05 throughput of this GPU per MMA kind (b200moe_mma_peak: one
-    CTA per SM, back-to-back MMAs on shared-memory operands, ~40 ms each), with
-    the SM clocks seen while they ran."""
+    CTA per SM, back-to-back MMAs on shared-memory operands, ~30 ms each), with
+    the SM clocks seen while they ran; measured once per process."""
     import ctypes
 
     from b200moe import _lib
 
-    out = {}
+    if _PEAKS:
+        return _PEAKS
+    out = _PEAKS
     clk = Clocks(dev)
     for kind, (name, iters) in PEAK_KINDS.items():
         tf, ms = ctypes.c_float(), ctypes.c_float()
@@ -536,7 +542,7 @@ def run_c1(job, m: int, layer=None, bank=None, main: bool = True) -> dict:
 
     args, dev = job.args, job.dev
     use_graph = not args.eager
-    f4 = args.gemm == "fp4"
+    f4 = args.gemm != "gemv"
     n_exp = args.experts
     rotations = 8 if m == 1 else 1
     own = layer is None
@@ -656,7 +662,7 @@ def run_c2(job, main: bool = True) -> dict:
 
     args, dev, m = job.args, job.dev, (job.args.m if main else 32)
     tier, tier_rank = tiers.zipf_tier(E, C2_HOT, seed=2)
-    f4 = args.gemm == "fp4"
+    f4 = args.gemm != "gemv"
     iq_types = tuple(int(t) for t in args.iq_types.split(",")) if main else (16, 16)
     layer = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, max_tokens=64, tier=tier, device=dev,
                               prefill_gemm="fp4" if f4 else "tcgen05", iq_types=iq_types)
@@ -781,10 +787,11 @@ def run_c3(job, main: bool = True) -> dict:
     from b200moe import moe, synth
 
     args, dev, T = job.args, job.dev, (job.args.tokens if main else 4096)
-    units = args.gemm == "fp4"  # the block-scaled layout's weight units also feed the tcgen05 prefill GEMM
+    mode = {"fp4": "fp4", "fp4-bs": "fp4-bs", "gemv": "tcgen05"}[args.gemm]
+    bs = mode == "fp4-bs"  # every launch on the block-scaled kernel (32-route chunks)
     layer = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, max_tokens=8,
                               tier=np.zeros(E, np.int8), fp4_format="mxfp4", device=dev, max_prefill_tokens=T,
-                              prefill_gemm="fp4" if units else "tcgen05")
+                              prefill_gemm=mode)
     bank = synth.make_fp4_bank(E, H, I, "mxfp4", 3000, dev)
     synth.load_bank(layer, bank)
     layer.check_errors()
@@ -802,9 +809,12 @@ def run_c3(job, main: bool = True) -> dict:
         return {"profile_run": True, "workload": "c3", "tokens": T}
     config = {"workload": f"configs[3] prefill layer: hidden {H}, {E} experts MXFP4, inter {I}, top-{K_TOP}, T={T}",
               "tokens_per_step": T, "format": "mxfp4",
-              "gemm": "tcgen05 grouped GEMM (kind::f16, TMEM accumulators) on " +
-                      ("the weight units of the block-scaled layout (one bulk copy per 256-K unit, per-row dequant)"
-                       if units else "the decode bank's units"),
+              "gemm": ("block-scaled tcgen05 grouped GEMM (kind::mxf4nvf4.block32: E2M1 weights read as stored, "
+                       "activations as four E2M1 planes with UE8M0 scales, 32 routes x 4 planes per MMA N, one "
+                       "TMEM accumulator per item)" if bs else
+                       "tcgen05 grouped GEMM (kind::f16, TMEM accumulators) on " +
+                       ("the weight units of the block-scaled layout (one bulk copy per 256-K unit, per-row dequant)"
+                        if mode == "fp4" else "the decode bank's units")),
               "l2": "inputs larger than L2 (all 384 experts, 5.1 GB, streamed per step)",
               "parallelism": "single GPU"}
 
@@ -824,16 +834,26 @@ def run_c3(job, main: bool = True) -> dict:
     steps = max(3, args.steps // 10)
     ms, clk = job.timed(step, steps)
     layer.check_errors()
-    per = per_launch(layer, [step], steps, 7)  # convert, plan, gather, W13, W2, combine
+    if bs:  # start, convert, plan, x planes, W13, SwiGLU planes, W2, combine
+        per = per_launch(layer, [step], steps, 8)
+        names = ["convert", "plan", "x_planes", "w13", "swiglu_planes", "w2", "combine"]
+        t13, t2 = float(per[3]), float(per[5])
+    else:  # start, convert, plan, gather, W13, W2, combine
+        per = per_launch(layer, [step], steps, 7)
+        names = ["convert", "plan", "gather", "w13", "w2", "combine"]
+        t13, t2 = float(per[3]), float(per[4])
     pk = peaks()
+    tp = tensor_peaks(dev)
+    fp4_peak = tp["kind::mxf4nvf4 block32 (E2M1, UE8M0 per 32, N 128)"]["tflops"]
+    f16_peak = tp["kind::f16 (f16 x f16, N 256)"]["tflops"]
+    mma_peak = fp4_peak if bs else f16_peak
     routes = T * K_TOP
     f13, f2 = 2.0 * routes * H * 2 * I, 2.0 * routes * I * H
-    t13, t2 = float(per[3]), float(per[4])
     ach = f13 / (t13 / 1e3) / 1e12
     layer_flops = f13 + f2
     layer_bytes = distinct * (MX_W13_BYTES + MX_W2_BYTES)
     layer_ms = float(per.sum())
-    bound_ms = max(layer_bytes / pk["hbm_gbs"] / 1e6, layer_flops / pk["bf16_tflops"] / 1e9)
+    bound_ms = max(layer_bytes / pk["hbm_gbs"] / 1e6, layer_flops / mma_peak / 1e9)
 
     hx = x.cpu().pin_memory()
     hl = logits.cpu().pin_memory()
@@ -853,27 +873,34 @@ def run_c3(job, main: bool = True) -> dict:
         cpu = cpu_fp4_layer(lambda e: fp4_expert(bank, e, 1), ids.cpu().numpy(), w.cpu().numpy(),
                             x.float().cpu().numpy(), T, sample_experts=3, reps=1)
     line = line_base(job, args, "MoE-layer tokens/s (prefill T=%d) & %% tensor roofline" % T, T / (ms / 1e3), ms,
-                     config, "f16 activations x mxfp4 weights dequantized to f16 on the SM, f32 accumulate",
-                     steps=steps)
+                     config, "e2m1x4 activations (UE8M0 block scales) x mxfp4 weights, f32 accumulate" if bs else
+                     "f16 activations x mxfp4 weights dequantized to f16 on the SM, f32 accumulate", steps=steps)
     line.update({
         "parity": par,
-        "roofline": {"bound": "tensor", "kernel": "tcgen05 grouped GEMM W13 (+SwiGLU)", "achieved": ach,
-                     "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": ach / pk["bf16_tflops"],
-                     "peak_source": pk["source"] + " bf16 dense (the MMAs are kind::f16 on dequantized weights)",
+        "roofline": {"bound": "tensor", "kernel": ("fp4_gemm_kernel (block-scaled, 32-route chunks)" if bs else
+                                                   "tcgen05 grouped GEMM") + " W13 (+SwiGLU)",
+                     "achieved": ach, "peak": mma_peak, "unit": "TFLOP/s", "frac": ach / mma_peak,
+                     "peak_source": "this run's tcgen05 microbenchmark (b200moe_mma_peak) of the MMA kind the "
+                                    "kernel issues: " + ("kind::mxf4nvf4 (dense FP4); the four activation planes "
+                                                         "make the MMAs 4x the algorithmic FLOPs" if bs else
+                                                         "kind::f16 (the MMAs run on dequantized weights)"),
+                     "frac_of_measured_bf16_cublas": ach / pk["bf16_tflops"],
+                     "frac_of_dense_fp4_peak": ach / fp4_peak,
                      "traffic": None, "algorithmic_flops_per_launch": f13, "launch_ms": t13},
         "layer_roofline": {"flops": layer_flops, "bytes": layer_bytes, "ms": layer_ms,
                            "tflops": layer_flops / (layer_ms / 1e3) / 1e12,
-                           "tensor_frac": layer_flops / (layer_ms / 1e3) / 1e12 / pk["bf16_tflops"],
+                           "tensor_frac": layer_flops / (layer_ms / 1e3) / 1e12 / mma_peak,
                            "hbm_frac": layer_bytes / (layer_ms / 1e3) / 1e9 / pk["hbm_gbs"],
                            "binding_bound_ms": bound_ms, "frac_of_binding_bound": bound_ms / layer_ms,
-                           "launch_ms": {"convert": float(per[0]), "plan": float(per[1]),
-                                         "gather": float(per[2]), "w13": t13, "w2": t2,
-                                         "combine": float(per[5])}},
+                           "binding_bound": "max(distinct expert bytes / measured HBM, FLOPs / measured peak of "
+                                            "the MMA kind)",
+                           "launch_ms": {k: float(v) for k, v in zip(names, per)}},
         "e2e": {"value": T / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": int(hx.numel() * 2 + hl.numel() * 4),
                 "d2h_bytes_per_step": int(hout.numel() * 4)},
-        # gating, [bf16 copy], plan, row gather (converts bf16 itself), W13, W2, combine
-        "gpu_launches": (6 if units else 7) * steps,
+        # block-scaled: gating, plan, x planes (read bf16 x), W13, SwiGLU planes, W2, combine;
+        # f16 GEMM: gating, [bf16 copy], plan, row gather (converts bf16 itself), W13, W2, combine
+        "gpu_launches": (7 if bs else 6 if mode == "fp4" else 7) * steps,
         "cpu_baseline": cpu,
         "clocks": clk,
     })
@@ -894,7 +921,7 @@ def run_default(job) -> dict:
     import torch
 
     args = job.args
-    f4 = args.gemm == "fp4"
+    f4 = args.gemm != "gemv"
     layer, bank = c1_layer(job, args.experts, f4)
     line = run_c1(job, 64, layer, bank, main=True)
     if args.no_also or args.experts != E:
@@ -942,11 +969,11 @@ def run_c4(job) -> dict:
         if world == 1:
             lay = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, max_tokens=min(T, 64),
                                     max_prefill_tokens=T, tier=tier, device=dev,
-                                    prefill_gemm="fp4" if args.gemm == "fp4" else "skinny")
+                                    prefill_gemm="fp4" if args.gemm != "gemv" else "skinny")
             local = lay
         else:
             lay = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, tokens=T, tier=tier,
-                                       device=dev, peer=peer, gemm="fp4" if args.gemm == "fp4" else "skinny",
+                                       device=dev, peer=peer, gemm="fp4" if args.gemm != "gemv" else "skinny",
                                        owner=owner)
             local = lay.layer
         n_hot, n_iq = int((local.fp4_slot >= 0).sum()), int((local.iq2_slot >= 0).sum())
@@ -1021,9 +1048,9 @@ def run_c4(job) -> dict:
         local = lay if world == 1 else lay.layer
         banks = int((local.fp4_slot >= 0).any()) + int((local.iq2_slot >= 0).any())
         launches_per_step += 1 + 2 * banks + (3 if world == 1 else 2) + (5 if world > 1 else 0)
-        if world == 1 and (args.gemm == "fp4" or T * K_TOP > 32):  # the combine launch
+        if world == 1 and (args.gemm != "gemv" or T * K_TOP > 32):  # the combine launch
             launches_per_step += 1
-        if args.gemm == "fp4" and (local.fp4_slot >= 0).any():  # x and SwiGLU planes
+        if args.gemm != "gemv" and (local.fp4_slot >= 0).any():  # x and SwiGLU planes
             launches_per_step += 2
     pk = peaks()
     achieved = local_bytes / (ms / 1e3) / 1e9
@@ -1076,12 +1103,12 @@ def run_c4(job) -> dict:
                   "parallelism": f"expert parallel x{world} (NVLink peer-memory exchange kernels)" if world > 1
                                  else "single GPU"}
         line = line_base(job, args, f"MoE-stack tokens/s ({n_layers} layers, decode batch {batch}) & % HBM roofline",
-                         value, ms, config, "nvfp4 bank: " + (DTYPE_FP4 if args.gemm == "fp4" else DTYPE_GEMV) +
+                         value, ms, config, "nvfp4 bank: " + (DTYPE_FP4 if args.gemm != "gemv" else DTYPE_GEMV) +
                          "; IQ bank: two int8 activation planes x int8 codebook weights", steps=steps)
         line["scaling"] = "strong"
         line.update({
             "roofline": {"bound": "hbm", "kernel": "all expert launches of the stack on rank 0 (whole step: " +
-                         ("fp4_gemm_kernel for the NVFP4 bank, gemv_kernel for IQ2)" if args.gemm == "fp4" else
+                         ("fp4_gemm_kernel for the NVFP4 bank, gemv_kernel for IQ2)" if args.gemm != "gemv" else
                           "gemv_kernel for both banks)"),
                          "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / pk["hbm_gbs"], "min_frac_over_ranks": frac_min,
@@ -1114,7 +1141,7 @@ def run_expert_parallel(job) -> dict | None:
         raise SystemExit(f"--m {m_box} must divide over {world} GPUs")
     m_rank = m_box // world
     tier = np.zeros(E, np.int8)
-    f4 = args.gemm == "fp4"
+    f4 = args.gemm != "gemv"
     layer = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, tokens=64, tier=tier, device=dev,
                                  exchange=args.exchange, gemm="fp4" if f4 else "skinny")
     n_local = int((layer.layer.fp4_slot >= 0).sum())

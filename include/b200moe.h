@@ -84,12 +84,15 @@ typedef struct {
   int32_t prefill_gemm;       /* FP4 bank kernels: 0 = the skinny decode kernels for every call,
                                  1 = forward_prefill on the tcgen05 grouped GEMM (f16 dequantized
                                  weight tiles, route tiles of 128), decode on the skinny kernels,
-                                 2 = hidden and inter multiples of 256: decode and short prefills
-                                 on the block-scaled FP4 tensor cores (tcgen05.mma.kind::mxf4nvf4
-                                 with the format's block scales in TMEM: E4M3 per 16 or E8M0 per
-                                 32; activations as four E2M1 planes, ~1e-4 relative), prefills of
-                                 >= 4096 routes on the tcgen05 f16 GEMM; both read the bank as
-                                 swizzled weight units; the fastest layout for decode and prefill */
+                                 2 = hidden and inter multiples of 256: decode and prefills below
+                                 4096 routes on the block-scaled FP4 tensor cores
+                                 (tcgen05.mma.kind::mxf4nvf4 with the format's block scales in
+                                 TMEM: E4M3 per 16 or E8M0 per 32; activations as four E2M1
+                                 planes, ~1e-4 relative), longer prefills on the tcgen05 f16
+                                 GEMM; both read the bank as swizzled weight units; the fastest
+                                 layout for decode and prefill,
+                                 3 = the layout of 2 with every call on the block-scaled kernel
+                                 (32-route chunks from 4096 routes; slower for long prefills) */
   int32_t iq_type13;          /* GGML type of bank 1's gate/up (W1, W3): 16 IQ2_XXS (0 = 16),
                                  17 IQ2_XS, 29 IQ1_M -- the routed-expert types GGUF layers mix,
                                  engine/.../experts/nvfp4_8r_tiers.py:35 */

@@ -418,6 +418,34 @@ def test_block_scaled_fp4_path(dev, pkg, m, mixed, fmt):
     layer.close()
 
 
+@pytest.mark.parametrize("gemm,fmt", [("fp4-bs", "nvfp4"), ("fp4-bs", "mxfp4"), ("fp4", "nvfp4")])
+def test_long_prefill_on_the_weight_units(dev, pkg, gemm, fmt):
+    """Prefills of >= 4096 routes of a block-scaled layer: "fp4-bs" runs them
+    on the block-scaled kernel with 32-route chunks (one accumulator buffer,
+    the epilogue in slices of four routes); "fp4" on the tcgen05 f16 GEMM over
+    the same weight units.  Both against the fp32 dequant reference, on a
+    skewed mixed-tier routing (experts with 1 to ~100 routes: full, partial
+    and single-route chunks)."""
+    from b200moe import tiers
+
+    H, I, E, K, m = 2048, 1024, 64, 8, 700
+    tier = tiers.zipf_tier(E, 40, seed=9)[0]
+    layer, dequant, _, _ = _make_layer(dev, H, I, E, K, 64, fmt=fmt, tier=tier, seed=19, max_prefill=m, gemm=gemm)
+    g = torch.Generator(device=dev).manual_seed(190)
+    x = torch.randn((m, H), generator=g, device=dev).to(torch.bfloat16)
+    logits = torch.randn((m, E), generator=g, device=dev)
+    logits[:, :8] += 2.0  # a few popular experts: chunks of 32 and partial ones
+    ids, w = layer.route(logits)
+    out = layer.forward_prefill(x, ids, w).clone()
+    layer.check_errors()
+    err = tr.rel_l2(out, tr.layer_forward(x, ids.long(), w, dequant))
+    assert err < 2e-3, err
+    again = layer.forward_prefill(x, ids, w)
+    layer.check_errors()
+    assert torch.equal(again, out)
+    layer.close()
+
+
 def test_prefill_and_apply(dev, pkg):
     from b200moe import moe
 

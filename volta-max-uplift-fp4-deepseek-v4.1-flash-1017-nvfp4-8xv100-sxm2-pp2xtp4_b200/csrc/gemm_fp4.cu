@@ -81,8 +81,13 @@ struct Fp4Stage {
   static constexpr int kStages = TILES == 2 ? 4 : 7;
   static constexpr uint32_t kSfCols = TILES == 2 ? 48 : 32;  // tile 0 (, tile 1), activations: 16 each
   static constexpr uint32_t kSfB = TILES == 2 ? 32 : 16;
+  // accumulator columns of one item (TILES x N) and how many items' accumulators TMEM holds below the
+  // scale columns: two (the epilogue of one item overlaps the next item's MMAs) up to N = 64, one at N = 128
+  static constexpr uint32_t kAccCols = uint32_t(TILES * kN);
+  static constexpr int kAccBufs = 2 * kAccCols <= kSfCol ? 2 : 1;
   static constexpr size_t kSmem = 1024 + size_t(kStages) * kBytes + 64 * 8;
   static_assert(kBytes % 1024 == 0, "128-byte swizzled tiles need 1024-byte aligned stages");
+  static_assert(kAccBufs * kAccCols <= kSfCol, "accumulators below the scale columns");
   static_assert(kSfCol + kStages * kSfCols <= kTmemCols, "TMEM columns");
   static_assert(kSmem <= 227 * 1024, "shared memory");
 };
@@ -254,13 +259,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Chunk ch = next;
         next = chunk_of_item(item + gridDim.x);
         if (!item_ok(ch)) continue;
-        const uint32_t b = acc_i & 1u, bph = (acc_i >> 1) & 1u;
+        const uint32_t b = St::kAccBufs == 2 ? (acc_i & 1u) : 0u;
+        const uint32_t bph = St::kAccBufs == 2 ? ((acc_i >> 1) & 1u) : (acc_i & 1u);
         if (*abort_ptr || !mbar_wait(&acc_empty[b], bph ^ 1u, a.err)) {
           *abort_ptr = 1;
           break;
         }
         fence_after();
-        const uint32_t dg = tmem + b * 128, du = dg + 64;
+        const uint32_t dg = tmem + b * St::kAccCols, du = dg + kN;
         bool ok = true;
         for (int kt = 0; kt < n_kt; ++kt, ++g) {
           const int s = g % kStages;
@@ -320,7 +326,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         gx_l = __ldg(a.gx + ch.begin + lane);
         if (EPI == 1) route_l = a.perm[ch.begin + lane];
       }
-      const uint32_t b = acc_i & 1u, bph = (acc_i >> 1) & 1u;
+      const uint32_t b = St::kAccBufs == 2 ? (acc_i & 1u) : 0u;
+      const uint32_t bph = St::kAccBufs == 2 ? ((acc_i >> 1) & 1u) : (acc_i & 1u);
       bool ok = !*abort_ptr && mbar_wait(&acc_full[b], bph, a.err);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) {
@@ -329,12 +336,59 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_after();
       const uint32_t lanes = uint32_t(quarter * 32) << 16;
+      if constexpr (kN > 64) {
+        // one accumulator buffer: read it four routes (16 columns per tile) at a time and hand it back to
+        // the MMA thread as soon as the last slice is in registers
+        const uint32_t acc0 = tmem + lanes + b * St::kAccCols;
+        const int n_slices = (ch.count + 3) / 4;
+        for (int sl = 0; sl < n_slices; ++sl) {
+          float s0[16], s1[16];
+          tmem_ld16(acc0 + sl * 16, s0);
+          tmem_ld16(acc0 + kN + sl * 16, s1);  // up / second tile
+          if (sl == n_slices - 1) {
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[b]);
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int n = sl * 4 + j;
+            if (n >= ch.count) break;
+            float v0 = 0.f, v1 = 0.f;
+#pragma unroll
+            for (int p = 0; p < kP; ++p) {
+              v0 += s0[j * kP + p];
+              v1 += s1[j * kP + p];
+            }
+            const float gx = __shfl_sync(0xffffffffu, gx_l, n);
+            if (EPI == 0) {
+              const int pos = ch.begin + n;
+              const float gh = __half2float(__float2half_rn(v0 * gx * gw0));
+              const float uh = __half2float(__float2half_rn(v1 * gx * gw1));
+              const __half h = swiglu1(gh, uh, a.limit);
+              a.inter[int64_t(pos) * a.inter_stride + rt * 128 + row] = h;
+              float hm = fabsf(__half2float(h));
+#pragma unroll
+              for (int o = 16; o; o >>= 1) hm = fmaxf(hm, __shfl_xor_sync(0xffffffffu, hm, o));
+              if (lane == 0) atomicMax(a.rowmax + pos, __float_as_uint(hm));
+            } else {
+              const int route = __shfl_sync(0xffffffffu, route_l, n);
+              __half* yrow = reinterpret_cast<__half*>(a.y2) + int64_t(route) * a.H + rt * 256 + row;
+              yrow[0] = __float2half_rn(v0 * gx * gw0);
+              yrow[128] = __float2half_rn(v1 * gx * gw0);
+            }
+          }
+        }
+        ++acc_i;
+        continue;
+      }
       float d0[kN], d1[TILES == 2 ? kN : 1];
 #pragma unroll
-      for (int c = 0; c < kN; c += 16) tmem_ld16(tmem + lanes + b * 128 + c, d0 + c);
+      for (int c = 0; c < kN; c += 16) tmem_ld16(tmem + lanes + b * St::kAccCols + c, d0 + c);
       if (TILES == 2) {
 #pragma unroll
-        for (int c = 0; c < kN; c += 16) tmem_ld16(tmem + lanes + b * 128 + 64 + c, d1 + c);  // up / second tile
+        for (int c = 0; c < kN; c += 16)
+          tmem_ld16(tmem + lanes + b * St::kAccCols + kN + c, d1 + c);  // up / second tile
       }
       fence_before();
       __syncwarp();
@@ -667,6 +721,9 @@ int launch_fp4_rc(cudaStream_t s, int epi, int rc, const Fp4Args& a, const void*
     case 16:
       return epi == 0 ? launch_fp4_one<0, 2, 16, MX>(s, a, map_x, grid)
                       : launch_fp4_one<1, 2, 16, MX>(s, a, map_x, grid);
+    case 32:
+      return epi == 0 ? launch_fp4_one<0, 2, 32, MX>(s, a, map_x, grid)
+                      : launch_fp4_one<1, 2, 32, MX>(s, a, map_x, grid);
     default: return -1;
   }
 }

@@ -14,7 +14,7 @@ constexpr int kRouteSlotsPerChunk = 16;
 
 // Block-scaled FP4 tensor path: activation planes and routes per chunk.
 constexpr int kFp4Planes = 4;
-constexpr int kFp4TcRoutes = 16;  // largest routes per chunk of the block-scaled FP4 path
+constexpr int kFp4TcRoutes = 32;  // largest routes per chunk of the block-scaled FP4 path
 
 // ---- packing (pack.cu)
 // MXFP4: per (slot, projection) global 2^(emax - 140) so the largest nonzero block maps to f16 exponent 28
@@ -141,7 +141,8 @@ struct Fp4Args {
 };
 int launch_fp4_gemm(cudaStream_t s, int epi, int rc, bool mx, const Fp4Args& a, const void* map_x, int grid);
 // routes per chunk of the block-scaled FP4 path for a call of S routes (the MMA's N is 4 x this)
-inline int fp4_routes_per_chunk(int S) { return S <= 64 ? 4 : S <= 1024 ? 8 : 16; }
+inline int fp4_routes_per_chunk(int S) { return S <= 64 ? 4 : S <= 1024 ? 8 : S < 4096 ? 16 : 32; }
+inline int fp4_rc_index(int rc) { return rc == 4 ? 0 : rc == 8 ? 1 : rc == 16 ? 2 : 3; }
 int launch_fp4_planes(cudaStream_t s, bool by_token, bool bf16, bool mx, const void* src, int64_t src_stride, int K,
                       const int32_t* inv, int top_k, const int32_t* chunk_of, int bank,
                       const int32_t* bank_range, int max_rows, uint32_t* rowmax, uint8_t* planes, int plane_rows,

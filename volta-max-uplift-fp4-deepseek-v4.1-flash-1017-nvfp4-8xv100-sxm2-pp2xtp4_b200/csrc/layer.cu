@@ -64,7 +64,7 @@ struct b200moe_layer {
   int32_t* f4_chunk_of = nullptr;              // [s_max]: (chunk << 8) | index in chunk of an FP4-bank position
   uint32_t* f4_rowmax = nullptr;               // [plane_rows]: amax bits of each SwiGLU row (W2 planes)
   int f4_plane_rows = 0, f4_max_chunks = 0;
-  alignas(128) unsigned char f4_map_x[2][3][128] = {};  // [W13, W2][4, 8, 16 routes per chunk]
+  alignas(128) unsigned char f4_map_x[2][4][128] = {};  // [W13, W2][4, 8, 16, 32 routes per chunk]
   // prefill on tcgen05: permuted fp16 token rows and the TMA maps of the two B operands
   __half* xperm = nullptr;
   alignas(128) unsigned char map_x[128] = {};
@@ -231,7 +231,7 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   // bf16 x feeds the block-scaled path's planes directly; only the GEMV banks (and the tcgen05 row gather,
   // which converts itself) want it in fp16
   const bool x_bf16_direct =
-      x_dtype == B200MOE_BF16 && c.prefill_gemm == 2 && c.n_fp4 > 0 && c.n_iq2 == 0 && ws.own;
+      x_dtype == B200MOE_BF16 && c.prefill_gemm >= 2 && c.n_fp4 > 0 && c.n_iq2 == 0 && ws.own;
   marks.mark();
   if (x_dtype == B200MOE_BF16 && !x_bf16_direct) {
     if (launch_convert_bf16(s, x, int64_t(m) * c.hidden, ws.x16)) return B200MOE_ERR_CUDA;
@@ -248,9 +248,12 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   if (c.n_iq2 > 0 && !rows && !quant_rows()) return B200MOE_ERR_CUDA;
   // prefill with the tcgen05 GEMM: the FP4 bank's chunks are 128-route token tiles
   // (NVFP4 weight units of the block-scaled layout feed the tcgen05 GEMM too: long prefills run there)
+  // prefill_gemm 2: prefills of >= kTcUnitsMinRoutes on the f16 GEMM over the weight units (measured faster
+  // than the block-scaled kernel with 32-route chunks: c3 T = 4,096 W13 1.84 against 2.47 ms); 3: every call
+  // on the block-scaled kernel
   const bool tc_units = c.prefill_gemm == 2 && S >= kTcUnitsMinRoutes;
   const bool tc = !rows && prefill && (c.prefill_gemm == 1 || tc_units) && c.n_fp4 > 0 && L->xperm;
-  const bool f4 = c.prefill_gemm == 2 && c.n_fp4 > 0 && !tc;
+  const bool f4 = c.prefill_gemm >= 2 && c.n_fp4 > 0 && !tc;
   // the block-scaled path's plane buffers are the layer's own (sized at create), also under the static array
   if (f4 && S > L->s_max) return B200MOE_ERR_RANGE;
   // W2 writes y2 rows only and one launch after it does the slot-order combine: fused into the W2
@@ -346,7 +349,7 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
         f.H = c.hidden;
         f.err = L->err;
         const int rc = fp4_routes_per_chunk(S);
-        if (launch_fp4_gemm(s, epi, rc, c.fp4_format == B200MOE_MXFP4, f, L->f4_map_x[epi][rc == 4 ? 0 : rc == 8 ? 1 : 2],
+        if (launch_fp4_gemm(s, epi, rc, c.fp4_format == B200MOE_MXFP4, f, L->f4_map_x[epi][fp4_rc_index(rc)],
                             L->grid))
           return B200MOE_ERR_CUDA;
         marks.mark();
@@ -354,7 +357,7 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
       }
       if (tc && b == 0) {
         TcArgs t{};
-        if (c.prefill_gemm == 2) {  // weight units: [slot][rt][kt] of 36 KB
+        if (c.prefill_gemm >= 2) {  // weight units: [slot][rt][kt] of 36 KB
           t.region = L->f4_units[epi];
           t.slot_stride = epi == 0 ? int64_t(2) * c.inter * (c.hidden / 2 + c.hidden / 16)
                                    : int64_t(c.hidden) * (c.inter / 2 + c.inter / 16);
@@ -378,7 +381,7 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
         t.y2 = ws.y2;
         t.H = c.hidden;
         t.err = L->err;
-        const int tfmt = c.prefill_gemm == 2 ? (c.fp4_format == B200MOE_NVFP4 ? 2 : 3) : c.fp4_format;
+        const int tfmt = c.prefill_gemm >= 2 ? (c.fp4_format == B200MOE_NVFP4 ? 2 : 3) : c.fp4_format;
         if (launch_tc_gemm(s, tfmt, epi, t, epi == 0 ? L->map_x : L->map_inter, L->grid))
           return B200MOE_ERR_CUDA;
         marks.mark();
@@ -474,9 +477,9 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
   if (c.n_iq2 > 0 && c.inter % 256) return B200MOE_ERR_INVALID_ARG;
   for (int t : {c.iq_type13, c.iq_type2})
     if (t != 0 && iq_fmt_of_type(t) < 0) return B200MOE_ERR_INVALID_ARG;
-  if (c.prefill_gemm < 0 || c.prefill_gemm > 2) return B200MOE_ERR_INVALID_ARG;
+  if (c.prefill_gemm < 0 || c.prefill_gemm > 3) return B200MOE_ERR_INVALID_ARG;
   // the block-scaled FP4 path: NVFP4 (E4M3 scales per 16), K tiles of 256 on both projections
-  if (c.prefill_gemm == 2 && (c.hidden % 256 || c.inter % 256))
+  if (c.prefill_gemm >= 2 && (c.hidden % 256 || c.inter % 256))
     return B200MOE_ERR_INVALID_ARG;
   DeviceGuard guard(device);
   cudaDeviceProp prop;
@@ -497,7 +500,7 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
   auto take = [&](int r) {
     if (st == B200MOE_OK) st = r;
   };
-  const bool f4 = c.prefill_gemm == 2;
+  const bool f4 = c.prefill_gemm >= 2;
   take(dalloc(&L->bank[0], f4 ? size_t(0) : size_t(c.n_fp4) * L->geom[0].slot_bytes));
   if (f4 && c.n_fp4 > 0) {
     const size_t H = c.hidden, I = c.inter, n = c.n_fp4;
@@ -544,9 +547,11 @@ int b200moe_layer_create(const b200moe_config* cfg, int device, b200moe_layer** 
         (make_u8_tile_map(L->f4_map_x[0][0], L->f4_planes[0], int64_t(P * R), H / 2, 128, 4 * kFp4Planes) ||
          make_u8_tile_map(L->f4_map_x[0][1], L->f4_planes[0], int64_t(P * R), H / 2, 128, 8 * kFp4Planes) ||
          make_u8_tile_map(L->f4_map_x[0][2], L->f4_planes[0], int64_t(P * R), H / 2, 128, 16 * kFp4Planes) ||
+         make_u8_tile_map(L->f4_map_x[0][3], L->f4_planes[0], int64_t(P * R), H / 2, 128, 32 * kFp4Planes) ||
          make_u8_tile_map(L->f4_map_x[1][0], L->f4_planes[1], int64_t(P * R), I / 2, 128, 4 * kFp4Planes) ||
          make_u8_tile_map(L->f4_map_x[1][1], L->f4_planes[1], int64_t(P * R), I / 2, 128, 8 * kFp4Planes) ||
-         make_u8_tile_map(L->f4_map_x[1][2], L->f4_planes[1], int64_t(P * R), I / 2, 128, 16 * kFp4Planes)))
+         make_u8_tile_map(L->f4_map_x[1][2], L->f4_planes[1], int64_t(P * R), I / 2, 128, 16 * kFp4Planes) ||
+         make_u8_tile_map(L->f4_map_x[1][3], L->f4_planes[1], int64_t(P * R), I / 2, 128, 32 * kFp4Planes)))
       st = B200MOE_ERR_CUDA;
   }
   if (c.prefill_gemm >= 1 && c.max_prefill_tokens > 0 && c.n_fp4 > 0) {
@@ -677,7 +682,7 @@ int b200moe_load_fp4(b200moe_layer* L, void* stream, int slot_begin, int n, cons
   if (c.fp4_format == B200MOE_NVFP4 &&
       cudaMemcpyAsync(gdst, globals, size_t(n) * 12, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
     return B200MOE_ERR_CUDA;
-  if (c.prefill_gemm == 2) {  // weight units for the block-scaled tensor path (and the tcgen05 prefill)
+  if (c.prefill_gemm >= 2) {  // weight units for the block-scaled tensor path (and the tcgen05 prefill)
     const size_t H = c.hidden, I = c.inter, b = size_t(slot_begin);
     const bool mx = c.fp4_format == B200MOE_MXFP4;
     if (mx && launch_mx_rebase(s, c.hidden, c.inter, n, w13c, w13s, w2c, w2s, gdst, L->span, L->err))

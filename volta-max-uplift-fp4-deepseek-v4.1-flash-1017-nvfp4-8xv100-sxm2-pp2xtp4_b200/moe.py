@@ -50,9 +50,11 @@ class B200NativeMoe:
     both) or "fp4" (hidden and inter multiples of 256: every FP4-bank launch,
     decode and prefill, on the block-scaled FP4 tensor cores,
     tcgen05.mma.kind::mxf4nvf4 with the format's own block scales (E4M3 per 16
-    or E8M0 per 32), the activations as four E2M1 planes (~1e-4 relative); the
-    fastest decode and, through the tcgen05 f16 GEMM over the same weight
-    units, the fastest long prefill).  IQ2_XXS experts always use their int8
+    or E8M0 per 32), the activations as four E2M1 planes (~1e-4 relative);
+    prefills of >= 4096 routes on the tcgen05 f16 GEMM over the same weight
+    units: the fastest decode and prefill) or "fp4-bs" (every call on the
+    block-scaled kernel, 32-route chunks for long prefills: slower there, kept
+    for comparison).  IQ experts always use their int8
     kernel.
     """
 
@@ -63,8 +65,8 @@ class B200NativeMoe:
                  iq_types: tuple[int, int] = (16, 16)):
         if fp4_format not in ("nvfp4", "mxfp4"):
             raise ValueError(f"fp4_format must be nvfp4 or mxfp4, got {fp4_format!r}")
-        if prefill_gemm not in ("tcgen05", "skinny", "fp4"):
-            raise ValueError(f"prefill_gemm must be tcgen05, skinny or fp4, got {prefill_gemm!r}")
+        if prefill_gemm not in ("tcgen05", "skinny", "fp4", "fp4-bs"):
+            raise ValueError(f"prefill_gemm must be tcgen05, skinny, fp4 or fp4-bs, got {prefill_gemm!r}")
         self.prefill_gemm = prefill_gemm
         if len(iq_types) != 2 or any(t not in IQ_BLOCK_BYTES for t in iq_types):
             raise ValueError(f"iq_types are GGML types (gate/up, down) of 16 IQ2_XXS, 17 IQ2_XS, 29 IQ1_M, "
@@ -85,7 +87,7 @@ class B200NativeMoe:
         self.fp4_slot, self.iq2_slot = fp4_map, iq2_map
         cfg = _lib.Config(hidden, inter, num_experts, top_k, max_tokens, max_prefill_tokens,
                           _lib.NVFP4 if fp4_format == "nvfp4" else _lib.MXFP4, self.n_fp4, self.n_iq2,
-                          float(swiglu_limit), {"skinny": 0, "tcgen05": 1, "fp4": 2}[prefill_gemm],
+                          float(swiglu_limit), {"skinny": 0, "tcgen05": 1, "fp4": 2, "fp4-bs": 3}[prefill_gemm],
                           self.iq_types[0], self.iq_types[1])
         handle = ctypes.c_void_p()
         L = _lib.lib()
