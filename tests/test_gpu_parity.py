@@ -137,13 +137,18 @@ def test_route_plan_large_and_repeated(dev, pkg):
 def test_gating_bit_exact(dev, pkg):
     from b200moe import moe
 
-    for (T, E, K) in ((8, 64, 6), (64, 384, 8), (300, 384, 8)):
+    for (T, E, K) in ((8, 64, 6), (64, 384, 8), (300, 384, 8), (16, 1000, 16), (6, 100, 3)):
         layer = moe.B200NativeMoe(hidden=256, inter=128, num_experts=E, top_k=K, max_tokens=8,
                                   tier=np.zeros(E, np.int8), device=dev)
         rng = np.random.default_rng(T)
         lg = rng.normal(0, 1, (T, E)).astype(np.float32)
         lg[0, :5] = 0.25  # ties
         lg[1, 7] = lg[1, 9] = 3.0
+        lg[2, :] = 0.5  # every logit equal: the K smallest ids
+        lg[3, :] = -1.0 - np.abs(lg[3, :])  # -0 and +0 on top tie: the smaller id first
+        lg[3, 40], lg[3, 3] = -0.0, 0.0
+        lg[4, 33::32] = 4.0  # ties in one lane's column across the K boundary
+        lg[5, [i for i in (1, 33, 65, 97) if i < E]] = 2.0  # a tie held by one lane in several columns
         ids, w = layer.route(torch.from_numpy(lg).to(dev))
         rid, rw = mo.route(lg, K)
         assert np.array_equal(ids.cpu().numpy(), rid)

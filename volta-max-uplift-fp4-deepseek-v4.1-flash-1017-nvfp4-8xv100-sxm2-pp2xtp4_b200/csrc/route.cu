@@ -458,9 +458,25 @@ int launch_plan(cudaStream_t s, const PlanArgs& a) {
 // One warp per token.  ids: the k largest logits, larger first, ties to the
 // smaller id.  weights: exp(l - l_max) in double for the k chosen, summed in
 // rank order, divided, rounded once to float.
+//
+// Each lane keeps the best of its own logits (ids lane + 32 j); a round takes
+// the warp's largest by one integer max reduction over order-preserving keys
+// of the lanes' bests, then the smallest id among the lanes holding that value
+// by one min reduction, and only the winner's lane rescans its logits.  Zeros
+// are keyed as +0, so -0 and +0 tie and the smaller id wins, as in a compare.
+__device__ __forceinline__ uint32_t order_key(float f) {
+  uint32_t u = __float_as_uint(f);
+  if (u == 0x80000000u) u = 0u;
+  return (u >> 31) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_value(uint32_t k) {
+  return __uint_as_float((k >> 31) ? (k & 0x7fffffffu) : ~k);
+}
+
 template <int MAXV>
 __global__ void gating_kernel(const float* __restrict__ logits, int T, int E, int k, int32_t* __restrict__ ids,
                               float* __restrict__ w, uint32_t* err) {
+  const unsigned full = 0xffffffffu;
   const int lane = threadIdx.x & 31;
   const int warps = (gridDim.x * blockDim.x) >> 5;
   for (int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < T; t += warps) {
@@ -469,56 +485,55 @@ __global__ void gating_kernel(const float* __restrict__ logits, int T, int E, in
 #pragma unroll
     for (int j = 0; j < MAXV; ++j) {
       const int idx = lane + 32 * j;
-      v[j] = idx < E ? row[idx] : -INFINITY;
+      v[j] = idx < E ? __ldg(row + idx) : -INFINITY;
       if (idx < E && !isfinite(v[j])) {
         set_error(err, kErrFormat);
         v[j] = -FLT_MAX;
       }
     }
-    // k rounds: warp argmax (larger value, then smaller id), the winner leaves.
-    // Lane r keeps the r-th winner (value, id), so the exps below run in parallel.
+    // this lane's best: the first (smallest id) of its largest logits
+    auto lane_best = [&](int& bj) {
+      float b = v[0];
+      bj = 0;
+#pragma unroll
+      for (int j = 1; j < MAXV; ++j)
+        if (v[j] > b) {
+          b = v[j];
+          bj = j;
+        }
+      return b;
+    };
+    int bj;
+    float bv = lane_best(bj);
     float my_v = 0.f;
     int my_i = 0;
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
       if (r >= k) break;
-      float best = -INFINITY;
-      int bi = 0x7fffffff;
-#pragma unroll
-      for (int j = 0; j < MAXV; ++j) {
-        const int idx = lane + 32 * j;
-        if (idx < E && v[j] != -INFINITY && (v[j] > best || (v[j] == best && idx < bi))) {
-          best = v[j];
-          bi = idx;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > best || (ov == best && oi < bi)) {
-          best = ov;
-          bi = oi;
-        }
-      }
+      const uint32_t key = order_key(bv);
+      const uint32_t kmax = __reduce_max_sync(full, key);
+      const uint32_t cand = key == kmax ? uint32_t(lane + 32 * bj) : 0xffffffffu;
+      const uint32_t imin = __reduce_min_sync(full, cand);
       if (lane == r) {
-        my_v = best;
-        my_i = bi;
+        my_v = key_value(kmax);
+        my_i = int(imin);
       }
-      if ((bi & 31) == lane) {  // only the owner lane drops it (static indices keep v in registers)
+      if (int(imin & 31u) == lane) {  // the winner leaves; only its lane looks again
+        const int wj = int(imin >> 5);
 #pragma unroll
         for (int j = 0; j < MAXV; ++j)
-          if (j == (bi >> 5)) v[j] = -INFINITY;
+          if (j == wj) v[j] = -INFINITY;
+        bv = lane_best(bj);
       }
     }
     // weights: exp(l - l_max) in double, summed in rank order, divided, rounded once
-    const float vmax = __shfl_sync(0xffffffffu, my_v, 0);
+    const float vmax = __shfl_sync(full, my_v, 0);
     const double ex = lane < k ? exp(double(my_v) - double(vmax)) : 0.0;
     double total = 0.0;
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
       if (r >= k) break;
-      total = total + __shfl_sync(0xffffffffu, ex, r);
+      total = total + __shfl_sync(full, ex, r);
     }
     if (lane < k) {
       ids[int64_t(t) * k + lane] = my_i;
