@@ -590,7 +590,7 @@ def run_c1(job, m: int, layer=None, bank=None, main: bool = True) -> dict:
     value = m / (ms / 1e3)
     del graphs
 
-    if f4:  # start, plan, x planes, W13, SwiGLU planes, W2, combine
+    if f4:  # start, convert (none for bf16 x), plan, x planes, W13 (+SwiGLU), SwiGLU planes, W2, combine
         per = per_launch(layer, fns, args.steps, 8)
         t_w13_ms = float(per[3])
         names = ["convert", "plan", "x_planes", "w13", "swiglu_planes", "w2", "combine"]
@@ -1041,17 +1041,22 @@ def run_c4(job) -> dict:
         local_bytes += int((local.fp4_slot[used] >= 0).sum()) * EXPERT_BYTES + \
             int((local.iq2_slot[used] >= 0).sum()) * (IQ_W13_BYTES + IQ_W2_BYTES)
     comm_max = job.maxall(comm)
-    # this library's launches per layer: gating; world 1: bf16 copy, x int8 blocks, plan, W13 and W2 per bank,
-    # SwiGLU int8 blocks; world > 1 adds owner plan, push, receive, return, combine (no bf16 copy)
+    # this library's launches per layer
     launches_per_step = 0
+    fp4_path = args.gemm != "gemv"
     for lay, _ in layers:
         local = lay if world == 1 else lay.layer
-        banks = int((local.fp4_slot >= 0).any()) + int((local.iq2_slot >= 0).any())
-        launches_per_step += 1 + 2 * banks + (3 if world == 1 else 2) + (5 if world > 1 else 0)
-        if world == 1 and (args.gemm != "gemv" or T * K_TOP > 32):  # the combine launch
-            launches_per_step += 1
-        if args.gemm != "gemv" and (local.fp4_slot >= 0).any():  # x and SwiGLU planes
-            launches_per_step += 2
+        has_fp4, has_iq = bool((local.fp4_slot >= 0).any()), bool((local.iq2_slot >= 0).any())
+        n = 1 + 1  # gating, route plan
+        if world == 1:
+            n += 1 if (has_iq or not fp4_path) else 0  # bf16 -> f16 copy of x (the FP4 planes read bf16 x)
+            n += 1 if (fp4_path or T * K_TOP > 32) else 0  # the combine launch
+        else:
+            n += 3  # push, return, combine
+        n += 2 if has_iq else 0  # int8 blocks of x and of the SwiGLU rows
+        n += 2 if (fp4_path and has_fp4) else 0  # x planes, SwiGLU planes
+        n += 2 * (int(has_fp4) + int(has_iq))  # W13 and W2 per bank
+        launches_per_step += n
     pk = peaks()
     achieved = local_bytes / (ms / 1e3) / 1e9
     frac_min = -job.maxall(-achieved / pk["hbm_gbs"])
@@ -1269,9 +1274,9 @@ def run_expert_parallel(job) -> dict | None:
             "e2e": {"value": world * m_rank / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": int(hx.numel() * hx.element_size() + hl.numel() * hl.element_size()),
                     "d2h_bytes_per_step": int(hout.numel() * hout.element_size())},
-            # p2p: gating; push; local plan, W13, W2; return; combine (fp4: + the two plane launches of the
-            # local run, and the combine of the local rows); nccl: gating; dispatch, local run, f32->f16, combine
-            "gpu_launches": (9 + (2 if f4 else 0)) * args.steps,
+            # p2p: gating; push; local plan (waits for every rank's push), W13, W2; return; combine
+            # (fp4: + the two plane launches of the local run)
+            "gpu_launches": (9 if f4 else 7) * args.steps,
             "cpu_baseline": None,
             "clocks": strong["clocks"],
         })

@@ -154,6 +154,92 @@ __device__ __forceinline__ __half swiglu1(float g, float u, float limit) {
   return __float2half_rn(__fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), u));
 }
 
+// ---------------------------------------------------------------- planes
+// Nearest E2M1 value (ties to even) of v >= 0, and its 3-bit magnitude code:
+// step 0.5 below 2, 1 below 4, 2 above, saturating at 6.
+__device__ __forceinline__ float e2m1_round(float v) {
+  const float q = v < 2.f ? rintf(v * 2.f) * 0.5f : v < 4.f ? rintf(v) : rintf(v * 0.5f) * 2.f;
+  return fminf(q, 6.f);
+}
+__device__ __forceinline__ uint32_t e2m1_code_of(float q) {  // q on the E2M1 grid
+  return q < 2.f ? uint32_t(q * 2.f) : q < 4.f ? uint32_t(q) + 2u : uint32_t(q * 0.5f) + 4u;
+}
+// Nearest E4M3 byte of x >= 0 (ties to even, saturating at 448) by the
+// hardware conversion; both halves of the pair convert x.
+__device__ __forceinline__ uint32_t e4m3_rn(float x) {
+  uint16_t pair;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %1;" : "=h"(pair) : "f"(x));
+  return pair & 0xFFu;
+}
+
+// One half-block (8 consecutive elements, thread of lane = half-block index
+// mod 32) of a row through the kP planes: per plane the E2M1 codes (w[p], 8
+// nibbles) and, on lane 8j of a warp, the scale word of the 64-wide K step the
+// lanes 8j .. 8j + 7 cover (word[p]).  g: the row's factor (its amax over
+// 6 * 448 for NVFP4, 1 for MXFP4), inv_g its inverse; r: the elements, left
+// holding the residual.  Every lane of the warp takes part (shuffles).
+template <int MX>
+__device__ __forceinline__ void quantize_planes8(float (&r)[8], bool own, float g, float inv_g, uint32_t (&w)[kP],
+                                                 uint32_t (&word)[kP]) {
+#pragma unroll
+  for (int p = 0; p < kP; ++p) {
+    float bm = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) bm = fmaxf(bm, fabsf(r[e]));
+    bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 1));  // the other half of the 16-block
+    if (MX) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 2));  // the 32-block: four half-blocks
+    uint32_t sc;
+    float scale;
+    if (MX) {  // UE8M0: the smallest 2^e with 6 * 2^e >= bm
+      const int e = bm > 0.f ? max(-126, min(127, mx_exponent(bm))) : -127;
+      sc = own && bm > 0.f ? uint32_t(e + 127) : 0u;
+      scale = sc ? __uint_as_float(sc << 23) : 0.f;  // 2^e, e >= -126: a normal float
+    } else {
+      sc = own ? e4m3_rn(bm / 6.f * inv_g) : 0u;
+      // the E4M3 byte's value (sc < 0x80), built from its bits: 2^(e - 7) (1 + m / 8) or m 2^-9
+      const uint32_t ex = sc >> 3, mn = sc & 7u;
+      const float sv = ex ? __uint_as_float(((ex + 120u) << 23) | (mn << 20)) : float(mn) * 0.001953125f;
+      scale = sv * g;
+    }
+    const float rs = scale > 0.f ? __frcp_rn(scale) : 0.f;  // = 1 / scale, rounded to nearest
+    uint32_t cw = 0u;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float v = r[e] * rs;
+      const float q = e2m1_round(fabsf(v));
+      r[e] -= copysignf(q, v) * scale;
+      cw |= (e2m1_code_of(q) | (v < 0.f ? 8u : 0u)) << (4 * e);
+    }
+    w[p] = cw;
+    // the scale bytes of one 64-wide K step as one word from lane 8j: NVFP4 blocks 4j .. 4j + 3 (lanes
+    // 8j, +2, +4, +6), MXFP4 blocks 2j, 2j + 1 (lanes 8j, 8j + 4)
+    uint32_t wd = sc;
+    if (MX) {
+      wd |= __shfl_down_sync(0xffffffffu, sc, 4) << 8;
+    } else {
+      wd |= __shfl_down_sync(0xffffffffu, sc, 2) << 8;
+      wd |= __shfl_down_sync(0xffffffffu, sc, 4) << 16;
+      wd |= __shfl_down_sync(0xffffffffu, sc, 6) << 24;
+    }
+    word[p] = wd;
+  }
+}
+
+// Store half-block hb's planes of sorted position pos (index n in its chunk,
+// the chunk's scale blocks at sfb_chunk) into the plane rows and scale blocks.
+__device__ __forceinline__ void store_planes8(const uint32_t (&w)[kP], const uint32_t (&word)[kP], int hb, int K,
+                                              int pos, int n, uint8_t* planes, uint8_t* sfb_chunk) {
+#pragma unroll
+  for (int p = 0; p < kP; ++p) {
+    *reinterpret_cast<uint32_t*>(planes + (int64_t(pos) * kP + p) * (K / 2) + hb * 4) = w[p];
+    if ((hb & 7) == 0) {
+      const int mr = n * kP + p;
+      *reinterpret_cast<uint32_t*>(sfb_chunk + (hb >> 3) * 512 + (mr & 31) * 16 + (mr >> 5) * 4) = word[p];
+    }
+  }
+}
+
+
 template <int EPI, int TILES, int RC, int MX>
 __global__ void __launch_bounds__(kThreads, 1)
     fp4_gemm_kernel(const Fp4Args a, const __grid_constant__ CUtensorMap map_x) {
@@ -443,24 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
 }
 
-// ---------------------------------------------------------------- planes
-// Nearest E2M1 value (ties to even) of v >= 0, and its 3-bit magnitude code:
-// step 0.5 below 2, 1 below 4, 2 above, saturating at 6.
-__device__ __forceinline__ float e2m1_round(float v) {
-  const float q = v < 2.f ? rintf(v * 2.f) * 0.5f : v < 4.f ? rintf(v) : rintf(v * 0.5f) * 2.f;
-  return fminf(q, 6.f);
-}
-__device__ __forceinline__ uint32_t e2m1_code_of(float q) {  // q on the E2M1 grid
-  return q < 2.f ? uint32_t(q * 2.f) : q < 4.f ? uint32_t(q) + 2u : uint32_t(q * 0.5f) + 4u;
-}
-// Nearest E4M3 byte of x >= 0 (ties to even, saturating at 448) by the
-// hardware conversion; both halves of the pair convert x.
-__device__ __forceinline__ uint32_t e4m3_rn(float x) {
-  uint16_t pair;
-  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %1;" : "=h"(pair) : "f"(x));
-  return pair & 0xFFu;
-}
-
+// ---------------------------------------------------------------- plane kernel
 // The activation rows of the FP4 bank as kP E2M1 planes with their blocked
 // scales in the chunk's SFB blocks (MMA row n * kP + p) and one FP32 factor g
 // per row (its amax over 6 * 448: plane 0's block scales use E4M3's range and
@@ -553,54 +622,11 @@ __global__ void __launch_bounds__(kPlaneThreads) fp4_planes_kernel(
     }
     // MXFP4: power-of-two block scales cover any row, so no row factor (g = 1)
     const float g = MX ? 1.f : amax / (6.f * 448.f);
-    const float inv_g = g > 0.f ? 1.f / g : 0.f;
-#pragma unroll
-    for (int p = 0; p < kP; ++p) {
-      float bm = 0.f;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) bm = fmaxf(bm, fabsf(r[e]));
-      bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 1));  // the other half of the 16-block
-      if (MX) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 2));  // the 32-block: four half-blocks
-      uint32_t sc;
-      float scale;
-      if (MX) {  // UE8M0: the smallest 2^e with 6 * 2^e >= bm
-        const int e = bm > 0.f ? max(-126, min(127, mx_exponent(bm))) : -127;
-        sc = own && bm > 0.f ? uint32_t(e + 127) : 0u;
-        scale = sc ? ldexpf(1.f, e) : 0.f;
-      } else {
-        sc = own ? e4m3_rn(bm / 6.f * inv_g) : 0u;
-        scale = e4m3_value(sc) * g;
-      }
-      const float rs = scale > 0.f ? 1.f / scale : 0.f;
-      uint32_t w = 0u;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float v = r[e] * rs;
-        const float q = e2m1_round(fabsf(v));
-        r[e] -= copysignf(q, v) * scale;
-        w |= (e2m1_code_of(q) | (v < 0.f ? 8u : 0u)) << (4 * e);
-      }
-      // the scale bytes of one 64-wide K step as one word from lane 8j: NVFP4 blocks 4j .. 4j + 3 (lanes
-      // 8j, +2, +4, +6), MXFP4 blocks 2j, 2j + 1 (lanes 8j, 8j + 4)
-      uint32_t word = sc;
-      if (MX) {
-        word |= __shfl_down_sync(0xffffffffu, sc, 4) << 8;
-      } else {
-        word |= __shfl_down_sync(0xffffffffu, sc, 2) << 8;
-        word |= __shfl_down_sync(0xffffffffu, sc, 4) << 16;
-        word |= __shfl_down_sync(0xffffffffu, sc, 6) << 24;
-      }
-      if (own) {
-        for (int d = 0; d < nd; ++d) {
-          const int pos = dst_pos[d];
-          *reinterpret_cast<uint32_t*>(planes + (int64_t(pos) * kP + p) * (K / 2) + hb * 4) = w;
-          if ((hb & 7) == 0) {
-            const int mr = dst_n[d] * kP + p;
-            *reinterpret_cast<uint32_t*>(sfb + dst_sf[d] + (blk >> 2) * 512 + (mr & 31) * 16 + (mr >> 5) * 4) = word;
-          }
-        }
-      }
-    }
+    const float inv_g = g > 0.f ? __frcp_rn(g) : 0.f;
+    uint32_t w[kP], word[kP];
+    quantize_planes8<MX>(r, own, g, inv_g, w, word);
+    if (own)
+      for (int d = 0; d < nd; ++d) store_planes8(w, word, hb, K, dst_pos[d], dst_n[d], planes, sfb + dst_sf[d]);
     if (blockIdx.y == 0 && t < nd) {
       gx[dst_pos[t]] = g;
       if (BY_TOKEN) rowmax[dst_pos[t]] = 0u;  // the W13 epilogue takes the W2 row maxima afresh
