@@ -105,7 +105,9 @@ def parse():
     ap.add_argument("--batch", type=int, default=256, help="c4: decode tokens of the whole box per step")
     ap.add_argument("--m", type=int, default=None, choices=[1, 8, 32, 64],
                     help="decode tokens per step (c1 default 64, c2 default 32; multi-GPU: of the whole box)")
-    ap.add_argument("--tokens", type=int, default=4096, choices=[4096, 16384], help="c3 prefill tokens")
+    ap.add_argument("--tokens", type=int, default=4096,
+                    help="c3 prefill tokens (4096 or 16384 for configs[3]; other values with --experts for a "
+                         "small ncu capture)")
     ap.add_argument("--eager", action="store_true", help="decode: launch each kernel instead of a graph replay")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="multi-GPU: the library's NVLink peer-memory exchange (default) or NCCL all-to-all")
@@ -787,6 +789,7 @@ def run_c3(job, main: bool = True) -> dict:
     from b200moe import moe, synth
 
     args, dev, T = job.args, job.dev, (job.args.tokens if main else 4096)
+    E = args.experts if main else globals()["E"]  # fewer experts only for a small ncu capture
     mode = {"fp4": "fp4", "fp4-bs": "fp4-bs", "gemv": "tcgen05"}[args.gemm]
     bs = mode == "fp4-bs"  # every launch on the block-scaled kernel (32-route chunks)
     layer = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K_TOP, max_tokens=8,

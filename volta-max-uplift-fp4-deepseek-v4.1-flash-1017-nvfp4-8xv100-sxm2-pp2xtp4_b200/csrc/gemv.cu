@@ -48,7 +48,11 @@ struct Fmt {
   static constexpr int STAGE = kConsumerWarps * U + kRouteSlots * XRS;
   static constexpr int CTAS = IQ ? 1 : 2;                                // CTAs per SM
   static constexpr int STAGES = CTAS == 2 ? 4 : 6;
-  static constexpr int TW = IQ ? iq_table_words(FMT) : 0;                // decode table words
+  static constexpr int TWG = IQ ? iq_table_words(FMT) : 0;               // decode table words (global)
+  // IQ2_XXS keeps 32 copies of its table in shared memory, word w of copy c at w * 32 + c: lane c reads
+  // its own copy, so the random grid / sign lookups of a warp never share a bank
+  static constexpr int TREP = FMT == 2 ? 32 : 1;
+  static constexpr int TW = TWG * TREP;                                  // decode table words (shared)
 };
 constexpr int kMaxStages = 6;
 
@@ -175,7 +179,8 @@ __device__ __forceinline__ void iq2_step(uint32_t wb, uint32_t xb, uint32_t tbl,
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) t[pl][mt][nt][i] = 0;
-  const uint32_t tsign = tbl + 256 * 4;
+  const uint32_t tl = tbl + lane * 4;  // this lane's copy of the tables (words 32 apart)
+  const uint32_t tsign = tl + 256 * 128;
 #pragma unroll 2
   for (int ibp = 0; ibp < 4; ++ibp) {
     uint4 qw[2][2];
@@ -207,7 +212,7 @@ __device__ __forceinline__ void iq2_step(uint32_t wb, uint32_t xb, uint32_t tbl,
           const uint32_t a1 = i2 == 0 ? qw[mt][h].y : qw[mt][h].w;
           const uint32_t gi = __byte_perm(a0, 0u, 0x4440u | uint32_t(q));  // byte q of a0
           const uint32_t si = (a1 >> (7 * q)) & 127u;
-          sel[h] = lds32(tbl + gi * 4) | lds32(tsign + si * 4);
+          sel[h] = lds32(tl + gi * 128) | lds32(tsign + si * 128);
           c[h] = int(((a1 >> 27) & 0x1Eu) | 1u);
         }
         const uint32_t a[4] = {__byte_perm(kPos, kNeg, sel[0]), __byte_perm(kPos, kNeg, sel[1]),
@@ -515,7 +520,7 @@ __device__ __forceinline__ void gemv_body(const GemvArgs& a, uint8_t* smem) {
     list[0] = 0;
   }
   if (F::IQ)
-    for (int i = threadIdx.x; i < F::TW; i += kGemvThreads) tables[i] = a.iq2_tables[i];
+    for (int i = threadIdx.x; i < F::TW; i += kGemvThreads) tables[i] = a.iq2_tables[i / F::TREP];
   __syncthreads();
 
   const int n_kt = a.K / F::KT;
