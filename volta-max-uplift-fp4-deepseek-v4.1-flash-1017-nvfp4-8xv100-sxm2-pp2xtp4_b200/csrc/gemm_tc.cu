@@ -62,8 +62,8 @@ struct TcFmt {
   static constexpr int RAW = kWeightUnits ? U : kUnits * U;
   static constexpr int KB_PER_RAW = kWeightUnits ? 4 : 2;  // 64-wide K blocks per raw stage
   static constexpr int KT = kWeightUnits ? 256 : kFp4KTile;  // K per unit
-  static constexpr int TOK_STAGES = kWeightUnits ? 4 : kTokStages;
-  static constexpr int W_STAGES = kWeightUnits ? 2 : kWStages;
+  static constexpr int TOK_STAGES = kWeightUnits ? 3 : kTokStages;
+  static constexpr int W_STAGES = kWeightUnits ? 3 : kWStages;
   static constexpr int RAW_STAGES = kRawStages;
 };
 
@@ -313,6 +313,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
       const Chunk ch = a.chunks[item / a.n_rt];
       if (!item_ok(ch)) continue;
+      // MXFP4 weight units: the rebase exponent of this thread's projection, once per item (global =
+      // 2^(gexp - 1)); a global load inside the K loop below stalled every block on its latency
+      int gexp = 0;
+      if (FMT == 3) frexpf(a.globals[ch.slot * 3 + (EPI == 0 ? ((dw * 32 + lane) >> 7) : 2)], &gexp);
       bool ok = true;
       for (int kb = 0; kb < n_kb && ok; ++kb, ++gk) {
         const int rs = graw % kRawStages;
@@ -346,8 +350,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             sc[2] = lo_half2(p23);
             sc[3] = hi_half2(p23);
           } else {  // two E8M0 scales, one per 32, as f16 2^(e - 127 - rebase)
-            int gexp;
-            frexpf(a.globals[ch.slot * 3 + (EPI == 0 ? tile : 2)], &gexp);  // global = 2^(gexp - 1)
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
               int f = int((sw4 >> (8 * j)) & 255u) - 127 - (gexp - 1) + 15;
