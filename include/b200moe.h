@@ -266,7 +266,8 @@ int b200moe_ep_combine(void* stream, const void* y2, const int32_t* route_pos, c
  * its owner's buffer and stores its fp16 row and expert id there; no rank
  * waits for another), ep_forward (the local top-1 layer on the rows received:
  * its first launch waits for every rank's push), ep_return (y2 rows back to
- * their home ranks), ep_combine_p2p (slot-order combine + residual).
+ * their home ranks; fused into ep_forward's W2 for FP4-only layers),
+ * ep_combine_p2p (slot-order combine + residual).
  * Waits are bounded (B200MOE_ERR_TIMEOUT through ep_check_errors).  All ranks
  * must be alive at destroy (call it after a host barrier).  No reference
  * counterpart: the reference refuses expert parallelism
@@ -282,9 +283,12 @@ int b200moe_ep_push(b200moe_ep* ep, void* stream, const void* x, int x_dtype, co
                     int k, int num_experts, const int32_t* owner_of_expert);
 /* The local experts of a top-1 layer (its owner map = this rank's experts) on
  * the rows this step brought in: waits (bounded) for every rank's push, then
- * b200moe_forward_rows on the receive buffers; y2 rows stay local for
- * ep_return. */
-int b200moe_ep_forward(b200moe_ep* ep, b200moe_layer* layer, void* stream);
+ * b200moe_forward_rows on the receive buffers.  fuse_return = 0: the y2 rows
+ * stay local for ep_return.  fuse_return = 1 (a prefill_gemm >= 2 layer whose
+ * experts are all FP4): the W2 epilogue stores each y2 row straight into its
+ * home rank's buffer and raises this rank's return flag, so no ep_return call
+ * follows; other layers return B200MOE_ERR_INVALID_ARG. */
+int b200moe_ep_forward(b200moe_ep* ep, b200moe_layer* layer, void* stream, int fuse_return);
 int b200moe_ep_return(b200moe_ep* ep, void* stream);
 int b200moe_ep_combine_p2p(b200moe_ep* ep, void* stream, const int32_t* topk_ids, const float* topk_weights,
                            int T, int k, int num_experts, const int32_t* owner_of_expert, const float* residual,

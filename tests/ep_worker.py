@@ -30,6 +30,9 @@ def main(out_path: str, exchange: str, gemm: str, placement: str) -> None:
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     H, I, E, K, T = 1024, 512, 64, 6, 48
     tier, pop_rank = tiers.zipf_tier(E, 40, seed=3)
+    if placement.endswith("-fp4only"):  # every expert FP4: the owners' W2 stores y2 at home (fused return)
+        tier = np.full(E, tiers.HOT, np.int8)
+        placement = placement[: -len("-fp4only")]
     n_hot, n_iq = int((tier == tiers.HOT).sum()), int((tier == tiers.WARM).sum())
     fp4 = synth.make_fp4_bank(n_hot, H, I, "nvfp4", 11, dev)
     iq2 = synth.make_iq2_bank(n_iq, H, I, 12, dev)

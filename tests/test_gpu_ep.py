@@ -101,7 +101,8 @@ def test_ep_world1_matches_layer(dev, pkg, exchange, gemm):
 
 
 @pytest.mark.parametrize("exchange,gemm,placement", [("p2p", "skinny", "range"), ("nccl", "skinny", "range"),
-                                                     ("p2p", "fp4", "range"), ("p2p", "fp4", "balanced")])
+                                                     ("p2p", "fp4", "range"), ("p2p", "fp4", "balanced"),
+                                                     ("p2p", "fp4", "range-fp4only")])
 def test_ep_two_gpus(tmp_path, exchange, gemm, placement):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -125,6 +126,36 @@ def test_ep_two_gpus(tmp_path, exchange, gemm, placement):
         # every route goes to rank 0's experts: rank 1 receives none
         assert res["one_owner_routes_in"] == 0 if rank == 1 else res["one_owner_routes_in"] > 0
         assert res["zipf_comm_ms"] > 0
+
+
+def test_ep_world1_fused_return_bit_equal(dev, pkg):
+    """An all-FP4 block-scaled layer: the owner's W2 epilogue stores each y2
+    row at its home (no return launch) and raises the return flag; the
+    result is bit-equal to the single-GPU layer on the same path, step after
+    step (the flags' epochs advance, the reservation counters reset)."""
+    from b200moe import ep, moe, synth
+
+    H, I, E, K, T = 1024, 512, 48, 8, 40
+    tier = np.zeros(E, np.int8)
+    bank = synth.make_fp4_bank(E, H, I, "nvfp4", 17, dev)
+    full = moe.B200NativeMoe(hidden=H, inter=I, num_experts=E, top_k=K, max_tokens=64, tier=tier, device=dev,
+                             prefill_gemm="fp4")
+    synth.load_bank(full, bank)
+    sharded = ep.ExpertParallelMoe(hidden=H, inter=I, num_experts=E, top_k=K, tokens=T, tier=tier, device=dev,
+                                   gemm="fp4")
+    assert sharded.fused_return
+    synth.load_bank(sharded.layer, bank)
+    g = torch.Generator(device=dev).manual_seed(8)
+    for step in range(3):
+        x = torch.randn((T - 7 * step, H), generator=g, device=dev).to(torch.bfloat16)
+        ids, w = sharded.route(torch.randn((x.shape[0], E), generator=g, device=dev))
+        want = full.forward(x, ids, w).clone()
+        got = sharded.forward(x, ids, w).clone()
+        sharded.check_errors()
+        full.check_errors()
+        assert torch.equal(got, want), step
+    sharded.close()
+    full.close()
 
 
 @pytest.mark.parametrize("gemm", ["skinny", "fp4"])

@@ -85,7 +85,7 @@ SIGNATURES = {
     "b200moe_ep_recv_buffers": ([P, P, P, P, P, P, P], I32),
     "b200moe_ep_push": ([P, P, P, I32, P, I32, I32, I32, P], I32),
     "b200moe_ep_return": ([P, P], I32),
-    "b200moe_ep_forward": ([P, P, P], I32),
+    "b200moe_ep_forward": ([P, P, P, I32], I32),
     "b200moe_ep_combine_p2p": ([P, P, P, P, I32, I32, I32, P, P, P], I32),
     "b200moe_ep_check_errors": ([P, P, P], I32),
     "b200moe_ep_received": ([P, P, P, P, I32], I32),

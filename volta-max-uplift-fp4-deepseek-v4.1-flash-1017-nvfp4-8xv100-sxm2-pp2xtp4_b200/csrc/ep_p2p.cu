@@ -430,6 +430,20 @@ int b200moe::ep_recv_wait(const b200moe_ep* E, EpRecvWait* w) {
   return B200MOE_OK;
 }
 
+int b200moe::ep_return_targets(const b200moe_ep* E, EpReturn* r) {
+  if (!E || !r || !connected(E) || E->world > kEpMaxPeers) return B200MOE_ERR_STATE;
+  *r = EpReturn{};
+  r->home = reinterpret_cast<const int32_t*>(E->shared + E->off_home);
+  for (int i = 0; i < E->world; ++i) r->peer[i] = E->peer[i];
+  r->off_y2home = int64_t(E->off_y2home);
+  r->off_mbox = int64_t(E->off_mbox);
+  r->world = E->world;
+  r->rank = E->rank;
+  r->epoch = E->epoch;
+  r->done = E->done;
+  return B200MOE_OK;
+}
+
 extern "C" {
 
 // Return the local experts' y2 rows (the buffer of b200moe_ep_recv_buffers) to their home ranks.

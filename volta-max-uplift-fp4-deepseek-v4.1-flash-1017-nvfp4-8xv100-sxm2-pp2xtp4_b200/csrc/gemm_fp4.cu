@@ -240,6 +240,19 @@ __device__ __forceinline__ void store_planes8(const uint32_t (&w)[kP], const uin
 }
 
 
+// Where W2 writes the fp16 y2 row of a route, column col: the layer's y2 by
+// route index, or (fused expert-parallel return) the home rank's y2home row,
+// code = (home rank << 24) | route index at home; null for a bad home rank.
+__device__ __forceinline__ __half* y2_row(const Fp4Args& a, int code, int col) {
+  if (!a.ep.home) return reinterpret_cast<__half*>(a.y2) + int64_t(code) * a.H + col;
+  const int hr = code >> 24, hp = code & 0xFFFFFF;
+  if (hr < 0 || hr >= a.ep.world) {
+    set_error(a.err, kErrBounds);
+    return nullptr;
+  }
+  return reinterpret_cast<__half*>(a.ep.peer[hr] + a.ep.off_y2home) + int64_t(hp) * a.H + col;
+}
+
 template <int EPI, int TILES, int RC, int MX>
 __global__ void __launch_bounds__(kThreads, 1)
     fp4_gemm_kernel(const Fp4Args a, const __grid_constant__ CUtensorMap map_x) {
@@ -411,6 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane < ch.count) {
         gx_l = __ldg(a.gx + ch.begin + lane);
         if (EPI == 1) route_l = a.perm[ch.begin + lane];
+        if (EPI == 1 && a.ep.home) route_l = a.ep.home[route_l];  // fused return: (home rank << 24) | route
       }
       const uint32_t b = St::kAccBufs == 2 ? (acc_i & 1u) : 0u;
       const uint32_t bph = St::kAccBufs == 2 ? ((acc_i >> 1) & 1u) : (acc_i & 1u);
@@ -459,9 +473,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (lane == 0) atomicMax(a.rowmax + pos, __float_as_uint(hm));
             } else {
               const int route = __shfl_sync(0xffffffffu, route_l, n);
-              __half* yrow = reinterpret_cast<__half*>(a.y2) + int64_t(route) * a.H + rt * 256 + row;
-              yrow[0] = __float2half_rn(v0 * gx * gw0);
-              yrow[128] = __float2half_rn(v1 * gx * gw0);
+              __half* yrow = y2_row(a, route, rt * 256 + row);
+              if (yrow) {
+                yrow[0] = __float2half_rn(v0 * gx * gw0);
+                yrow[128] = __float2half_rn(v1 * gx * gw0);
+              }
             }
           }
         }
@@ -508,7 +524,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (n >= ch.count) break;
           const int route = __shfl_sync(0xffffffffu, route_l, n);
           const float gx = __shfl_sync(0xffffffffu, gx_l, n);
-          __half* yrow = reinterpret_cast<__half*>(a.y2) + int64_t(route) * a.H + rt * (128 * TILES) + row;
+          __half* yrow = y2_row(a, route, rt * (128 * TILES) + row);
+          if (!yrow) continue;
           float v = 0.f;
 #pragma unroll
           for (int p = 0; p < kP; ++p) v += d0[n * kP + p];
@@ -527,6 +544,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   fence_before();
   __syncthreads();
   if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  if (EPI == 1 && a.ep.home && threadIdx.x == 0) {
+    // fused return: once every CTA's y2 stores are visible, the last CTA raises this rank's return flag
+    // on every rank (the combines wait for them)
+    __threadfence_system();
+    if (atomicAdd(a.ep.done, 1) == int(gridDim.x) - 1) {
+      __threadfence_system();
+      const int e = *a.ep.epoch;
+      for (int r = 0; r < a.ep.world; ++r)
+        st_release_sys(reinterpret_cast<int*>(a.ep.peer[r] + a.ep.off_mbox) + a.ep.world + a.ep.rank, e);
+      *a.ep.done = 0;
+    }
+  }
 }
 
 // ---------------------------------------------------------------- plane kernel

@@ -64,6 +64,20 @@ struct EpRecvWait {
   int device;
 };
 
+// Expert-parallel return fused into the W2 epilogue of an owner's FP4 bank:
+// each route's y2 row goes straight into its home rank's y2home buffer
+// (home[row] = (rank << 24) | route index at home), and the kernel's last CTA
+// raises this rank's return flag on every rank (mbox word world + rank).
+constexpr int kEpMaxPeers = 16;
+struct EpReturn {
+  const int32_t* home;           // null: no fused return
+  uint8_t* peer[kEpMaxPeers];    // every rank's shared exchange allocation
+  int64_t off_y2home, off_mbox;  // offsets in it
+  int world, rank;
+  const int* epoch;              // the step in flight
+  int* done;                     // CTAs finished (reset by the last)
+};
+
 struct PlanArgs {
   const int32_t* ids;  // [n] expert id per route (flat t*k + slot)
   int n;
@@ -138,6 +152,7 @@ struct Fp4Args {
   float* out;
   int H;
   uint32_t* err;
+  EpReturn ep;  // W2 only, optional
 };
 int launch_fp4_gemm(cudaStream_t s, int epi, int rc, bool mx, const Fp4Args& a, const void* map_x, int grid);
 // routes per chunk of the block-scaled FP4 path for a call of S routes (the MMA's N is 4 x this)
@@ -157,6 +172,8 @@ int make_u8_tile_map(void* map_out, const void* base, int64_t rows, int64_t row_
 size_t plan_smem_bytes(int n_keys);
 // the receive of this rank's expert-parallel exchange object (the C ABI's b200moe_ep)
 int ep_recv_wait(const ::b200moe_ep* E, EpRecvWait* w);
+// the fused return's targets (ep_p2p.cu)
+int ep_return_targets(const ::b200moe_ep* E, EpReturn* r);
 // fp16 rows -> int8 blocks of kIq2XBlockBytes per 256-wide K tile (IQ2 activations)
 int launch_quant_s8(cudaStream_t s, const __half* src, int64_t src_stride, int K, int rows, const int32_t* range,
                     uint8_t* dst);

@@ -211,7 +211,8 @@ struct Marks {
 
 int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const void* x, int x_dtype,
                 const int32_t* ids, const float* w, float* out, int m, bool prefill = false,
-                const RowsMode* rows = nullptr, const EpRecvWait* recv = nullptr) {
+                const RowsMode* rows = nullptr, const EpRecvWait* recv = nullptr,
+                const EpReturn* ep_ret = nullptr) {
   const auto& c = L->cfg;
   Marks marks{L, s};
   if (!L->maps_set) return B200MOE_ERR_STATE;
@@ -348,6 +349,7 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
         f.out = out;
         f.H = c.hidden;
         f.err = L->err;
+        if (epi == 1 && ep_ret) f.ep = *ep_ret;  // y2 rows straight to their home ranks
         const int rc = fp4_routes_per_chunk(S);
         if (launch_fp4_gemm(s, epi, rc, c.fp4_format == B200MOE_MXFP4, f, L->f4_map_x[epi][fp4_rc_index(rc)],
                             L->grid))
@@ -749,15 +751,20 @@ int b200moe_forward_rows(b200moe_layer* L, void* stream, const void* rows, const
                      nullptr, nullptr, max_rows, true, &rm);
 }
 
-int b200moe_ep_forward(b200moe_ep* ep, b200moe_layer* L, void* stream) {
+int b200moe_ep_forward(b200moe_ep* ep, b200moe_layer* L, void* stream, int fuse_return) {
   if (!ep || !L) return B200MOE_ERR_INVALID_ARG;
   EpRecvWait w{};
   if (int st = ep_recv_wait(ep, &w)) return st;
   if (w.device != L->device || L->cfg.top_k != 1 || w.max_rows > L->t_max) return B200MOE_ERR_INVALID_ARG;
+  EpReturn r{};
+  if (fuse_return) {  // only a block-scaled FP4-only layer writes every y2 row in one epilogue
+    if (L->cfg.prefill_gemm < 2 || L->cfg.n_iq2 > 0 || L->cfg.n_fp4 < 1) return B200MOE_ERR_INVALID_ARG;
+    if (int st = ep_return_targets(ep, &r)) return st;
+  }
   DeviceGuard guard(L->device);
   RowsMode rm{w.out, w.out + 1, static_cast<__half*>(w.y2)};
   return run_forward(L, layer_workspace(L), static_cast<cudaStream_t>(stream), w.rows, B200MOE_F16, w.expert_ids,
-                     nullptr, nullptr, w.max_rows, true, &rm, &w);
+                     nullptr, nullptr, w.max_rows, true, &rm, &w, fuse_return ? &r : nullptr);
 }
 
 int b200moe_check_errors(b200moe_layer* L, void* stream, uint32_t* bits) {

@@ -187,6 +187,8 @@ class ExpertParallelMoe:
         self._timed = False
         self.last_routes_in = 0
         self._peer, self._own_peer = None, False
+        # FP4-only block-scaled owners store their y2 rows at home from the W2 epilogue (no return launch)
+        self.fused_return = exchange == "p2p" and gemm == "fp4" and self.layer.n_iq2 == 0 and self.layer.n_fp4 > 0
         if exchange == "p2p":
             if peer is None:
                 peer, self._own_peer = PeerExchange(hidden, S, group, dev), True
@@ -290,13 +292,14 @@ class ExpertParallelMoe:
         plan_events = user_events if len(user_events) >= 3 else (self._plan_ev if timed else [])
         if timed and plan_events is self._plan_ev:
             self.layer.set_timing_events(self._plan_ev)
-        _lib.check("b200moe_ep_forward", L.b200moe_ep_forward(pe.handle, self.layer._h, st))
+        _lib.check("b200moe_ep_forward", L.b200moe_ep_forward(pe.handle, self.layer._h, st, int(self.fused_return)))
         if timed and plan_events is self._plan_ev:
             self.layer.set_timing_events(user_events or None)
         self._last_plan_events = plan_events if timed else []
         if timed:
             ev[2].record()
-        _lib.check("b200moe_ep_return", L.b200moe_ep_return(pe.handle, st))
+        if not self.fused_return:  # otherwise the owner's W2 epilogue stored the y2 rows at home
+            _lib.check("b200moe_ep_return", L.b200moe_ep_return(pe.handle, st))
         _lib.check("b200moe_ep_combine_p2p", L.b200moe_ep_combine_p2p(
             pe.handle, st, ids.data_ptr(), w.data_ptr(), T, k, self.num_experts, self.owner.data_ptr(),
             _lib.ptr(residual), out.data_ptr()))
