@@ -69,6 +69,7 @@ SIGNATURES = {
     "b200moe_debug_inter": ([P, P, P, I32], I32),
     "b200moe_set_timing_events": ([P, P, I32], I32),
     "b200moe_set_split_k": ([P, I32, I32], I32),
+    "b200moe_set_decode_fusion": ([P, I32], I32),
     "b200moe_route_plan": ([P, P, I32, I32, P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P], I32),
     "b200moe_quantize_nvfp4": ([P, P, I32, I32, P, P, P], I32),
     "b200moe_quantize_mxfp4": ([P, P, I32, I32, P, P, P], I32),

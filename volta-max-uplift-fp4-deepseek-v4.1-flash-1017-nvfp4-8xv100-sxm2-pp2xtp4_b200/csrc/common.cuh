@@ -8,6 +8,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include "../../include/b200moe.h"
 
@@ -36,6 +37,53 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 
 __device__ __forceinline__ void set_error(uint32_t* err, uint32_t bits) {
   if (err) atomicOr(err, bits);
+}
+
+// Programmatic dependent launch.  The kernels of the forward chain (gating,
+// route plan, planes, expert GEMMs, combine) are launched with programmatic
+// stream serialization, so a launch may be scheduled, and run its set-up
+// (barriers, TMEM, tensor maps), while the previous one finishes.  Each such
+// kernel calls pdl_wait() in every thread before it reads or writes memory
+// that an earlier launch of the stream touches, and before any early return:
+// the wait ends when the previous grid has completed with its writes visible,
+// so the completion of any grid of the chain implies that of every earlier
+// one.  pdl_trigger() lets the stream's next launch be scheduled: the small
+// kernels call it right after their wait, the expert GEMMs only at their end
+// (measured on B200: CTAs of the next launch waiting beside a GEMM's for its
+// whole run slowed the configs[1] decode step by 1-2 %, while a trigger at
+// the end saved 3 us of the 64 us M = 1 step).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Whether chain launches carry the programmatic attribute (B200MOE_PDL=0 turns it off).
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("B200MOE_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+// Launch a chain kernel (one that calls pdl_wait() as above) on stream s.
+template <typename... P, typename... A>
+inline cudaError_t launch_chain_attr(bool pdl, void (*kernel)(P...), dim3 grid, dim3 block, size_t smem,
+                                     cudaStream_t s, A&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<A&&>(args)...);
+}
+template <typename... P, typename... A>
+inline cudaError_t launch_chain(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                A&&... args) {
+  return launch_chain_attr(pdl_enabled(), kernel, grid, block, smem, s, static_cast<A&&>(args)...);
 }
 
 // System-scope acquire load / release store (flags written over NVLink by peer GPUs).

@@ -41,204 +41,12 @@
 #include <atomic>
 
 #include "common.cuh"
+#include "fp4_device.cuh"
 #include "internal.h"
 #include "layout.cuh"
 
 namespace b200moe {
 namespace {
-
-constexpr int kP = kFp4Planes;             // activation planes
-constexpr int kATile = 128 * 128;          // weight tile: 128 rows x 256 FP4 = 16 KB
-constexpr int kSFBytes = 4 * 512;          // the scale blocks of one 256-wide K tile
-constexpr int kThreads = 6 * 32;           // producer, MMA, 4 epilogue warps
-constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kSfCol = 256;           // scale columns start after the two accumulator buffers
-
-// Stage layout by weight tiles per unit and routes per chunk (RC: the MMA's N
-// is 4 planes x RC; small batches use small chunks, so the tensor pipe does not
-// spend its time on empty columns).  Two tiles (W13: the gate and up tiles; W2:
-// two adjacent 128-row tiles) make stages of 36 KB + the plane tile, 4 of them;
-// one tile 18 KB + the plane tile, 7 stages.  Each stage has its own TMEM scale
-// columns: a scale copy never lands under an MMA still in flight.
-template <int TILES, int RC, int MX = 0>
-struct Fp4Stage {
-  static constexpr int kRC = RC;         // routes per chunk
-  static constexpr int kN = kP * RC;     // MMA N: 16, 32 or 64
-  static constexpr int kBTile = kN * 128;  // activation tile: kN rows x 256 FP4
-  // kind::mxf4nvf4: A and B E2M1 (1), K-major, N = kN, M = 128; scales UE4M3 per 16 (NVFP4) or, bit 23,
-  // UE8M0 per 32 (MXFP4)
-  static constexpr uint32_t kIdesc = (1u << 7) | (1u << 10) | (uint32_t(kN >> 3) << 17) | (uint32_t(MX) << 23) |
-                                     (uint32_t(128 >> 4) << 24);
-  static constexpr int kTiles = TILES;  // weight tiles per unit
-  static constexpr int kUnit = kTiles * (kATile + kSFBytes);  // one weight unit, one bulk copy
-  static constexpr int kOffAG = 0;
-  static constexpr int kOffAU = kATile;  // W13 only
-  static constexpr int kOffSFG = kTiles * kATile;
-  static constexpr int kOffSFU = kOffSFG + kSFBytes;  // W13 only
-  static constexpr int kOffB = kUnit;
-  static constexpr int kOffSFB = kOffB + kBTile;
-  static constexpr int kBytes = kOffSFB + kSFBytes;
-  static constexpr int kStages = TILES == 2 ? 4 : 7;
-  static constexpr uint32_t kSfCols = TILES == 2 ? 48 : 32;  // tile 0 (, tile 1), activations: 16 each
-  static constexpr uint32_t kSfB = TILES == 2 ? 32 : 16;
-  // accumulator columns of one item (TILES x N) and how many items' accumulators TMEM holds below the
-  // scale columns: two (the epilogue of one item overlaps the next item's MMAs) up to N = 64, one at N = 128
-  static constexpr uint32_t kAccCols = uint32_t(TILES * kN);
-  static constexpr int kAccBufs = 2 * kAccCols <= kSfCol ? 2 : 1;
-  static constexpr size_t kSmem = 1024 + size_t(kStages) * kBytes + 64 * 8;
-  static_assert(kBytes % 1024 == 0, "128-byte swizzled tiles need 1024-byte aligned stages");
-  static_assert(kAccBufs * kAccCols <= kSfCol, "accumulators below the scale columns");
-  static_assert(kSfCol + kStages * kSfCols <= kTmemCols, "TMEM columns");
-  static_assert(kSmem <= 227 * 1024, "shared memory");
-};
-
-__device__ __forceinline__ uint64_t desc_sw128(uint32_t addr) {
-  return uint64_t((addr >> 4) & 0x3FFF) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) | (uint64_t(1) << 46) |
-         (uint64_t(2) << 61);
-}
-// a 512-byte scale block: K-major, no swizzle, 8-row core matrices of 16 B rows 128 B apart
-__device__ __forceinline__ uint64_t desc_sf(uint32_t addr) {
-  return uint64_t((addr >> 4) & 0x3FFF) | (uint64_t(1) << 16) | (uint64_t(128 >> 4) << 32) | (uint64_t(1) << 46);
-}
-
-__device__ __forceinline__ void sf_copy(uint32_t tcol, uint32_t smem) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(tcol), "l"(desc_sf(smem)));
-}
-
-template <int MX>
-__device__ __forceinline__ void mma_fp4(uint32_t d, uint64_t a, uint64_t b, uint32_t sfa, uint32_t sfb,
-                                        uint32_t accumulate, uint32_t idesc) {
-  if (MX)
-    asm volatile(
-        "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n"
-        "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p; }" ::"r"(d),
-        "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb));
-  else
-    asm volatile(
-        "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n"
-        "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p; }" ::"r"(d),
-        "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb));
-}
-
-__device__ __forceinline__ void commit_to(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ __half swiglu1(float g, float u, float limit) {
-  g = g > limit ? limit : g;
-  u = u > limit ? limit : u;
-  u = u < -limit ? -limit : u;
-  return __float2half_rn(__fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), u));
-}
-
-// ---------------------------------------------------------------- planes
-// Nearest E2M1 value (ties to even) of v >= 0, and its 3-bit magnitude code:
-// step 0.5 below 2, 1 below 4, 2 above, saturating at 6.
-__device__ __forceinline__ float e2m1_round(float v) {
-  const float q = v < 2.f ? rintf(v * 2.f) * 0.5f : v < 4.f ? rintf(v) : rintf(v * 0.5f) * 2.f;
-  return fminf(q, 6.f);
-}
-__device__ __forceinline__ uint32_t e2m1_code_of(float q) {  // q on the E2M1 grid
-  return q < 2.f ? uint32_t(q * 2.f) : q < 4.f ? uint32_t(q) + 2u : uint32_t(q * 0.5f) + 4u;
-}
-// Nearest E4M3 byte of x >= 0 (ties to even, saturating at 448) by the
-// hardware conversion; both halves of the pair convert x.
-__device__ __forceinline__ uint32_t e4m3_rn(float x) {
-  uint16_t pair;
-  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %1;" : "=h"(pair) : "f"(x));
-  return pair & 0xFFu;
-}
-
-// One half-block (8 consecutive elements, thread of lane = half-block index
-// mod 32) of a row through the kP planes: per plane the E2M1 codes (w[p], 8
-// nibbles) and, on lane 8j of a warp, the scale word of the 64-wide K step the
-// lanes 8j .. 8j + 7 cover (word[p]).  g: the row's factor (its amax over
-// 6 * 448 for NVFP4, 1 for MXFP4), inv_g its inverse; r: the elements, left
-// holding the residual.  Every lane of the warp takes part (shuffles).
-template <int MX>
-__device__ __forceinline__ void quantize_planes8(float (&r)[8], bool own, float g, float inv_g, uint32_t (&w)[kP],
-                                                 uint32_t (&word)[kP]) {
-#pragma unroll
-  for (int p = 0; p < kP; ++p) {
-    float bm = 0.f;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) bm = fmaxf(bm, fabsf(r[e]));
-    bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 1));  // the other half of the 16-block
-    if (MX) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 2));  // the 32-block: four half-blocks
-    uint32_t sc;
-    float scale;
-    if (MX) {  // UE8M0: the smallest 2^e with 6 * 2^e >= bm
-      const int e = bm > 0.f ? max(-126, min(127, mx_exponent(bm))) : -127;
-      sc = own && bm > 0.f ? uint32_t(e + 127) : 0u;
-      scale = sc ? __uint_as_float(sc << 23) : 0.f;  // 2^e, e >= -126: a normal float
-    } else {
-      sc = own ? e4m3_rn(bm / 6.f * inv_g) : 0u;
-      // the E4M3 byte's value (sc < 0x80), built from its bits: 2^(e - 7) (1 + m / 8) or m 2^-9
-      const uint32_t ex = sc >> 3, mn = sc & 7u;
-      const float sv = ex ? __uint_as_float(((ex + 120u) << 23) | (mn << 20)) : float(mn) * 0.001953125f;
-      scale = sv * g;
-    }
-    const float rs = scale > 0.f ? __frcp_rn(scale) : 0.f;  // = 1 / scale, rounded to nearest
-    uint32_t cw = 0u;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float v = r[e] * rs;
-      const float q = e2m1_round(fabsf(v));
-      r[e] -= copysignf(q, v) * scale;
-      cw |= (e2m1_code_of(q) | (v < 0.f ? 8u : 0u)) << (4 * e);
-    }
-    w[p] = cw;
-    // the scale bytes of one 64-wide K step as one word from lane 8j: NVFP4 blocks 4j .. 4j + 3 (lanes
-    // 8j, +2, +4, +6), MXFP4 blocks 2j, 2j + 1 (lanes 8j, 8j + 4)
-    uint32_t wd = sc;
-    if (MX) {
-      wd |= __shfl_down_sync(0xffffffffu, sc, 4) << 8;
-    } else {
-      wd |= __shfl_down_sync(0xffffffffu, sc, 2) << 8;
-      wd |= __shfl_down_sync(0xffffffffu, sc, 4) << 16;
-      wd |= __shfl_down_sync(0xffffffffu, sc, 6) << 24;
-    }
-    word[p] = wd;
-  }
-}
-
-// Store half-block hb's planes of sorted position pos (index n in its chunk,
-// the chunk's scale blocks at sfb_chunk) into the plane rows and scale blocks.
-__device__ __forceinline__ void store_planes8(const uint32_t (&w)[kP], const uint32_t (&word)[kP], int hb, int K,
-                                              int pos, int n, uint8_t* planes, uint8_t* sfb_chunk) {
-#pragma unroll
-  for (int p = 0; p < kP; ++p) {
-    *reinterpret_cast<uint32_t*>(planes + (int64_t(pos) * kP + p) * (K / 2) + hb * 4) = w[p];
-    if ((hb & 7) == 0) {
-      const int mr = n * kP + p;
-      *reinterpret_cast<uint32_t*>(sfb_chunk + (hb >> 3) * 512 + (mr & 31) * 16 + (mr >> 5) * 4) = word[p];
-    }
-  }
-}
-
 
 // Where W2 writes the fp16 y2 row of a route, column col: the layer's y2 by
 // route index, or (fused expert-parallel return) the home rank's y2home row,
@@ -293,6 +101,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   fence_after();
   const uint32_t tmem = tmem_base_sh;
+  pdl_wait();  // the plan, planes and (W2) SwiGLU rows of the launches before are complete
   const int n_kt = a.K / 256;
   const int n_ks = a.K / 64;
   const int n_items = a.n_chunks[a.bank] * a.n_rt;
@@ -544,6 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   fence_before();
   __syncthreads();
   if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  pdl_trigger();  // the next launch may take this SM (and its TMEM) now
   if (EPI == 1 && a.ep.home && threadIdx.x == 0) {
     // fused return: once every CTA's y2 stores are visible, the last CTA raises this rank's return flag
     // on every rank (the combines wait for them)
@@ -572,22 +382,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 // of one sorted position, its amax taken by the W13 epilogue (rowmax).
 constexpr int kPlaneThreads = 128;
 constexpr int kSlice = kPlaneThreads * 8;
-// eight 16-bit values (f16, or bf16 when BF16) as floats
-template <int BF16>
-__device__ __forceinline__ void load8(const uint4& v, float (&r)[8]) {
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    if (BF16) {
-      r[2 * e] = __uint_as_float(w[e] << 16);
-      r[2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
-    } else {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
-      r[2 * e] = f.x;
-      r[2 * e + 1] = f.y;
-    }
-  }
-}
 template <int BY_TOKEN, int BF16, int MX>
 __global__ void __launch_bounds__(kPlaneThreads) fp4_planes_kernel(
     const uint16_t* __restrict__ src, int64_t src_stride, int K, const int32_t* __restrict__ inv, int top_k,
@@ -600,6 +394,8 @@ __global__ void __launch_bounds__(kPlaneThreads) fp4_planes_kernel(
   const int nhb = K / 8, n_ks = K / 64;
   const int hb = blockIdx.y * kPlaneThreads + t, blk = hb >> 1;  // this thread's half-block
   const bool own = hb < nhb;
+  pdl_wait();
+  pdl_trigger();
   const int lo = bank_range[2 * bank], hi = bank_range[2 * bank + 1];
   const int rows = BY_TOKEN ? n_tokens : hi - lo;
   for (int ri = blockIdx.x; ri < rows; ri += gridDim.x) {
@@ -672,6 +468,8 @@ __global__ void fp4_combine_kernel(const __half* __restrict__ y2, const int32_t*
                                    const int32_t* __restrict__ bank_range, int n_banks, const float* __restrict__ w,
                                    int T, int k, int H, float* __restrict__ out) {
   const int per_row = H / 4;
+  pdl_wait();
+  pdl_trigger();
   const int end = bank_range[2 * (n_banks - 1) + 1];
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < int64_t(T) * per_row;
        i += int64_t(gridDim.x) * blockDim.x) {
@@ -762,8 +560,10 @@ int launch_fp4_one(cudaStream_t s, const Fp4Args& a, const void* map_x, int grid
       return -1;
     attr_set.fetch_or(uint64_t(1) << dev);
   }
-  fp4_gemm_kernel<EPI, TILES, RC, MX><<<grid, kThreads, smem, s>>>(a, *static_cast<const CUtensorMap*>(map_x));
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_chain(fp4_gemm_kernel<EPI, TILES, RC, MX>, dim3(grid), dim3(kThreads), smem, s, a,
+                      *static_cast<const CUtensorMap*>(map_x)) == cudaSuccess
+             ? 0
+             : -1;
 }
 
 template <int MX>
@@ -802,9 +602,10 @@ int launch_fp4_planes(cudaStream_t s, bool by_token, bool bf16, bool mx, const v
                                  : (mx ? fp4_planes_kernel<1, 0, 1> : fp4_planes_kernel<1, 0, 0>))
                          : (mx ? fp4_planes_kernel<0, 0, 1> : fp4_planes_kernel<0, 0, 0>);
   if (!by_token && bf16) return -1;  // SwiGLU rows are fp16
-  kernel<<<grid, kPlaneThreads, 0, s>>>(x, src_stride, K, inv, top_k, chunk_of, bank, bank_range, by_token ? max_rows : 0,
-                                        rowmax, planes, plane_rows, sfb, gx);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_chain(kernel, grid, dim3(kPlaneThreads), 0, s, x, src_stride, K, inv, top_k, chunk_of, bank,
+                      bank_range, by_token ? max_rows : 0, rowmax, planes, plane_rows, sfb, gx) == cudaSuccess
+             ? 0
+             : -1;
 }
 
 int launch_route_combine(cudaStream_t s, const __half* y2, const int32_t* inv, const int32_t* bank_range,
@@ -812,8 +613,10 @@ int launch_route_combine(cudaStream_t s, const __half* y2, const int32_t* inv, c
   if (H % 4 || T < 1) return -1;
   const int64_t n = int64_t(T) * (H / 4);
   const int blocks = int(std::min<int64_t>((n + 255) / 256, 148 * 16));
-  fp4_combine_kernel<<<std::max(blocks, 1), 256, 0, s>>>(y2, inv, bank_range, n_banks, w, T, k, H, out);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_chain(fp4_combine_kernel, dim3(std::max(blocks, 1)), dim3(256), 0, s, y2, inv, bank_range, n_banks,
+                      w, T, k, H, out) == cudaSuccess
+             ? 0
+             : -1;
 }
 
 int launch_fp4_tile(cudaStream_t s, bool mx, const uint8_t* codes, const uint8_t* scales, int n_slots,

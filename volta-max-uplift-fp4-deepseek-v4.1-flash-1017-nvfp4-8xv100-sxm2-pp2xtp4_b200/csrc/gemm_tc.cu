@@ -192,6 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
+  pdl_wait();  // the plan, gathered rows and (W2) SwiGLU rows of the launches before are complete
 
   const int n_kb = a.K / BK;
   const int n_kt = a.K / F::KT;
@@ -498,6 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols));
   }
+  pdl_trigger();  // the next launch may take this SM (and its TMEM) now
 }
 
 // ---------------------------------------------------------------- host side
@@ -542,8 +544,10 @@ static int launch_tc_one(cudaStream_t s, const TcArgs& a, const void* map, int g
       return -1;
     attr_dev_mask |= 1 << dev;
   }
-  tc_gemm_kernel<FMT, EPI><<<grid, kThreads, smem, s>>>(a, *static_cast<const CUtensorMap*>(map));
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_chain(tc_gemm_kernel<FMT, EPI>, dim3(grid), dim3(kThreads), smem, s, a,
+                      *static_cast<const CUtensorMap*>(map)) == cudaSuccess
+             ? 0
+             : -1;
 }
 
 int make_u8_tile_map(void* map_out, const void* base, int64_t rows, int64_t row_bytes, int box_bytes, int box_rows) {
@@ -573,6 +577,8 @@ int launch_tc_gemm(cudaStream_t s, int fmt, int epi, const TcArgs& a, const void
 __global__ void gather_rows_kernel(const uint16_t* __restrict__ x, int bf16, const int32_t* __restrict__ perm,
                                    int S, int k, int H, uint16_t* __restrict__ xperm) {
   const int per_row = H / 8;
+  pdl_wait();
+  pdl_trigger();
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < int64_t(S) * per_row;
        i += int64_t(gridDim.x) * blockDim.x) {
     const int p = int(i / per_row), c = int(i % per_row);
@@ -595,9 +601,11 @@ int launch_gather_rows(cudaStream_t s, const void* x, int bf16, const int32_t* p
                        void* xperm) {
   int64_t n = int64_t(S) * (H / 8);
   int blocks = int(std::min<int64_t>((n + 255) / 256, 148 * 16));
-  gather_rows_kernel<<<blocks < 1 ? 1 : blocks, 256, 0, s>>>(static_cast<const uint16_t*>(x), bf16, perm, S, k, H,
-                                                             static_cast<uint16_t*>(xperm));
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_chain(gather_rows_kernel, dim3(blocks < 1 ? 1 : blocks), dim3(256), 0, s,
+                      static_cast<const uint16_t*>(x), bf16, perm, S, k, H, static_cast<uint16_t*>(xperm)) ==
+                 cudaSuccess
+             ? 0
+             : -1;
 }
 
 }  // namespace b200moe

@@ -756,6 +756,8 @@ __global__ void quant_s8_kernel(const __half* __restrict__ src, int64_t src_stri
                                 const int32_t* __restrict__ range, uint8_t* __restrict__ dst) {
   const int lane = threadIdx.x & 31;
   const int n_kt = K / kIq2KTile;
+  pdl_wait();
+  pdl_trigger();
   const int lo = range ? range[0] : 0, hi = range ? min(range[1], rows) : rows;
   const int64_t n_blocks = int64_t(max(hi - lo, 0)) * n_kt;
   for (int64_t blk = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) / 32; blk < n_blocks;
@@ -798,8 +800,10 @@ int launch_quant_s8(cudaStream_t s, const __half* src, int64_t src_stride, int K
   if (rows <= 0) return 0;
   const int64_t warps = int64_t(rows) * (K / kIq2KTile);
   const int64_t blocks = std::min<int64_t>((warps + 7) / 8, 148 * 16);
-  quant_s8_kernel<<<int(blocks), 256, 0, s>>>(src, src_stride, K, rows, range, dst);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_chain(quant_s8_kernel, dim3(int(blocks)), dim3(256), 0, s, src, src_stride, K, rows, range, dst) ==
+                 cudaSuccess
+             ? 0
+             : -1;
 }
 
 // One kernel per format and epilogue; the split-K is read from the device
@@ -808,6 +812,7 @@ int launch_quant_s8(cudaStream_t s, const __half* src, int64_t src_stride, int K
 template <int FMT, int EPI>
 __global__ void __launch_bounds__(kGemvThreads, Fmt<FMT>::CTAS) gemv_kernel(const GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
+  pdl_wait();
   switch (a.ks_sel[a.bank]) {
     case 1: gemv_body<FMT, EPI, 1>(a, smem); break;
     case 2: gemv_body<FMT, EPI, 2>(a, smem); break;
@@ -816,6 +821,7 @@ __global__ void __launch_bounds__(kGemvThreads, Fmt<FMT>::CTAS) gemv_kernel(cons
     default:
       if (threadIdx.x == 0) set_error(a.err, kErrRange);
   }
+  pdl_trigger();
 }
 
 template <int FMT, int EPI>
@@ -830,8 +836,7 @@ static int launch_one(cudaStream_t s, const GemvArgs& a) {
       return -1;
     attr_set.fetch_or(uint64_t(1) << dev);
   }
-  gemv_kernel<FMT, EPI><<<a.grid, kGemvThreads, smem, s>>>(a);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_chain(gemv_kernel<FMT, EPI>, dim3(a.grid), dim3(kGemvThreads), smem, s, a) == cudaSuccess ? 0 : -1;
 }
 
 int launch_gemv(cudaStream_t s, const GemvArgs& a) {

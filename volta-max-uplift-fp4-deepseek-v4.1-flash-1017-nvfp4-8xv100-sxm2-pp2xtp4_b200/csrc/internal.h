@@ -155,6 +155,40 @@ struct Fp4Args {
   EpReturn ep;  // W2 only, optional
 };
 int launch_fp4_gemm(cudaStream_t s, int epi, int rc, bool mx, const Fp4Args& a, const void* map_x, int grid);
+
+// Fused small-batch decode of an FP4-only layer (decode.cu): two launches, W13
+// and W2, each planning the call's routes itself, quantizing its chunks'
+// activation rows into shared memory and (W2) combining the token rows.
+constexpr int kDecodeMaxRoutes = 64;
+struct DecArgs {
+  const uint8_t* wt;          // weight units of this projection [slot][n_rt][K/256]
+  const float* globals;       // NVFP4 [slot][3] FP32 global scales, null for MXFP4
+  int K;                      // H (W13) or I (W2)
+  int n_rt;                   // items per chunk: W13 I/128, W2 H/256
+  int n_slots;
+  const void* src;            // W13: token rows x [M][H] (f16 or bf16); W2: the SwiGLU rows [S][inter] (f16)
+  int64_t src_stride;         // elements
+  const int32_t* ids;         // [S] expert ids (route = token * top_k + slot)
+  const float* w_in;          // [S] routing weights
+  int S;
+  int top_k;
+  int num_experts;
+  const int32_t* key_of_expert;  // expert -> bank-0 slot (n_keys: none)
+  int n_keys;
+  __half* inter;              // W13 out: SwiGLU rows at sorted positions, stride inter_stride
+  int inter_stride;
+  float limit;
+  __half* y2;                 // W2: fp16 rows by route [S][H]
+  int32_t* counters;          // W2: [M][H/32] completion counts (zero between calls)
+  float* out;                 // W2: [M][H]
+  int H;
+  int32_t* perm_out;          // W13: the sorted order, written by CTA 0
+  uint32_t* err;
+  int stages;                 // weight stages in shared memory
+};
+// 0 when the fused decode launches, -1 when the shape does not fit it (the caller takes the chained path)
+int launch_fp4_decode(cudaStream_t s, int epi, bool mx, bool bf16, const DecArgs& a, int grid);
+bool fp4_decode_fits(int K);
 // routes per chunk of the block-scaled FP4 path for a call of S routes (the MMA's N is 4 x this)
 inline int fp4_routes_per_chunk(int S) { return S <= 64 ? 4 : S <= 1024 ? 8 : S < 4096 ? 16 : 32; }
 inline int fp4_rc_index(int rc) { return rc == 4 ? 0 : rc == 8 ? 1 : rc == 16 ? 2 : 3; }

@@ -36,6 +36,7 @@ struct b200moe_layer {
   int32_t* key_of_expert = nullptr;
   bool maps_set = false, tables_set = false;  // tables_set: both projections' tables
   int ks_fixed[2] = {0, 0};  // split-K per bank set by the caller (0: chosen per launch)
+  int fuse_max_routes = 0;  // decode calls of at most this many routes take the fused launches (0: off)
 
   // workspace
   int s_max = 0, t_max = 0;
@@ -229,16 +230,62 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   }
   const int S = m * c.top_k;
   const __half* xsrc = static_cast<const __half*>(x);
+  // the fused small-batch decode (decode.cu, off unless set: measured slower): an FP4-only layer on the
+  // block-scaled path, at most fuse_max_routes routes, the layer's own routing (not expert-parallel rows),
+  // no y13 capture
+  const bool fused = !rows && c.prefill_gemm >= 2 && c.n_fp4 > 0 && c.n_iq2 == 0 && S <= L->fuse_max_routes &&
+                     S <= kDecodeMaxRoutes && !ws.dbg_y13 && ws_in.counters && fp4_decode_fits(c.hidden) &&
+                     fp4_decode_fits(c.inter);
   // bf16 x feeds the block-scaled path's planes directly; only the GEMV banks (and the tcgen05 row gather,
   // which converts itself) want it in fp16
   const bool x_bf16_direct =
-      x_dtype == B200MOE_BF16 && c.prefill_gemm >= 2 && c.n_fp4 > 0 && c.n_iq2 == 0 && ws.own;
+      x_dtype == B200MOE_BF16 && c.prefill_gemm >= 2 && c.n_fp4 > 0 && c.n_iq2 == 0 && (ws.own || fused);
   marks.mark();
   if (x_dtype == B200MOE_BF16 && !x_bf16_direct) {
     if (launch_convert_bf16(s, x, int64_t(m) * c.hidden, ws.x16)) return B200MOE_ERR_CUDA;
     xsrc = ws.x16;
   }
   marks.mark();  // after the bf16 conversion (or none): the event layout does not depend on x's dtype
+  if (fused) {
+    DecArgs d{};
+    d.n_slots = c.n_fp4;
+    d.ids = ids;
+    d.w_in = w;
+    d.S = S;
+    d.top_k = c.top_k;
+    d.num_experts = c.num_experts;
+    d.key_of_expert = L->key_of_expert;
+    d.n_keys = c.n_fp4 + c.n_iq2;
+    d.globals = c.fp4_format == B200MOE_NVFP4 ? L->globals : nullptr;
+    d.H = c.hidden;
+    d.err = L->err;
+    const bool mx = c.fp4_format == B200MOE_MXFP4;
+    // W13 (+ SwiGLU): the token rows of x planed in each CTA
+    d.wt = L->f4_units[0];
+    d.K = c.hidden;
+    d.n_rt = c.inter / 128;
+    d.src = x_bf16_direct ? x : static_cast<const void*>(xsrc);
+    d.src_stride = c.hidden;
+    d.inter = ws.inter;
+    d.inter_stride = c.inter;
+    d.limit = c.swiglu_limit;
+    d.perm_out = ws.perm;
+    if (launch_fp4_decode(s, 0, mx, x_bf16_direct, d, L->grid)) return B200MOE_ERR_CUDA;
+    marks.mark();
+    // W2 (+ combine): the SwiGLU rows planed in each CTA, the token rows summed by the CTA that completes them
+    d.wt = L->f4_units[1];
+    d.K = c.inter;
+    d.n_rt = c.hidden / 256;
+    d.src = ws.inter;
+    d.src_stride = c.inter;
+    d.y2 = ws.y2;
+    d.counters = ws_in.counters;
+    d.out = out;
+    d.perm_out = nullptr;
+    if (launch_fp4_decode(s, 1, mx, false, d, L->grid)) return B200MOE_ERR_CUDA;
+    marks.mark();
+    return B200MOE_OK;
+  }
   // int8 blocks of the token rows for the IQ2 bank's W13 (in rows mode after the plan, which may be the
   // launch that learns how many rows this call has)
   auto quant_rows = [&]() {
@@ -805,6 +852,12 @@ int b200moe_set_timing_events(b200moe_layer* L, void* const* events, int n) {
   if (!L || n < 0 || n > 16 || (n > 0 && !events)) return B200MOE_ERR_INVALID_ARG;
   for (int i = 0; i < n; ++i) L->events[i] = static_cast<cudaEvent_t>(events[i]);
   L->n_events = n;
+  return B200MOE_OK;
+}
+
+int b200moe_set_decode_fusion(b200moe_layer* L, int max_routes) {
+  if (!L || max_routes < 0) return B200MOE_ERR_INVALID_ARG;
+  L->fuse_max_routes = std::min(max_routes, kDecodeMaxRoutes);
   return B200MOE_OK;
 }
 

@@ -220,6 +220,8 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanArgs a) {
   int* aux = start + nk;        // [nk]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   __shared__ int s_recv;
+  pdl_wait();
+  pdl_trigger();
   if (a.recv.flags) {
     // expert-parallel receive: every source rank's rows are in once its data
     // flag reaches this step's epoch; the rows received are the reservation
@@ -439,8 +441,7 @@ int launch_plan(cudaStream_t s, const PlanArgs& a) {
   const size_t smem = plan_smem_bytes(nk);
   if (smem > 200 * 1024) return -1;
   if (product && a.n <= 32) {  // the one-warp path needs neither the block nor the shared histograms
-    plan_kernel<<<1, 32, 0, s>>>(a);
-    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+    return launch_chain(plan_kernel, dim3(1), dim3(32), 0, s, a) == cudaSuccess ? 0 : -1;
   }
   static std::atomic<uint64_t> attr_set{0};  // devices whose attribute is set
   int dev = 0;
@@ -450,8 +451,7 @@ int launch_plan(cudaStream_t s, const PlanArgs& a) {
       return -1;
     attr_set.fetch_or(uint64_t(1) << dev);
   }
-  plan_kernel<<<1, kPlanThreads, smem, s>>>(a);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_chain(plan_kernel, dim3(1), dim3(kPlanThreads), smem, s, a) == cudaSuccess ? 0 : -1;
 }
 
 // ------------------------------------------------------------------ gating
@@ -479,6 +479,8 @@ __global__ void gating_kernel(const float* __restrict__ logits, int T, int E, in
   const unsigned full = 0xffffffffu;
   const int lane = threadIdx.x & 31;
   const int warps = (gridDim.x * blockDim.x) >> 5;
+  pdl_wait();
+  pdl_trigger();
   for (int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < T; t += warps) {
     const float* row = logits + int64_t(t) * E;
     float v[MAXV];
@@ -548,15 +550,16 @@ int launch_gating(cudaStream_t s, const float* logits, int T, int E, int k, int3
   int blocks = (T + 7) / 8;
   if (blocks > 148 * 16) blocks = 148 * 16;
   if (blocks < 1) blocks = 1;
-  if (E <= 128) gating_kernel<4><<<blocks, threads, 0, s>>>(logits, T, E, k, ids, w, err);
-  else if (E <= 256) gating_kernel<8><<<blocks, threads, 0, s>>>(logits, T, E, k, ids, w, err);
-  else if (E <= 512) gating_kernel<16><<<blocks, threads, 0, s>>>(logits, T, E, k, ids, w, err);
-  else gating_kernel<32><<<blocks, threads, 0, s>>>(logits, T, E, k, ids, w, err);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  auto kernel = E <= 128 ? gating_kernel<4> : E <= 256 ? gating_kernel<8> : E <= 512 ? gating_kernel<16>
+                                                                                    : gating_kernel<32>;
+  return launch_chain(kernel, dim3(blocks), dim3(threads), 0, s, logits, T, E, k, ids, w, err) == cudaSuccess ? 0
+                                                                                                               : -1;
 }
 
 // ------------------------------------------------------- bf16 -> f16 copy
 __global__ void convert_bf16_kernel(const uint4* __restrict__ x, int64_t n8, uint4* __restrict__ y) {
+  pdl_wait();
+  pdl_trigger();
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n8; i += int64_t(gridDim.x) * blockDim.x) {
     uint4 v = x[i];
     uint32_t in[4] = {v.x, v.y, v.z, v.w}, out[4];
@@ -575,8 +578,10 @@ int launch_convert_bf16(cudaStream_t s, const void* x, int64_t n, void* x16) {
   int blocks = int((n8 + 255) / 256);
   if (blocks > 148 * 8) blocks = 148 * 8;
   if (blocks < 1) blocks = 1;
-  convert_bf16_kernel<<<blocks, 256, 0, s>>>(static_cast<const uint4*>(x), n8, static_cast<uint4*>(x16));
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_chain(convert_bf16_kernel, dim3(blocks), dim3(256), 0, s, static_cast<const uint4*>(x), n8,
+                      static_cast<uint4*>(x16)) == cudaSuccess
+             ? 0
+             : -1;
 }
 
 }  // namespace b200moe

@@ -251,6 +251,13 @@ class B200NativeMoe:
         Layers with the same fixed split-K give bit-equal rows per route."""
         _lib.check("b200moe_set_split_k", _lib.lib().b200moe_set_split_k(self._h, int(ks_fp4), int(ks_iq2)))
 
+    def set_decode_fusion(self, max_routes: int = 64) -> None:
+        """Route-count limit (<= 64) of the fused two-launch decode of an FP4-only
+        layer on the block-scaled path; 0 (the layer's default) runs every call
+        on the chained launches, measured faster on B200.  Both give the same
+        output bits."""
+        _lib.check("b200moe_set_decode_fusion", _lib.lib().b200moe_set_decode_fusion(self._h, int(max_routes)))
+
     def set_timing_events(self, events) -> None:
         """Record torch.cuda.Event objects between the forward's launches (None: off)."""
         events = list(events or [])
