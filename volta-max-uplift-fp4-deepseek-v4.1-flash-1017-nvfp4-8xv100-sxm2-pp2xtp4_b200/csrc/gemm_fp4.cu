@@ -369,94 +369,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------- plane kernel
-// The activation rows of the FP4 bank as kP E2M1 planes with their blocked
-// scales in the chunk's SFB blocks (MMA row n * kP + p) and one FP32 factor g
-// per row (its amax over 6 * 448: plane 0's block scales use E4M3's range and
-// the later planes, each ~10x smaller, stay inside it).  With g fixed per row
-// the planes are block-local: a CTA takes a 1024-wide slice of a row, a
-// thread one half-block of 8 elements through all planes.
-// BY_TOKEN (W13): a token row of x, written to every FP4-bank route of the
-// token (found through the plan's inverse permutation), so a token is
-// quantized once for its top_k routes; the CTA finds the row amax itself and
-// clears the W2 row maxima of those positions.  Otherwise (W2): the SwiGLU row
-// of one sorted position, its amax taken by the W13 epilogue (rowmax).
-constexpr int kPlaneThreads = 128;
-constexpr int kSlice = kPlaneThreads * 8;
+// planes_row (fp4_device.cuh) over the bank's rows: a CTA per (row, 1024-wide
+// slice); W13 (BY_TOKEN) takes the token rows of x, W2 the SwiGLU rows.
 template <int BY_TOKEN, int BF16, int MX>
 __global__ void __launch_bounds__(kPlaneThreads) fp4_planes_kernel(
     const uint16_t* __restrict__ src, int64_t src_stride, int K, const int32_t* __restrict__ inv, int top_k,
     const int32_t* __restrict__ chunk_of, int bank, const int32_t* __restrict__ bank_range, int n_tokens,
     uint32_t* rowmax, uint8_t* planes, int plane_rows, uint8_t* sfb, float* gx) {
-  __shared__ float red[kPlaneThreads / 32];
-  __shared__ int dst_pos[32], dst_sf[32], dst_n[32];
-  __shared__ int n_dst;
-  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  const int nhb = K / 8, n_ks = K / 64;
-  const int hb = blockIdx.y * kPlaneThreads + t, blk = hb >> 1;  // this thread's half-block
-  const bool own = hb < nhb;
+  __shared__ PlaneScratch sm;
   pdl_wait();
   pdl_trigger();
   const int lo = bank_range[2 * bank], hi = bank_range[2 * bank + 1];
   const int rows = BY_TOKEN ? n_tokens : hi - lo;
-  for (int ri = blockIdx.x; ri < rows; ri += gridDim.x) {
-    __syncthreads();  // the previous row's destinations are read
-    if (warp == 0) {
-      int pos = -1;
-      if (BY_TOKEN) {
-        if (lane < top_k) {
-          const int q = inv[int64_t(ri) * top_k + lane];
-          if (q >= lo && q < hi) pos = q;
-        }
-      } else if (lane == 0) {
-        pos = lo + ri;
-      }
-      const int cn = pos >= 0 ? chunk_of[pos] : 0;
-      const unsigned have = __ballot_sync(0xffffffffu, pos >= 0);
-      if (pos >= 0) {
-        const int i = __popc(have & ((1u << lane) - 1u));
-        dst_pos[i] = pos;
-        dst_sf[i] = (cn >> 8) * n_ks * 512;
-        dst_n[i] = cn & 255;
-      }
-      if (lane == 0) n_dst = __popc(have);
-    }
-    const uint16_t* row = src + (BY_TOKEN ? int64_t(ri) : int64_t(lo + ri)) * src_stride;
-    float r[8];
-    load8<BF16>(own ? *reinterpret_cast<const uint4*>(row + hb * 8) : make_uint4(0, 0, 0, 0), r);
-    float amax = 0.f;
-    if (BY_TOKEN) {  // the whole row's amax (every slice's CTA reads the row: it is L2-resident)
-      for (int j = t; j < nhb; j += kPlaneThreads) {
-        float f[8];
-        load8<BF16>(*reinterpret_cast<const uint4*>(row + j * 8), f);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
-      }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      if (lane == 0) red[warp] = amax;
-    }
-    __syncthreads();
-    const int nd = n_dst;
-    if (nd == 0) continue;
-    if (BY_TOKEN) {
-      amax = red[0];
-#pragma unroll
-      for (int w = 1; w < kPlaneThreads / 32; ++w) amax = fmaxf(amax, red[w]);
-    } else {
-      amax = __uint_as_float(rowmax[dst_pos[0]]);
-    }
-    // MXFP4: power-of-two block scales cover any row, so no row factor (g = 1)
-    const float g = MX ? 1.f : amax / (6.f * 448.f);
-    const float inv_g = g > 0.f ? __frcp_rn(g) : 0.f;
-    uint32_t w[kP], word[kP];
-    quantize_planes8<MX>(r, own, g, inv_g, w, word);
-    if (own)
-      for (int d = 0; d < nd; ++d) store_planes8(w, word, hb, K, dst_pos[d], dst_n[d], planes, sfb + dst_sf[d]);
-    if (blockIdx.y == 0 && t < nd) {
-      gx[dst_pos[t]] = g;
-      if (BY_TOKEN) rowmax[dst_pos[t]] = 0u;  // the W13 epilogue takes the W2 row maxima afresh
-    }
-  }
+  for (int ri = blockIdx.x; ri < rows; ri += gridDim.x)
+    planes_row<BY_TOKEN, BF16, MX>(sm, src, src_stride, K, inv, top_k, chunk_of, lo, hi, ri, rowmax, planes, sfb, gx);
 }
 
 // --------------------------------------------------------------- combine

@@ -212,6 +212,9 @@ int ep_return_targets(const ::b200moe_ep* E, EpReturn* r);
 int launch_quant_s8(cudaStream_t s, const __half* src, int64_t src_stride, int K, int rows, const int32_t* range,
                     uint8_t* dst);
 int launch_plan(cudaStream_t s, const PlanArgs& a);
+// the plan of <= 32 routes and the FP4 planes of the token rows in one launch (x: f16, or bf16 when bf16)
+int launch_plan_planes(cudaStream_t s, const PlanArgs& a, bool bf16, bool mx, const void* x, int64_t src_stride,
+                       int K, int n_tokens, uint32_t* rowmax, uint8_t* planes, uint8_t* sfb, float* gx);
 int launch_gating(cudaStream_t s, const float* logits, int T, int E, int k, int32_t* ids, float* w,
                   uint32_t* err);
 int launch_convert_bf16(cudaStream_t s, const void* x, int64_t n, void* x16);

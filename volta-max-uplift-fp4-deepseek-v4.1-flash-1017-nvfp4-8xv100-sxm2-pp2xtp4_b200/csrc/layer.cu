@@ -344,7 +344,16 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   p.ks_sel = ws.ks_sel;
   p.bank_range = ws.bank_range;
   p.err = L->err;
-  if (launch_plan(s, p)) return B200MOE_ERR_CUDA;
+  // decode of <= 32 routes on the block-scaled path: the plan and the token rows' planes are one launch
+  const bool plan_with_planes = f4 && !rows && !recv && S <= 32;
+  if (plan_with_planes) {
+    if (launch_plan_planes(s, p, x_bf16_direct, c.fp4_format == B200MOE_MXFP4,
+                           x_bf16_direct ? x : static_cast<const void*>(xsrc), c.hidden, c.hidden, m, L->f4_rowmax,
+                           L->f4_planes[0], L->f4_sfb[0], L->f4_gx[0]))
+      return B200MOE_ERR_CUDA;
+  } else if (launch_plan(s, p)) {
+    return B200MOE_ERR_CUDA;
+  }
   marks.mark();
   if (c.n_iq2 > 0 && rows && !quant_rows()) return B200MOE_ERR_CUDA;
   if (tc) {
@@ -353,7 +362,8 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
     marks.mark();
   }
   for (int epi = 0; epi < 2; ++epi) {
-    if (f4) {  // the FP4 bank's activation rows as E2M1 planes for its block-scaled GEMM
+    if (f4 && epi == 0 && plan_with_planes) marks.mark();  // made with the plan: an empty interval
+    if (f4 && !(epi == 0 && plan_with_planes)) {  // the FP4 bank's activation rows as E2M1 planes
       if (launch_fp4_planes(s, epi == 0, epi == 0 && x_bf16_direct, c.fp4_format == B200MOE_MXFP4,
                             epi == 0 ? (x_bf16_direct ? x : static_cast<const void*>(xsrc)) : ws.inter,
                             epi == 0 ? c.hidden : c.inter,

@@ -12,10 +12,12 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <float.h>
 
 #include "common.cuh"
+#include "fp4_device.cuh"
 #include "internal.h"
 
 namespace b200moe {
@@ -452,6 +454,61 @@ int launch_plan(cudaStream_t s, const PlanArgs& a) {
     attr_set.fetch_or(uint64_t(1) << dev);
   }
   return launch_chain(plan_kernel, dim3(1), dim3(kPlanThreads), smem, s, a) == cudaSuccess ? 0 : -1;
+}
+
+// Route plan and the token rows' FP4 planes in one launch, for decode calls of
+// at most 32 routes on the block-scaled path: every CTA of the plane grid
+// (token row x 1024-wide slice) runs the one-warp plan itself -- CTA (0, 0)
+// into the layer's plan buffers, the others into shared memory, the same
+// values -- and then quantizes its slice, which needs the token's sorted
+// positions the plan just made.  Saves the plan's own launch.
+template <int BF16, int MX>
+__global__ void __launch_bounds__(kPlaneThreads) plan_planes_kernel(PlanArgs a, const uint16_t* __restrict__ src,
+                                                                   int64_t src_stride, int K, int n_tokens,
+                                                                   uint32_t* rowmax, uint8_t* planes, uint8_t* sfb,
+                                                                   float* gx) {
+  __shared__ PlaneScratch sm;
+  __shared__ int s_perm[32], s_inv[32], s_chunk_of[32], s_nch[2], s_range[4];
+  __shared__ Chunk s_chunks[2][32];
+  pdl_wait();
+  pdl_trigger();
+  PlanArgs p = a;
+  if (blockIdx.x != 0 || blockIdx.y != 0) {  // a private copy of the plan: only CTA (0, 0) writes the layer's
+    p.perm = s_perm;
+    p.inv = s_inv;
+    p.chunk_of = s_chunk_of;
+    p.chunks[0] = s_chunks[0];
+    p.chunks[1] = s_chunks[1];
+    p.n_chunks = s_nch;
+    p.bank_range = s_range;
+    p.w_eff = nullptr;
+    p.key_counts = nullptr;
+    p.ks_sel = nullptr;
+    p.y2 = nullptr;
+    p.counters = nullptr;
+  }
+  if (threadIdx.x < 32) plan_small(p, a.n, a.n_keys);
+  __syncthreads();
+  const int lo = p.bank_range[0], hi = p.bank_range[1];
+  for (int ri = blockIdx.x; ri < n_tokens; ri += gridDim.x)
+    planes_row<1, BF16, MX>(sm, src, src_stride, K, p.inv, a.top_k, p.chunk_of, lo, hi, ri, rowmax, planes, sfb, gx);
+}
+
+int launch_plan_planes(cudaStream_t s, const PlanArgs& a, bool bf16, bool mx, const void* x, int64_t src_stride,
+                       int K, int n_tokens, uint32_t* rowmax, uint8_t* planes, uint8_t* sfb, float* gx) {
+  // the one-warp plan's shape (product keys, <= 32 routes, the layer's own routing) and the x planes' (bank 0)
+  if (!a.key_of_expert || a.n < 1 || a.n > 32 || a.recv.flags || a.n_valid || !a.inv || !a.chunk_of ||
+      !a.bank_range || a.top_k > 32 || K % 256 || n_tokens < 1)
+    return -1;
+  for (int b = 0; b < a.n_banks; ++b)
+    if (a.max_chunks[b] < a.n) return -1;  // the private copies hold up to 32 chunks per bank
+  const dim3 grid(std::min(n_tokens, 148 * 8), (K + kSlice - 1) / kSlice);
+  auto kernel = bf16 ? (mx ? plan_planes_kernel<1, 1> : plan_planes_kernel<1, 0>)
+                     : (mx ? plan_planes_kernel<0, 1> : plan_planes_kernel<0, 0>);
+  return launch_chain(kernel, grid, dim3(kPlaneThreads), 0, s, a, static_cast<const uint16_t*>(x), src_stride, K,
+                      n_tokens, rowmax, planes, sfb, gx) == cudaSuccess
+             ? 0
+             : -1;
 }
 
 // ------------------------------------------------------------------ gating
