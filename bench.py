@@ -592,10 +592,12 @@ def run_c1(job, m: int, layer=None, bank=None, main: bool = True) -> dict:
     value = m / (ms / 1e3)
     del graphs
 
-    if f4:  # start, convert (none for bf16 x), plan, x planes, W13 (+SwiGLU), SwiGLU planes, W2, combine
-        per = per_launch(layer, fns, args.steps, 8)
+    if f4:  # start, convert (none for bf16 x), plan, x planes (made with the plan up to 32 routes), W13
+        #     (+SwiGLU), SwiGLU planes, W2, combine (in the W2 epilogue up to 64 routes)
+        fused_combine = m * K_TOP <= 64
+        per = per_launch(layer, fns, args.steps, 7 if fused_combine else 8)
         t_w13_ms = float(per[3])
-        names = ["convert", "plan", "x_planes", "w13", "swiglu_planes", "w2", "combine"]
+        names = ["convert", "plan", "x_planes", "w13", "swiglu_planes", "w2"] + ([] if fused_combine else ["combine"])
     else:  # convert, plan, W13, W2 (+SwiGLU or combine: fused up to 32 routes)
         sep = m * K_TOP > 32
         per = per_launch(layer, fns, args.steps, 6 if sep else 5)
@@ -630,9 +632,11 @@ def run_c1(job, m: int, layer=None, bank=None, main: bool = True) -> dict:
                            "frac": layer_bytes / (per.sum() / 1e3) / 1e9 / pk["hbm_gbs"],
                            "launch_ms": {k: float(v) for k, v in zip(names, per)}},
         "e2e": e2e,
-        # fp4: gating, route plan, x planes (read bf16 x directly), W13 (+SwiGLU), SwiGLU planes, W2, combine;
+        # fp4: gating, route plan, x planes (read bf16 x directly; with the plan up to 32 routes), W13 (+SwiGLU),
+        # SwiGLU planes, W2, combine (fused into W2 up to 64 routes);
         # gemv: gating, bf16 copy, route plan, W13 (+SwiGLU), W2, combine (fused into W2 up to 32 routes)
-        "gpu_launches": (7 if f4 else 6 if m * K_TOP > 32 else 5) * args.steps,
+        "gpu_launches": ((5 if m * K_TOP <= 32 else 6 if m * K_TOP <= 64 else 7) if f4 else
+                         6 if m * K_TOP > 32 else 5) * args.steps,
         "cpu_baseline": cpu,
         "clocks": clk,
     })

@@ -346,6 +346,39 @@ __global__ void __launch_bounds__(kThreads, 1)
             yrow[128] = __float2half_rn(v1 * gx * gw0);
           }
         }
+        if (a.counters) {
+          // fused combine (small decode calls): each route stored counts once per 32-column tile of this
+          // warp (rt * 4 TILES + 4 h + quarter); the warp that completes a token's tile sums the token's
+          // routes in slot order, the separate combine's arithmetic (a route without an expert has a zero
+          // y2 row and weight, both written by the route plan, which also counts it)
+          __threadfence();
+          __syncwarp();
+          const int tiles = a.H / 32;
+#pragma unroll 1
+          for (int n = 0; n < ch.count; ++n) {
+            const int tok = __shfl_sync(0xffffffffu, route_l, n) / a.top_k;
+#pragma unroll
+            for (int h = 0; h < TILES; ++h) {
+              const int tile = rt * (4 * TILES) + 4 * h + quarter;
+              int* cp = a.counters + int64_t(tok) * tiles + tile;
+              int done = 0;
+              if (lane == 0) done = atomicAdd(cp, 1) == a.top_k - 1;
+              if (__shfl_sync(0xffffffffu, done, 0)) {
+                __threadfence();
+                const int col = tile * 32 + lane;
+                float sum = 0.f;
+                for (int slot = 0; slot < a.top_k; ++slot) {
+                  const int r = tok * a.top_k + slot;
+                  const float y = __half2float(__ushort_as_half(
+                      __ldcg(reinterpret_cast<const unsigned short*>(a.y2) + int64_t(r) * a.H + col)));
+                  sum = __fmaf_rn(y, __ldcg(a.w_eff + r), sum);
+                }
+                a.out[int64_t(tok) * a.H + col] = sum;
+                if (lane == 0) *cp = 0;
+              }
+            }
+          }
+        }
       }
       ++acc_i;
     }

@@ -160,6 +160,8 @@ int launch_fp4_gemm(cudaStream_t s, int epi, int rc, bool mx, const Fp4Args& a, 
 // and W2, each planning the call's routes itself, quantizing its chunks'
 // activation rows into shared memory and (W2) combining the token rows.
 constexpr int kDecodeMaxRoutes = 64;
+// decode calls of at most this many routes combine in the block-scaled W2 epilogue (no combine launch)
+constexpr int kFusedCombineRoutes = 64;
 struct DecArgs {
   const uint8_t* wt;          // weight units of this projection [slot][n_rt][K/256]
   const float* globals;       // NVFP4 [slot][3] FP32 global scales, null for MXFP4

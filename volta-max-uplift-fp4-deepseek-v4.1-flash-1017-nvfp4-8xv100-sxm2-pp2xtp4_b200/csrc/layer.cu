@@ -307,9 +307,10 @@ int run_forward(b200moe_layer* L, const Workspace& ws_in, cudaStream_t s, const 
   // W2 writes y2 rows only and one launch after it does the slot-order combine: fused into the W2
   // epilogue the combine's fences, atomics and re-reads stall the pipeline (measured on B200: the
   // decode GEMV at M = 64 0.849 against 0.877 ms, the tcgen05 prefill W2 1.10 against 2.12 ms).
-  // The GEMV keeps the fused form for the smallest batches (at most 32 routes, where it is as fast
-  // and saves a launch) and in the allocation-free decode.
-  const bool sep_combine = !rows && (f4 || tc || (ws.own && S > 32));
+  // Small decode calls keep the fused form, where it saves a launch: the block-scaled W2 up to
+  // kFusedCombineRoutes routes, the GEMV up to 32 (and in the allocation-free decode); a layer with
+  // both banks fuses in both W2 launches or in neither (they share the completion counts).
+  const bool sep_combine = !rows && (tc || (f4 && S > kFusedCombineRoutes) || (!f4 && ws.own && S > 32));
   if (sep_combine) ws.counters = nullptr;
   PlanArgs p{};
   p.ids = ids;
