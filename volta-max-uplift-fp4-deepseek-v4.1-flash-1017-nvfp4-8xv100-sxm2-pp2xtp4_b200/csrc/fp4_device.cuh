@@ -18,7 +18,7 @@ namespace {
 constexpr int kP = kFp4Planes;             // activation planes
 constexpr int kATile = 128 * 128;          // weight tile: 128 rows x 256 FP4 = 16 KB
 constexpr int kSFBytes = 4 * 512;          // the scale blocks of one 256-wide K tile
-constexpr int kThreads = 6 * 32;           // producer, MMA, 4 epilogue warps
+constexpr int kThreads = 7 * 32;           // producer, MMA, 4 epilogue warps, scale copier
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSfCol = 256;           // scale columns start after the two accumulator buffers
 

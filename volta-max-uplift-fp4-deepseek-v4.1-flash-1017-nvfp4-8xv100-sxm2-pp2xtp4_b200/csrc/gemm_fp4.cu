@@ -76,6 +76,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + kStages;
   uint64_t* acc_full = empty + kStages;  // [2]
   uint64_t* acc_empty = acc_full + 2;    // [2]
+  uint64_t* sf_full = acc_empty + 2;     // [kStages] the stage's scales are in TMEM (copier commit)
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
   volatile int* abort_ptr = &abort_flag;
@@ -84,6 +85,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&sf_full[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -179,19 +181,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kt = 0; kt < n_kt; ++kt, ++g) {
           const int s = g % kStages;
           const uint32_t ph = (g / kStages) & 1u;
-          if (*abort_ptr || !mbar_wait(&full[s], ph, a.err)) {
+          // the stage's operands (producer) and its scales in TMEM (copier warp)
+          if (*abort_ptr || !mbar_wait(&full[s], ph, a.err) || !mbar_wait(&sf_full[s], ph, a.err)) {
             ok = false;
             break;
           }
           fence_after();
           const uint32_t st = smem_u32(stages + s * kStage);
           const uint32_t sfg = tmem + kSfCol + s * St::kSfCols, sfu = sfg + 16, sfb = sfg + St::kSfB;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            sf_copy(sfg + 4 * j, st + St::kOffSFG + 512 * j);
-            if (TILES == 2) sf_copy(sfu + 4 * j, st + St::kOffSFU + 512 * j);
-            sf_copy(sfb + 4 * j, st + St::kOffSFB + 512 * j);
-          }
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const uint32_t acc = (kt | j) != 0;
@@ -213,6 +210,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (committed) mbar_wait(&acc_full[last_b], last_ph, a.err);
+    }
+  } else if (warp == 6) {
+    // ------------------------------------------------------------ scale copier
+    // the stage's block scales (weight tiles, activation planes) into its TMEM columns, committed to
+    // sf_full[s]: issued from a thread of their own, the 12 copies of a stage overlap the MMA thread's
+    // issue of the previous stage (one thread issuing both took ~0.84 us per 36 KB stage on B200,
+    // under the HBM rate of an SM at small batches)
+    if (lane == 0) {
+      uint32_t g = 0, issued = 0, parity = 0;
+      for (int item = blockIdx.x; item < n_items && !*abort_ptr; item += gridDim.x) {
+        const Chunk ch = chunk_of_item(item);
+        if (!item_ok(ch)) continue;
+        for (int kt = 0; kt < n_kt; ++kt, ++g) {
+          const int s = g % kStages;
+          const uint32_t ph = (g / kStages) & 1u;
+          if (*abort_ptr || !mbar_wait(&full[s], ph, a.err)) {
+            *abort_ptr = 1;
+            break;
+          }
+          fence_after();
+          const uint32_t st = smem_u32(stages + s * kStage);
+          const uint32_t sfg = tmem + kSfCol + s * St::kSfCols, sfu = sfg + 16, sfb = sfg + St::kSfB;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            sf_copy(sfg + 4 * j, st + St::kOffSFG + 512 * j);
+            if (TILES == 2) sf_copy(sfu + 4 * j, st + St::kOffSFU + 512 * j);
+            sf_copy(sfb + 4 * j, st + St::kOffSFB + 512 * j);
+          }
+          commit_to(&sf_full[s]);
+          issued |= 1u << s;
+          parity = (parity & ~(1u << s)) | (ph << s);
+        }
+      }
+      // no copy may be in flight when TMEM is freed
+      for (int s = 0; s < kStages; ++s)
+        if (issued & (1u << s)) mbar_wait(&sf_full[s], (parity >> s) & 1u, a.err);
     }
   } else {
     // ------------------------------------------------------------ epilogue
