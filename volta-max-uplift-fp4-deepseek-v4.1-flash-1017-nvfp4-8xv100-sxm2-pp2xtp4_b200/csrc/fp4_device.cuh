@@ -26,7 +26,7 @@ constexpr uint32_t kSfCol = 256;           // scale columns start after the two 
 // is 4 planes x RC; small batches use small chunks, so the tensor pipe does not
 // spend its time on empty columns).  Two tiles (W13: the gate and up tiles; W2:
 // two adjacent 128-row tiles) make stages of 36 KB + the plane tile, 4 of them
-// (5 where they fit, at <= 8 routes per chunk, measured no faster on B200);
+// (5 where they fit measured slower on B200: configs[1] M = 64 639 -> 692 us);
 // one tile 18 KB + the plane tile, 7 stages.  Each stage has its own TMEM scale
 // columns: a scale copy never lands under an MMA still in flight.
 template <int TILES, int RC, int MX = 0>
