@@ -88,7 +88,7 @@ TOL_LAYER = 1e-2  # the reference's layer rule (harness/benchmarks/nvfp4_8r/acce
 # of `python bench.py --profile` (dram__bytes_read.sum + dram__bytes_write.sum
 # of that launch over its 289 distinct experts), kept with the capture's
 # command in profiles/fp4_w13_c1_decode.md and profiles/gemv_w13_c1_decode.md.
-NCU_W13_TRAFFIC_PER_EXPERT = {"fp4": 2.744e9 / 289, "gemv": None}
+NCU_W13_TRAFFIC_PER_EXPERT = {"fp4": 2.7447e9 / 289, "gemv": None}
 
 DTYPE_FP4 = "e2m1x4 activations (E4M3 block scales) x nvfp4 weights, f32 accumulate"
 DTYPE_GEMV = "f16 activations x nvfp4 weights dequantized to f16, f32 accumulate"
