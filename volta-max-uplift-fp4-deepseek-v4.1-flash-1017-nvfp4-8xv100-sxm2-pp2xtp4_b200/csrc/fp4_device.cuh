@@ -147,9 +147,20 @@ __device__ __forceinline__ uint32_t e4m3_rn(float x) {
 // lanes 8j .. 8j + 7 cover (word[p]).  g: the row's factor (its amax over
 // 6 * 448 for NVFP4, 1 for MXFP4), inv_g its inverse; r: the elements, left
 // holding the residual.  Every lane of the warp takes part (shuffles).
+// The chain from one plane to the next is the scale: no division or rounded
+// reciprocal on it (the E4M3 target is bm times a per-row constant; the
+// reciprocal of the scale is the hardware approximation, or exact for MXFP4's
+// powers of two): a code a rounding step off is absorbed by the next plane,
+// which quantizes the residual taken with the exact scale.
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 template <int MX>
 __device__ __forceinline__ void quantize_planes8(float (&r)[8], bool own, float g, float inv_g, uint32_t (&w)[kP],
                                                  uint32_t (&word)[kP]) {
+  const float inv6g = inv_g * (1.f / 6.f);
 #pragma unroll
   for (int p = 0; p < kP; ++p) {
     float bm = 0.f;
@@ -158,19 +169,21 @@ __device__ __forceinline__ void quantize_planes8(float (&r)[8], bool own, float 
     bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 1));  // the other half of the 16-block
     if (MX) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 2));  // the 32-block: four half-blocks
     uint32_t sc;
-    float scale;
+    float scale, rs;
     if (MX) {  // UE8M0: the smallest 2^e with 6 * 2^e >= bm
       const int e = bm > 0.f ? max(-126, min(127, mx_exponent(bm))) : -127;
       sc = own && bm > 0.f ? uint32_t(e + 127) : 0u;
       scale = sc ? __uint_as_float(sc << 23) : 0.f;  // 2^e, e >= -126: a normal float
+      // 2^-e exactly: a normal float up to e = 126, 2^-127 (subnormal) at e = 127
+      rs = sc == 0u ? 0.f : sc <= 253u ? __uint_as_float((254u - sc) << 23) : __uint_as_float(0x00200000u);
     } else {
-      sc = own ? e4m3_rn(bm / 6.f * inv_g) : 0u;
+      sc = own ? e4m3_rn(bm * inv6g) : 0u;
       // the E4M3 byte's value (sc < 0x80), built from its bits: 2^(e - 7) (1 + m / 8) or m 2^-9
       const uint32_t ex = sc >> 3, mn = sc & 7u;
       const float sv = ex ? __uint_as_float(((ex + 120u) << 23) | (mn << 20)) : float(mn) * 0.001953125f;
       scale = sv * g;
+      rs = scale > 0.f ? rcp_approx(scale) : 0.f;
     }
-    const float rs = scale > 0.f ? __frcp_rn(scale) : 0.f;  // = 1 / scale, rounded to nearest
     uint32_t cw = 0u;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
