@@ -200,15 +200,15 @@ int b200moe_set_split_k(b200moe_layer* layer, int ks_fp4, int ks_iq2);
 
 /* Fused small-batch decode.  On a layer whose experts all sit in the FP4 bank
  * (n_iq2 = 0) with prefill_gemm 2 or 3, a forward of at most max_routes routes
- * (M * top_k; at most 64; hidden and inter at most 4096) runs as two launches,
- * W13 and W2, instead of the chained six (route plan, x planes, W13, SwiGLU
- * planes, W2, combine): each CTA plans the call itself, quantizes its chunk's
- * rows into shared memory and the W2 launch combines each token's rows once
- * their last route is stored.  Same output bits as the chained path.  The
- * default is 0 (off): on B200 the fused form is slower (configs[1] M = 1:
- * 72 against 61 us; M = 8: 284 against 187 us), because every CTA quantizes
- * its chunk's whole rows before its first MMA, a chain the chained path
- * spreads over many CTAs.  No reference counterpart (the reference's decode is
+ * (M * top_k; at most 64) runs as two launches, W13 and W2, instead of the
+ * chained ones (route plan with the x planes, W13, SwiGLU planes, W2 with the
+ * combine): each CTA plans the call itself, quantizes its chunk's rows into
+ * shared memory and the W2 launch combines each token's rows once their last
+ * route is stored.  Same output bits as the chained path.  The default is 0
+ * (off): on B200 the fused form is slower (configs[1] M = 1: 63.8 against
+ * 57.6 us; M = 8: 264 against 170 us), because every CTA quantizes its
+ * chunk's whole rows before its first MMA, a chain the chained path spreads
+ * over many CTAs.  No reference counterpart (the reference's decode is
  * the QPN launch chain of engine/.../experts/nvfp4_8r_native.py:929-960). */
 int b200moe_set_decode_fusion(b200moe_layer* layer, int max_routes);
 

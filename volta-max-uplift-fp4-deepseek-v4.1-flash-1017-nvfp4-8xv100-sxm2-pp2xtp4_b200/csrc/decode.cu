@@ -17,12 +17,9 @@
 // the tokens' rows of x; W2: the SwiGLU rows W13 stored) as four E2M1 planes
 // with their block scales straight into a shared-memory operand that holds
 // the whole K, publishing it one 256-wide K tile at a time (warp w takes the
-// tiles w, w + 4, ...: the half-blocks its lanes loaded), so the MMA warp's
-// tcgen05.mma.kind::mxf4nvf4 on the first weight stage waits for one tile,
-// not the row.  The weight stream starts once the first chunk's rows are in
-// registers: row loads issued behind 144 KB of bulk copies wait for them
-// (measured on B200: ~4 us per load at the stream's start).  Four epilogue
-// warps drain the TMEM accumulators: W13 stores the
+// tiles w, w + 4, ...), so the MMA warp's tcgen05.mma.kind::mxf4nvf4 on the
+// first weight stage waits for one tile, not the row.  Four epilogue warps
+// drain the TMEM accumulators: W13 stores the
 // limited SwiGLU rows, W2 the fp16 y2 rows and then, through a completion
 // count per (token, 256-column unit), the CTA that stores a unit's last route
 // sums the token's routes in slot order into the output, the separate
@@ -32,10 +29,11 @@
 // Measured on B200 (configs[1], in-kernel %globaltimer stamps): the row
 // quantization is the critical path.  One warp's call of the four-plane
 // quantizer on a K tile takes ~5 us (a long dependent chain per half-block),
-// so at M = 1 the first MMA starts ~11 us after the plan and the step takes
-// 72 us against 61 us chained, where the x-plane launch spreads the same
-// work over many CTAs.  The layer therefore leaves this path off unless the
-// caller turns it on (b200moe_set_decode_fusion).
+// so at M = 1 the first MMA starts ~9 us after the plan and the step takes
+// 63.8 us against 57.6 us chained (M = 8: 264 against 170 us), where the
+// plane launches spread the same work over many CTAs.  The layer therefore
+// leaves this path off unless the caller turns it on
+// (b200moe_set_decode_fusion).
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -53,16 +51,15 @@ constexpr int kDecRC = 4;                     // routes per chunk: the MMA's N i
 constexpr int kDecBTile = kP * kDecRC * 128;  // one 256-wide K tile of a chunk's plane rows (2 KB)
 constexpr int kDecThreads = 320;              // producer, MMA, 4 epilogue warps, 4 quantizer warps
 constexpr size_t kDecSmemLimit = 220 * 1024;  // dynamic part (the static plan arrays take the rest)
-constexpr int kDecMaxK = 4096;                // a quantizer thread holds K / 1024 half-blocks per route
 
 size_t decode_smem(int K, int stages) {
   const int n_kt = K / 256;
   return 1024 + size_t(stages) * Fp4Stage<2, kDecRC, 0>::kUnit + size_t(n_kt) * (kDecBTile + kSFBytes) +
-         size_t(2 * stages + 6 + n_kt) * 8;
+         size_t(2 * stages + 5 + n_kt) * 8;
 }
 
 int decode_stages(int K) {
-  if (K % 256 || K < 256 || K > kDecMaxK) return 0;
+  if (K % 256 || K < 256) return 0;
   for (int st = 4; st >= 2; --st)
     if (decode_smem(K, st) <= kDecSmemLimit) return st;
   return 0;
@@ -94,8 +91,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) fp4_decode_kernel(const DecArg
   uint64_t* acc_full = empty + n_st;  // [2]
   uint64_t* acc_empty = acc_full + 2;  // [2]
   uint64_t* b_empty = acc_empty + 2;   // the MMAs that read the operand are complete (MMA commit)
-  uint64_t* rows_in = b_empty + 1;     // the first chunk's rows are in the quantizers' registers
-  uint64_t* bk_full = rows_in + 1;     // [n_kt] K tile kt of the chunk's planes is written (quantizer warp)
+  uint64_t* bk_full = b_empty + 1;     // [n_kt] K tile kt of the chunk's planes is written (quantizer warp)
   __shared__ int s_key[kDecodeMaxRoutes];     // bank-0 slot of route i (n_keys: no expert)
   __shared__ int s_perm[kDecodeMaxRoutes];    // route at sorted position
   __shared__ int s_pkey[kDecodeMaxRoutes];    // slot at sorted position
@@ -118,7 +114,6 @@ __global__ void __launch_bounds__(kDecThreads, 1) fp4_decode_kernel(const DecArg
       mbar_init(&acc_empty[b], 4);
     }
     mbar_init(b_empty, 1);
-    mbar_init(rows_in, 1);
     for (int kt = 0; kt < n_kt; ++kt) mbar_init(&bk_full[kt], 1);
     fence_barrier_init();
     abort_flag = 0;
@@ -206,19 +201,11 @@ __global__ void __launch_bounds__(kDecThreads, 1) fp4_decode_kernel(const DecArg
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
       uint32_t g = 0, issued = 0, parity = 0;
-      bool started = false;
       for (int item = i0; item < i1 && !*abort_ptr; ++item) {
         const int4 ch = s_chunk[item / a.n_rt];
         if (!item_ok(ch)) {
           set_error(a.err, kErrBounds);
           continue;
-        }
-        if (!started) {  // the quantizers' row loads go out before the weight stream
-          if (!mbar_wait(rows_in, 0, a.err)) {
-            *abort_ptr = 1;
-            break;
-          }
-          started = true;
         }
         const int rt = item % a.n_rt;
         const uint8_t* wu = a.wt + (int64_t(ch.x) * a.n_rt + rt) * n_kt * St::kUnit;
@@ -324,55 +311,40 @@ __global__ void __launch_bounds__(kDecThreads, 1) fp4_decode_kernel(const DecArg
         if (qq == 0) *abort_ptr = 1;
         break;
       }
-      // this thread's half-blocks hb = qq + 128 j of every route (K tile qw + 4 j), loaded once
-      uint4 xr[kDecRC][kDecMaxK / 1024];
-      float am[kDecRC];
+      // the rows' amax (the plane factor g): four independent loads in flight per thread
 #pragma unroll
       for (int n = 0; n < kDecRC; ++n) {
-        am[n] = 0.f;
-#pragma unroll
-        for (int j = 0; j < kDecMaxK / 1024; ++j) {
-          const int hb = qq + 128 * j;
-          xr[n][j] = (n < ch.z && hb < nhb) ? *reinterpret_cast<const uint4*>(row_of(ch.y + n) + hb * 8)
-                                            : make_uint4(0u, 0u, 0u, 0u);
-        }
-      }
-#pragma unroll
-      for (int n = 0; n < kDecRC; ++n) {
-#pragma unroll
-        for (int j = 0; j < kDecMaxK / 1024; ++j) {
+        if (n >= ch.z) break;
+        const uint16_t* rp = row_of(ch.y + n);
+        float am = 0.f;
+#pragma unroll 4
+        for (int hb = qq; hb < nhb; hb += 128) {
           float f[8];
-          load8<BF16>(xr[n][j], f);
+          load8<BF16>(*reinterpret_cast<const uint4*>(rp + hb * 8), f);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) am[n] = fmaxf(am[n], fabsf(f[e]));
+          for (int e = 0; e < 8; ++e) am = fmaxf(am, fabsf(f[e]));
         }
 #pragma unroll
-        for (int o = 16; o; o >>= 1) am[n] = fmaxf(am[n], __shfl_xor_sync(0xffffffffu, am[n], o));
-        if (lane == 0) s_red[qw][n] = am[n];
+        for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+        if (lane == 0) s_red[qw][n] = am;
       }
       named_bar(2, 128);
-      if (qq == 0 && nq == 0) mbar_arrive(rows_in);  // the weight stream may start
       if (qq < ch.z) {
         const float m = fmaxf(fmaxf(s_red[0][qq], s_red[1][qq]), fmaxf(s_red[2][qq], s_red[3][qq]));
         // MXFP4: power-of-two block scales cover any row (g = 1); NVFP4: the row's amax over 6 * 448
         s_gx[ci][qq] = MX ? 1.f : m / (6.f * 448.f);
       }
       named_bar(2, 128);
-      // K tile kt = qw + 4 j: 32 half-blocks, one per lane, of every route of the chunk; then publish it
-#pragma unroll
-      for (int j = 0; j < kDecMaxK / 1024; ++j) {
-        const int kt = qw + 4 * j;
-        if (kt >= n_kt) break;
+      // K tile kt (32 half-blocks: one per lane) of every route of the chunk, then publish it
+      for (int kt = qw; kt < n_kt; kt += 4) {
         const int hb = kt * 32 + lane;
         uint8_t* tb = btile + kt * kDecBTile;
         const int c16 = lane >> 2, sub = (lane & 3) * 4;
-#pragma unroll
-        for (int n = 0; n < kDecRC; ++n) {
-          if (n >= ch.z) break;
+        for (int n = 0; n < ch.z; ++n) {
           const float g = s_gx[ci][n];
           const float inv_g = g > 0.f ? __frcp_rn(g) : 0.f;
           float r[8];
-          load8<BF16>(xr[n][j], r);
+          load8<BF16>(*reinterpret_cast<const uint4*>(row_of(ch.y + n) + hb * 8), r);
           uint32_t w[kP], word[kP];
           quantize_planes8<MX>(r, true, g, inv_g, w, word);
           // 16-byte chunk lane / 4 of plane row n * 4 + p, 128-byte swizzled; the scale words from lanes 8j
