@@ -630,6 +630,9 @@ def run_c1(job, m: int, layer=None, bank=None, main: bool = True) -> dict:
         "layer_roofline": {"bytes": layer_bytes, "ms": float(per.sum()),
                            "achieved_gbs": layer_bytes / (per.sum() / 1e3) / 1e9,
                            "frac": layer_bytes / (per.sum() / 1e3) / 1e9 / pk["hbm_gbs"],
+                           # the whole timed step (gating included, one graph replay) against the same bytes
+                           "gbs_over_step": layer_bytes / (ms / 1e3) / 1e9,
+                           "frac_over_step": layer_bytes / (ms / 1e3) / 1e9 / pk["hbm_gbs"],
                            "launch_ms": {k: float(v) for k, v in zip(names, per)}},
         "e2e": e2e,
         # fp4: gating, route plan, x planes (read bf16 x directly; with the plan up to 32 routes), W13 (+SwiGLU),
@@ -772,6 +775,8 @@ def run_c2(job, main: bool = True) -> dict:
         "layer_roofline": {"bytes": layer_bytes, "ms": float(per.sum()),
                            "achieved_gbs": layer_bytes / (per.sum() / 1e3) / 1e9,
                            "frac": layer_bytes / (per.sum() / 1e3) / 1e9 / pk["hbm_gbs"],
+                           "gbs_over_step": layer_bytes / (ms / 1e3) / 1e9,
+                           "frac_over_step": layer_bytes / (ms / 1e3) / 1e9 / pk["hbm_gbs"],
                            "launch_ms": {"convert": float(per[0]), "x_int8": float(per[1]), "plan": float(per[2]),
                                          **{k: float(per[v]) for k, v in extra.items()},
                                          **{k: float(v[0]) for k, v in launches.items()}}},
