@@ -643,3 +643,47 @@ def test_layer_route_stats(dev, pkg):
     assert got["stat"].tolist()[:2] == [2, int(want.sum())] and got["stat"][2] == 0
     layer.check_errors()
     layer.close()
+
+
+def test_back_to_back_calls_match_isolated_calls(dev, pkg):
+    """The forward's launches overlap their predecessors' tails (programmatic
+    dependent launch): a kernel may start while the one before it finishes and
+    must wait before touching that kernel's memory.  Calls of every shape class
+    on two block-scaled layers (FP4-only and mixed tier), queued back to back
+    on one stream without synchronization, give the bits each call gives when
+    run alone: 1 and 4 tokens (plan and planes in one launch, combine in the W2
+    epilogue), 8 (combine in the epilogue), 32 (separate combine), a 600-token
+    prefill (the tcgen05 GEMM), in an order that makes every pair of shapes
+    neighbours."""
+    from b200moe import tiers
+
+    H, I, E, K = 2048, 1024, 64, 8
+    a, _, _, _ = _make_layer(dev, H, I, E, K, 64, seed=41, max_prefill=600, gemm="fp4")
+    b, _, _, _ = _make_layer(dev, H, I, E, K, 64, tier=tiers.zipf_tier(E, 40, seed=6)[0], seed=43, max_prefill=600,
+                             gemm="fp4")
+    try:
+        g = torch.Generator(device=dev).manual_seed(410)
+        calls = []
+        for layer, m in ((a, 1), (b, 32), (a, 600), (b, 4), (a, 8), (b, 600), (a, 32), (b, 1), (a, 4), (b, 8)):
+            x = torch.randn((m, H), generator=g, device=dev).to(torch.bfloat16)
+            ids, w = layer.route(torch.randn((m, E), generator=g, device=dev))
+            calls.append((layer, x, ids, w, m > 64))
+        torch.cuda.synchronize()
+
+        def run(layer, x, ids, w, prefill):
+            out = layer.forward_prefill(x, ids, w) if prefill else layer.forward(x, ids, w)
+            return out.clone()
+
+        alone = []
+        for c in calls:
+            alone.append(run(*c))
+            torch.cuda.synchronize()
+        queued = [run(*c) for c in calls]  # no synchronization between calls
+        torch.cuda.synchronize()
+        a.check_errors()
+        b.check_errors()
+        for i, (p, q) in enumerate(zip(alone, queued)):
+            assert torch.equal(p, q), f"call {i} differs when queued behind the others"
+    finally:
+        a.close()
+        b.close()

@@ -43,7 +43,9 @@ def layer(pkg, request):
 def test_static_forward_matches_forward_on_two_calls(layer):
     dev = layer.device
     g = torch.Generator(device=dev).manual_seed(123)
-    for m, dtype in ((16, torch.bfloat16), (5, torch.float16)):  # two calls in a row, different shapes
+    # calls in a row, different shapes: 16 tokens (separate combine launch), 5 (combine in the W2 epilogue),
+    # 2 (route plan and x planes in one launch on the block-scaled path)
+    for m, dtype in ((16, torch.bfloat16), (5, torch.float16), (2, torch.bfloat16)):
         x = torch.randn((m, layer.hidden), generator=g, device=dev).to(dtype)
         ids, w = layer.route(torch.randn((m, layer.num_experts), generator=g, device=dev))
         out = torch.full((m, layer.hidden), float("nan"), dtype=torch.float32, device=dev)
