@@ -704,7 +704,7 @@ static int set_iq_tables(b200moe_layer* L, int fmt, const int8_t* grid, int n_en
     for (int si = 0; si < 128; ++si)
       for (int j = 0; j < 8; ++j) t[n_entries + si] |= ((uint32_t(ksigns[si]) >> j) & 1u) << (4 * j + 2);
   if (fmt != 2) {  // the upper-half copy (layout.cuh)
-    const int half = fmt == 3 ? kIq2xsHalfWords : kIq1mHalfWords;
+    const int half = fmt == 3 ? kIq2xsGridWords : kIq1mHalfWords;  // grid words only
     const int upper = fmt == 3 ? kIq2xsUpper : kIq1mUpper;
     for (int i = 0; i < half; ++i) t[upper + i] = t[i] >> 16;
   }

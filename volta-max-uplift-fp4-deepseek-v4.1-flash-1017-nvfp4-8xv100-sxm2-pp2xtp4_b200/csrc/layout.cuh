@@ -73,17 +73,20 @@ inline BankGeom fp4_geom(int fmt, int hidden, int inter) {
 // Codebook formats of the IQ bank, by kernel format id (2, 3, 4) and GGML type.
 constexpr int kIq2xsUnitBytes = 2 * 1024 + 2 * 128 + 2 * 32;
 constexpr int kIq1mUnitBytes = 2 * 512 + 2 * 256 + 2 * 128;
-// IQ2_XS / IQ1_M tables come twice: as built, then each word shifted right by
+// IQ2_XS / IQ1_M grid words come twice: as built, then each shifted right by
 // 16 (the selector nibbles of an entry's elements 4..7), so a lane that owns
-// the upper half of its entries reads its byte-permute selectors directly.
-// The copy starts 16 words (half the banks) past the first: the two lanes that
-// read the same entry then hit different banks instead of one bank twice.
+// the upper half of its entries reads its byte-permute selectors directly
+// (IQ2_XS sign nibbles are read from the first copy only, so the second holds
+// the grid words alone).  The copy starts 16 words (half the banks) past the
+// first: the two lanes that read the same entry then hit different banks
+// instead of one bank twice.
 constexpr int kIq2xsHalfWords = 512 + 128;   // grid magnitude codes [512], sign nibbles [128]
+constexpr int kIq2xsGridWords = 512;
 constexpr int kIq1mHalfWords = 2048;         // grid value codes [2048]
 constexpr int kIqUpperPad = 16;
 constexpr int kIq2xsUpper = kIq2xsHalfWords + kIqUpperPad;  // word offset of the shifted copy
 constexpr int kIq1mUpper = kIq1mHalfWords + kIqUpperPad;
-constexpr int kIq2xsTableWords = kIq2xsUpper + kIq2xsHalfWords;
+constexpr int kIq2xsTableWords = kIq2xsUpper + kIq2xsGridWords;
 constexpr int kIq1mTableWords = kIq1mUpper + kIq1mHalfWords;
 constexpr int kGgmlIq2xxs = 16, kGgmlIq2xs = 17, kGgmlIq1m = 29;
 
