@@ -687,3 +687,51 @@ def test_back_to_back_calls_match_isolated_calls(dev, pkg):
     finally:
         a.close()
         b.close()
+
+
+_PLAIN_LAUNCH_SCRIPT = r"""
+import sys, numpy as np, torch
+for sub in ("", "/tests", "/tests/golden"):
+    sys.path.insert(0, sys.argv[1] + sub)
+from __graft_entry__ import load_package
+load_package()
+from test_gpu_parity import _make_layer
+dev = torch.device("cuda", 0)
+layer, _, _, _ = _make_layer(dev, 2048, 1024, 64, 8, 64, seed=51, gemm="fp4")
+g = torch.Generator(device=dev).manual_seed(510)
+outs = []
+for m in (1, 8, 64):
+    x = torch.randn((m, 2048), generator=g, device=dev).to(torch.bfloat16)
+    ids, w = layer.route(torch.randn((m, 64), generator=g, device=dev))
+    outs.append(layer.forward(x, ids, w).clone().cpu().numpy())
+layer.check_errors()
+np.savez(sys.argv[2], *outs)
+"""
+
+
+def test_plain_launches_give_the_same_bits(dev, pkg, tmp_path):
+    """B200MOE_PDL=0 launches every forward kernel without programmatic stream
+    serialization (read once per process): a child process run that way gives
+    the bits of this process's programmatic launches, at 1, 8 and 64 tokens."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    out = tmp_path / "plain.npz"
+    env = dict(os.environ, B200MOE_PDL="0")
+    subprocess.run([sys.executable, "-c", _PLAIN_LAUNCH_SCRIPT, str(root), str(out)], env=env, check=True,
+                   timeout=600)
+    plain = np.load(out)
+    layer, _, _, _ = _make_layer(dev, 2048, 1024, 64, 8, 64, seed=51, gemm="fp4")
+    try:
+        g = torch.Generator(device=dev).manual_seed(510)
+        for i, m in enumerate((1, 8, 64)):
+            x = torch.randn((m, 2048), generator=g, device=dev).to(torch.bfloat16)
+            ids, w = layer.route(torch.randn((m, 64), generator=g, device=dev))
+            got = layer.forward(x, ids, w).clone().cpu().numpy()
+            assert np.array_equal(got.view(np.uint32), plain[f"arr_{i}"].view(np.uint32)), m
+        layer.check_errors()
+    finally:
+        layer.close()
