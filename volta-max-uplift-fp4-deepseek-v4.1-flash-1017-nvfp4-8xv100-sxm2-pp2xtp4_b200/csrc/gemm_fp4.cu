@@ -454,32 +454,38 @@ __global__ void __launch_bounds__(kPlaneThreads) fp4_planes_kernel(
 // --------------------------------------------------------------- combine
 // out[t] = sum over slots, in slot order, of fma(f32(y2[route]), w[route]):
 // the fused combine's arithmetic, with a route that has no expert (sorted
-// past the last bank, inv[route] >= end) taken as a zero row.  Thread: 4
-// consecutive columns of a token.
+// past the last bank, inv[route] >= end) taken as a zero row.  Thread: 8
+// consecutive columns of a token (one 16-byte load per route).
 __global__ void fp4_combine_kernel(const __half* __restrict__ y2, const int32_t* __restrict__ inv,
                                    const int32_t* __restrict__ bank_range, int n_banks, const float* __restrict__ w,
                                    int T, int k, int H, float* __restrict__ out) {
-  const int per_row = H / 4;
+  const int per_row = H / 8;  // 8 columns (one 16-byte load of y2) per thread
   pdl_wait();
   pdl_trigger();
   const int end = bank_range[2 * (n_banks - 1) + 1];
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < int64_t(T) * per_row;
        i += int64_t(gridDim.x) * blockDim.x) {
-    const int t = int(i / per_row), c = int(i % per_row) * 4;
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    const int t = int(i / per_row), c = int(i % per_row) * 8;
+    float sum[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sum[e] = 0.f;
+#pragma unroll 4
     for (int slot = 0; slot < k; ++slot) {
       const int route = t * k + slot;
       const float wr = w[route];
-      uint2 v = make_uint2(0u, 0u);
-      if (inv[route] < end) v = *reinterpret_cast<const uint2*>(y2 + int64_t(route) * H + c);
-      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
-      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
-      s0 = __fmaf_rn(a.x, wr, s0);
-      s1 = __fmaf_rn(a.y, wr, s1);
-      s2 = __fmaf_rn(b.x, wr, s2);
-      s3 = __fmaf_rn(b.y, wr, s3);
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (inv[route] < end) v = *reinterpret_cast<const uint4*>(y2 + int64_t(route) * H + c);
+      const uint32_t h[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h[e]));
+        sum[2 * e] = __fmaf_rn(f.x, wr, sum[2 * e]);
+        sum[2 * e + 1] = __fmaf_rn(f.y, wr, sum[2 * e + 1]);
+      }
     }
-    *reinterpret_cast<float4*>(out + int64_t(t) * H + c) = make_float4(s0, s1, s2, s3);
+    float4* o = reinterpret_cast<float4*>(out + int64_t(t) * H + c);
+    o[0] = make_float4(sum[0], sum[1], sum[2], sum[3]);
+    o[1] = make_float4(sum[4], sum[5], sum[6], sum[7]);
   }
 }
 
@@ -602,8 +608,8 @@ int launch_fp4_planes(cudaStream_t s, bool by_token, bool bf16, bool mx, const v
 
 int launch_route_combine(cudaStream_t s, const __half* y2, const int32_t* inv, const int32_t* bank_range,
                          int n_banks, const float* w, int T, int k, int H, float* out) {
-  if (H % 4 || T < 1) return -1;
-  const int64_t n = int64_t(T) * (H / 4);
+  if (H % 8 || T < 1) return -1;
+  const int64_t n = int64_t(T) * (H / 8);
   const int blocks = int(std::min<int64_t>((n + 255) / 256, 148 * 16));
   return launch_chain(fp4_combine_kernel, dim3(std::max(blocks, 1)), dim3(256), 0, s, y2, inv, bank_range, n_banks,
                       w, T, k, H, out) == cudaSuccess
