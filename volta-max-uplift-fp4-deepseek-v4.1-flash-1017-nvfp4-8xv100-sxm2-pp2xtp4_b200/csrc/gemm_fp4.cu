@@ -469,18 +469,33 @@ __global__ void fp4_combine_kernel(const __half* __restrict__ y2, const int32_t*
     float sum[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) sum[e] = 0.f;
-#pragma unroll 4
-    for (int slot = 0; slot < k; ++slot) {
-      const int route = t * k + slot;
-      const float wr = w[route];
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (inv[route] < end) v = *reinterpret_cast<const uint4*>(y2 + int64_t(route) * H + c);
-      const uint32_t h[4] = {v.x, v.y, v.z, v.w};
+    // eight slots at a time: their positions and weights, then their rows, are loaded before the first add
+    for (int s0 = 0; s0 < k; s0 += 8) {
+      const int ns = min(8, k - s0);
+      int pos[8];
+      float wr[8];
+      uint4 v[8];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h[e]));
-        sum[2 * e] = __fmaf_rn(f.x, wr, sum[2 * e]);
-        sum[2 * e + 1] = __fmaf_rn(f.y, wr, sum[2 * e + 1]);
+      for (int j = 0; j < 8; ++j)
+        if (j < ns) {
+          pos[j] = inv[t * k + s0 + j];
+          wr[j] = w[t * k + s0 + j];
+        }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[j] = make_uint4(0u, 0u, 0u, 0u);
+        if (j < ns && pos[j] < end) v[j] = *reinterpret_cast<const uint4*>(y2 + int64_t(t * k + s0 + j) * H + c);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (j >= ns) break;
+        const uint32_t h[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h[e]));
+          sum[2 * e] = __fmaf_rn(f.x, wr[j], sum[2 * e]);
+          sum[2 * e + 1] = __fmaf_rn(f.y, wr[j], sum[2 * e + 1]);
+        }
       }
     }
     float4* o = reinterpret_cast<float4*>(out + int64_t(t) * H + c);

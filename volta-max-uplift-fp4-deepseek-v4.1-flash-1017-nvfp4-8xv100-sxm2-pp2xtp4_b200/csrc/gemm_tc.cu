@@ -573,35 +573,55 @@ int launch_tc_gemm(cudaStream_t s, int fmt, int epi, const TcArgs& a, const void
 }
 
 // ---------------------------------------------------- permuted fp16 rows
-// xperm[p] = fp16(x[perm[p] / k]) for p < S (x fp16 or bf16).
-__global__ void gather_rows_kernel(const uint16_t* __restrict__ x, int bf16, const int32_t* __restrict__ perm,
-                                   int S, int k, int H, uint16_t* __restrict__ xperm) {
+// xperm[p] = fp16(x[perm[p] / k]) for p < S (x fp16 or bf16).  One warp per sorted row: the row's token is
+// one load, then the lanes issue all of a 4 KB slice's 16-byte loads before the first store, so each warp keeps
+// the slice in flight instead of one dependent perm -> x -> store chain per thread.
+__device__ __forceinline__ uint4 row_to_f16(uint4 v, int bf16) {
+  if (!bf16) return v;
+  uint32_t in[4] = {v.x, v.y, v.z, v.w}, o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    __half2 h2 = __floats2half2_rn(__uint_as_float(in[j] << 16), __uint_as_float(in[j] & 0xffff0000u));
+    o[j] = *reinterpret_cast<uint32_t*>(&h2);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+constexpr int kGatherThreads = 256;
+
+__global__ void __launch_bounds__(kGatherThreads) gather_rows_kernel(const uint16_t* __restrict__ x, int bf16,
+                                                                     const int32_t* __restrict__ perm, int S, int k,
+                                                                     int H, uint16_t* __restrict__ xperm) {
+  constexpr int kU = 8;  // 16-byte loads in flight per lane
   const int per_row = H / 8;
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (kGatherThreads / 32);
   pdl_wait();
   pdl_trigger();
-  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < int64_t(S) * per_row;
-       i += int64_t(gridDim.x) * blockDim.x) {
-    const int p = int(i / per_row), c = int(i % per_row);
-    const int tok = perm[p] / k;
-    uint4 v = reinterpret_cast<const uint4*>(x + int64_t(tok) * H)[c];
-    if (bf16) {
-      uint32_t in[4] = {v.x, v.y, v.z, v.w}, o[4];
+  for (int p = blockIdx.x * (kGatherThreads / 32) + threadIdx.x / 32; p < S; p += warps) {
+    const uint4* src = reinterpret_cast<const uint4*>(x + int64_t(perm[p] / k) * H);
+    uint4* dst = reinterpret_cast<uint4*>(xperm + int64_t(p) * H);
+    for (int c0 = 0; c0 < per_row; c0 += 32 * kU) {
+      uint4 v[kU];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        __half2 h2 = __floats2half2_rn(__uint_as_float(in[j] << 16), __uint_as_float(in[j] & 0xffff0000u));
-        o[j] = *reinterpret_cast<uint32_t*>(&h2);
+      for (int u = 0; u < kU; ++u) {
+        const int c = c0 + 32 * u + lane;
+        if (c < per_row) v[u] = src[c];
       }
-      v = make_uint4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int c = c0 + 32 * u + lane;
+        if (c < per_row) dst[c] = row_to_f16(v[u], bf16);
+      }
     }
-    reinterpret_cast<uint4*>(xperm + int64_t(p) * H)[c] = v;
   }
 }
 
 int launch_gather_rows(cudaStream_t s, const void* x, int bf16, const int32_t* perm, int S, int k, int H,
                        void* xperm) {
-  int64_t n = int64_t(S) * (H / 8);
-  int blocks = int(std::min<int64_t>((n + 255) / 256, 148 * 16));
-  return launch_chain(gather_rows_kernel, dim3(blocks < 1 ? 1 : blocks), dim3(256), 0, s,
+  const int rows_per_block = kGatherThreads / 32;
+  const int blocks = std::min((S + rows_per_block - 1) / rows_per_block, 148 * 8);
+  return launch_chain(gather_rows_kernel, dim3(blocks < 1 ? 1 : blocks), dim3(kGatherThreads), 0, s,
                       static_cast<const uint16_t*>(x), bf16, perm, S, k, H, static_cast<uint16_t*>(xperm)) ==
                  cudaSuccess
              ? 0
