@@ -103,7 +103,7 @@ __device__ __forceinline__ int plan_key(const PlanArgs& a, int i, int sentinel) 
 
 // The lanes of this warp whose key equals this lane's (keys in [0, 2^bits), or -1 for no route): the bit-by-bit
 // ballot split of a radix multisplit, a vote per key bit instead of one match.any, which serialises over the
-// distinct keys (measured on B200 at 32,768 routes over 385 keys: each pass 40 against 6 us).
+// distinct keys (measured on B200, one CTA planning 32,768 routes over 385 keys: 76 against 95 us).
 __device__ __forceinline__ unsigned warp_match_key(int key, int bits) {
   const unsigned valid = __ballot_sync(0xffffffffu, key >= 0);
   unsigned m = key >= 0 ? valid : ~valid;
