@@ -135,23 +135,35 @@ __device__ __forceinline__ void plan_keys(const PlanArgs& a, int base0, int stri
 
 // Routes per chunk for the split-K with the least modelled time, given the
 // bank's chunk counts at 16, 8, 4 and 2 routes per chunk.
-__device__ __forceinline__ int model_rc(const KsModel& m, const int (&chunks_at)[4]) {
+// Modelled time of split-K ks = 2^j for a bank with `chunks_j` chunks at 16 >> j routes per chunk.
+__device__ __forceinline__ float model_t(const KsModel& m, int j, int chunks_j) {
+  const int ks = 1 << j;
+  const float chunks = fmaxf(1.f, float(chunks_j));
+  float t = 0.f;
+  for (int p = 0; p < 2; ++p) {
+    const float items = chunks * m.tiles[p] / (8.f / ks);
+    const float bytes = (8.f / ks) * m.kdim[p] * m.bpe;
+    const float waves = ceilf(items / m.slots);
+    t += waves * (fmaxf(bytes / m.bw_cta, fminf(items, m.slots) * bytes / m.bw_hbm) + m.per_wave);
+  }
+  return t;
+}
+
+// Called by a whole warp: lanes j = lane & 3 model the four split-Ks side by side (the divisions of one
+// thread's four models in a row were a microsecond on the plan's critical path), then every lane picks the
+// first allowed one with the least time.
+__device__ __forceinline__ int model_rc_warp(const KsModel& m, int c0, int c1, int c2, int c3) {
+  const int jm = threadIdx.x & 3;
+  const float tm = model_t(m, jm, jm == 0 ? c0 : jm == 1 ? c1 : jm == 2 ? c2 : c3);
   int best = 1;
   float best_t = 3.0e38f;
+#pragma unroll
   for (int j = 0; j < 4; ++j) {
+    const float t = __shfl_sync(0xffffffffu, tm, j);
     if (!(m.allowed >> j & 1)) continue;
-    const int ks = 1 << j;
-    const float chunks = fmaxf(1.f, float(chunks_at[j]));
-    float t = 0.f;
-    for (int p = 0; p < 2; ++p) {
-      const float items = chunks * m.tiles[p] / (8.f / ks);
-      const float bytes = (8.f / ks) * m.kdim[p] * m.bpe;
-      const float waves = ceilf(items / m.slots);
-      t += waves * (fmaxf(bytes / m.bw_cta, fminf(items, m.slots) * bytes / m.bw_hbm) + m.per_wave);
-    }
     if (t < best_t * 0.999999f) {
       best_t = t;
-      best = ks;
+      best = 1 << j;
     }
   }
   return kRouteSlotsPerChunk / best;
@@ -216,7 +228,7 @@ __device__ void plan_small(const PlanArgs& a, int n, int sentinel) {
       at[j] = v;
     }
     int rc = a.rc[b];
-    if (rc == 0) rc = model_rc(a.ks_model[b], at);
+    if (rc == 0) rc = model_rc_warp(a.ks_model[b], at[0], at[1], at[2], at[3]);
     if (lane == 0 && a.ks_sel) a.ks_sel[b] = max(1, kRouteSlotsPerChunk / rc);
     const int lo = __popc(__ballot_sync(full, lane < n && pkey < a.key_lo[b]));
     const int hi = __popc(__ballot_sync(full, lane < n && pkey < a.key_hi[b]));
@@ -333,10 +345,19 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanArgs a) {
   const int len = r_hi - r_lo;
   const int per_warp = ((len + 31) / 32 + 31) / 32 * 32;
   const int wlo = r_lo + min(len, warp * per_warp), whi = min(r_hi, wlo + per_warp);
+  // a warp with at most kBatch batches keeps their keys and weights in registers from pass 1 to pass 2
+  const bool cached = per_warp <= 32 * kBatch;
+  int keys[kBatch];
+  float wv[kBatch];  // the routes' weights, loaded before the scatter's stores
+  auto load_weights = [&](int base0) {
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u)
+      wv[u] = product && a.w_eff && keys[u] >= 0 && keys[u] < a.n_keys ? a.w_in[base0 + 32 * u + lane] : 0.f;
+  };
   // pass 1: per-warp key counts, eight 32-route batches at a time (plan_keys)
   for (int base0 = wlo; base0 < whi; base0 += 32 * kBatch) {
-    int keys[kBatch];
     plan_keys<kBatch>(a, base0, 32, whi, lane, sentinel, keys);
+    if (cached) load_weights(base0);
 #pragma unroll
     for (int u = 0; u < kBatch; ++u) {
       if (base0 + 32 * u >= whi) break;  // warp-uniform
@@ -362,12 +383,10 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanArgs a) {
   block_exclusive_scan(start, nk, wsum);
   // pass 2: stable scatter (the same batches, keys looked up ahead)
   for (int base0 = wlo; base0 < whi; base0 += 32 * kBatch) {
-    int keys[kBatch];
-    plan_keys<kBatch>(a, base0, 32, whi, lane, sentinel, keys);
-    float wv[kBatch];  // the routes' weights, loaded before this batch's stores
-#pragma unroll
-    for (int u = 0; u < kBatch; ++u)
-      wv[u] = product && a.w_eff && keys[u] >= 0 && keys[u] < a.n_keys ? a.w_in[base0 + 32 * u + lane] : 0.f;
+    if (!cached) {
+      plan_keys<kBatch>(a, base0, 32, whi, lane, sentinel, keys);
+      load_weights(base0);
+    }
 #pragma unroll
     for (int u = 0; u < kBatch; ++u) {
       if (base0 + 32 * u >= whi) break;  // warp-uniform
@@ -437,17 +456,19 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanArgs a) {
         }
       }
     __syncthreads();
-    if (tid < a.n_banks) {
-      const int b = tid;
-      int rc = a.rc[b];
-      if (rc == 0) rc = model_rc(a.ks_model[b], st[b]);  // split-K of this bank from this plan's chunk counts
-      rc_sel[b] = rc;
-      if (a.ks_sel) a.ks_sel[b] = max(1, kRouteSlotsPerChunk / rc);
-      if (a.bank_range) {
-        a.bank_range[2 * b] = start[a.key_lo[b]];
-        a.bank_range[2 * b + 1] = start[a.key_hi[b]];
+    if (warp == 0)
+      for (int b = 0; b < a.n_banks; ++b) {
+        int rc = a.rc[b];
+        if (rc == 0) rc = model_rc_warp(a.ks_model[b], st[b][0], st[b][1], st[b][2], st[b][3]);  // split-K of
+        if (lane == 0) {                                                                          // this bank
+          rc_sel[b] = rc;
+          if (a.ks_sel) a.ks_sel[b] = max(1, kRouteSlotsPerChunk / rc);
+          if (a.bank_range) {
+            a.bank_range[2 * b] = start[a.key_lo[b]];
+            a.bank_range[2 * b + 1] = start[a.key_hi[b]];
+          }
+        }
       }
-    }
     __syncthreads();
   }
 
@@ -455,6 +476,10 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanArgs a) {
     // route chunks of every bank: ceil(count / rc) chunks per non-empty key
     for (int b = 0; b < a.n_banks; ++b) {
       const int lo = a.key_lo[b], hi = a.key_hi[b], rc = rc_sel[b];
+      if (hi <= lo) {  // a bank without keys has no chunks
+        if (tid == 0) a.n_chunks[b] = 0;
+        continue;
+      }
       int* nch = hist;  // hist is free now: reuse as [nk]
       for (int key = tid; key < nk; key += kPlanThreads)
         nch[key] = (key >= lo && key < hi) ? (aux[key] + rc - 1) / rc : 0;
