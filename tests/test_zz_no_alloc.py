@@ -58,6 +58,35 @@ def test_static_forward_matches_forward_on_two_calls(layer):
         assert torch.equal(got, want)  # same kernels, same order: bit-equal in practice
 
 
+def test_static_forward_graph_replay(layer):
+    """forward_static captured in a CUDA graph (its array's address is looked
+    up when the layer is made, so no call has to come first outside a
+    capture): every replay gives the eager call's bits."""
+    dev = layer.device
+    g = torch.Generator(device=dev).manual_seed(321)
+    m = 8
+    x = torch.randn((m, layer.hidden), generator=g, device=dev).to(torch.bfloat16)
+    ids, w = layer.route(torch.randn((m, layer.num_experts), generator=g, device=dev))
+    eager = layer.forward_static(x, ids, w, torch.empty((m, layer.hidden), dtype=torch.float32, device=dev)).clone()
+    layer.check_errors()
+    out = torch.full((m, layer.hidden), float("nan"), dtype=torch.float32, device=dev)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        layer.forward_static(x, ids, w, out)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        layer.forward_static(x, ids, w, out)
+    for _ in range(3):
+        out.fill_(float("nan"))
+        graph.replay()
+    torch.cuda.synchronize()
+    layer.check_errors()
+    assert torch.equal(out, eager)
+    del graph
+
+
 def test_static_forward_refuses_sizes_beyond_its_array(layer):
     from b200moe import _lib
 
