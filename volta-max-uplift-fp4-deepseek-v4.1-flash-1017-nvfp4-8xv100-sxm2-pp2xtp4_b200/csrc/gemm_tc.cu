@@ -122,11 +122,6 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// Byte offset of (row, 16-byte chunk) in a K-major 128B-swizzled [rows x 64 f16] tile.
-__device__ __forceinline__ uint32_t sw128_off(int row, int chunk) {
-  return uint32_t((row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4));
-}
-
 __device__ __forceinline__ __half swiglu1(float g, float u, float limit) {
   g = g > limit ? limit : g;
   u = u > limit ? limit : u;
